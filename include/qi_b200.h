@@ -1,0 +1,120 @@
+/*
+ * qi_b200 — C ABI of the B200-native (sm_100a) quantized-linear kernels.
+ *
+ * Drop-in boundary for hongzicong/qi's quantized nn.Linear hot path.  Each
+ * entry point below names the reference interface it replaces (paths inside
+ * the reference project, src/qi/quantization/...).
+ *
+ * Conventions shared by every entry point:
+ *   - all pointers are device pointers on the current CUDA device; tensors
+ *     are dense row-major; bf16 = IEEE bfloat16 bits, fp8 = E4M3 ("fn")
+ *     codes, int8 = two's complement;
+ *   - work is enqueued on `stream`; nothing synchronizes, nothing allocates
+ *     (callers own every buffer), so calls can be captured in CUDA graphs;
+ *   - the return value is a status code (QI_B200_OK = 0); a non-zero code
+ *     means nothing was enqueued, except QI_B200_ECUDA which reports a launch
+ *     error from the CUDA runtime;
+ *   - device-side pipeline waits are bounded; a wait that runs out of time
+ *     records its site in the device status word (qi_b200_device_status) and
+ *     the kernel returns instead of hanging.
+ */
+#ifndef QI_B200_H_
+#define QI_B200_H_
+
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QI_B200_ABI_VERSION 1
+
+/* status codes */
+#define QI_B200_OK 0
+#define QI_B200_EINVAL 1  /* null pointer, bad enum or flag */
+#define QI_B200_ESHAPE 2  /* unsupported dimensions */
+#define QI_B200_EALIGN 3  /* pointer not 16-byte aligned */
+#define QI_B200_ECUDA 4   /* CUDA runtime reported a launch error */
+#define QI_B200_ETMAP 5   /* TMA descriptor could not be encoded */
+#define QI_B200_EARCH 6   /* current device is not sm_100 */
+#define QI_B200_ETOOBIG 7 /* size above an entry point's fixed maximum */
+
+/* GEMM operand kinds for qi_b200_gemm */
+#define QI_B200_KIND_INT8 0     /* int8 x int8 -> int32 (tcgen05 kind::i8) */
+#define QI_B200_KIND_FP8_E4M3 1 /* e4m3 x e4m3 -> fp32 (kind::f8f6f4)      */
+#define QI_B200_KIND_BF16 2     /* bf16 x bf16 -> fp32 (kind::f16)         */
+
+/* epilogue flags for qi_b200_gemm / qi_b200_fp8_linear */
+#define QI_B200_EPI_GELU 1    /* GELU(tanh) of the bf16-rounded linear output */
+#define QI_B200_EPI_RAW_ACC 2 /* store raw 32-bit accumulators instead of bf16 (debug) */
+
+int qi_b200_abi_version(void);
+const char* qi_b200_error_string(int code);
+
+/* Device status word of the current device: out4[0] = error (0 none, 1 a
+ * bounded wait timed out), out4[1] = kernel tag, out4[2] = wait site,
+ * out4[3] = block index.  Synchronous (reads device memory); not for use
+ * inside stream capture.  clear != 0 resets it. */
+int qi_b200_device_status(unsigned int* out4, int clear);
+
+/* ---- activation quantizers --------------------------------------------
+ * Replaces qi_quantize_int8_rowwise (csrc/int8_w8a8/quantize_int8.cuh:7-13,
+ * kernel quantize_int8.cu:7-59): per row s = max(amax/127, 1e-10),
+ * q = clamp(rint(x * (1/s)), -127, 127) (IEEE reciprocal). */
+int qi_b200_quantize_int8_rowwise(const void* x_bf16, void* q_int8, float* scales, int rows, int cols,
+                                  cudaStream_t stream);
+
+/* Per-token FP8: s = max(amax/448, 1e-12), q = e4m3_rn(clamp(x/s, +-448)).
+ * Generalises backends/flashrt_fp8_ops.py:38-48 (per tensor) to per row. */
+int qi_b200_quantize_fp8_rowwise(const void* x_bf16, void* q_fp8, float* scales, int rows, int cols,
+                                 cudaStream_t stream);
+
+/* Static per-tensor FP8 with a calibrated device scale; replaces FlashRT's
+ * quantize_fp8_static as called at backends/flashrt_fp8_ops.py:210-216. */
+int qi_b200_quantize_fp8_static(const void* x_bf16, const float* scale, void* q_fp8, int rows, int cols,
+                                cudaStream_t stream);
+
+/* ---- GEMMs -------------------------------------------------------------
+ * Replaces qi_cutlass_int8_rowwise_bf16out / _bias (csrc/int8_w8a8/
+ * bindings.cpp:20-85, kernels cutlass_int8_rowwise*.cu):
+ *   D[M,N] = bf16( (float(sum_k A[m,k] B[n,k]) * act_scale[m]) * weight_scale[n] (+ bias[n]) )
+ * A int8 [M,K], B int8 [N,K] (nn.Linear weight), scales fp32, bias/D bf16.
+ * Needs N % 8 == 0, K % 16 == 0 (the reference needs N, K % 64 == 0). */
+int qi_b200_int8_rowwise_bf16out(const void* A, const void* B, const void* act_scale, const void* weight_scale,
+                                 void* D, int M, int N, int K, cudaStream_t stream);
+int qi_b200_int8_rowwise_bf16out_bias(const void* A, const void* B, const void* act_scale, const void* weight_scale,
+                                      const void* bias, void* D, int M, int N, int K, cudaStream_t stream);
+
+/* General form of the GEMM above for every operand kind (replaces the
+ * tile-specific variants _t64x128/_t64x256/_t32x128/_t128x64 of
+ * bindings.cpp:31-85 and FlashRT's GemmRunner.fp8_run_dev called at
+ * backends/flashrt_fp8_ops.py:68-89):
+ *   D[m, n] (row stride ldd) = epi( acc[m,n] * a_scale[m*a_scale_stride] * b_scale[n*b_scale_stride] + bias[n] )
+ * a_scale / b_scale / bias may be NULL; a stride of 0 broadcasts one scale.
+ * tile_n = 0 picks the tile width; 64, 128 or 256 forces one. */
+int qi_b200_gemm(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
+                 const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd, int M, int N,
+                 int K, int flags, int tile_n, cudaStream_t stream);
+
+/* ---- whole quantized linears -----------------------------------------
+ * Replaces the torch op qi_int8_w8a8::linear (csrc/int8_w8a8/bindings.cpp:
+ * 87-157, schema :159-165): quantize x per token into the caller's
+ * workspace (ws_q int8 [M,K], ws_scales fp32 [M]) then run the INT8 GEMM. */
+int qi_b200_int8_linear(const void* x_bf16, const void* qweight, const float* weight_scale, const void* bias,
+                        void* out_bf16, void* ws_q, float* ws_scales, int M, int N, int K, cudaStream_t stream);
+
+/* Replaces FlashRTFP8Backend.linear's device work (backends/flashrt_fp8_ops.py:
+ * 207-229): static per-tensor (static_act_scale != NULL) or dynamic per-token
+ * (static_act_scale == NULL, scales into ws_scales) activation quantization,
+ * then the FP8 GEMM with per-tensor or per-channel weight scales, bias and
+ * optional GELU fused into the epilogue. */
+int qi_b200_fp8_linear(const void* x_bf16, const void* weight_fp8, const float* weight_scale,
+                       int weight_scale_per_channel, const float* static_act_scale, const void* bias,
+                       void* out_bf16, void* ws_q, float* ws_scales, int M, int N, int K, int flags,
+                       cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QI_B200_H_ */

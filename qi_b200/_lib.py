@@ -1,0 +1,99 @@
+"""Loader for ``libqi_b200.so`` (the C ABI in ``include/qi_b200.h``).
+
+The library is found next to this file (built in-tree by
+``python -m qi_b200.build``).  There is no fallback: if the library is
+missing or the device is not a B200, calls raise ``QiB200Unavailable``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libqi_b200.so"
+
+# status codes (include/qi_b200.h)
+OK, EINVAL, ESHAPE, EALIGN, ECUDA, ETMAP, EARCH, ETOOBIG = range(8)
+KIND_INT8, KIND_FP8_E4M3, KIND_BF16 = 0, 1, 2
+EPI_GELU, EPI_RAW_ACC = 1, 2
+
+
+class QiB200Unavailable(RuntimeError):
+    """The native library is missing or cannot run on this device."""
+
+
+class QiB200Error(RuntimeError):
+    """A C-ABI entry point returned a non-zero status."""
+
+    def __init__(self, fn: str, code: int, msg: str):
+        super().__init__(f"{fn} failed with status {code}: {msg}")
+        self.code = code
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_LL = ctypes.c_longlong
+
+# name -> argtypes (restype is int unless listed in _RESTYPES)
+SIGNATURES = {
+    "qi_b200_abi_version": [],
+    "qi_b200_error_string": [_I],
+    "qi_b200_device_status": [_P, _I],
+    "qi_b200_quantize_int8_rowwise": [_P, _P, _P, _I, _I, _P],
+    "qi_b200_quantize_fp8_rowwise": [_P, _P, _P, _I, _I, _P],
+    "qi_b200_quantize_fp8_static": [_P, _P, _P, _I, _I, _P],
+    "qi_b200_int8_rowwise_bf16out": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
+    "qi_b200_int8_rowwise_bf16out_bias": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
+    "qi_b200_gemm": [_I, _P, _P, _P, _I, _P, _I, _P, _P, _LL, _I, _I, _I, _I, _I, _P],
+    "qi_b200_int8_linear": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
+    "qi_b200_fp8_linear": [_P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
+}
+_RESTYPES = {"qi_b200_error_string": ctypes.c_char_p}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load(path: Path | None = None) -> ctypes.CDLL:
+    """Load the library once (thread-safe) and bind every declared symbol."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path is not None else LIB_PATH
+        if not p.exists():
+            raise QiB200Unavailable(
+                f"{p} is missing; build it with `python -m qi_b200.build` (nvcc, sm_100a)."
+            )
+        lib = ctypes.CDLL(str(p))
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = _RESTYPES.get(name, ctypes.c_int)
+        if lib.qi_b200_abi_version() != 1:
+            raise QiB200Unavailable("libqi_b200 ABI version mismatch")
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def check(fn_name: str, rc: int) -> None:
+    if rc != OK:
+        msg = load().qi_b200_error_string(rc).decode()
+        if rc == EARCH:
+            raise QiB200Unavailable(f"{fn_name}: {msg}")
+        raise QiB200Error(fn_name, rc, msg)
+
+
+def call(fn_name: str, *args) -> None:
+    """Call a C-ABI entry point and raise on a non-zero status."""
+    check(fn_name, getattr(load(), fn_name)(*args))
+
+
+def device_status(clear: bool = False) -> tuple[int, int, int, int]:
+    buf = (ctypes.c_uint * 4)()
+    check("qi_b200_device_status", load().qi_b200_device_status(ctypes.cast(buf, _P), int(clear)))
+    return tuple(int(v) for v in buf)

@@ -1,0 +1,320 @@
+// Persistent, warp-specialized tcgen05 GEMM with a fused dequantization
+// epilogue:  D[M,N] = epilogue( A[M,K] . B[N,K]^T ).
+//
+//   A: activations, K-major (row-major [M,K]);  B: nn.Linear weight, K-major
+//   ([N,K] row-major, i.e. the column-major B operand of the GEMM).
+//
+// Roles (256 threads, one CTA per SM, grid = min(#tiles, #SMs)):
+//   warp 0      TMA producer: 128-byte-swizzled A and B tiles into a ring of
+//               STAGES shared-memory stages (cp.async.bulk.tensor, no multicast)
+//   warp 1      TMEM allocator + single-thread MMA issuer (tcgen05.mma, M=128,
+//               N=BN, accumulators in tensor memory, double buffered so the
+//               epilogue of tile i overlaps the main loop of tile i+1)
+//   warps 4..7  epilogue: tcgen05.ld 32 columns at a time, apply per-token /
+//               per-channel scales, bias and optional GELU in fp32, store bf16
+//
+// Kinds: kind::i8 (int8 x int8 -> s32), kind::f8f6f4 (e4m3 x e4m3 -> f32),
+// kind::f16 (bf16 x bf16 -> f32).
+//
+// INT8 epilogue reproduces the reference EVT (cutlass_int8_rowwise.cu:43-71):
+//   y = bf16_rn( fp32( fp32( float(acc) * s_tok[m] ) * s_ch[n] ) + bias[n] ).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "sm100_ptx.cuh"
+
+namespace qib {
+
+enum class MmaKind : int { I8 = 0, F8 = 1, BF16 = 2 };
+
+// epilogue flags
+constexpr int kEpiGelu = 1;     // GELU(tanh) of the bf16-rounded linear output
+constexpr int kEpiRawAcc = 2;   // debug: store raw 32-bit accumulators (int32 / fp32), ld = ldd
+
+struct EpiParams {
+  const float* sa;  // per-row (token) scale, or nullptr (= 1)
+  int sa_stride;    // 0 = one scale for all rows
+  const float* sb;  // per-column (channel) scale, or nullptr (= 1)
+  int sb_stride;    // 0 = one scale for all columns
+  const __nv_bfloat16* bias;  // [N] or nullptr
+  void* D;                    // bf16 [M, ldd] (or 32-bit [M, ldd] with kEpiRawAcc)
+  long long ldd;
+  int M, N, K;
+  int flags;
+};
+
+template <MmaKind KIND, int BN_, int STAGES_>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BN = BN_;
+  static constexpr int STAGES = STAGES_;
+  static constexpr int ELEM = (KIND == MmaKind::BF16) ? 2 : 1;
+  static constexpr int BK = 128 / ELEM;                          // one 128-B swizzle row per operand row
+  static constexpr int UMMA_K = (KIND == MmaKind::BF16) ? 16 : 32;  // 32 bytes of K per MMA
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int ACC_COLS = BN;  // fp32/s32 accumulator: one TMEM column per output column
+  static constexpr int TMEM_COLS = (2 * ACC_COLS <= 32) ? 32 : (2 * ACC_COLS <= 64) ? 64 : (2 * ACC_COLS <= 128) ? 128 : (2 * ACC_COLS <= 256) ? 256 : 512;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;  // + alignment slack
+  static constexpr uint32_t IDESC =
+      (KIND == MmaKind::I8)   ? make_idesc(kDS32, kFmtS8, kFmtS8, BM, BN)
+      : (KIND == MmaKind::F8) ? make_idesc(kDF32, kFmtE4M3, kFmtE4M3, BM, BN)
+                              : make_idesc(kDF32, kFmtBF16, kFmtBF16, BM, BN);
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  static_assert(2 * ACC_COLS <= 512, "TMEM");
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
+};
+
+__device__ __forceinline__ float gelu_tanh_f32(float v) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
+  const float k1 = 0.044715f;
+  float inner = k0 * (v + k1 * v * v * v);
+  return 0.5f * v * (1.0f + tanhf(inner));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <MmaKind KIND>
+__device__ __forceinline__ void mma_issue(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  if constexpr (KIND == MmaKind::I8) mma_i8(d, a, b, idesc, acc);
+  else if constexpr (KIND == MmaKind::F8) mma_f8(d, a, b, idesc, acc);
+  else mma_bf16(d, a, b, idesc, acc);
+}
+
+// Epilogue for one 32-column chunk of one row (this thread's row).
+template <MmaKind KIND>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], const EpiParams& p, int m, int n0,
+                                               float sa) {
+  if (p.flags & kEpiRawAcc) {
+    uint32_t* drow = static_cast<uint32_t*>(p.D) + static_cast<long long>(m) * p.ldd;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      if (n0 + j < p.N) *reinterpret_cast<uint4*>(drow + n0 + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+    }
+    return;
+  }
+  float y[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float v;
+    if constexpr (KIND == MmaKind::I8) v = __int2float_rn(static_cast<int>(r[j]));
+    else v = __uint_as_float(r[j]);
+    y[j] = v;
+  }
+  const int n_valid = p.N - n0;  // >= 1; multiple of 8 when < 32 (N % 8 == 0)
+  if (KIND != MmaKind::BF16 || p.sa != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) y[j] = __fmul_rn(y[j], sa);
+  }
+  if (p.sb != nullptr) {
+    if (p.sb_stride == 0) {
+      const float s = __ldg(p.sb);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) y[j] = __fmul_rn(y[j], s);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        float4 s4 = (j < n_valid) ? __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        y[j] = __fmul_rn(y[j], s4.x);
+        y[j + 1] = __fmul_rn(y[j + 1], s4.y);
+        y[j + 2] = __fmul_rn(y[j + 2], s4.z);
+        y[j + 3] = __fmul_rn(y[j + 3], s4.w);
+      }
+    }
+  }
+  if (p.bias != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      uint4 b4 = (j < n_valid) ? __ldg(reinterpret_cast<const uint4*>(p.bias + n0 + j)) : make_uint4(0, 0, 0, 0);
+      const __nv_bfloat162* bh = reinterpret_cast<const __nv_bfloat162*>(&b4);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 bf = __bfloat1622float2(bh[i]);
+        y[j + 2 * i] = __fadd_rn(y[j + 2 * i], bf.x);
+        y[j + 2 * i + 1] = __fadd_rn(y[j + 2 * i + 1], bf.y);
+      }
+    }
+  }
+  uint32_t packed[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) packed[j] = pack_bf16x2(y[2 * j], y[2 * j + 1]);
+  if (p.flags & kEpiGelu) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&packed[j]);
+      float2 f = __bfloat1622float2(h);
+      packed[j] = pack_bf16x2(gelu_tanh_f32(f.x), gelu_tanh_f32(f.y));
+    }
+  }
+  __nv_bfloat16* drow = static_cast<__nv_bfloat16*>(p.D) + static_cast<long long>(m) * p.ldd;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (8 * j < n_valid)
+      *reinterpret_cast<uint4*>(drow + n0 + 8 * j) =
+          make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+  }
+}
+
+template <MmaKind KIND, int BN, int STAGES>
+__global__ void __launch_bounds__(256, 1)
+k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const EpiParams p) {
+  using C = GemmCfg<KIND, BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * C::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  constexpr unsigned int kTag = 0x100u + static_cast<unsigned int>(KIND) * 16u;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&tmA);
+    tma_prefetch_map(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int m_tiles = (p.M + C::BM - 1) / C::BM;
+  const int n_tiles = (p.N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (p.K + C::BK - 1) / C::BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int mb = tile % m_tiles, nb = tile / m_tiles;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kTag, 1)) { ok = false; break; }
+          mbar_expect_tx(&full[stage], C::STAGE_BYTES);
+          tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * C::BK, mb * C::BM);
+          tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * C::BK, nb * BN);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok) {
+        // Drain: wait (bounded) until every issued copy has landed so no TMA
+        // write targets this CTA's shared memory after it exits.
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          if (--s < 0) { s = STAGES - 1; ph ^= 1u; }
+          mbar_wait_drain(&full[s], ph);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t tph = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[buf], tph ^ 1u, abort_flag, kTag, 2)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * C::ACC_COLS);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, kTag, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk) {
+            const uint64_t ad = sw128_kmajor_desc(a0 + kk * 32);
+            const uint64_t bd = sw128_kmajor_desc(b0 + kk * 32);
+            mma_issue<KIND>(d_tmem, ad, bd, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) tc_commit(&tfull[buf]);
+      }
+      if (!ok) {
+        // make sure no MMA is still reading shared memory / writing TMEM
+        tc_commit(drain);
+        mbar_wait_drain(drain, 0);
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- epilogue ----------------
+    const int wq = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int mb = tile % m_tiles, nb = tile / m_tiles;
+      const int buf = local & 1;
+      const uint32_t tph = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[buf], tph, abort_flag, kTag, 4)) break;
+      tc_fence_after();
+      const int row = wq * 32 + lane;
+      const int m = mb * C::BM + row;
+      float sa = 1.0f;
+      if (p.sa != nullptr && m < p.M) sa = __ldg(p.sa + static_cast<long long>(m) * p.sa_stride);
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + static_cast<uint32_t>(buf * C::ACC_COLS);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int n0 = nb * BN + c * 32;
+        if (n0 >= p.N) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        tmem_ld_wait();
+        if (m < p.M) epilogue_chunk<KIND>(r, p, m, n0, sa);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace qib

@@ -1,0 +1,309 @@
+// libqi_b200: the C-ABI of the B200-native quantized-linear kernels.
+//
+// One translation unit (the device status word and the kernels live in the
+// same module).  Every entry point:
+//   * takes plain device pointers, sizes and a cudaStream_t,
+//   * launches asynchronously on that stream, never synchronizes, never
+//     allocates (callers own all memory), so calls can be captured in CUDA
+//     graphs,
+//   * returns an int status (0 = ok), see include/qi_b200.h.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "gemm_tc.cuh"
+#include "quantize_act.cuh"
+#include "sm100_ptx.cuh"
+#include "../../include/qi_b200.h"
+
+namespace qib {
+
+// ---------------------------------------------------------------------------
+// per-device host state
+// ---------------------------------------------------------------------------
+struct DeviceInfo {
+  int checked = 0;  // 0 unknown, 1 ok, -1 wrong arch
+  int num_sms = 0;
+};
+constexpr int kMaxDevices = 64;
+static DeviceInfo g_dev[kMaxDevices];
+static std::mutex g_dev_mu;
+
+static int device_info(DeviceInfo** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QI_B200_ECUDA;
+  DeviceInfo& d = g_dev[dev];
+  if (d.checked == 0) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (d.checked == 0) {
+      int major = 0, minor = 0, sms = 0;
+      cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      d.num_sms = sms;
+      d.checked = (major == 10 && minor == 0) ? 1 : -1;
+    }
+  }
+  *out = &d;
+  return d.checked == 1 ? QI_B200_OK : QI_B200_EARCH;
+}
+
+// ---------------------------------------------------------------------------
+// TMA descriptors (cuTensorMapEncodeTiled through the runtime's driver
+// entry-point lookup, so the library does not link libcuda directly)
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D row-major tensor [rows, inner] with a byte row stride, 128-byte
+// swizzled boxes of [box_rows, box_inner].  Out-of-range box elements read 0.
+static int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner, uint64_t rows,
+                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return QI_B200_ETMAP;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QI_B200_OK : QI_B200_ETMAP;
+}
+
+static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// GEMM launch
+// ---------------------------------------------------------------------------
+template <MmaKind KIND, int BN, int STAGES>
+static int launch_gemm_cfg(const void* A, const void* B, const EpiParams& p, int num_sms, cudaStream_t stream) {
+  using C = GemmCfg<KIND, BN, STAGES>;
+  const CUtensorMapDataType dt =
+      (KIND == MmaKind::BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A, dt, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)p.K * C::ELEM, C::BK, C::BM);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, B, dt, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)p.K * C::ELEM, C::BK, BN);
+  if (rc) return rc;
+  static bool attr_done[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev]) {
+    if (cudaFuncSetAttribute(k_gemm_tc<KIND, BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::SMEM_BYTES) != cudaSuccess)
+      return QI_B200_ECUDA;
+    attr_done[dev] = true;
+  }
+  const int tiles = ((p.M + C::BM - 1) / C::BM) * ((p.N + BN - 1) / BN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  k_gemm_tc<KIND, BN, STAGES><<<grid, 256, C::SMEM_BYTES, stream>>>(ta, tb, p);
+  return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+// Column-tile width: minimise (tiles per CTA) x (BN + fixed per-tile cost).
+static int pick_bn(int M, int N, int num_sms) {
+  const int mt = (M + 127) / 128;
+  int best_bn = 256;
+  long best = -1;
+  for (int bn : {256, 128, 64}) {
+    const long tiles = (long)mt * ((N + bn - 1) / bn);
+    const long waves = (tiles + num_sms - 1) / num_sms;
+    const long cost = waves * (bn + 64);
+    if (best < 0 || cost < best) {
+      best = cost;
+      best_bn = bn;
+    }
+  }
+  return best_bn;
+}
+
+template <MmaKind KIND>
+static int launch_gemm(const void* A, const void* B, const EpiParams& p, cudaStream_t stream, int force_bn) {
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const int bn = force_bn > 0 ? force_bn : pick_bn(p.M, p.N, di->num_sms);
+  switch (bn) {
+    case 256: return launch_gemm_cfg<KIND, 256, 4>(A, B, p, di->num_sms, stream);
+    case 128: return launch_gemm_cfg<KIND, 128, 6>(A, B, p, di->num_sms, stream);
+    case 64: return launch_gemm_cfg<KIND, 64, 8>(A, B, p, di->num_sms, stream);
+    default: return QI_B200_EINVAL;
+  }
+}
+
+static int check_gemm_args(int kind, const void* A, const void* B, const float* sa, int sa_stride, const float* sb,
+                           int sb_stride, const void* bias, const void* D, long long ldd, int M, int N, int K,
+                           int flags) {
+  if (A == nullptr || B == nullptr || D == nullptr) return QI_B200_EINVAL;
+  if (kind < 0 || kind > 2) return QI_B200_EINVAL;
+  if (M <= 0 || N <= 0 || K <= 0) return QI_B200_ESHAPE;
+  const int elem = (kind == 2) ? 2 : 1;
+  if (N % 8 != 0 || (K * elem) % 16 != 0) return QI_B200_ESHAPE;
+  if (ldd < N || ldd % 8 != 0) return QI_B200_ESHAPE;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(D)) return QI_B200_EALIGN;
+  if (bias != nullptr && !aligned16(bias)) return QI_B200_EALIGN;
+  if (sb != nullptr && sb_stride != 0 && (sb_stride != 1 || !aligned16(sb))) return QI_B200_EALIGN;
+  if (sa != nullptr && sa_stride < 0) return QI_B200_EINVAL;
+  if (flags & ~(kEpiGelu | kEpiRawAcc)) return QI_B200_EINVAL;
+  return QI_B200_OK;
+}
+
+static int gemm_dispatch(int kind, const void* A, const void* B, const float* sa, int sa_stride, const float* sb,
+                         int sb_stride, const void* bias, void* D, long long ldd, int M, int N, int K, int flags,
+                         int force_bn, cudaStream_t stream) {
+  int rc = check_gemm_args(kind, A, B, sa, sa_stride, sb, sb_stride, bias, D, ldd, M, N, K, flags);
+  if (rc) return rc;
+  EpiParams p;
+  p.sa = sa;
+  p.sa_stride = sa_stride;
+  p.sb = sb;
+  p.sb_stride = sb_stride;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.D = D;
+  p.ldd = ldd;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.flags = flags;
+  switch (kind) {
+    case QI_B200_KIND_INT8: return launch_gemm<MmaKind::I8>(A, B, p, stream, force_bn);
+    case QI_B200_KIND_FP8_E4M3: return launch_gemm<MmaKind::F8>(A, B, p, stream, force_bn);
+    default: return launch_gemm<MmaKind::BF16>(A, B, p, stream, force_bn);
+  }
+}
+
+static int quant_status(cudaError_t e) { return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA; }
+
+}  // namespace qib
+
+using namespace qib;
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+int qi_b200_abi_version(void) { return QI_B200_ABI_VERSION; }
+
+const char* qi_b200_error_string(int code) {
+  switch (code) {
+    case QI_B200_OK: return "ok";
+    case QI_B200_EINVAL: return "invalid argument";
+    case QI_B200_ESHAPE: return "unsupported shape (need M,N,K > 0, N % 8 == 0, K*elem % 16 == 0)";
+    case QI_B200_EALIGN: return "pointer not 16-byte aligned";
+    case QI_B200_ECUDA: return "CUDA launch error";
+    case QI_B200_ETMAP: return "TMA descriptor encoding failed";
+    case QI_B200_EARCH: return "current device is not sm_100 (B200)";
+    case QI_B200_ETOOBIG: return "size exceeds the entry point's fixed maximum";
+    default: return "unknown status";
+  }
+}
+
+int qi_b200_device_status(unsigned int* out4, int clear) {
+  unsigned int h[4] = {0, 0, 0, 0};
+  if (cudaMemcpyFromSymbol(h, g_status, sizeof(h)) != cudaSuccess) return QI_B200_ECUDA;
+  if (out4 != nullptr)
+    for (int i = 0; i < 4; ++i) out4[i] = h[i];
+  if (clear) {
+    unsigned int z[4] = {0, 0, 0, 0};
+    if (cudaMemcpyToSymbol(g_status, z, sizeof(z)) != cudaSuccess) return QI_B200_ECUDA;
+  }
+  return QI_B200_OK;
+}
+
+int qi_b200_quantize_int8_rowwise(const void* x_bf16, void* q_int8, float* scales, int rows, int cols,
+                                  cudaStream_t stream) {
+  if (rows < 0 || cols < 0) return QI_B200_ESHAPE;
+  if (rows == 0 || cols == 0) return QI_B200_OK;
+  if (x_bf16 == nullptr || q_int8 == nullptr || scales == nullptr) return QI_B200_EINVAL;
+  return quant_status(launch_rowquant<QuantInt8>(x_bf16, q_int8, scales, nullptr, rows, cols, stream));
+}
+
+int qi_b200_quantize_fp8_rowwise(const void* x_bf16, void* q_fp8, float* scales, int rows, int cols,
+                                 cudaStream_t stream) {
+  if (rows < 0 || cols < 0) return QI_B200_ESHAPE;
+  if (rows == 0 || cols == 0) return QI_B200_OK;
+  if (x_bf16 == nullptr || q_fp8 == nullptr || scales == nullptr) return QI_B200_EINVAL;
+  return quant_status(launch_rowquant<QuantFp8>(x_bf16, q_fp8, scales, nullptr, rows, cols, stream));
+}
+
+int qi_b200_quantize_fp8_static(const void* x_bf16, const float* scale, void* q_fp8, int rows, int cols,
+                                cudaStream_t stream) {
+  if (rows < 0 || cols < 0) return QI_B200_ESHAPE;
+  if (rows == 0 || cols == 0) return QI_B200_OK;
+  if (x_bf16 == nullptr || q_fp8 == nullptr || scale == nullptr) return QI_B200_EINVAL;
+  return quant_status(launch_rowquant<QuantFp8Static>(x_bf16, q_fp8, nullptr, scale, rows, cols, stream));
+}
+
+int qi_b200_gemm(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
+                 const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd, int M, int N,
+                 int K, int flags, int tile_n, cudaStream_t stream) {
+  return gemm_dispatch(kind, A, B, a_scale, a_scale_stride, b_scale, b_scale_stride, bias, D, ldd, M, N, K, flags,
+                       tile_n, stream);
+}
+
+int qi_b200_int8_rowwise_bf16out(const void* A, const void* B, const void* act_scale, const void* weight_scale,
+                                 void* D, int M, int N, int K, cudaStream_t stream) {
+  return gemm_dispatch(QI_B200_KIND_INT8, A, B, static_cast<const float*>(act_scale), 1,
+                       static_cast<const float*>(weight_scale), 1, nullptr, D, N, M, N, K, 0, 0, stream);
+}
+
+int qi_b200_int8_rowwise_bf16out_bias(const void* A, const void* B, const void* act_scale, const void* weight_scale,
+                                      const void* bias, void* D, int M, int N, int K, cudaStream_t stream) {
+  return gemm_dispatch(QI_B200_KIND_INT8, A, B, static_cast<const float*>(act_scale), 1,
+                       static_cast<const float*>(weight_scale), 1, bias, D, N, M, N, K, 0, 0, stream);
+}
+
+int qi_b200_int8_linear(const void* x_bf16, const void* qweight, const float* weight_scale, const void* bias,
+                        void* out_bf16, void* ws_q, float* ws_scales, int M, int N, int K, cudaStream_t stream) {
+  if (M == 0) return QI_B200_OK;
+  if (ws_q == nullptr || ws_scales == nullptr || weight_scale == nullptr) return QI_B200_EINVAL;
+  int rc = check_gemm_args(QI_B200_KIND_INT8, ws_q, qweight, ws_scales, 1, weight_scale, 1, bias, out_bf16, N, M, N,
+                           K, 0);
+  if (rc) return rc;
+  rc = qi_b200_quantize_int8_rowwise(x_bf16, ws_q, ws_scales, M, K, stream);
+  if (rc) return rc;
+  return gemm_dispatch(QI_B200_KIND_INT8, ws_q, qweight, ws_scales, 1, weight_scale, 1, bias, out_bf16, N, M, N, K,
+                       0, 0, stream);
+}
+
+int qi_b200_fp8_linear(const void* x_bf16, const void* weight_fp8, const float* weight_scale,
+                       int weight_scale_per_channel, const float* static_act_scale, const void* bias,
+                       void* out_bf16, void* ws_q, float* ws_scales, int M, int N, int K, int flags,
+                       cudaStream_t stream) {
+  if (M == 0) return QI_B200_OK;
+  if (ws_q == nullptr || weight_scale == nullptr) return QI_B200_EINVAL;
+  if (static_act_scale == nullptr && ws_scales == nullptr) return QI_B200_EINVAL;
+  const float* sa = static_act_scale != nullptr ? static_act_scale : ws_scales;
+  const int sa_stride = static_act_scale != nullptr ? 0 : 1;
+  const int sb_stride = weight_scale_per_channel ? 1 : 0;
+  int rc = check_gemm_args(QI_B200_KIND_FP8_E4M3, ws_q, weight_fp8, sa, sa_stride, weight_scale, sb_stride, bias,
+                           out_bf16, N, M, N, K, flags);
+  if (rc) return rc;
+  rc = static_act_scale != nullptr ? qi_b200_quantize_fp8_static(x_bf16, static_act_scale, ws_q, M, K, stream)
+                                   : qi_b200_quantize_fp8_rowwise(x_bf16, ws_q, ws_scales, M, K, stream);
+  if (rc) return rc;
+  return gemm_dispatch(QI_B200_KIND_FP8_E4M3, ws_q, weight_fp8, sa, sa_stride, weight_scale, sb_stride, bias,
+                       out_bf16, N, M, N, K, flags, 0, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,194 @@
+// Per-token activation quantizers (bf16 rows -> int8 / fp8-e4m3 + fp32 scale).
+//
+// Row-parallel, HBM-bound: each row is read once with 16-byte vector loads and
+// held in registers (up to 8 x uint4 per thread) across the absmax reduction
+// (warp shuffles, then shared memory when a row spans several warps) and the
+// quantization pass, so HBM traffic is exactly K*2 bytes in + K bytes out per
+// row plus one fp32 scale.
+//
+// Semantics (restated from the reference):
+//   int8  (csrc/int8_w8a8/quantize_int8.cu:7-59): s = max(amax/127, 1e-10),
+//         q = clamp(rint(x * (1/s)), -127, 127) with an IEEE reciprocal.
+//   fp8   (backends/flashrt_fp8_ops.py:38-48, one scale per row instead of one
+//         per tensor): s = max(amax/448, 1e-12), q = e4m3_rn(clamp(x/s, +-448)).
+//   fp8 static (flashrt_fp8_ops.py:207-216): q = e4m3_rn(clamp(x/s_static, +-448)).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace qib {
+
+constexpr int kQuantThreads = 256;
+constexpr int kQuantMaxChunks = 8;  // uint4 chunks (8 bf16 each) held per thread
+
+struct QuantInt8 {
+  static constexpr bool kNeedsAmax = true;
+  __device__ __forceinline__ static float scale_from_amax(float amax) {
+    return fmaxf(__fdiv_rn(amax, 127.0f), 1e-10f);
+  }
+  __device__ __forceinline__ static float aux(float s) { return __frcp_rn(s); }
+  __device__ __forceinline__ static uint8_t q1(float x, float /*s*/, float inv) {
+    int q = __float2int_rn(__fmul_rn(x, inv));
+    q = q < -127 ? -127 : (q > 127 ? 127 : q);
+    return static_cast<uint8_t>(static_cast<int8_t>(q));
+  }
+};
+
+struct QuantFp8 {
+  static constexpr bool kNeedsAmax = true;
+  __device__ __forceinline__ static float scale_from_amax(float amax) {
+    return fmaxf(__fdiv_rn(amax, 448.0f), 1e-12f);
+  }
+  __device__ __forceinline__ static float aux(float s) { return s; }
+  __device__ __forceinline__ static uint8_t q1(float x, float s, float /*aux*/) {
+    float v = fminf(fmaxf(__fdiv_rn(x, s), -448.0f), 448.0f);
+    return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+  }
+};
+
+struct QuantFp8Static : QuantFp8 {
+  static constexpr bool kNeedsAmax = false;
+};
+
+__device__ __forceinline__ float absmax_bf16x8(const uint4& v) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+  }
+  return m;
+}
+
+template <class Op>
+__device__ __forceinline__ uint2 quant_bf16x8(const uint4& v, float s, float aux) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    uint32_t b0 = Op::q1(f.x, s, aux), b1 = Op::q1(f.y, s, aux);
+    uint32_t pair = b0 | (b1 << 8);
+    if (i < 2) lo |= pair << (16 * i);
+    else hi |= pair << (16 * (i - 2));
+  }
+  return make_uint2(lo, hi);
+}
+
+// TPR threads per row, kQuantThreads / TPR rows per block.  cols % 8 == 0,
+// row starts 16-byte aligned, ceil(cols/8 / TPR) <= kQuantMaxChunks.
+template <class Op, int TPR>
+__global__ void __launch_bounds__(kQuantThreads)
+k_rowquant_vec(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, float* __restrict__ scales,
+               const float* __restrict__ static_scale, int rows, int cols) {
+  constexpr int RPB = kQuantThreads / TPR;
+  constexpr int WPR = TPR / 32;
+  __shared__ float red[RPB][WPR];
+  const int r_local = threadIdx.x / TPR;
+  const int t = threadIdx.x % TPR;
+  const int row = blockIdx.x * RPB + r_local;
+  const bool valid = row < rows;
+  const int nvec = cols >> 3;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(valid ? row : 0) * cols);
+
+  uint4 v[kQuantMaxChunks];
+  float amax = 0.f;
+#pragma unroll
+  for (int c = 0; c < kQuantMaxChunks; ++c) {
+    const int idx = c * TPR + t;
+    if (valid && idx < nvec) {
+      v[c] = __ldg(xr + idx);
+      if (Op::kNeedsAmax) amax = fmaxf(amax, absmax_bf16x8(v[c]));
+    }
+  }
+  float s;
+  if (Op::kNeedsAmax) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    if (WPR > 1) {
+      if ((threadIdx.x & 31) == 0) red[r_local][t >> 5] = amax;
+      __syncthreads();
+      amax = red[r_local][0];
+#pragma unroll
+      for (int w = 1; w < WPR; ++w) amax = fmaxf(amax, red[r_local][w]);
+    }
+    s = Op::scale_from_amax(amax);
+    if (valid && t == 0 && scales != nullptr) scales[row] = s;
+  } else {
+    s = __ldg(static_scale);
+  }
+  const float aux = Op::aux(s);
+  uint2* qr = reinterpret_cast<uint2*>(q + static_cast<size_t>(valid ? row : 0) * cols);
+#pragma unroll
+  for (int c = 0; c < kQuantMaxChunks; ++c) {
+    const int idx = c * TPR + t;
+    if (valid && idx < nvec) qr[idx] = quant_bf16x8<Op>(v[c], s, aux);
+  }
+}
+
+// Any cols / alignment: one warp per row, two scalar passes (second pass hits L1/L2).
+template <class Op>
+__global__ void __launch_bounds__(kQuantThreads)
+k_rowquant_scalar(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, float* __restrict__ scales,
+                  const float* __restrict__ static_scale, int rows, int cols) {
+  const int row = blockIdx.x * (kQuantThreads / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const __nv_bfloat16* xr = x + static_cast<size_t>(row) * cols;
+  float s;
+  if (Op::kNeedsAmax) {
+    float amax = 0.f;
+    for (int j = lane; j < cols; j += 32) amax = fmaxf(amax, fabsf(__bfloat162float(xr[j])));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    s = Op::scale_from_amax(amax);
+    if (lane == 0 && scales != nullptr) scales[row] = s;
+  } else {
+    s = __ldg(static_scale);
+  }
+  const float aux = Op::aux(s);
+  uint8_t* qr = q + static_cast<size_t>(row) * cols;
+  for (int j = lane; j < cols; j += 32) qr[j] = Op::q1(__bfloat162float(xr[j]), s, aux);
+}
+
+template <class Op>
+inline cudaError_t launch_rowquant(const void* x, void* q, float* scales, const float* static_scale, int rows,
+                                   int cols, cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0) return cudaSuccess;
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  auto* qb = static_cast<uint8_t*>(q);
+  const bool aligned = (cols % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(q) % 8 == 0);
+  const int nvec = cols / 8;
+  if (aligned) {
+    auto fits = [&](int tpr) { return (nvec + tpr - 1) / tpr <= kQuantMaxChunks; };
+    if (fits(32)) {
+      constexpr int RPB = kQuantThreads / 32;
+      k_rowquant_vec<Op, 32><<<(rows + RPB - 1) / RPB, kQuantThreads, 0, stream>>>(xb, qb, scales, static_scale,
+                                                                                     rows, cols);
+    } else if (fits(64)) {
+      constexpr int RPB = kQuantThreads / 64;
+      k_rowquant_vec<Op, 64><<<(rows + RPB - 1) / RPB, kQuantThreads, 0, stream>>>(xb, qb, scales, static_scale,
+                                                                                     rows, cols);
+    } else if (fits(128)) {
+      constexpr int RPB = kQuantThreads / 128;
+      k_rowquant_vec<Op, 128><<<(rows + RPB - 1) / RPB, kQuantThreads, 0, stream>>>(xb, qb, scales,
+                                                                                       static_scale, rows, cols);
+    } else if (fits(256)) {
+      k_rowquant_vec<Op, 256><<<rows, kQuantThreads, 0, stream>>>(xb, qb, scales, static_scale, rows, cols);
+    } else {
+      k_rowquant_scalar<Op><<<(rows + 7) / 8, kQuantThreads, 0, stream>>>(xb, qb, scales, static_scale, rows,
+                                                                          cols);
+    }
+  } else {
+    k_rowquant_scalar<Op><<<(rows + 7) / 8, kQuantThreads, 0, stream>>>(xb, qb, scales, static_scale, rows,
+                                                                        cols);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace qib
