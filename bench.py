@@ -1,0 +1,435 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 quantized-linear hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config fp8|int8] [--impl ours|reference]
+
+One step = one quantized linear forward over one batch of synthetic input
+(activation quantization kernel + tcgen05 GEMM with fused epilogue; for N > 1
+also the NCCL all-gather of the column-sharded outputs).  Default config is
+BASELINE config 2 (FP8-E4M3 FFN up-projection, M=4096 N=14336 K=3072,
+per-token activations, per-channel weights, bias + GELU).
+
+Prints ONE JSON line on rank 0.  ``value`` = whole-job TOPS (2*M*N*K per
+step / max-over-ranks device time), inputs resident in HBM; ``e2e`` = the
+same through the public module API (``WeightOnlyLinear.forward``) with the
+activations copied in from pinned host memory and the output copied back
+every step.  ``--impl reference`` times the reference's own CPU algorithm
+(the dequantise-then-matmul port in ``oracle/reference_port.py``) on this
+host's cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from qi_b200.synthetic import CFG_FP8, CFG_INT8, make_linear_inputs  # noqa: E402
+
+CONFIGS = {
+    "fp8": dict(case=CFG_FP8, kind="fp8", gelu=True, dtype="fp8_e4m3 (fp32 accumulate)"),
+    "int8": dict(case=CFG_INT8, kind="int8", gelu=False, dtype="int8 (int32 accumulate)"),
+}
+L2_BYTES = 126 * 2**20
+
+
+def peaks():
+    """Roofline denominators: MEASURED_PEAKS.json (driver-measured on this
+    pool), else the profiling recipe's fallback."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured (MEASURED_PEAKS.json)"
+    except Exception:
+        return 6650.0, 1590.0, "fallback (profiling recipe)"
+
+
+# --------------------------------------------------------------------------
+# clocks sampled during the timed region (NVML, background thread)
+# --------------------------------------------------------------------------
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+            0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+            0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    def __init__(self, device_index: int):
+        self.samples, self.reasons, self.ok = [], 0, False
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+
+    def _poll(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._poll, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        names = [n for b, n in _REASONS.items() if self.reasons & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------------------
+# distributed plumbing
+# --------------------------------------------------------------------------
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(v: float, world: int, device) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------
+# workload
+# --------------------------------------------------------------------------
+
+
+def build_layer(cfg_name: str, w_shard: torch.Tensor, b_shard: torch.Tensor, device):
+    """One WeightOnlyLinear (the public module API) for this rank's column shard."""
+    from qi_b200.quantization import WeightActivationQuantConfig, WeightOnlyLinear
+    from qi_b200.quantization.backends import get_backend
+    from qi_b200.quantization.quantize import quantize_linear_weight
+
+    c = CONFIGS[cfg_name]
+    if c["kind"] == "fp8":
+        qcfg = WeightActivationQuantConfig(enabled=True, algo="rtn", quant_dtype="fp8", backend="b200",
+                                           activation_granularity="per_token", weight_granularity="per_channel")
+    else:
+        qcfg = WeightActivationQuantConfig(enabled=True, algo="rtn", quant_dtype="int", backend="b200",
+                                           activation_granularity="per_token", weight_granularity="per_channel")
+    q = quantize_linear_weight(w_shard.to(device), qcfg)
+    lin = torch.nn.Linear(w_shard.shape[1], w_shard.shape[0], bias=True)
+    with torch.no_grad():
+        lin.bias.copy_(b_shard.float())
+    layer = WeightOnlyLinear.from_linear(lin, q, qcfg, get_backend("b200")).to(device)
+    layer.bias = layer.bias.to(torch.bfloat16)
+    layer.fuse_gelu = c["gelu"]
+    return layer
+
+
+def run_ours(args):
+    from qi_b200 import _lib, kernels as K
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    c = CONFIGS[args.config]
+    case = c["case"]
+    M, N, Kd = case.M, case.N, case.K
+    if N % (8 * world):
+        raise SystemExit(f"N={N} not divisible into {world} shards of multiples of 8")
+    Nl = N // world
+    x_cpu, w_cpu, b_cpu = make_linear_inputs(case)
+    w_shard, b_shard = w_cpu[rank * Nl:(rank + 1) * Nl], b_cpu[rank * Nl:(rank + 1) * Nl]
+
+    layer = build_layer(args.config, w_shard, b_shard, device)
+    kind = _lib.KIND_FP8_E4M3 if c["kind"] == "fp8" else _lib.KIND_INT8
+    wq = layer.weight_fp8 if c["kind"] == "fp8" else layer.qweight
+    ws = layer.weight_scale if c["kind"] == "fp8" else layer.scales[:, 0].contiguous()
+
+    # rotate input copies so consecutive steps touch more distinct bytes than L2
+    per_copy = x_cpu.numel() * 2 + wq.numel()
+    ncopy = max(2, -(-3 * L2_BYTES // per_copy))
+    xs = [x_cpu.to(device) for _ in range(ncopy)]
+    wqs = [wq.clone() for _ in range(ncopy)]
+    bias = layer.bias
+    gathered = torch.empty((world, M, Nl), dtype=torch.bfloat16, device=device) if world > 1 else None
+    stream = torch.cuda.current_stream(device)
+
+    quant = K.quantize_fp8_rowwise if c["kind"] == "fp8" else K.quantize_int8_rowwise
+
+    def step(i, ev=None):
+        x, w = xs[i % ncopy], wqs[i % ncopy]
+        q, s = quant(x)
+        cur = torch.cuda.current_stream(device)  # the capture stream inside torch.cuda.graph
+        if ev is not None:
+            ev[0].record(cur)
+        y = K.gemm(kind, q, w, s, ws, bias, gelu=c["gelu"])
+        if ev is not None:
+            ev[1].record(cur)
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(gathered, y)
+        return y
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    # Single GPU: the K timed steps are captured once in a CUDA graph (the
+    # reference deploys its DiT under CUDA graphs too) so host launch latency
+    # does not leak into the device time of small configs; per-step events
+    # around the GEMM are event-record nodes inside the graph.  Multi-GPU:
+    # eager steps (the all-gather dominates; NCCL stays outside capture).
+    use_graph = world == 1 and not args.eager
+    for i in range(args.warmup):
+        step(i)
+    barrier()
+    evs = [(torch.cuda.Event(enable_timing=True, external=use_graph),
+            torch.cuda.Event(enable_timing=True, external=use_graph)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    graph = None
+    if use_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(args.steps):
+                step(i, evs[i])
+        graph.replay()  # untimed: uploads the graph
+        barrier()
+    with ClockSampler(local) as clk:
+        barrier()
+        t0.record(stream)
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(args.steps):
+                step(i, evs[i])
+        t1.record(stream)
+        barrier()
+    ms_total = max_over_ranks(t0.elapsed_time(t1), world, device)
+    try:
+        gemm_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        gemm_src = "cuda events around each GEMM launch in the timed region"
+    except Exception:
+        # event-record nodes not timeable: time K back-to-back GEMM launches instead
+        gemm_ms, gemm_src = time_gemm_alone(step, args.steps, stream), "cuda events, GEMM-only graph"
+    gemm_ms = max_over_ranks(gemm_ms, world, device)
+    st = _lib.device_status()
+    if st[0] != 0:
+        raise SystemExit(f"device status word reports a timed-out wait: {st}")
+
+    flops_total = 2.0 * M * N * Kd
+    ms_step = ms_total / args.steps
+    value = flops_total / (ms_step * 1e-3) / 1e12
+
+    # ---- e2e through the public module API with host buffers
+    x_host = x_cpu.pin_memory()
+    x_dev = torch.empty_like(xs[0])
+    out_shape = (world, M, Nl) if world > 1 else (M, N)
+    y_host = torch.empty(out_shape, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        y = layer(x_dev)
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(gathered, y)
+            y = gathered
+        y_host.copy_(y, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, device) / args.steps
+    h2d = x_host.numel() * 2
+    d2h = y_host.numel() * 2
+
+    # ---- roofline of the dominant kernel (the GEMM) against the dtype's dense peak
+    hbm_gbs, bf16_tf, src = peaks()
+    gemm_flops_launch = 2.0 * M * Nl * Kd
+    achieved = gemm_flops_launch / (gemm_ms * 1e-3) / 1e12
+    peak = 2.0 * bf16_tf  # 8-bit tensor-core rate is 2x the bf16 rate on B200
+    traffic = load_traffic(args.config, world)
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "peak_source": f"2 x bf16 dense, {src}", "kernel": f"k_gemm_tc<{c['kind']}>",
+                "kernel_ms": round(gemm_ms, 5), "kernel_timing": gemm_src}
+
+    result = {
+        "metric": "quantized_gemm_tops", "value": round(value, 2), "unit": "TOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": c["dtype"], "data": "synthetic (seeded, BASELINE shapes)",
+        "config": {"workload": case.name, "M": M, "N": N, "K": Kd, "bias": True, "gelu": c["gelu"],
+                   "act_quant": "per_token", "weight_quant": "per_channel",
+                   "parallelism": f"N-shard x{world} + NCCL all_gather" if world > 1 else "single GPU",
+                   "launch": "cuda_graph" if use_graph else "eager",
+                   "l2": f"{ncopy} rotating input copies ({ncopy * per_copy / 2**20:.0f} MiB > L2)"},
+        "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
+                "api": "qi_b200.quantization.WeightOnlyLinear.forward"},
+        "gpu_launches": 2 * args.steps,
+        "roofline": roofline,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(args.config, samples=3)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def time_gemm_alone(step, steps, stream):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(steps):
+            step(i)
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    g.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def load_traffic(cfg_name: str, world: int):
+    """DRAM bytes per GEMM launch from a committed ncu capture, if any."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        v = d.get(f"{cfg_name}_x{world}")
+        return None if v is None else v["bytes_per_launch"]
+    except Exception:
+        return None
+
+
+# --------------------------------------------------------------------------
+# CPU baseline: the reference's own algorithm (port) on this host's cores
+# --------------------------------------------------------------------------
+
+
+def _cpu_sample(cfg_name: str):
+    """Inputs and a callable for one bounded CPU call of the reference path."""
+    from oracle import reference_port as RP
+    from qi_b200.quantization.quantize import quantize_to_fp8_e4m3_rowwise, quantize_weight_rtn
+
+    c = CONFIGS[cfg_name]
+    case = c["case"]
+    x, w, b = make_linear_inputs(case)
+    rows = min(case.M, 512 if c["kind"] == "int8" else 256)
+    xs = x[:rows].contiguous()
+    if c["kind"] == "int8":
+        qw, sw, _ = quantize_weight_rtn(w, 8, -1, True)
+        fn = lambda: RP.reference_linear(xs, qw, sw, None, b, 8, -1, True, activation_granularity="per_token")
+        desc = f"ReferenceBackend.linear port (bf16 input, per-token int8 fake-quant, dequant loop, F.linear), {rows} of {case.M} rows"
+    else:
+        wq, ws = quantize_to_fp8_e4m3_rowwise(w)
+        fn = lambda: RP.fp8_linear_port(xs, wq, ws, b, gelu=c["gelu"])
+        desc = f"dequantise-then-F.linear FP8 port (per-token fake-quant, fp32 compute, GELU), {rows} of {case.M} rows"
+    return fn, rows, case, desc
+
+
+def cpu_baseline(cfg_name: str, samples: int = 3):
+    torch.set_num_threads(os.cpu_count() or 1)
+    fn, rows, case, desc = _cpu_sample(cfg_name)
+    fn()
+    ts = []
+    for _ in range(samples):
+        t = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t)
+    t = statistics.median(ts)
+    return {"value": round(2.0 * rows * case.N * case.K / t / 1e12, 5), "unit": "TOPS",
+            "cores": torch.get_num_threads(), "kind": "port", "sample": desc + f", median of {samples}",
+            "ms_per_call": round(t * 1e3, 2)}
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    fn, rows, case, desc = _cpu_sample(args.config)
+    for _ in range(args.warmup):
+        fn()
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        fn()
+    dt = (time.perf_counter() - t) / args.steps
+    value = 2.0 * rows * case.N * case.K / dt / 1e12
+    print(json.dumps({
+        "impl": "reference", "metric": "quantized_gemm_tops", "value": round(value, 5), "unit": "TOPS",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": CONFIGS[args.config]["dtype"],
+        "data": "synthetic (seeded, BASELINE shapes)",
+        "config": {"workload": case.name, "M": case.M, "N": case.N, "K": case.K, "sample_rows": rows},
+        "cpu_baseline": {"value": round(value, 5), "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": round(value, 5), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="fp8", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="no CUDA graph for the timed steps")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -35,6 +35,12 @@ enum class MmaKind : int { I8 = 0, F8 = 1, BF16 = 2 };
 constexpr int kEpiGelu = 1;     // GELU(tanh) of the bf16-rounded linear output
 constexpr int kEpiRawAcc = 2;   // debug: store raw 32-bit accumulators (int32 / fp32), ld = ldd
 
+// CTA shape: warp 0 TMA, warp 1 MMA + TMEM, warps 2-3 idle, warps 4-11 epilogue
+constexpr int kFirstEpiWarp = 4;
+constexpr int kEpiWarps = 8;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kGemmThreads = (kFirstEpiWarp + kEpiWarps) * 32;
+
 struct EpiParams {
   const float* sa;  // per-row (token) scale, or nullptr (= 1)
   int sa_stride;    // 0 = one scale for all rows
@@ -60,22 +66,31 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int ACC_COLS = BN;  // fp32/s32 accumulator: one TMEM column per output column
   static constexpr int TMEM_COLS = (2 * ACC_COLS <= 32) ? 32 : (2 * ACC_COLS <= 64) ? 64 : (2 * ACC_COLS <= 128) ? 128 : (2 * ACC_COLS <= 256) ? 256 : 512;
+  static constexpr int COLPARAM_BYTES = 2 * BN * (4 + 2);  // double-buffered column scales + bias
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;  // + alignment slack
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + COLPARAM_BYTES + BAR_BYTES + 1024;  // + alignment slack
   static constexpr uint32_t IDESC =
       (KIND == MmaKind::I8)   ? make_idesc(kDS32, kFmtS8, kFmtS8, BM, BN)
       : (KIND == MmaKind::F8) ? make_idesc(kDF32, kFmtE4M3, kFmtE4M3, BM, BN)
                               : make_idesc(kDF32, kFmtBF16, kFmtBF16, BM, BN);
-  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
   static_assert(2 * ACC_COLS <= 512, "TMEM");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
-__device__ __forceinline__ float gelu_tanh_f32(float v) {
+// GELU, tanh form: 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3))), with the
+// hardware tanh approximation (tanh.approx.f32, relative error ~2^-11, below
+// the bf16 rounding that follows).
+__device__ __forceinline__ float tanh_hw(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float gelu_tanh_fast(float v) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
   const float k1 = 0.044715f;
-  float inner = k0 * (v + k1 * v * v * v);
-  return 0.5f * v * (1.0f + tanhf(inner));
+  const float inner = k0 * fmaf(k1 * v * v, v, v);
+  return 0.5f * v * (1.0f + tanh_hw(inner));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -90,55 +105,49 @@ __device__ __forceinline__ void mma_issue(uint32_t d, uint64_t a, uint64_t b, ui
   else mma_bf16(d, a, b, idesc, acc);
 }
 
-// Epilogue for one 32-column chunk of one row (this thread's row).
+// Epilogue for one 32-column chunk of one row (this thread's row).  Column
+// scales and bias come from the per-tile shared-memory copy (sb_s, bias_s,
+// indexed from the chunk's first column); the row scale is in a register.
 template <MmaKind KIND>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], const EpiParams& p, int m, int n0,
-                                               float sa) {
+                                               float sa, const float* sb_s, const __nv_bfloat16* bias_s) {
+  const int n_valid = p.N - n0;  // >= 1; a multiple of 8 when < 32 (N % 8 == 0)
   if (p.flags & kEpiRawAcc) {
     uint32_t* drow = static_cast<uint32_t*>(p.D) + static_cast<long long>(m) * p.ldd;
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
-      if (n0 + j < p.N) *reinterpret_cast<uint4*>(drow + n0 + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+      if (j < n_valid) *reinterpret_cast<uint4*>(drow + n0 + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
     }
     return;
   }
   float y[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    float v;
-    if constexpr (KIND == MmaKind::I8) v = __int2float_rn(static_cast<int>(r[j]));
-    else v = __uint_as_float(r[j]);
-    y[j] = v;
+    if constexpr (KIND == MmaKind::I8) y[j] = __int2float_rn(static_cast<int>(r[j]));
+    else y[j] = __uint_as_float(r[j]);
   }
-  const int n_valid = p.N - n0;  // >= 1; multiple of 8 when < 32 (N % 8 == 0)
   if (KIND != MmaKind::BF16 || p.sa != nullptr) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) y[j] = __fmul_rn(y[j], sa);
   }
   if (p.sb != nullptr) {
-    if (p.sb_stride == 0) {
-      const float s = __ldg(p.sb);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) y[j] = __fmul_rn(y[j], s);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        float4 s4 = (j < n_valid) ? __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        y[j] = __fmul_rn(y[j], s4.x);
-        y[j + 1] = __fmul_rn(y[j + 1], s4.y);
-        y[j + 2] = __fmul_rn(y[j + 2], s4.z);
-        y[j + 3] = __fmul_rn(y[j + 3], s4.w);
-      }
+    for (int j = 0; j < 32; j += 4) {
+      const float4 s4 = *reinterpret_cast<const float4*>(sb_s + j);
+      y[j] = __fmul_rn(y[j], s4.x);
+      y[j + 1] = __fmul_rn(y[j + 1], s4.y);
+      y[j + 2] = __fmul_rn(y[j + 2], s4.z);
+      y[j + 3] = __fmul_rn(y[j + 3], s4.w);
     }
   }
   if (p.bias != nullptr) {
 #pragma unroll
     for (int j = 0; j < 32; j += 8) {
-      uint4 b4 = (j < n_valid) ? __ldg(reinterpret_cast<const uint4*>(p.bias + n0 + j)) : make_uint4(0, 0, 0, 0);
+      const uint4 b4 = *reinterpret_cast<const uint4*>(bias_s + j);
       const __nv_bfloat162* bh = reinterpret_cast<const __nv_bfloat162*>(&b4);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        float2 bf = __bfloat1622float2(bh[i]);
+        const float2 bf = __bfloat1622float2(bh[i]);
         y[j + 2 * i] = __fadd_rn(y[j + 2 * i], bf.x);
         y[j + 2 * i + 1] = __fadd_rn(y[j + 2 * i + 1], bf.y);
       }
@@ -150,9 +159,8 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], const Ep
   if (p.flags & kEpiGelu) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&packed[j]);
-      float2 f = __bfloat1622float2(h);
-      packed[j] = pack_bf16x2(gelu_tanh_f32(f.x), gelu_tanh_f32(f.y));
+      const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&packed[j]));
+      packed[j] = pack_bf16x2(gelu_tanh_fast(f.x), gelu_tanh_fast(f.y));
     }
   }
   __nv_bfloat16* drow = static_cast<__nv_bfloat16*>(p.D) + static_cast<long long>(m) * p.ldd;
@@ -165,19 +173,23 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], const Ep
 }
 
 template <MmaKind KIND, int BN, int STAGES>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const EpiParams p) {
   using C = GemmCfg<KIND, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * C::B_BYTES);
+  // per-tile column parameters, double buffered: [2][BN] fp32 scales, [2][BN] bf16 bias
+  float* col_scale = reinterpret_cast<float*>(sB + STAGES * C::B_BYTES);
+  __nv_bfloat16* col_bias = reinterpret_cast<__nv_bfloat16*>(col_scale + 2 * BN);
+  uint64_t* full = reinterpret_cast<uint64_t*>(col_bias + 2 * BN);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* epi_sync = drain + 1;  // [2]: epilogue threads' column parameters are staged
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_sync + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -191,7 +203,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], kEpiThreads);
+      mbar_init(&epi_sync[b], kEpiThreads);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -279,29 +292,55 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         mbar_wait_drain(drain, 0);
       }
     }
-  } else if (warp >= 4) {
-    // ---------------- epilogue ----------------
-    const int wq = warp & 3;  // TMEM lane quarter this warp may access
+  } else if (warp >= kFirstEpiWarp) {
+    // ---------------- epilogue (8 warps) ----------------
+    // Warp w may only touch TMEM lanes 32*(w%4)..+31; the two warps sharing
+    // a lane quarter split the tile's columns in halves.
+    const int et = threadIdx.x - kFirstEpiWarp * 32;  // 0..kEpiThreads-1
+    const int wq = warp & 3;
+    const int half = (warp - kFirstEpiWarp) >> 2;
+    constexpr int COLS = BN / 2;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int mb = tile % m_tiles, nb = tile / m_tiles;
       const int buf = local & 1;
       const uint32_t tph = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[buf], tph, abort_flag, kTag, 4)) break;
-      tc_fence_after();
+      // stage this tile's column scales / bias in shared memory
+      float* sb_t = col_scale + buf * BN;
+      __nv_bfloat16* bias_t = col_bias + buf * BN;
+      for (int j = et; j < BN; j += kEpiThreads) {
+        const int n = nb * BN + j;
+        float sv = 1.0f;
+        if (p.sb != nullptr) sv = (n < p.N) ? __ldg(p.sb + static_cast<long long>(n) * p.sb_stride) : 0.0f;
+        sb_t[j] = sv;
+        bias_t[j] = (p.bias != nullptr && n < p.N) ? p.bias[n] : __float2bfloat16_rn(0.0f);
+      }
       const int row = wq * 32 + lane;
       const int m = mb * C::BM + row;
       float sa = 1.0f;
       if (p.sa != nullptr && m < p.M) sa = __ldg(p.sa + static_cast<long long>(m) * p.sa_stride);
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + static_cast<uint32_t>(buf * C::ACC_COLS);
+      // all epilogue threads have staged the parameters (bounded mbarrier wait
+      // rather than a named barrier, so an aborting CTA cannot block here)
+      mbar_arrive(&epi_sync[buf]);
+      if (!mbar_wait(&epi_sync[buf], tph, abort_flag, kTag, 5)) break;
+      if (!mbar_wait(&tfull[buf], tph, abort_flag, kTag, 4)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) +
+                             static_cast<uint32_t>(buf * C::ACC_COLS + half * COLS);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int n0 = nb * BN + c * 32;
+      for (int c = 0; c < COLS; c += 64) {
+        const int n0 = nb * BN + half * COLS + c;
         if (n0 >= p.N) break;  // warp-uniform
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        uint32_t r0[32], r1[32];
+        const bool two = (COLS - c) >= 64;
+        tmem_ld_32x32b_x32(taddr + c, r0);
+        if (two) tmem_ld_32x32b_x32(taddr + c + 32, r1);
         tmem_ld_wait();
-        if (m < p.M) epilogue_chunk<KIND>(r, p, m, n0, sa);
+        if (m < p.M) {
+          const int j0 = half * COLS + c;
+          epilogue_chunk<KIND>(r0, p, m, n0, sa, sb_t + j0, bias_t + j0);
+          if (two && n0 + 32 < p.N) epilogue_chunk<KIND>(r1, p, m, n0 + 32, sa, sb_t + j0 + 32, bias_t + j0 + 32);
+        }
       }
       tc_fence_before();
       mbar_arrive(&tempty[buf]);

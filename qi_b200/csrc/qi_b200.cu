@@ -115,7 +115,7 @@ static int launch_gemm_cfg(const void* A, const void* B, const EpiParams& p, int
   }
   const int tiles = ((p.M + C::BM - 1) / C::BM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < num_sms ? tiles : num_sms;
-  k_gemm_tc<KIND, BN, STAGES><<<grid, 256, C::SMEM_BYTES, stream>>>(ta, tb, p);
+  k_gemm_tc<KIND, BN, STAGES><<<grid, kGemmThreads, C::SMEM_BYTES, stream>>>(ta, tb, p);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 

@@ -128,10 +128,10 @@ def gemm(kind: int, a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor | No
 
 
 def int8_linear(x_bf16_2d: torch.Tensor, qweight: torch.Tensor, weight_scales: torch.Tensor,
-                bias: torch.Tensor | None = None) -> torch.Tensor:
+                bias: torch.Tensor | None = None, gelu: bool = False) -> torch.Tensor:
     """Same contract as the reference torch op
     ``qi_int8_w8a8::linear(Tensor x_bf16_2d, Tensor qweight, Tensor weight_scales, Tensor? bias)``
-    (``bindings.cpp:87-165``)."""
+    (``bindings.cpp:87-165``); ``gelu`` additionally fuses GELU(tanh) into the epilogue."""
     _check(x_bf16_2d, "x_bf16_2d", torch.bfloat16, 2)
     dev = x_bf16_2d.device
     _check(qweight, "qweight", torch.int8, 2, dev)
@@ -148,6 +148,9 @@ def int8_linear(x_bf16_2d: torch.Tensor, qweight: torch.Tensor, weight_scales: t
             raise ValueError("bias length must match qweight N dimension.")
     ws_q = torch.empty((M, K), dtype=torch.int8, device=dev)
     ws_s = torch.empty((M,), dtype=torch.float32, device=dev)
+    if gelu:
+        quantize_int8_rowwise(x_bf16_2d, ws_q, ws_s)
+        return gemm(_lib.KIND_INT8, ws_q, qweight, ws_s, weight_scales, bias, gelu=True)
     out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
     _lib.call("qi_b200_int8_linear", _ptr(x_bf16_2d), _ptr(qweight), _ptr(weight_scales), _ptr(bias),
               _ptr(out), _ptr(ws_q), _ptr(ws_s), M, N, K, _stream(dev))

@@ -189,3 +189,31 @@ def test_bf16_gemm_vs_fp64(M, N, Kd):
     y = K.gemm(_lib.KIND_BF16, a.to(DEV), b.to(DEV), None, None)
     ref = a.double() @ b.double().T
     assert O.rel_fro(y.float().cpu().numpy(), ref.numpy()) <= 5e-3
+
+
+# --------------------------------------------------------------------------
+# CUDA-graph capture (the reference runs its DiT under CUDA graphs by default)
+# --------------------------------------------------------------------------
+
+def test_linears_capture_in_cuda_graph_and_replay():
+    x, w, b = make_small_case(64, 512, 1024, seed=21)
+    qw, sw, _ = O.quantize_weight_rtn(w.numpy(), 8, -1, True)
+    fq, fs = O.quantize_fp8_rowwise(w.numpy())
+    qw_d, sw_d = torch.from_numpy(qw).to(DEV), torch.from_numpy(sw[:, 0]).contiguous().to(DEV)
+    fq_d, fs_d, b_d = torch.from_numpy(fq).to(DEV), torch.from_numpy(fs).to(DEV), b.to(DEV)
+    x_static = x.to(DEV)
+    # warm up outside capture (first-call host state: attributes, descriptors)
+    K.int8_linear(x_static, qw_d, sw_d, b_d)
+    K.fp8_linear(x_static, fq_d, fs_d, None, b_d, gelu=True)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        y8 = K.int8_linear(x_static, qw_d, sw_d, b_d)
+        yf = K.fp8_linear(x_static, fq_d, fs_d, None, b_d, gelu=True)
+    x2, _, _ = make_small_case(64, 512, 1024, seed=22)
+    x_static.copy_(x2.to(DEV))
+    g.replay()
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(bits(y8), O.int8_linear(bits(x2), qw, sw[:, 0], bits(b))[0])
+    qa, sa = O.quantize_fp8_rowwise(O.bf16_to_f32(bits(x2)))
+    assert O.rel_fro(O.bf16_to_f32(bits(yf)), O.bf16_to_f32(O.fp8_linear(qa, sa, fq, fs, bits(b), gelu=True))) <= 2e-3
