@@ -113,6 +113,32 @@ int qi_b200_fp8_linear(const void* x_bf16, const void* weight_fp8, const float* 
                        void* out_bf16, void* ws_q, float* ws_scales, int M, int N, int K, int flags,
                        cudaStream_t stream);
 
+/* ---- INT8 linear that allocates nothing --------------------------------
+ * No counterpart in the reference.  Same result as qi_b200_int8_linear (same
+ * kernels, bit-identical output), for callers that cannot provide or
+ * allocate scratch memory: hosts that pass the library only the layer's
+ * input and output (an FFI plugin inside a runtime that owns all device
+ * memory), or real-time loops where cudaMalloc's implicit device-wide
+ * synchronization is not allowed.
+ *
+ * The quantized activations go to fixed scratch arrays inside the library's
+ * device image (one copy per device that loads the library, resident until
+ * the process exits): at most QI_B200_NOALLOC_MAX_ROWS rows and
+ * QI_B200_NOALLOC_MAX_ACT_BYTES activation elements (M*K); larger calls
+ * return QI_B200_ETOOBIG and enqueue nothing.
+ *
+ * The first call on a device looks up the scratch arrays' device addresses
+ * (and may make the CUDA runtime load the library's device code); make that
+ * first call before any stream capture.  All calls on a device share the
+ * scratch: calls whose kernels can overlap on the GPU race and may return
+ * wrong results, so issue them on one stream (or otherwise order them).
+ * Nothing needs clearing between calls: every scratch byte a call reads is
+ * first written by that call. */
+#define QI_B200_NOALLOC_MAX_ROWS 16384
+#define QI_B200_NOALLOC_MAX_ACT_BYTES (8 * 1024 * 1024)
+int qi_b200_int8_linear_noalloc(const void* x_bf16, const void* qweight, const float* weight_scale,
+                                const void* bias, void* out_bf16, int M, int N, int K, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

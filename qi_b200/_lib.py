@@ -48,6 +48,7 @@ SIGNATURES = {
     "qi_b200_gemm": [_I, _P, _P, _P, _I, _P, _I, _P, _P, _LL, _I, _I, _I, _I, _I, _P],
     "qi_b200_int8_linear": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "qi_b200_fp8_linear": [_P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "qi_b200_int8_linear_noalloc": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
 }
 _RESTYPES = {"qi_b200_error_string": ctypes.c_char_p}
 

@@ -307,3 +307,76 @@ int qi_b200_fp8_linear(const void* x_bf16, const void* weight_fp8, const float* 
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// INT8 linear without caller-provided workspace.
+//
+// qi_b200_int8_linear needs scratch for the quantized activations (int8
+// [M,K] + fp32 [M]).  Some callers cannot obtain it: a host that hands this
+// library only the layer's input and output buffers (an FFI plugin inside a
+// runtime that owns all device memory, or a real-time control loop where
+// cudaMalloc's implicit device-wide synchronization would stall the control
+// thread).  For them the scratch lives in fixed arrays in this library's
+// device image, so a call allocates nothing.
+//
+// The arrays exist once per device that loads the library and stay resident
+// until the process exits.  All calls on a device share them: two calls whose
+// kernels overlap on the GPU (different streams without ordering between
+// them) race on the scratch and may produce wrong results; serialize them on
+// one stream.  The quantize kernel overwrites every scratch byte a call reads
+// before it is read, so nothing needs clearing between calls.
+// ===========================================================================
+namespace qib {
+
+static __device__ __align__(256) int8_t g_noalloc_q[QI_B200_NOALLOC_MAX_ACT_BYTES];
+static __device__ __align__(256) float g_noalloc_scales[QI_B200_NOALLOC_MAX_ROWS];
+
+struct NoAllocScratch {
+  int ready = 0;
+  void* q = nullptr;
+  float* scales = nullptr;
+};
+static NoAllocScratch g_noalloc[kMaxDevices];
+static std::mutex g_noalloc_mu;
+
+// Device addresses of the scratch arrays for the current device.  In host
+// code the array names are host-side shadows, not device addresses, so the
+// addresses are looked up once per device (with that device current) and
+// cached.  The first lookup may make the CUDA runtime load this library's
+// device code onto the device.
+static int noalloc_scratch(void** q, float** scales) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QI_B200_ECUDA;
+  NoAllocScratch& e = g_noalloc[dev];
+  if (!e.ready) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!e.ready) {
+      void* pq = nullptr;
+      void* ps = nullptr;
+      if (cudaGetSymbolAddress(&pq, g_noalloc_q) != cudaSuccess) return QI_B200_ECUDA;
+      if (cudaGetSymbolAddress(&ps, g_noalloc_scales) != cudaSuccess) return QI_B200_ECUDA;
+      e.q = pq;
+      e.scales = static_cast<float*>(ps);
+      e.ready = 1;
+    }
+  }
+  *q = e.q;
+  *scales = e.scales;
+  return QI_B200_OK;
+}
+
+}  // namespace qib
+
+extern "C" int qi_b200_int8_linear_noalloc(const void* x_bf16, const void* qweight, const float* weight_scale,
+                                           const void* bias, void* out_bf16, int M, int N, int K,
+                                           cudaStream_t stream) {
+  if (M == 0) return QI_B200_OK;
+  if (M < 0 || K <= 0) return QI_B200_ESHAPE;
+  if (M > QI_B200_NOALLOC_MAX_ROWS || static_cast<long long>(M) * K > QI_B200_NOALLOC_MAX_ACT_BYTES)
+    return QI_B200_ETOOBIG;
+  void* q = nullptr;
+  float* scales = nullptr;
+  int rc = noalloc_scratch(&q, &scales);
+  if (rc) return rc;
+  return qi_b200_int8_linear(x_bf16, qweight, weight_scale, bias, out_bf16, q, scales, M, N, K, stream);
+}
