@@ -33,12 +33,17 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from qi_b200.synthetic import CFG_FP8, CFG_INT8, make_linear_inputs  # noqa: E402
+from qi_b200.synthetic import CFG_FP8, CFG_INT8, CFG_NVFP4, CFG_W4A16, make_linear_inputs  # noqa: E402
 
 CONFIGS = {
     "fp8": dict(case=CFG_FP8, kind="fp8", gelu=True, dtype="fp8_e4m3 (fp32 accumulate)"),
     "int8": dict(case=CFG_INT8, kind="int8", gelu=False, dtype="int8 (int32 accumulate)"),
+    "nvfp4": dict(case=CFG_NVFP4, kind="nvfp4", gelu=False,
+                  dtype="nvfp4 e2m1 + e4m3 block16 scales (fp32 accumulate)"),
 }
+for _m in (1, 16, 256, 4096):
+    CONFIGS[f"w4a16_m{_m}"] = dict(case=CFG_W4A16[_m], kind="w4a16", gelu=False, group=128,
+                                   dtype="bf16 x int4-g128 (fp32 accumulate)")
 L2_BYTES = 126 * 2**20
 
 
@@ -137,10 +142,18 @@ def build_layer(cfg_name: str, w_shard: torch.Tensor, b_shard: torch.Tensor, dev
     from qi_b200.quantization.backends import get_backend
     from qi_b200.quantization.quantize import quantize_linear_weight
 
+    from qi_b200.quantization import WeightOnlyQuantConfig
+
     c = CONFIGS[cfg_name]
     if c["kind"] == "fp8":
         qcfg = WeightActivationQuantConfig(enabled=True, algo="rtn", quant_dtype="fp8", backend="b200",
                                            activation_granularity="per_token", weight_granularity="per_channel")
+    elif c["kind"] == "w4a16":
+        qcfg = WeightOnlyQuantConfig(enabled=True, algo="rtn", bits=4, group_size=c["group"], symmetric=False,
+                                     backend="b200")
+    elif c["kind"] == "nvfp4":
+        qcfg = WeightActivationQuantConfig(enabled=True, algo="rtn", quant_dtype="nvfp4", bits=4,
+                                           activation_bits=4, backend="b200")
     else:
         qcfg = WeightActivationQuantConfig(enabled=True, algo="rtn", quant_dtype="int", backend="b200",
                                            activation_granularity="per_token", weight_granularity="per_channel")
@@ -174,12 +187,19 @@ def run_ours(args):
     w_shard, b_shard = w_cpu[rank * Nl:(rank + 1) * Nl], b_cpu[rank * Nl:(rank + 1) * Nl]
 
     layer = build_layer(args.config, w_shard, b_shard, device)
-    kind = _lib.KIND_FP8_E4M3 if c["kind"] == "fp8" else _lib.KIND_INT8
-    wq = layer.weight_fp8 if c["kind"] == "fp8" else layer.qweight
-    ws = layer.weight_scale if c["kind"] == "fp8" else layer.scales[:, 0].contiguous()
+    kind = {"fp8": _lib.KIND_FP8_E4M3, "int8": _lib.KIND_INT8, "w4a16": None, "nvfp4": None}[c["kind"]]
+    if c["kind"] == "fp8":
+        wq, ws = layer.weight_fp8, layer.weight_scale
+    elif c["kind"] == "int8":
+        wq, ws = layer.qweight, layer.scales[:, 0].contiguous()
+    elif c["kind"] == "nvfp4":
+        wq, ws = layer.qweight_packed, layer.weight_global_scale
+    else:
+        wq, ws = layer.qweight_packed, None
+        wq_bytes = wq.numel() * 4 + layer.scale_factors.numel() * 2 + layer.zeros.numel() * 4
 
     # rotate input copies so consecutive steps touch more distinct bytes than L2
-    per_copy = x_cpu.numel() * 2 + wq.numel()
+    per_copy = x_cpu.numel() * 2 + wq.numel() * wq.element_size()
     ncopy = max(2, -(-3 * L2_BYTES // per_copy))
     xs = [x_cpu.to(device) for _ in range(ncopy)]
     wqs = [wq.clone() for _ in range(ncopy)]
@@ -188,14 +208,26 @@ def run_ours(args):
     stream = torch.cuda.current_stream(device)
 
     quant = K.quantize_fp8_rowwise if c["kind"] == "fp8" else K.quantize_int8_rowwise
+    # kernels per step: w4a16 1; nvfp4 3 (amax, quantize, GEMM; plus a 4-byte memset); int8/fp8 2
+    launches_per_step = {"w4a16": 1, "nvfp4": 3}.get(c["kind"], 2)
 
     def step(i, ev=None):
         x, w = xs[i % ncopy], wqs[i % ncopy]
-        q, s = quant(x)
         cur = torch.cuda.current_stream(device)  # the capture stream inside torch.cuda.graph
-        if ev is not None:
-            ev[0].record(cur)
-        y = K.gemm(kind, q, w, s, ws, bias, gelu=c["gelu"])
+        if c["kind"] == "w4a16":
+            if ev is not None:
+                ev[0].record(cur)
+            y = K.w4a16_linear(x, w, layer.scale_factors, layer.zeros, c["group"], bias)
+        elif c["kind"] == "nvfp4":
+            qa, sfa, ga = K.quantize_nvfp4(x, K.NVFP4_DYNAMIC_TENSOR)
+            if ev is not None:
+                ev[0].record(cur)
+            y = K.nvfp4_gemm(qa, sfa, w, layer.scale_factors, ga, ws, bias)
+        else:
+            q, s = quant(x)
+            if ev is not None:
+                ev[0].record(cur)
+            y = K.gemm(kind, q, w, s, ws, bias, gelu=c["gelu"])
         if ev is not None:
             ev[1].record(cur)
         if world > 1:
@@ -283,30 +315,52 @@ def run_ours(args):
     h2d = x_host.numel() * 2
     d2h = y_host.numel() * 2
 
-    # ---- roofline of the dominant kernel (the GEMM) against the dtype's dense peak
+    # ---- roofline of the dominant kernel (the GEMM)
     hbm_gbs, bf16_tf, src = peaks()
     gemm_flops_launch = 2.0 * M * Nl * Kd
-    achieved = gemm_flops_launch / (gemm_ms * 1e-3) / 1e12
-    peak = 2.0 * bf16_tf  # 8-bit tensor-core rate is 2x the bf16 rate on B200
     traffic = load_traffic(args.config, world)
-    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4), "traffic": traffic,
-                "peak_source": f"2 x bf16 dense, {src}", "kernel": f"k_gemm_tc<{c['kind']}>",
-                "kernel_ms": round(gemm_ms, 5), "kernel_timing": gemm_src}
+    if c["kind"] == "w4a16":
+        alg_bytes = wq_bytes + Nl * 2 + M * Kd * 2 + M * Nl * 2
+        hbm_bound = M <= 16
+    elif c["kind"] == "nvfp4":
+        # GEMM operands: packed A and B, their block scales, bias, bf16 output
+        alg_bytes = (M + Nl) * Kd // 2 + (M + Nl) * Kd // 16 + Nl * 2 + M * Nl * 2
+        hbm_bound = False
+    else:
+        alg_bytes = wq.numel() + Nl * 8 + M * Kd + M * 4 + M * Nl * 2
+        hbm_bound = False
+    if hbm_bound:
+        achieved = alg_bytes / (gemm_ms * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_gbs, "unit": "GB/s",
+                    "frac": round(achieved / hbm_gbs, 4), "traffic": traffic, "algorithmic_bytes": alg_bytes,
+                    "peak_source": src}
+    else:
+        achieved = gemm_flops_launch / (gemm_ms * 1e-3) / 1e12
+        # dense tensor rate relative to bf16 on B200: 8-bit 2x, fp4 4x
+        mult = {"w4a16": 1.0, "nvfp4": 4.0}.get(c["kind"], 2.0)
+        peak = mult * bf16_tf
+        roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                    "frac": round(achieved / peak, 4), "traffic": traffic, "algorithmic_bytes": alg_bytes,
+                    "peak_source": f"{mult:g} x bf16 dense, " + src}
+    roofline.update({"kernel": "k_gemm_w4a16" if c["kind"] == "w4a16" else f"k_gemm_tc<{c['kind']}>",
+                     "kernel_ms": round(gemm_ms, 5), "kernel_timing": gemm_src})
 
     result = {
         "metric": "quantized_gemm_tops", "value": round(value, 2), "unit": "TOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": c["dtype"], "data": "synthetic (seeded, BASELINE shapes)",
         "config": {"workload": case.name, "M": M, "N": N, "K": Kd, "bias": True, "gelu": c["gelu"],
-                   "act_quant": "per_token", "weight_quant": "per_channel",
+                   "act_quant": {"w4a16": "none (bf16)",
+                                 "nvfp4": "nvfp4 block16, dynamic per-tensor global scale"}.get(c["kind"], "per_token"),
+                   "weight_quant": {"w4a16": "int4 asym g128 packed",
+                                    "nvfp4": "nvfp4 block16 + per-tensor global scale"}.get(c["kind"], "per_channel"),
                    "parallelism": f"N-shard x{world} + NCCL all_gather" if world > 1 else "single GPU",
                    "launch": "cuda_graph" if use_graph else "eager",
                    "l2": f"{ncopy} rotating input copies ({ncopy * per_copy / 2**20:.0f} MiB > L2)"},
         "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
                 "api": "qi_b200.quantization.WeightOnlyLinear.forward"},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": launches_per_step * args.steps,
         "roofline": roofline,
         "clocks": clk.summary(),
     }
@@ -362,7 +416,16 @@ def _cpu_sample(cfg_name: str):
     x, w, b = make_linear_inputs(case)
     rows = min(case.M, 512 if c["kind"] == "int8" else 256)
     xs = x[:rows].contiguous()
-    if c["kind"] == "int8":
+    if c["kind"] == "nvfp4":
+        from qi_b200.quantization.quantize import quantize_nvfp4
+        wp, wsf, wg = quantize_nvfp4(w)
+        fn = lambda: RP.nvfp4_linear_port(xs, wp, wsf, wg, b)
+        desc = f"dequantise-then-F.linear NVFP4 port (per-tensor fake-quant, fp32 compute), {rows} of {case.M} rows"
+    elif c["kind"] == "w4a16":
+        qw, sw, zw = quantize_weight_rtn(w, 4, c["group"], False)
+        fn = lambda: RP.reference_linear(xs, qw, sw, zw, b, 4, c["group"], False)
+        desc = f"ReferenceBackend.linear port (bf16 input, int4 g{c['group']} dequant loop, F.linear), {rows} of {case.M} rows"
+    elif c["kind"] == "int8":
         qw, sw, _ = quantize_weight_rtn(w, 8, -1, True)
         fn = lambda: RP.reference_linear(xs, qw, sw, None, b, 8, -1, True, activation_granularity="per_token")
         desc = f"ReferenceBackend.linear port (bf16 input, per-token int8 fake-quant, dequant loop, F.linear), {rows} of {case.M} rows"

@@ -57,6 +57,12 @@ const char* qi_b200_error_string(int code);
  * inside stream capture.  clear != 0 resets it. */
 int qi_b200_device_status(unsigned int* out4, int clear);
 
+/* Launch plan of the calling thread's most recent GEMM launch, for
+ * diagnostics: out6 = {kernel (1 int8, 2 fp8, 3 bf16, 4 nvfp4, 5 w4a16 tiles,
+ * 6 w4a16 split-K clusters), grid, cluster size, tile N (or padded M for
+ * kernel 6), pipeline stages, dynamic shared memory bytes}. */
+int qi_b200_last_launch(int* out6);
+
 /* ---- activation quantizers --------------------------------------------
  * Replaces qi_quantize_int8_rowwise (csrc/int8_w8a8/quantize_int8.cuh:7-13,
  * kernel quantize_int8.cu:7-59): per row s = max(amax/127, 1e-10),
@@ -95,6 +101,46 @@ int qi_b200_int8_rowwise_bf16out_bias(const void* A, const void* B, const void* 
 int qi_b200_gemm(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
                  const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd, int M, int N,
                  int K, int flags, int tile_n, cudaStream_t stream);
+
+/* ---- W4A16 (INT4 weight-only) ----------------------------------------
+ * Replaces the weight-only INT4 path of ReferenceBackend.linear
+ * (backends/reference.py:48-91, dequantize_weight at quantize.py:81-119) and
+ * the reserved CudaExtBackend (backends/reference.py:94-96):
+ *   out[M,N] = bf16( x_bf16 . W^T + bias ),  W[n,k] = bf16( (q[n,k] - z[n,g]) * s[n,g] )
+ * qweight_packed int32 [N, K/8] (element 8w+j in bits 4j..4j+3 of word w),
+ * scales_fp16 [N, G], zeros_packed int32 [N, ceil(G/8)] (uint4, group g in
+ * word g/8 nibble g%8), G = ceil(K / group_size); group_size <= 0 means one
+ * group per row.  Needs K % 32 == 0, N % 8 == 0, group_size % 32 == 0.
+ * M <= 256 runs a split-K kernel over a thread-block cluster. */
+int qi_b200_w4a16_linear(const void* x_bf16, const void* qweight_packed, const void* scales_fp16,
+                         const void* zeros_packed, int group_size, const void* bias, void* out_bf16, int M, int N,
+                         int K, cudaStream_t stream);
+
+/* ---- NVFP4 W4A4 (no counterpart in the reference, which only names the
+ * buffers qweight_packed / scale_factors / weight_global_scale at
+ * src/qi/quantization/modules.py:21-23) ------------------------------------
+ * Values E2M1 (two per byte, element 2j in the low nibble); E4M3 scale per 16
+ * elements along K in the scale-factor atom layout (512-byte atoms of 128 rows
+ * x 4 scales, atoms K-fastest, row r0 + 32 r1 at byte r0*16 + r1*4 + j; rows
+ * padded to a multiple of 128); fp32 second-level scale g.
+ *   g = max(amax / 2688, 1e-12); sf = e4m3(min(amax16 / (6 g), 448));
+ *   q = e2m1(clamp(x / (sf g), +-6)).
+ * Activation quantization, g_mode: 0 = static per-tensor g (g_in), 1 =
+ * dynamic per-tensor (two passes; ws_amax is one uint32 of scratch; g_out[0]),
+ * 2 = dynamic per-row (g_out[rows]).  cols % 64 == 0. */
+int qi_b200_quantize_nvfp4(const void* x_bf16, int rows, int cols, int g_mode, const float* g_in,
+                           unsigned int* ws_amax, float* g_out, void* q_packed, void* sf_atoms, cudaStream_t stream);
+/* D = bf16( (acc * a_g[m or 0]) * b_g[0] + bias ), acc = sum over 16-blocks of
+ * (q_a q_b) sf_a sf_b on tcgen05 kind::mxf4nvf4 (block16).  K % 256 == 0. */
+int qi_b200_nvfp4_gemm(const void* A_packed, const void* A_sf, const void* B_packed, const void* B_sf,
+                       const float* a_global_scale, int a_scale_per_row, const float* b_global_scale,
+                       const void* bias, void* D, long long ldd, int M, int N, int K, int flags, cudaStream_t stream);
+/* Quantize x (act_scale_mode as g_mode above) into the caller's workspace
+ * (ws_q [M, K/2], ws_sf atoms, ws_g [1 or M], ws_amax [1]) then the GEMM. */
+int qi_b200_nvfp4_linear(const void* x_bf16, const void* weight_packed, const void* weight_sf,
+                         const float* weight_global_scale, int act_scale_mode, const float* act_global_scale,
+                         const void* bias, void* out_bf16, void* ws_q, void* ws_sf, float* ws_g,
+                         unsigned int* ws_amax, int M, int N, int K, int flags, cudaStream_t stream);
 
 /* ---- whole quantized linears -----------------------------------------
  * Replaces the torch op qi_int8_w8a8::linear (csrc/int8_w8a8/bindings.cpp:

@@ -372,13 +372,14 @@ def nvfp4_dequant(nib, sf, g) -> np.ndarray:
 
 
 def nvfp4_linear(qa_nib, sfa, ga, qw_nib, sfw, gw, bias_bf16=None):
-    """y = bf16( sum_blocks (sum q_a q_w) sf_a sf_w * (g_a g_w) + bias ).
-    The block sums are exact in float64; the tensor scales are applied in
-    fp32 in the epilogue as the kernel does."""
+    """y = bf16( (acc * g_a) * g_w + bias ), acc = sum_blocks (sum q_a q_w) sf_a sf_w
+    (exact in float64, rounded to fp32); g_a is one scale per tensor or per
+    row, g_w per tensor; the epilogue multiplies in fp32 in that order."""
     a = nvfp4_dequant(qa_nib, sfa, 1.0)
     w = nvfp4_dequant(qw_nib, sfw, 1.0)
     acc = (a @ w.T).astype(np.float32)
-    y = acc * (F32(ga) * F32(gw))
+    ga = np.asarray(ga, np.float32).reshape(-1, 1)
+    y = (acc * ga) * np.asarray(gw, np.float32).reshape(1, -1)
     if bias_bf16 is not None:
         y = y + bf16_to_f32(bias_bf16)[None, :]
     return f32_to_bf16(y)

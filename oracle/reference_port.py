@@ -70,3 +70,27 @@ def fp8_linear_port(x_bf16, weight_fp8_u8, weight_scale, bias=None, gelu=False):
     if gelu:
         y = F.gelu(y.float(), approximate="tanh").to(torch.bfloat16)
     return y
+
+
+_E2M1 = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0])
+
+
+def _nvfp4_dequant(packed_u8, sf_u8_rowmajor, g):
+    """[R, K/2] packed E2M1 + [R, K/16] E4M3 scales + fp32 g -> fp32 [R, K]."""
+    lo = _E2M1[(packed_u8 & 0xF).long()]
+    hi = _E2M1[(packed_u8 >> 4).long()]
+    v = torch.stack([lo, hi], dim=-1).reshape(packed_u8.shape[0], -1)
+    s = sf_u8_rowmajor.view(torch.float8_e4m3fn).float().repeat_interleave(16, dim=1)
+    return v * s * g.float()
+
+
+def nvfp4_linear_port(x_bf16, w_packed, w_sf_rowmajor, w_g, bias=None):
+    """NVFP4 W4A4 linear in the reference's style: fake-quantise the
+    activation (per-tensor global scale), dequantise the weight, ``F.linear``
+    in fp32, bf16 out."""
+    from qi_b200.quantization.quantize import quantize_nvfp4
+
+    xp, xsf, xg = quantize_nvfp4(x_bf16.float())
+    xq = _nvfp4_dequant(xp, xsf, xg)
+    w = _nvfp4_dequant(w_packed, w_sf_rowmajor, w_g)
+    return F.linear(xq, w, None if bias is None else bias.float()).to(torch.bfloat16)

@@ -40,6 +40,7 @@ SIGNATURES = {
     "qi_b200_abi_version": [],
     "qi_b200_error_string": [_I],
     "qi_b200_device_status": [_P, _I],
+    "qi_b200_last_launch": [_P],
     "qi_b200_quantize_int8_rowwise": [_P, _P, _P, _I, _I, _P],
     "qi_b200_quantize_fp8_rowwise": [_P, _P, _P, _I, _I, _P],
     "qi_b200_quantize_fp8_static": [_P, _P, _P, _I, _I, _P],
@@ -49,6 +50,10 @@ SIGNATURES = {
     "qi_b200_int8_linear": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "qi_b200_fp8_linear": [_P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qi_b200_int8_linear_noalloc": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
+    "qi_b200_w4a16_linear": [_P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _P],
+    "qi_b200_quantize_nvfp4": [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P],
+    "qi_b200_nvfp4_gemm": [_P, _P, _P, _P, _P, _I, _P, _P, _P, _LL, _I, _I, _I, _I, _P],
+    "qi_b200_nvfp4_linear": [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
 }
 _RESTYPES = {"qi_b200_error_string": ctypes.c_char_p}
 
@@ -92,6 +97,16 @@ def check(fn_name: str, rc: int) -> None:
 def call(fn_name: str, *args) -> None:
     """Call a C-ABI entry point and raise on a non-zero status."""
     check(fn_name, getattr(load(), fn_name)(*args))
+
+
+def last_launch() -> dict:
+    """Plan of this thread's most recent GEMM launch (see qi_b200_last_launch)."""
+    buf = (ctypes.c_int * 6)()
+    check("qi_b200_last_launch", load().qi_b200_last_launch(ctypes.cast(buf, _P)))
+    names = {1: "gemm_int8", 2: "gemm_fp8", 3: "gemm_bf16", 4: "gemm_nvfp4", 5: "w4a16_tiles", 6: "w4a16_splitk"}
+    v = list(buf)
+    return {"kernel": names.get(v[0], "none"), "grid": v[1], "cluster": v[2], "tile_n": v[3], "stages": v[4],
+            "smem": v[5]}
 
 
 def device_status(clear: bool = False) -> tuple[int, int, int, int]:

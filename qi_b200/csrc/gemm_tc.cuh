@@ -29,7 +29,7 @@
 
 namespace qib {
 
-enum class MmaKind : int { I8 = 0, F8 = 1, BF16 = 2 };
+enum class MmaKind : int { I8 = 0, F8 = 1, BF16 = 2, NVF4 = 3 };
 
 // epilogue flags
 constexpr int kEpiGelu = 1;     // GELU(tanh) of the bf16-rounded linear output
@@ -51,6 +51,11 @@ struct EpiParams {
   long long ldd;
   int M, N, K;
   int flags;
+  // NVFP4 only: block-scale atoms of A and B (see quantize_nvfp4.cuh) and
+  // the number of 4-scale atoms per 128-row block (= K / 64)
+  const uint8_t* sfa;
+  const uint8_t* sfb;
+  int sf_ka;
 };
 
 template <MmaKind KIND, int BN_, int STAGES_>
@@ -58,23 +63,31 @@ struct GemmCfg {
   static constexpr int BM = 128;
   static constexpr int BN = BN_;
   static constexpr int STAGES = STAGES_;
-  static constexpr int ELEM = (KIND == MmaKind::BF16) ? 2 : 1;
+  static constexpr bool NVF4 = (KIND == MmaKind::NVF4);
+  static constexpr int ELEM = (KIND == MmaKind::BF16) ? 2 : 1;    // bytes per TMA element (fp4: packed bytes)
   static constexpr int BK = 128 / ELEM;                          // one 128-B swizzle row per operand row
-  static constexpr int UMMA_K = (KIND == MmaKind::BF16) ? 16 : 32;  // 32 bytes of K per MMA
+  static constexpr int UMMA_K = (KIND == MmaKind::BF16) ? 16 : 32;  // 32 bytes of K per MMA (64 fp4)
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BN * 128;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  // NVFP4: per stage (256 K elements) 4 scale atoms for A, 4 x BN/128 for B
+  static constexpr int SFA_BYTES = NVF4 ? 4 * 512 : 0;
+  static constexpr int SFB_BYTES = NVF4 ? 4 * 512 * (BN / 128) : 0;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
   static constexpr int ACC_COLS = BN;  // fp32/s32 accumulator: one TMEM column per output column
-  static constexpr int TMEM_COLS = (2 * ACC_COLS <= 32) ? 32 : (2 * ACC_COLS <= 64) ? 64 : (2 * ACC_COLS <= 128) ? 128 : (2 * ACC_COLS <= 256) ? 256 : 512;
+  static constexpr int SF_COLS = NVF4 ? 4 * 4 + 4 * (BN / 32) : 0;  // scale factors in TMEM
+  static constexpr int TMEM_NEED = 2 * ACC_COLS + SF_COLS;
+  static constexpr int TMEM_COLS = (TMEM_NEED <= 32) ? 32 : (TMEM_NEED <= 64) ? 64 : (TMEM_NEED <= 128) ? 128 : (TMEM_NEED <= 256) ? 256 : 512;
   static constexpr int COLPARAM_BYTES = 2 * BN * (4 + 2);  // double-buffered column scales + bias
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + COLPARAM_BYTES + BAR_BYTES + 1024;  // + alignment slack
   static constexpr uint32_t IDESC =
       (KIND == MmaKind::I8)   ? make_idesc(kDS32, kFmtS8, kFmtS8, BM, BN)
       : (KIND == MmaKind::F8) ? make_idesc(kDF32, kFmtE4M3, kFmtE4M3, BM, BN)
+      : (KIND == MmaKind::NVF4) ? make_idesc_nvf4(BM, BN)
                               : make_idesc(kDF32, kFmtBF16, kFmtBF16, BM, BN);
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
-  static_assert(2 * ACC_COLS <= 512, "TMEM");
+  static_assert(TMEM_NEED <= 512, "TMEM");
+  static_assert(!NVF4 || BN == 128, "NVFP4 tiles are 128 x 128");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
@@ -102,7 +115,7 @@ template <MmaKind KIND>
 __device__ __forceinline__ void mma_issue(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   if constexpr (KIND == MmaKind::I8) mma_i8(d, a, b, idesc, acc);
   else if constexpr (KIND == MmaKind::F8) mma_f8(d, a, b, idesc, acc);
-  else mma_bf16(d, a, b, idesc, acc);
+  else if constexpr (KIND == MmaKind::BF16) mma_bf16(d, a, b, idesc, acc);
 }
 
 // Epilogue for one 32-column chunk of one row (this thread's row).  Column
@@ -180,8 +193,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint8_t* sSFA = sB + STAGES * C::B_BYTES;      // NVFP4 only
+  uint8_t* sSFB = sSFA + STAGES * C::SFA_BYTES;  // NVFP4 only
   // per-tile column parameters, double buffered: [2][BN] fp32 scales, [2][BN] bf16 bias
-  float* col_scale = reinterpret_cast<float*>(sB + STAGES * C::B_BYTES);
+  float* col_scale = reinterpret_cast<float*>(sSFB + STAGES * C::SFB_BYTES);
   __nv_bfloat16* col_bias = reinterpret_cast<__nv_bfloat16*>(col_scale + 2 * BN);
   uint64_t* full = reinterpret_cast<uint64_t*>(col_bias + 2 * BN);
   uint64_t* empty = full + STAGES;
@@ -226,7 +241,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
   const int m_tiles = (p.M + C::BM - 1) / C::BM;
   const int n_tiles = (p.N + BN - 1) / BN;
   const int num_tiles = m_tiles * n_tiles;
-  const int k_blocks = (p.K + C::BK - 1) / C::BK;
+  const int k_units = C::NVF4 ? p.K / 2 : p.K;  // K in TMA elements
+  const int k_blocks = (k_units + C::BK - 1) / C::BK;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -242,6 +258,13 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
           mbar_expect_tx(&full[stage], C::STAGE_BYTES);
           tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * C::BK, mb * C::BM);
           tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * C::BK, nb * BN);
+          if constexpr (C::NVF4) {
+            // the stage's 4 scale atoms are contiguous per 128-row block
+            bulk_load(sSFA + stage * C::SFA_BYTES, p.sfa + (static_cast<long long>(mb) * p.sf_ka + kb * 4) * 512,
+                      C::SFA_BYTES, &full[stage]);
+            bulk_load(sSFB + stage * C::SFB_BYTES, p.sfb + (static_cast<long long>(nb) * p.sf_ka + kb * 4) * 512,
+                      C::SFB_BYTES, &full[stage]);
+          }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -275,11 +298,28 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
           const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
+          if constexpr (C::NVF4) {
+            // scale factors -> TMEM (in issue order with the MMAs that read them)
+            const uint32_t tsfa = tmem_base + 2 * C::ACC_COLS;
+            const uint32_t tsfb = tsfa + 16;
+            const uint32_t sfa0 = smem_u32(sSFA + stage * C::SFA_BYTES);
+            const uint32_t sfb0 = smem_u32(sSFB + stage * C::SFB_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk) {
-            const uint64_t ad = sw128_kmajor_desc(a0 + kk * 32);
-            const uint64_t bd = sw128_kmajor_desc(b0 + kk * 32);
-            mma_issue<KIND>(d_tmem, ad, bd, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk) {
+              tc_cp_32x128b_warpx4(tsfa + 4 * kk, sf_atom_desc(sfa0 + kk * 512));
+              tc_cp_32x128b_warpx4(tsfb + 4 * kk, sf_atom_desc(sfb0 + kk * 512));
+            }
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_nvf4(d_tmem, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32), C::IDESC,
+                       tsfa + 4 * kk, tsfb + 4 * kk, (kb | kk) != 0 ? 1u : 0u);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk) {
+              const uint64_t ad = sw128_kmajor_desc(a0 + kk * 32);
+              const uint64_t bd = sw128_kmajor_desc(b0 + kk * 32);
+              mma_issue<KIND>(d_tmem, ad, bd, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+            }
           }
           tc_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -343,7 +383,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty[buf]);
+      mbar_arrive_relaxed(&tempty[buf]);  // accumulator read (wait::ld); output stores need no ordering
     }
   }
 

@@ -13,10 +13,13 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <algorithm>
 #include <mutex>
 
 #include "gemm_tc.cuh"
+#include "gemm_w4a16.cuh"
 #include "quantize_act.cuh"
+#include "quantize_nvfp4.cuh"
 #include "sm100_ptx.cuh"
 #include "../../include/qi_b200.h"
 
@@ -76,7 +79,8 @@ static EncodeTiledFn encode_fn() {
 // 2-D row-major tensor [rows, inner] with a byte row stride, 128-byte
 // swizzled boxes of [box_rows, box_inner].  Out-of-range box elements read 0.
 static int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner, uint64_t rows,
-                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows,
+                        CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return QI_B200_ETMAP;
   cuuint64_t dims[2] = {inner, rows};
@@ -84,12 +88,21 @@ static int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType 
   cuuint32_t box[2] = {box_inner, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? QI_B200_OK : QI_B200_ETMAP;
 }
 
 static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launch plan of the calling thread's most recent GEMM launch (diagnostics:
+// kernel id, grid, cluster size, tile N, stages, dynamic shared memory).
+struct LaunchPlan {
+  int kernel, grid, cluster, tile_n, stages, smem;
+};
+static thread_local LaunchPlan g_last_plan = {0, 0, 0, 0, 0, 0};
+enum PlanKernel { kPlanGemmI8 = 1, kPlanGemmF8 = 2, kPlanGemmBF16 = 3, kPlanGemmNVF4 = 4, kPlanW4Tile = 5,
+                  kPlanW4Skinny = 6 };
 
 // ---------------------------------------------------------------------------
 // GEMM launch
@@ -99,10 +112,11 @@ static int launch_gemm_cfg(const void* A, const void* B, const EpiParams& p, int
   using C = GemmCfg<KIND, BN, STAGES>;
   const CUtensorMapDataType dt =
       (KIND == MmaKind::BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const uint64_t ku = C::NVF4 ? (uint64_t)p.K / 2 : (uint64_t)p.K;  // K in TMA elements (fp4: packed bytes)
   CUtensorMap ta, tb;
-  int rc = make_tmap_2d(&ta, A, dt, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)p.K * C::ELEM, C::BK, C::BM);
+  int rc = make_tmap_2d(&ta, A, dt, ku, (uint64_t)p.M, ku * C::ELEM, C::BK, C::BM);
   if (rc) return rc;
-  rc = make_tmap_2d(&tb, B, dt, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)p.K * C::ELEM, C::BK, BN);
+  rc = make_tmap_2d(&tb, B, dt, ku, (uint64_t)p.N, ku * C::ELEM, C::BK, BN);
   if (rc) return rc;
   static bool attr_done[kMaxDevices] = {};
   int dev = 0;
@@ -115,6 +129,7 @@ static int launch_gemm_cfg(const void* A, const void* B, const EpiParams& p, int
   }
   const int tiles = ((p.M + C::BM - 1) / C::BM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < num_sms ? tiles : num_sms;
+  g_last_plan = {1 + static_cast<int>(KIND), grid, 1, BN, STAGES, C::SMEM_BYTES};
   k_gemm_tc<KIND, BN, STAGES><<<grid, kGemmThreads, C::SMEM_BYTES, stream>>>(ta, tb, p);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
@@ -141,12 +156,16 @@ static int launch_gemm(const void* A, const void* B, const EpiParams& p, cudaStr
   DeviceInfo* di = nullptr;
   int rc = device_info(&di);
   if (rc) return rc;
-  const int bn = force_bn > 0 ? force_bn : pick_bn(p.M, p.N, di->num_sms);
-  switch (bn) {
-    case 256: return launch_gemm_cfg<KIND, 256, 4>(A, B, p, di->num_sms, stream);
-    case 128: return launch_gemm_cfg<KIND, 128, 6>(A, B, p, di->num_sms, stream);
-    case 64: return launch_gemm_cfg<KIND, 64, 8>(A, B, p, di->num_sms, stream);
-    default: return QI_B200_EINVAL;
+  if constexpr (KIND == MmaKind::NVF4) {
+    return launch_gemm_cfg<KIND, 128, 6>(A, B, p, di->num_sms, stream);
+  } else {
+    const int bn = force_bn > 0 ? force_bn : pick_bn(p.M, p.N, di->num_sms);
+    switch (bn) {
+      case 256: return launch_gemm_cfg<KIND, 256, 4>(A, B, p, di->num_sms, stream);
+      case 128: return launch_gemm_cfg<KIND, 128, 6>(A, B, p, di->num_sms, stream);
+      case 64: return launch_gemm_cfg<KIND, 64, 8>(A, B, p, di->num_sms, stream);
+      default: return QI_B200_EINVAL;
+    }
   }
 }
 
@@ -193,6 +212,188 @@ static int gemm_dispatch(int kind, const void* A, const void* B, const float* sa
 
 static int quant_status(cudaError_t e) { return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA; }
 
+// ---------------------------------------------------------------------------
+// NVFP4
+// ---------------------------------------------------------------------------
+static int nvfp4_quantize(const void* x, int rows, int cols, int g_mode, const float* g_in, unsigned int* ws_amax,
+                          float* g_out, void* q, void* sf, cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0) return QI_B200_ESHAPE;
+  if (cols % 64 != 0) return QI_B200_ESHAPE;
+  if (x == nullptr || q == nullptr || sf == nullptr) return QI_B200_EINVAL;
+  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u)) return QI_B200_EALIGN;
+  if (g_mode == 0 && g_in == nullptr) return QI_B200_EINVAL;
+  if (g_mode == 1 && (ws_amax == nullptr || g_out == nullptr)) return QI_B200_EINVAL;
+  if (g_mode == 2 && g_out == nullptr) return QI_B200_EINVAL;
+  if (g_mode < 0 || g_mode > 2) return QI_B200_EINVAL;
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const int ka = cols / 64;
+  const int rows_pad = (rows + 127) & ~127;
+  const long long blocks = (long long)rows_pad * (cols / 16);
+  const int grid_flat = (int)std::min<long long>((blocks + 255) / 256, (long long)di->num_sms * 16);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  auto* qb = static_cast<uint8_t*>(q);
+  auto* sb = static_cast<uint8_t*>(sf);
+  if (g_mode == 1) {
+    if (cudaMemsetAsync(ws_amax, 0, sizeof(unsigned int), stream) != cudaSuccess) return QI_B200_ECUDA;
+    const long long n = (long long)rows * cols;
+    const int g2 = (int)std::min<long long>((n / 8 + 255) / 256 + 1, (long long)di->num_sms * 8);
+    k_amax_bf16<<<g2, 256, 0, stream>>>(xb, n, ws_amax);
+    k_quant_nvfp4<1><<<grid_flat, 256, 0, stream>>>(xb, rows, cols, nullptr, ws_amax, g_out, qb, sb, ka);
+  } else if (g_mode == 0) {
+    k_quant_nvfp4<0><<<grid_flat, 256, 0, stream>>>(xb, rows, cols, g_in, nullptr, nullptr, qb, sb, ka);
+  } else {
+    const int g3 = std::min(rows_pad, di->num_sms * 8);
+    k_quant_nvfp4<2><<<g3, 256, 0, stream>>>(xb, rows, cols, nullptr, nullptr, g_out, qb, sb, ka);
+  }
+  return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+static int nvfp4_gemm(const void* A, const void* SFA, const void* B, const void* SFB, const float* a_g,
+                      int a_g_stride, const float* b_g, const void* bias, void* D, long long ldd, int M, int N, int K,
+                      int flags, cudaStream_t stream) {
+  if (A == nullptr || B == nullptr || SFA == nullptr || SFB == nullptr || D == nullptr) return QI_B200_EINVAL;
+  if (M <= 0 || N <= 0 || K <= 0) return QI_B200_ESHAPE;
+  if (K % 256 != 0 || N % 8 != 0 || ldd < N || ldd % 8 != 0) return QI_B200_ESHAPE;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(D) || !aligned16(SFA) || !aligned16(SFB)) return QI_B200_EALIGN;
+  if (flags & ~(kEpiGelu | kEpiRawAcc)) return QI_B200_EINVAL;
+  EpiParams p = {};
+  p.sa = a_g;
+  p.sa_stride = a_g_stride;
+  p.sb = b_g;
+  p.sb_stride = 0;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.D = D;
+  p.ldd = ldd;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.flags = flags;
+  p.sfa = static_cast<const uint8_t*>(SFA);
+  p.sfb = static_cast<const uint8_t*>(SFB);
+  p.sf_ka = K / 64;
+  return launch_gemm<MmaKind::NVF4>(A, B, p, stream, 128);
+}
+
+// ---------------------------------------------------------------------------
+// W4A16 launch: skinny split-K kernel for M <= 256, 256x128 tiles above.
+// ---------------------------------------------------------------------------
+template <int MP>
+static int launch_w4_skinny(const void* X, const EpiParams& p, const W4Params& q,
+                            int num_sms, cudaStream_t stream) {
+  using C = W4Cfg<MP>;
+  CUtensorMap tx;
+  int rc = make_tmap_2d(&tx, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)p.K * 2,
+                        w4::BK, MP);
+  if (rc) return rc;
+  static bool attr_done[kMaxDevices] = {};
+  int adev = 0;
+  cudaGetDevice(&adev);
+  if (!attr_done[adev]) {
+    if (cudaFuncSetAttribute(k_gemm_w4a16_skinny<MP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::SMEM_BYTES) != cudaSuccess)
+      return QI_B200_ECUDA;
+    attr_done[adev] = true;
+  }
+  const int n_tiles = (p.N + w4::BN - 1) / w4::BN;
+  const int k_blocks = (p.K + w4::BK - 1) / w4::BK;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(w4::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // K split = cluster size: the largest (<= 8) for which every cluster of
+  // the grid is resident at once (cluster placement is per GPC, so this is
+  // asked of the occupancy API rather than derived from the SM count).
+  static int ks_cache[kMaxDevices][64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int key = n_tiles < 64 ? n_tiles : 63;
+  int ks = ks_cache[dev][key];
+  if (ks == 0) {
+    ks = 1;
+    for (int cand = 8; cand >= 2; --cand) {
+      if (cand > k_blocks || n_tiles * cand > num_sms) continue;
+      int nclusters = 0;
+      attr[0].val.clusterDim.x = cand;
+      cfg.gridDim = dim3(n_tiles * cand, 1, 1);
+      if (cudaOccupancyMaxActiveClusters(&nclusters, k_gemm_w4a16_skinny<MP>, &cfg) == cudaSuccess &&
+          nclusters >= n_tiles) {
+        ks = cand;
+        break;
+      }
+    }
+    cudaGetLastError();  // clear a failed occupancy query
+    ks_cache[dev][key] = ks;
+  }
+  if (ks > k_blocks) ks = k_blocks;
+  const int kbc = (k_blocks + ks - 1) / ks;
+  ks = (k_blocks + kbc - 1) / kbc;  // every CTA of the cluster gets >= 1 K block
+  cfg.gridDim = dim3(n_tiles * ks, 1, 1);
+  attr[0].val.clusterDim.x = ks;
+  g_last_plan = {kPlanW4Skinny, n_tiles * ks, ks, MP, C::STAGES, C::SMEM_BYTES};
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_w4a16_skinny<MP>, tx, p, q, kbc);
+  return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+static int launch_w4a16(const void* X, const void* wq, const void* scales, const void* zeros, int group,
+                        const void* bias, void* D, long long ldd, int M, int N, int K, cudaStream_t stream) {
+  if (X == nullptr || wq == nullptr || scales == nullptr || zeros == nullptr || D == nullptr) return QI_B200_EINVAL;
+  if (M <= 0 || N <= 0 || K <= 0) return QI_B200_ESHAPE;
+  if (group <= 0 || group > K) group = K;
+  if (K % 32 != 0 || N % 8 != 0 || group % 32 != 0) return QI_B200_ESHAPE;
+  if (ldd < N || ldd % 8 != 0) return QI_B200_ESHAPE;
+  if (!aligned16(X) || !aligned16(wq) || !aligned16(D)) return QI_B200_EALIGN;
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  EpiParams p = {};
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.D = D;
+  p.ldd = ldd;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  W4Params q;
+  q.G = (K + group - 1) / group;
+  q.zw = (q.G + 7) / 8;
+  q.group = group;
+  q.group_shift = ((group & (group - 1)) == 0) ? __builtin_ctz(static_cast<unsigned>(group)) : -1;
+  q.scales = static_cast<const __half*>(scales);
+  q.zeros = static_cast<const int32_t*>(zeros);
+  q.wq = static_cast<const int32_t*>(wq);
+  q.kw = K / 8;
+  if (M <= 16) return launch_w4_skinny<16>(X, p, q, di->num_sms, stream);
+  if (M <= 32) return launch_w4_skinny<32>(X, p, q, di->num_sms, stream);
+  if (M <= 64) return launch_w4_skinny<64>(X, p, q, di->num_sms, stream);
+  if (M <= 128) return launch_w4_skinny<128>(X, p, q, di->num_sms, stream);
+  if (M <= 256) return launch_w4_skinny<256>(X, p, q, di->num_sms, stream);
+  CUtensorMap tx;
+  rc = make_tmap_2d(&tx, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, w4::BK,
+                    256);
+  if (rc) return rc;
+  static bool attr_done[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev]) {
+    if (cudaFuncSetAttribute(k_gemm_w4a16, cudaFuncAttributeMaxDynamicSharedMemorySize, W4Cfg<256>::SMEM_BYTES) !=
+        cudaSuccess)
+      return QI_B200_ECUDA;
+    attr_done[dev] = true;
+  }
+  const int tiles = ((M + 255) / 256) * ((N + w4::BN - 1) / w4::BN);
+  const int grid = tiles < di->num_sms ? tiles : di->num_sms;
+  g_last_plan = {kPlanW4Tile, grid, 1, 256, W4Cfg<256>::STAGES, W4Cfg<256>::SMEM_BYTES};
+  k_gemm_w4a16<<<grid, w4::kThreads, W4Cfg<256>::SMEM_BYTES, stream>>>(tx, p, q);
+  return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
 }  // namespace qib
 
 using namespace qib;
@@ -216,6 +417,14 @@ const char* qi_b200_error_string(int code) {
     case QI_B200_ETOOBIG: return "size exceeds the entry point's fixed maximum";
     default: return "unknown status";
   }
+}
+
+int qi_b200_last_launch(int* out6) {
+  if (out6 == nullptr) return QI_B200_EINVAL;
+  const LaunchPlan& p = g_last_plan;
+  const int v[6] = {p.kernel, p.grid, p.cluster, p.tile_n, p.stages, p.smem};
+  for (int i = 0; i < 6; ++i) out6[i] = v[i];
+  return QI_B200_OK;
 }
 
 int qi_b200_device_status(unsigned int* out4, int clear) {
@@ -271,6 +480,41 @@ int qi_b200_int8_rowwise_bf16out_bias(const void* A, const void* B, const void* 
                                       const void* bias, void* D, int M, int N, int K, cudaStream_t stream) {
   return gemm_dispatch(QI_B200_KIND_INT8, A, B, static_cast<const float*>(act_scale), 1,
                        static_cast<const float*>(weight_scale), 1, bias, D, N, M, N, K, 0, 0, stream);
+}
+
+int qi_b200_w4a16_linear(const void* x_bf16, const void* qweight_packed, const void* scales_fp16,
+                         const void* zeros_packed, int group_size, const void* bias, void* out_bf16, int M, int N,
+                         int K, cudaStream_t stream) {
+  if (M == 0) return QI_B200_OK;
+  return launch_w4a16(x_bf16, qweight_packed, scales_fp16, zeros_packed, group_size, bias, out_bf16, N, M, N, K,
+                      stream);
+}
+
+int qi_b200_quantize_nvfp4(const void* x_bf16, int rows, int cols, int g_mode, const float* g_in,
+                           unsigned int* ws_amax, float* g_out, void* q_packed, void* sf_atoms, cudaStream_t stream) {
+  if (rows == 0) return QI_B200_OK;
+  return nvfp4_quantize(x_bf16, rows, cols, g_mode, g_in, ws_amax, g_out, q_packed, sf_atoms, stream);
+}
+
+int qi_b200_nvfp4_gemm(const void* A_packed, const void* A_sf, const void* B_packed, const void* B_sf,
+                       const float* a_global_scale, int a_scale_per_row, const float* b_global_scale,
+                       const void* bias, void* D, long long ldd, int M, int N, int K, int flags, cudaStream_t stream) {
+  return nvfp4_gemm(A_packed, A_sf, B_packed, B_sf, a_global_scale, a_scale_per_row ? 1 : 0, b_global_scale, bias, D,
+                    ldd, M, N, K, flags, stream);
+}
+
+int qi_b200_nvfp4_linear(const void* x_bf16, const void* weight_packed, const void* weight_sf,
+                         const float* weight_global_scale, int act_scale_mode, const float* act_global_scale,
+                         const void* bias, void* out_bf16, void* ws_q, void* ws_sf, float* ws_g,
+                         unsigned int* ws_amax, int M, int N, int K, int flags, cudaStream_t stream) {
+  if (M == 0) return QI_B200_OK;
+  if (weight_global_scale == nullptr) return QI_B200_EINVAL;
+  const float* ag = act_scale_mode == 0 ? act_global_scale : ws_g;
+  if (ag == nullptr) return QI_B200_EINVAL;
+  int rc = nvfp4_quantize(x_bf16, M, K, act_scale_mode, act_global_scale, ws_amax, ws_g, ws_q, ws_sf, stream);
+  if (rc) return rc;
+  return nvfp4_gemm(ws_q, ws_sf, weight_packed, weight_sf, ag, act_scale_mode == 2 ? 1 : 0, weight_global_scale, bias,
+                    out_bf16, N, M, N, K, flags, stream);
 }
 
 int qi_b200_int8_linear(const void* x_bf16, const void* qweight, const float* weight_scale, const void* bias,

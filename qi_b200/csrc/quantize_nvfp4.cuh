@@ -1,0 +1,179 @@
+// NVFP4 activation quantization: bf16 [rows, cols] -> E2M1 codes (two per
+// byte, element 2j in the low nibble), E4M3 block scales (one per 16
+// elements along K) in the tensor-core scale-factor atom layout, and an fp32
+// second-level scale g (per tensor or per row).
+//
+// Recipe (NVFP4 as published by NVIDIA; restated in oracle/qi_oracle.py):
+//   g  = max(amax / (6 * 448), 1e-12)                   amax of the tensor or row
+//   sf = e4m3_rn( min(amax_16 / (6 g), 448) )           per 16-element block
+//   q  = e2m1_rn( clamp(x / (f32(sf) g), +-6) ), 0 where sf == 0
+// Scale-factor atom layout: 512-byte atoms of 128 rows x 4 block scales,
+// atoms ordered K-fastest then by 128-row block; row r = r0 + 32 r1 of an
+// atom at byte r0*16 + r1*4 + j.  Exactly what tcgen05.cp 32x128b.warpx4
+// copies into tensor memory for the block-scaled MMA.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "quantize_act.cuh"
+
+namespace qib {
+
+constexpr float kNvfp4GDiv = 6.0f * 448.0f;
+
+__device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 t;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\t"
+      "cvt.u32.u8 %0, t;\n\t}\n"
+      : "=r"(out)
+      : "f"(hi), "f"(lo));
+  return out;
+}
+
+__device__ __forceinline__ float nvfp4_g_from_amax(float amax) { return fmaxf(__fdiv_rn(amax, kNvfp4GDiv), 1e-12f); }
+
+__device__ __forceinline__ long long sf_atom_offset(int row, int blk, int ka_per_rowblock) {
+  const int ra = row >> 7, r = row & 127, ka = blk >> 2, j = blk & 3;
+  return (static_cast<long long>(ra) * ka_per_rowblock + ka) * 512 + (r & 31) * 16 + (r >> 5) * 4 + j;
+}
+
+// amax of a whole bf16 tensor into *amax_bits (float bits; must start at 0)
+__global__ void __launch_bounds__(256)
+k_amax_bf16(const __nv_bfloat16* __restrict__ x, long long n, unsigned int* __restrict__ amax_bits) {
+  float m = 0.f;
+  const long long nvec = n / 8;
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < nvec; i += 256ll * gridDim.x) {
+    const uint4 v = __ldg(xv + i);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __bfloat1622float2(h[k]);
+      m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+  for (long long i = nvec * 8 + blockIdx.x * 256ll + threadIdx.x; i < n; i += 256ll * gridDim.x)
+    m = fmaxf(m, fabsf(__bfloat162float(x[i])));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  __shared__ float wm[8];
+  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, wm[w]);
+    atomicMax(amax_bits, __float_as_uint(m));  // non-negative floats order like their bits
+  }
+}
+
+// Quantize one 16-element block: returns the packed E2M1 codes (8 bytes) and
+// the E4M3 block-scale code.
+__device__ __forceinline__ uint2 nvfp4_block(const uint4& v0, const uint4& v1, float g, uint8_t& sfc) {
+  float f[16];
+  const __nv_bfloat162* h0 = reinterpret_cast<const __nv_bfloat162*>(&v0);
+  const __nv_bfloat162* h1 = reinterpret_cast<const __nv_bfloat162*>(&v1);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 a = __bfloat1622float2(h0[k]), c = __bfloat1622float2(h1[k]);
+    f[2 * k] = a.x;
+    f[2 * k + 1] = a.y;
+    f[8 + 2 * k] = c.x;
+    f[8 + 2 * k + 1] = c.y;
+  }
+  float bm = 0.f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) bm = fmaxf(bm, fabsf(f[k]));
+  const float sfv = fminf(__fdiv_rn(bm, __fmul_rn(6.0f, g)), 448.0f);
+  sfc = static_cast<uint8_t>(__nv_cvt_float_to_fp8(sfv, __NV_SATFINITE, __NV_E4M3));
+  __half_raw hr = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(sfc), __NV_E4M3);
+  const float sff = __half2float(__half(hr));
+  const float denom = __fmul_rn(sff, g);
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float a = denom > 0.f ? fminf(fmaxf(__fdiv_rn(f[2 * k], denom), -6.f), 6.f) : 0.f;
+    const float c = denom > 0.f ? fminf(fmaxf(__fdiv_rn(f[2 * k + 1], denom), -6.f), 6.f) : 0.f;
+    const uint32_t byte = e2m1x2(a, c);
+    if (k < 4) lo |= byte << (8 * k);
+    else hi |= byte << (8 * (k - 4));
+  }
+  return make_uint2(lo, hi);
+}
+
+// One thread per 16-element block.  GMODE: 0 = per-tensor g from *g_in,
+// 1 = per-tensor g from *amax_bits (g written to g_out[0]), 2 = per-row g
+// (the row's amax is reduced here first; g written to g_out[row]).
+// cols % 16 == 0.  Scale-factor entries of the padding rows (up to the next
+// multiple of 128) are written as zero so the GEMM never reads stale bytes.
+template <int GMODE>
+__global__ void __launch_bounds__(256)
+k_quant_nvfp4(const __nv_bfloat16* __restrict__ x, int rows, int cols, const float* __restrict__ g_in,
+              const unsigned int* __restrict__ amax_bits, float* __restrict__ g_out, uint8_t* __restrict__ q,
+              uint8_t* __restrict__ sf, int ka_per_rowblock) {
+  const int bpr = cols >> 4;  // blocks per row
+  const int rows_pad = (rows + 127) & ~127;
+  if (GMODE == 2) {
+    __shared__ float wm[8];
+    __shared__ float g_sh;
+    for (int row = blockIdx.x; row < rows_pad; row += gridDim.x) {
+      if (row >= rows) {
+        for (int b = threadIdx.x; b < bpr; b += 256) sf[sf_atom_offset(row, b, ka_per_rowblock)] = 0;
+        continue;
+      }
+      const __nv_bfloat16* xr = x + static_cast<long long>(row) * cols;
+      float m = 0.f;
+      for (int b = threadIdx.x; b < bpr; b += 256) {
+        const uint4* p = reinterpret_cast<const uint4*>(xr + b * 16);
+        const uint4 v0 = __ldg(p), v1 = __ldg(p + 1);
+        m = fmaxf(m, fmaxf(absmax_bf16x8(v0), absmax_bf16x8(v1)));
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+      if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; ++w) m = fmaxf(m, wm[w]);
+        g_sh = nvfp4_g_from_amax(m);
+        g_out[row] = g_sh;
+      }
+      __syncthreads();
+      const float g = g_sh;
+      for (int b = threadIdx.x; b < bpr; b += 256) {
+        const uint4* p = reinterpret_cast<const uint4*>(xr + b * 16);
+        uint8_t sfc;
+        const uint2 packed = nvfp4_block(__ldg(p), __ldg(p + 1), g, sfc);
+        *reinterpret_cast<uint2*>(q + static_cast<long long>(row) * (cols >> 1) + b * 8) = packed;
+        sf[sf_atom_offset(row, b, ka_per_rowblock)] = sfc;
+      }
+      __syncthreads();
+    }
+    return;
+  }
+  float g;
+  if (GMODE == 0) {
+    g = __ldg(g_in);
+  } else {
+    g = nvfp4_g_from_amax(__uint_as_float(*amax_bits));
+    if (blockIdx.x == 0 && threadIdx.x == 0) g_out[0] = g;
+  }
+  const long long total = static_cast<long long>(rows_pad) * bpr;
+  for (long long t = blockIdx.x * 256ll + threadIdx.x; t < total; t += 256ll * gridDim.x) {
+    const int row = static_cast<int>(t / bpr);
+    const int b = static_cast<int>(t - static_cast<long long>(row) * bpr);
+    if (row >= rows) {
+      sf[sf_atom_offset(row, b, ka_per_rowblock)] = 0;
+      continue;
+    }
+    const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<long long>(row) * cols + b * 16);
+    uint8_t sfc;
+    const uint2 packed = nvfp4_block(__ldg(p), __ldg(p + 1), g, sfc);
+    *reinterpret_cast<uint2*>(q + static_cast<long long>(row) * (cols >> 1) + b * 8) = packed;
+    sf[sf_atom_offset(row, b, ka_per_rowblock)] = sfc;
+  }
+}
+
+}  // namespace qib

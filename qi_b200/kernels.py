@@ -157,6 +157,103 @@ def int8_linear(x_bf16_2d: torch.Tensor, qweight: torch.Tensor, weight_scales: t
     return out
 
 
+def w4a16_linear(x_bf16_2d: torch.Tensor, qweight_packed: torch.Tensor, scales_fp16: torch.Tensor,
+                 zeros_packed: torch.Tensor, group_size: int, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """INT4 weight-only linear on the packed layout (see include/qi_b200.h,
+    ``qi_b200_w4a16_linear``): y = bf16(x . bf16((q - z) s)^T + bias)."""
+    _check(x_bf16_2d, "x_bf16_2d", torch.bfloat16, 2)
+    dev = x_bf16_2d.device
+    _check(qweight_packed, "qweight_packed", torch.int32, 2, dev)
+    _check(scales_fp16, "scale_factors", torch.float16, 2, dev)
+    _check(zeros_packed, "zeros", torch.int32, 2, dev)
+    M, K = x_bf16_2d.shape
+    N = qweight_packed.shape[0]
+    if qweight_packed.shape[1] * 8 != K:
+        raise ValueError(f"W4A16 K mismatch: activation K={K}, packed weight K={qweight_packed.shape[1] * 8}.")
+    g = K if group_size <= 0 or group_size > K else group_size
+    G = -(-K // g)
+    if tuple(scales_fp16.shape) != (N, G) or tuple(zeros_packed.shape) != (N, -(-G // 8)):
+        raise ValueError(f"W4A16 scales/zeros must be [{N},{G}] fp16 and [{N},{-(-G // 8)}] int32.")
+    if bias is not None:
+        _check(bias, "bias", torch.bfloat16, device=dev)
+        if bias.numel() != N:
+            raise ValueError(f"bias must have {N} values.")
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    _lib.call("qi_b200_w4a16_linear", _ptr(x_bf16_2d), _ptr(qweight_packed), _ptr(scales_fp16),
+              _ptr(zeros_packed), int(g), _ptr(bias), _ptr(out), M, N, K, _stream(dev))
+    return out
+
+
+NVFP4_STATIC, NVFP4_DYNAMIC_TENSOR, NVFP4_DYNAMIC_ROW = 0, 1, 2
+
+
+def nvfp4_sf_bytes(rows: int, cols: int) -> int:
+    """Bytes of the scale-factor atom buffer for a [rows, cols] tensor."""
+    return -(-rows // 128) * 128 * (cols // 16)
+
+
+def quantize_nvfp4(x: torch.Tensor, mode: int = NVFP4_DYNAMIC_TENSOR, global_scale: torch.Tensor | None = None):
+    """bf16 [M,K] -> (packed uint8 [M,K/2], scale atoms uint8, g fp32 [1] or [M])."""
+    _check(x, "x", torch.bfloat16, 2)
+    M, Kd = x.shape
+    q = torch.empty((M, Kd // 2), dtype=_U8, device=x.device)
+    sf = torch.empty((nvfp4_sf_bytes(M, Kd),), dtype=_U8, device=x.device)
+    amax = torch.empty((1,), dtype=torch.int32, device=x.device) if mode == NVFP4_DYNAMIC_TENSOR else None
+    if mode == NVFP4_STATIC:
+        if global_scale is None:
+            raise ValueError("static NVFP4 quantization needs global_scale")
+        _check(global_scale, "global_scale", torch.float32, device=x.device)
+        g = global_scale
+    else:
+        g = torch.empty((M if mode == NVFP4_DYNAMIC_ROW else 1,), dtype=torch.float32, device=x.device)
+    _lib.call("qi_b200_quantize_nvfp4", _ptr(x), M, Kd, mode, _ptr(global_scale), _ptr(amax),
+              None if mode == NVFP4_STATIC else _ptr(g), _ptr(q), _ptr(sf), _stream(x.device))
+    return q, sf, g
+
+
+def nvfp4_gemm(a_packed, a_sf, b_packed, b_sf, a_g, b_g, bias=None, out=None, raw_acc=False):
+    M, Kh = a_packed.shape
+    N = b_packed.shape[0]
+    if b_packed.shape[1] != Kh:
+        raise ValueError("NVFP4 K mismatch")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32 if raw_acc else torch.bfloat16, device=a_packed.device)
+    _lib.call("qi_b200_nvfp4_gemm", _ptr(a_packed), _ptr(a_sf), _ptr(b_packed), _ptr(b_sf), _ptr(a_g),
+              int(a_g.numel() > 1), _ptr(b_g), _ptr(bias), _ptr(out), out.stride(0), M, N, 2 * Kh,
+              _lib.EPI_RAW_ACC if raw_acc else 0, _stream(a_packed.device))
+    return out
+
+
+def nvfp4_linear(x_bf16_2d: torch.Tensor, weight_packed: torch.Tensor, weight_sf: torch.Tensor,
+                 weight_global_scale: torch.Tensor, act_global_scale: torch.Tensor | None = None,
+                 bias: torch.Tensor | None = None, per_row: bool = False, gelu: bool = False) -> torch.Tensor:
+    """NVFP4 W4A4 linear.  ``act_global_scale`` (fp32 [1]) selects static
+    activation quantization; otherwise dynamic per tensor (or per row)."""
+    _check(x_bf16_2d, "x_bf16_2d", torch.bfloat16, 2)
+    dev = x_bf16_2d.device
+    _check(weight_packed, "qweight_packed", torch.uint8, 2, dev)
+    _check(weight_sf, "scale_factors", torch.uint8, None, dev)
+    _check(weight_global_scale, "weight_global_scale", torch.float32, None, dev)
+    M, Kd = x_bf16_2d.shape
+    N = weight_packed.shape[0]
+    if weight_packed.shape[1] * 2 != Kd:
+        raise ValueError(f"NVFP4 K mismatch: activation K={Kd}, weight K={weight_packed.shape[1] * 2}.")
+    if weight_sf.numel() != nvfp4_sf_bytes(N, Kd):
+        raise ValueError(f"NVFP4 weight scale atoms must have {nvfp4_sf_bytes(N, Kd)} bytes.")
+    mode = NVFP4_STATIC if act_global_scale is not None else (NVFP4_DYNAMIC_ROW if per_row else NVFP4_DYNAMIC_TENSOR)
+    if bias is not None:
+        _check(bias, "bias", torch.bfloat16, device=dev)
+    ws_q = torch.empty((M, Kd // 2), dtype=_U8, device=dev)
+    ws_sf = torch.empty((nvfp4_sf_bytes(M, Kd),), dtype=_U8, device=dev)
+    ws_g = torch.empty((M if per_row else 1,), dtype=torch.float32, device=dev)
+    ws_amax = torch.empty((1,), dtype=torch.int32, device=dev)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    _lib.call("qi_b200_nvfp4_linear", _ptr(x_bf16_2d), _ptr(weight_packed), _ptr(weight_sf),
+              _ptr(weight_global_scale), mode, _ptr(act_global_scale), _ptr(bias), _ptr(out), _ptr(ws_q),
+              _ptr(ws_sf), _ptr(ws_g), _ptr(ws_amax), M, N, Kd, _lib.EPI_GELU if gelu else 0, _stream(dev))
+    return out
+
+
 def fp8_linear(x_bf16_2d: torch.Tensor, weight_fp8: torch.Tensor, weight_scale: torch.Tensor,
                activation_scale: torch.Tensor | None = None, bias: torch.Tensor | None = None,
                gelu: bool = False) -> torch.Tensor:

@@ -108,9 +108,18 @@ class B200Backend:
                           weight_scale if weight_scale is not None else weight_global_scale,
                           activation_scale, activation_granularity, bias, gelu)
         elif qweight_packed is not None and qweight_packed.dtype == torch.uint8:
-            raise NotImplementedError("NVFP4 W4A4 path is not built yet.")
+            if scale_factors is None or weight_global_scale is None:
+                raise ValueError("NVFP4 backend requires scale_factors and weight_global_scale buffers.")
+            n = qweight_packed.shape[0]
+            y = K.nvfp4_linear(x2, qweight_packed.contiguous(), scale_factors.contiguous(),
+                               weight_global_scale.contiguous().float(),
+                               None if activation_scale is None else activation_scale.contiguous().float(),
+                               _bias_bf16(bias, n, x2.device), per_row=activation_granularity == "per_token",
+                               gelu=gelu)
         elif qweight_packed is not None and qweight_packed.dtype == torch.int32:
-            raise NotImplementedError("W4A16 path is not built yet.")
+            y = self._w4a16(x2, qweight_packed, scale_factors, zeros, group_size, bias)
+            if gelu:
+                raise ValueError("GELU fusion is not available on the W4A16 path.")
         elif bits == 8 and activation_granularity == "per_token":
             y = self._int8(x2, qweight, scales, group_size, symmetric, weight_granularity, bias, gelu)
         else:
@@ -140,6 +149,16 @@ class B200Backend:
             ws = ws[:, 0]
         ws = ws.contiguous().float()
         return K.int8_linear(x2, qweight.contiguous(), ws, _bias_bf16(bias, n, x2.device), gelu=gelu)
+
+    def _w4a16(self, x2, qp, s16, zp, group_size, bias):
+        if s16 is None or zp is None:
+            raise ValueError("W4A16 backend requires scale_factors (fp16) and packed zeros.")
+        if zp.dtype != torch.int32:
+            raise ValueError("W4A16 backend requires zeros packed as int32 (8 uint4 per word); "
+                             "repack reference tensors with qi_b200.quantization.quantize.pack_w4a16.")
+        n = qp.shape[0]
+        return K.w4a16_linear(x2, qp.contiguous(), s16.contiguous(), zp.contiguous(), int(group_size),
+                              _bias_bf16(bias, n, x2.device))
 
     def _fp8(self, x2, wq, ws, act_scale, activation_granularity, bias, gelu):
         if wq is None or ws is None:

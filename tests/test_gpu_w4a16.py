@@ -1,0 +1,106 @@
+"""GPU parity of the W4A16 (INT4 weight-only) kernels through the C ABI.
+
+* Dequantization is bit-exact: with one-hot activation rows the GEMM output
+  is exactly bf16(W) (+0 bias), compared bitwise with the oracle's
+  ``bf16((q - z) * s)`` (reference quantize.py:110-117 on the packed layout).
+* Outputs: relative Frobenius <= 2e-3 vs the oracle (fp32 accumulation
+  order), <= 5e-3 vs the reference's own output (golden fixture).
+* Both kernels: the split-K cluster kernel (M <= 256) and the 256x128 tile
+  kernel (M > 256); BASELINE config 3 (N=K=3072, g=128, M in 1/16/256/4096).
+"""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import qi_oracle as O
+from qi_b200 import _lib, kernels as K
+from qi_b200.synthetic import CFG_W4A16, make_linear_inputs, make_small_case
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+GOLD = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _device():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    _lib.load()
+    torch.cuda.set_device(0)
+    yield
+    torch.cuda.synchronize()
+    st = _lib.device_status(clear=True)
+    assert st[0] == 0, f"device status word reports a timed-out wait: {st}"
+
+
+def bits(t):
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def packed(w: np.ndarray, group: int, symmetric: bool = False):
+    q, s, z = O.quantize_weight_rtn(w, 4, group, symmetric)
+    if symmetric:
+        q = (q.astype(np.int16) + 8).astype(np.int8)
+        z = np.full(s.shape, 8, np.int16)
+    return O.pack_w4a16(q, s, z)
+
+
+def dev(*arrs):
+    return [torch.from_numpy(np.ascontiguousarray(a)).to(DEV) for a in arrs]
+
+
+@pytest.mark.parametrize("N,Kd,group", [(128, 256, 128), (192, 512, 64), (136, 384, 32), (64, 256, -1)])
+@pytest.mark.parametrize("M", [16, 300])
+def test_w4a16_dequant_bit_exact_one_hot(N, Kd, group, M):
+    g = torch.Generator().manual_seed(N + Kd)
+    w = (torch.randn(N, Kd, generator=g) * 0.02).numpy()
+    qp, s16, zp = packed(w, group)
+    # rows of the identity (cycled): y[m, n] = W[n, m % K] exactly
+    x = np.zeros((M, Kd), np.float32)
+    x[np.arange(M), np.arange(M) % Kd] = 1.0
+    xb = O.f32_to_bf16(x)
+    xt =torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).to(DEV)
+    qp_d, zp_d = dev(qp, zp)
+    s_d = torch.from_numpy(s16).to(DEV)
+    y = K.w4a16_linear(xt, qp_d, s_d, zp_d, group)
+    wb = O.w4a16_dequant_bf16(qp, s16, zp, Kd, group)
+    np.testing.assert_array_equal(bits(y), wb[:, np.arange(M) % Kd].T)
+
+
+@pytest.mark.parametrize("M", [1, 3, 16, 17, 64, 100, 256, 257, 512])
+@pytest.mark.parametrize("N,Kd,group", [(256, 512, 128), (136, 1024, 64)])
+def test_w4a16_linear_vs_oracle(M, N, Kd, group):
+    x, w, b = make_small_case(M, N, Kd, seed=M * 3 + N)
+    qp, s16, zp = packed(w.numpy(), group, symmetric=(M % 2 == 1))
+    qp_d, zp_d = dev(qp, zp)
+    y = K.w4a16_linear(x.to(DEV), qp_d, torch.from_numpy(s16).to(DEV), zp_d, group, b.to(DEV))
+    yo = O.w4a16_linear(bits(x), qp, s16, zp, group, bits(b))
+    e = O.rel_fro(O.bf16_to_f32(bits(y)), O.bf16_to_f32(yo))
+    assert e <= 2e-3, e
+
+
+def test_w4a16_vs_reference_fixture():
+    f = dict(np.load(GOLD / "linear_w4a16_M9_N128_K384.npz"))
+    qp, s16, zp = O.pack_w4a16(f["qweight"], f["scales"], f["zeros"])
+    x = torch.from_numpy(f["x"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    qp_d, zp_d = dev(qp, zp)
+    b = torch.from_numpy(f["bias"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    y = K.w4a16_linear(x, qp_d, torch.from_numpy(s16).to(DEV), zp_d, 128, b)
+    e = O.rel_fro(O.bf16_to_f32(bits(y)), O.bf16_to_f32(f["y_ref_bf16in"]))
+    assert e <= 5e-3, e
+
+
+@pytest.mark.parametrize("M", [1, 16, 256, 4096])
+def test_w4a16_config3_full_size(M):
+    """BASELINE config 3 at full size; the oracle runs on a row sample for M=4096."""
+    x, w, b = make_linear_inputs(CFG_W4A16[M])
+    qp, s16, zp = packed(w.numpy(), 128)
+    qp_d, zp_d = dev(qp, zp)
+    y = K.w4a16_linear(x.to(DEV), qp_d, torch.from_numpy(s16).to(DEV), zp_d, 128, b.to(DEV))
+    rows = np.arange(M) if M <= 256 else np.r_[0:64, 2048:2080, 4064:4096]
+    yo = O.w4a16_linear(bits(x)[rows], qp, s16, zp, 128, bits(b))
+    e = O.rel_fro(O.bf16_to_f32(bits(y)[rows]), O.bf16_to_f32(yo))
+    assert e <= 2e-3, e

@@ -123,3 +123,51 @@ def test_nvfp4_roundtrip_error_small():
     xh = O.nvfp4_dequant(q, sf, g)
     assert O.rel_fro(xh, x) < 0.12
     np.testing.assert_array_equal(O.unpack_fp4(O.pack_fp4(q)), q)
+
+
+def test_torch_packing_matches_oracle():
+    """qi_b200.quantization's packed INT4 layout equals the oracle's."""
+    from qi_b200.quantization.quantize import pack_w4a16, quantize_weight_rtn as qrtn
+    g = torch.Generator().manual_seed(3)
+    w = torch.randn(40, 256, generator=g) * 0.02
+    q, s, z = qrtn(w, 4, 64, False)
+    qo, so, zo = O.quantize_weight_rtn(w.numpy(), 4, 64, False)
+    np.testing.assert_array_equal(q.numpy(), qo)
+    np.testing.assert_array_equal(s.numpy().view(np.uint32), so.view(np.uint32))
+    np.testing.assert_array_equal(z.numpy(), zo)
+    qp, s16, zp = pack_w4a16(q, s, z)
+    qpo, s16o, zpo = O.pack_w4a16(qo, so, zo)
+    np.testing.assert_array_equal(qp.numpy(), qpo)
+    np.testing.assert_array_equal(s16.numpy(), s16o)
+    np.testing.assert_array_equal(zp.numpy(), zpo)
+
+
+def test_torch_quantizers_match_reference_fixtures():
+    """The product's vectorised RTN / FP8 quantizers give the reference's bytes."""
+    from qi_b200.quantization.quantize import quantize_to_fp8_e4m3, quantize_weight_rtn as qrtn
+    for name in ["rtn_int8_sym_pc", "rtn_int4_asym_g128", "rtn_int4_sym_g64", "rtn_int4_asym_ragged",
+                 "rtn_int8_asym_g32"]:
+        f = load(name)
+        N, K, bits, group, sym = (int(v) for v in f["meta"])
+        q, s, z = qrtn(torch.from_numpy(f["w"]), bits, group, bool(sym))
+        np.testing.assert_array_equal(q.numpy(), f["qweight"])
+        np.testing.assert_array_equal(s.numpy().view(np.uint32), f["scales"].view(np.uint32))
+        if not sym:
+            np.testing.assert_array_equal(z.numpy(), f["zeros"])
+    f = load("fp8_per_tensor")
+    q, s = quantize_to_fp8_e4m3(torch.from_numpy(f["x"]))
+    np.testing.assert_array_equal(q.numpy(), f["q"])
+    np.testing.assert_array_equal(s.numpy().view(np.uint32), f["s"].view(np.uint32))
+
+
+def test_torch_nvfp4_matches_oracle():
+    from qi_b200.quantization.quantize import quantize_nvfp4, sf_atom_layout
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(130, 64, generator=g)
+    packed, sf, gs = quantize_nvfp4(x)
+    go = O.nvfp4_global_scale(np.abs(x.numpy()).max())
+    assert gs.numpy()[0] == go
+    qo, sfo = O.quantize_nvfp4(x.numpy(), go)
+    np.testing.assert_array_equal(sf.numpy(), sfo)
+    np.testing.assert_array_equal(packed.numpy(), O.pack_fp4(qo))
+    np.testing.assert_array_equal(sf_atom_layout(sf).numpy(), O.sf_to_atom_layout(sfo))
