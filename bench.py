@@ -136,8 +136,10 @@ def max_over_ranks(v: float, world: int, device) -> float:
 # --------------------------------------------------------------------------
 
 
-def build_layer(cfg_name: str, w_shard: torch.Tensor, b_shard: torch.Tensor, device):
-    """One WeightOnlyLinear (the public module API) for this rank's column shard."""
+def build_layer(cfg_name: str, w_shard: torch.Tensor, b_shard: torch.Tensor, device, nvfp4_global=None):
+    """One WeightOnlyLinear (the public module API) for this rank's column shard.
+    ``nvfp4_global``: the per-tensor NVFP4 scale of the WHOLE weight, so every
+    shard quantizes exactly as the unsharded weight would."""
     from qi_b200.quantization import WeightActivationQuantConfig, WeightOnlyLinear
     from qi_b200.quantization.backends import get_backend
     from qi_b200.quantization.quantize import quantize_linear_weight
@@ -157,7 +159,13 @@ def build_layer(cfg_name: str, w_shard: torch.Tensor, b_shard: torch.Tensor, dev
     else:
         qcfg = WeightActivationQuantConfig(enabled=True, algo="rtn", quant_dtype="int", backend="b200",
                                            activation_granularity="per_token", weight_granularity="per_channel")
-    q = quantize_linear_weight(w_shard.to(device), qcfg)
+    if c["kind"] == "nvfp4" and nvfp4_global is not None:
+        from qi_b200.quantization.quantize import QuantizedLinearWeight, quantize_nvfp4, sf_atom_layout
+        packed, sf, g = quantize_nvfp4(w_shard.to(device), global_scale=nvfp4_global.to(device))
+        q = QuantizedLinearWeight(qweight=None, scales=None, zeros=None, qweight_packed=packed,
+                                  scale_factors=sf_atom_layout(sf), weight_global_scale=g)
+    else:
+        q = quantize_linear_weight(w_shard.to(device), qcfg)
     lin = torch.nn.Linear(w_shard.shape[1], w_shard.shape[0], bias=True)
     with torch.no_grad():
         lin.bias.copy_(b_shard.float())
@@ -171,6 +179,8 @@ def run_ours(args):
     from qi_b200 import _lib, kernels as K
 
     world, rank, local = dist_env()
+    if world > 1:
+        print(f"[bench] rank {rank}/{world} local {local} start", file=sys.stderr, flush=True)
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
@@ -186,7 +196,11 @@ def run_ours(args):
     x_cpu, w_cpu, b_cpu = make_linear_inputs(case)
     w_shard, b_shard = w_cpu[rank * Nl:(rank + 1) * Nl], b_cpu[rank * Nl:(rank + 1) * Nl]
 
-    layer = build_layer(args.config, w_shard, b_shard, device)
+    g_full = None
+    if c["kind"] == "nvfp4":
+        from qi_b200.quantization.quantize import nvfp4_global_scale
+        g_full = nvfp4_global_scale(w_cpu.float().abs().amax())
+    layer = build_layer(args.config, w_shard, b_shard, device, nvfp4_global=g_full)
     kind = {"fp8": _lib.KIND_FP8_E4M3, "int8": _lib.KIND_INT8, "w4a16": None, "nvfp4": None}[c["kind"]]
     if c["kind"] == "fp8":
         wq, ws = layer.weight_fp8, layer.weight_scale
@@ -204,7 +218,8 @@ def run_ours(args):
     xs = [x_cpu.to(device) for _ in range(ncopy)]
     wqs = [wq.clone() for _ in range(ncopy)]
     bias = layer.bias
-    gathered = torch.empty((world, M, Nl), dtype=torch.bfloat16, device=device) if world > 1 else None
+    # NCCL all-gather target: rank-major [P*M, N/P] (the layout ColumnShardedLinear's "rank" gather returns)
+    gathered = torch.empty((world * M, Nl), dtype=torch.bfloat16, device=device) if world > 1 else None
     stream = torch.cuda.current_stream(device)
 
     quant = K.quantize_fp8_rowwise if c["kind"] == "fp8" else K.quantize_int8_rowwise
@@ -287,20 +302,20 @@ def run_ours(args):
     ms_step = ms_total / args.steps
     value = flops_total / (ms_step * 1e-3) / 1e12
 
-    # ---- e2e through the public module API with host buffers
+    # ---- e2e through the public module API with host buffers (N > 1: the
+    # column-parallel wrapper around this rank's shard, rank-major gather)
     x_host = x_cpu.pin_memory()
     x_dev = torch.empty_like(xs[0])
     out_shape = (world, M, Nl) if world > 1 else (M, N)
     y_host = torch.empty(out_shape, dtype=torch.bfloat16).pin_memory()
+    api_layer = layer
+    if world > 1:
+        from qi_b200.sharding import GATHER_RANK_MAJOR, ColumnShardedLinear
+        api_layer = ColumnShardedLinear.from_shard(layer, N, gather=GATHER_RANK_MAJOR)
 
     def e2e_step():
         x_dev.copy_(x_host, non_blocking=True)
-        y = layer(x_dev)
-        if world > 1:
-            import torch.distributed as dist
-            dist.all_gather_into_tensor(gathered, y)
-            y = gathered
-        y_host.copy_(y, non_blocking=True)
+        y_host.copy_(api_layer(x_dev), non_blocking=True)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
@@ -359,7 +374,8 @@ def run_ours(args):
                    "l2": f"{ncopy} rotating input copies ({ncopy * per_copy / 2**20:.0f} MiB > L2)"},
         "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
-                "api": "qi_b200.quantization.WeightOnlyLinear.forward"},
+                "api": "qi_b200.quantization.WeightOnlyLinear.forward" if world == 1
+                       else "qi_b200.sharding.ColumnShardedLinear.forward"},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": roofline,
         "clocks": clk.summary(),
@@ -370,6 +386,8 @@ def run_ours(args):
         import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
+    if world > 1:
+        print(f"[bench] rank {rank} done", file=sys.stderr, flush=True)
     if rank == 0:
         print(json.dumps(result), flush=True)
 

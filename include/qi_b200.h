@@ -70,6 +70,27 @@ int qi_b200_last_launch(int* out6);
 int qi_b200_quantize_int8_rowwise(const void* x_bf16, void* q_int8, float* scales, int rows, int cols,
                                   cudaStream_t stream);
 
+/* INT8 quantization with caller-provided per-row scales (no counterpart in
+ * the reference): q = clamp(rint(x * (1/s[row])), -127, 127).  Used when a
+ * row's K extent is split over ranks: the per-row scales are first reduced
+ * with MAX across ranks, so every rank quantizes with the single-GPU scale. */
+int qi_b200_quantize_int8_rowwise_given(const void* x_bf16, const float* scales, void* q_int8, int rows, int cols,
+                                        cudaStream_t stream);
+
+/* Only the INT8 per-row scales s = max(amax/127, 1e-10) of a bf16 [rows, cols]
+ * block (no counterpart in the reference; K1's scale half,
+ * quantize_int8.cu:7-59).  For rows split over ranks by K, the MAX over ranks
+ * of these scales is exactly the scale of the whole row (division and max are
+ * monotone), which qi_b200_quantize_int8_rowwise_given then applies. */
+int qi_b200_int8_row_scales(const void* x_bf16, float* scales, int rows, int cols, cudaStream_t stream);
+
+/* The INT8 GEMM epilogue on its own (same operation order as the fused one,
+ * cutlass_int8_rowwise.cu:43-71): out = bf16(((float)acc * act_scale[m]) *
+ * weight_scale[n] + bias[n]) (+ GELU with QI_B200_EPI_GELU).  Used after a
+ * cross-rank int32 sum of K-sharded partial accumulators. */
+int qi_b200_int8_epilogue(const void* acc_int32, const float* act_scale, const float* weight_scale,
+                          const void* bias, void* out_bf16, int M, int N, int flags, cudaStream_t stream);
+
 /* Per-token FP8: s = max(amax/448, 1e-12), q = e4m3_rn(clamp(x/s, +-448)).
  * Generalises backends/flashrt_fp8_ops.py:38-48 (per tensor) to per row. */
 int qi_b200_quantize_fp8_rowwise(const void* x_bf16, void* q_fp8, float* scales, int rows, int cols,

@@ -223,13 +223,24 @@ def quantize_int8_rowwise(x_bf16: np.ndarray):
     approximate reciprocal is a build artefact; the kernels here are IEEE).
     Returns (q int8 [M,K], s float32 [M]).
     """
+    s = int8_row_scales(x_bf16)
+    return quantize_int8_rowwise_given(x_bf16, s), s
+
+
+def int8_row_scales(x_bf16: np.ndarray) -> np.ndarray:
+    """The scale half of ``quantize_int8.cu:7-59``: s = max(amax/127, 1e-10)."""
     x = bf16_to_f32(x_bf16)
     amax = np.abs(x).max(axis=1) if x.shape[1] else np.zeros(x.shape[0], np.float32)
-    s = np.maximum(amax / F32(127.0), F32(1e-10)).astype(np.float32)
-    inv = (F32(1.0) / s).astype(np.float32)
+    return np.maximum(amax / F32(127.0), F32(1e-10)).astype(np.float32)
+
+
+def quantize_int8_rowwise_given(x_bf16: np.ndarray, s: np.ndarray) -> np.ndarray:
+    """The code half of ``quantize_int8.cu:7-59`` with given per-row scales:
+    q = clamp(rint(x * (1/s)), -127, 127)."""
+    x = bf16_to_f32(x_bf16)
+    inv = (F32(1.0) / np.asarray(s, np.float32)).astype(np.float32)
     v = x * inv[:, None]
-    q = np.clip(np.rint(v), -127, 127).astype(np.int8)
-    return q, s
+    return np.clip(np.rint(v), -127, 127).astype(np.int8)
 
 
 def int8_gemm_acc(qa: np.ndarray, qw: np.ndarray) -> np.ndarray:

@@ -42,6 +42,9 @@ SIGNATURES = {
     "qi_b200_device_status": [_P, _I],
     "qi_b200_last_launch": [_P],
     "qi_b200_quantize_int8_rowwise": [_P, _P, _P, _I, _I, _P],
+    "qi_b200_quantize_int8_rowwise_given": [_P, _P, _P, _I, _I, _P],
+    "qi_b200_int8_row_scales": [_P, _P, _I, _I, _P],
+    "qi_b200_int8_epilogue": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
     "qi_b200_quantize_fp8_rowwise": [_P, _P, _P, _I, _I, _P],
     "qi_b200_quantize_fp8_static": [_P, _P, _P, _I, _I, _P],
     "qi_b200_int8_rowwise_bf16out": [_P, _P, _P, _P, _P, _I, _I, _I, _P],

@@ -6,7 +6,7 @@
 //
 // Roles (256 threads, one CTA per SM, grid = min(#tiles, #SMs)):
 //   warp 0      TMA producer: 128-byte-swizzled A and B tiles into a ring of
-//               STAGES shared-memory stages (cp.async.bulk.tensor, no multicast)
+//               STAGES shared-memory stages (cp.async.bulk.tensor, one destination CTA)
 //   warp 1      TMEM allocator + single-thread MMA issuer (tcgen05.mma, M=128,
 //               N=BN, accumulators in tensor memory, double buffered so the
 //               epilogue of tile i overlaps the main loop of tile i+1)
@@ -109,6 +109,24 @@ __device__ __forceinline__ float gelu_tanh_fast(float v) {
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Standalone INT8 epilogue over raw int32 accumulators, used after a
+// cross-rank sum of K-sharded partial accumulators.  Same operation order as
+// the fused epilogue: bf16(((float)acc * sa[m]) * sb[n] + bias[n]), then GELU
+// on the bf16 value.  Elementwise and HBM-bound (4 B in, 2 B out).
+__global__ void __launch_bounds__(256)
+k_int8_epilogue(const int32_t* __restrict__ acc, const float* __restrict__ sa, const float* __restrict__ sb,
+                const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out, int M, int N, int gelu) {
+  const long long total = static_cast<long long>(M) * N;
+  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < total; i += 256ll * gridDim.x) {
+    const int m = static_cast<int>(i / N), n = static_cast<int>(i - static_cast<long long>(m) * N);
+    float y = __fmul_rn(__fmul_rn(__int2float_rn(acc[i]), __ldg(sa + m)), __ldg(sb + n));
+    if (bias != nullptr) y = __fadd_rn(y, __bfloat162float(bias[n]));
+    __nv_bfloat16 h = __float2bfloat16_rn(y);
+    if (gelu) h = __float2bfloat16_rn(gelu_tanh_fast(__bfloat162float(h)));
+    out[i] = h;
+  }
 }
 
 template <MmaKind KIND>

@@ -447,6 +447,40 @@ int qi_b200_quantize_int8_rowwise(const void* x_bf16, void* q_int8, float* scale
   return quant_status(launch_rowquant<QuantInt8>(x_bf16, q_int8, scales, nullptr, rows, cols, stream));
 }
 
+int qi_b200_quantize_int8_rowwise_given(const void* x_bf16, const float* scales, void* q_int8, int rows, int cols,
+                                        cudaStream_t stream) {
+  if (rows < 0 || cols < 0) return QI_B200_ESHAPE;
+  if (rows == 0 || cols == 0) return QI_B200_OK;
+  if (x_bf16 == nullptr || q_int8 == nullptr || scales == nullptr) return QI_B200_EINVAL;
+  return quant_status(
+      launch_rowquant<QuantInt8Given>(x_bf16, q_int8, const_cast<float*>(scales), nullptr, rows, cols, stream));
+}
+
+int qi_b200_int8_row_scales(const void* x_bf16, float* scales, int rows, int cols, cudaStream_t stream) {
+  if (rows < 0 || cols < 0) return QI_B200_ESHAPE;
+  if (rows == 0 || cols == 0) return QI_B200_OK;
+  if (x_bf16 == nullptr || scales == nullptr) return QI_B200_EINVAL;
+  return quant_status(launch_rowquant<QuantInt8ScalesOnly>(x_bf16, nullptr, scales, nullptr, rows, cols, stream));
+}
+
+int qi_b200_int8_epilogue(const void* acc_int32, const float* act_scale, const float* weight_scale,
+                          const void* bias, void* out_bf16, int M, int N, int flags, cudaStream_t stream) {
+  if (M < 0 || N < 0) return QI_B200_ESHAPE;
+  if (M == 0 || N == 0) return QI_B200_OK;
+  if (acc_int32 == nullptr || act_scale == nullptr || weight_scale == nullptr || out_bf16 == nullptr)
+    return QI_B200_EINVAL;
+  if (flags & ~kEpiGelu) return QI_B200_EINVAL;
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const long long total = (long long)M * N;
+  const int grid = (int)std::min<long long>((total + 255) / 256, (long long)di->num_sms * 8);
+  k_int8_epilogue<<<grid, 256, 0, stream>>>(static_cast<const int32_t*>(acc_int32), act_scale, weight_scale,
+                                             static_cast<const __nv_bfloat16*>(bias),
+                                             static_cast<__nv_bfloat16*>(out_bf16), M, N, flags & kEpiGelu);
+  return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
 int qi_b200_quantize_fp8_rowwise(const void* x_bf16, void* q_fp8, float* scales, int rows, int cols,
                                  cudaStream_t stream) {
   if (rows < 0 || cols < 0) return QI_B200_ESHAPE;

@@ -26,6 +26,7 @@ constexpr int kQuantMaxChunks = 8;  // uint4 chunks (8 bf16 each) held per threa
 
 struct QuantInt8 {
   static constexpr bool kNeedsAmax = true;
+  static constexpr bool kStoreQ = true;
   __device__ __forceinline__ static float scale_from_amax(float amax) {
     return fmaxf(__fdiv_rn(amax, 127.0f), 1e-10f);
   }
@@ -37,8 +38,22 @@ struct QuantInt8 {
   }
 };
 
+// int8 with per-row scales supplied by the caller (e.g. reduced across ranks
+// that each hold a K-slice of the row): q = clamp(rint(x * (1/s)), -127, 127).
+struct QuantInt8Given : QuantInt8 {
+  static constexpr bool kNeedsAmax = false;
+};
+
+// Only the int8 per-row scales, no codes (q may be null).  For a row split over
+// ranks by K, the MAX over ranks of these local scales equals the scale of the
+// whole row, because fp32 division by 127 and max() are both monotone.
+struct QuantInt8ScalesOnly : QuantInt8 {
+  static constexpr bool kStoreQ = false;
+};
+
 struct QuantFp8 {
   static constexpr bool kNeedsAmax = true;
+  static constexpr bool kStoreQ = true;
   __device__ __forceinline__ static float scale_from_amax(float amax) {
     return fmaxf(__fdiv_rn(amax, 448.0f), 1e-12f);
   }
@@ -119,8 +134,10 @@ k_rowquant_vec(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, flo
     s = Op::scale_from_amax(amax);
     if (valid && t == 0 && scales != nullptr) scales[row] = s;
   } else {
-    s = __ldg(static_scale);
+    // given scale: one per tensor (static_scale) or one per row (scales, read)
+    s = static_scale != nullptr ? __ldg(static_scale) : (valid ? __ldg(scales + row) : 1.0f);
   }
+  if (!Op::kStoreQ) return;
   const float aux = Op::aux(s);
   uint2* qr = reinterpret_cast<uint2*>(q + static_cast<size_t>(valid ? row : 0) * cols);
 #pragma unroll
@@ -148,8 +165,9 @@ k_rowquant_scalar(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, 
     s = Op::scale_from_amax(amax);
     if (lane == 0 && scales != nullptr) scales[row] = s;
   } else {
-    s = __ldg(static_scale);
+    s = static_scale != nullptr ? __ldg(static_scale) : __ldg(scales + row);
   }
+  if (!Op::kStoreQ) return;
   const float aux = Op::aux(s);
   uint8_t* qr = q + static_cast<size_t>(row) * cols;
   for (int j = lane; j < cols; j += 32) qr[j] = Op::q1(__bfloat162float(xr[j]), s, aux);
@@ -192,3 +210,4 @@ inline cudaError_t launch_rowquant(const void* x, void* q, float* scales, const 
 }
 
 }  // namespace qib
+

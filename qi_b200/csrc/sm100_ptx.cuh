@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the Blackwell (sm_100a) features the kernels
-// use: mbarriers with bounded waits, TMA tiled loads (never multicast),
+// use: mbarriers with bounded waits, TMA tiled loads (one destination CTA each),
 // tcgen05 tensor-memory allocation, MMA, commit and loads.
 //
 // Every wait in this file is bounded: after QI_WAIT_TIMEOUT_NS of wall time
@@ -116,7 +116,7 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
 }
 
 // --------------------------------------------------------------------------
-// TMA (tiled, no multicast)
+// TMA (tiled, one destination CTA)
 // --------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

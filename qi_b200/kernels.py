@@ -54,6 +54,36 @@ def quantize_int8_rowwise(x: torch.Tensor, out: torch.Tensor | None = None,
     return q, s
 
 
+def int8_row_scales(x: torch.Tensor) -> torch.Tensor:
+    """bf16 [M,K] -> fp32 [M] per-row INT8 scales max(amax/127, 1e-10), no codes."""
+    _check(x, "x", torch.bfloat16, 2)
+    M, K = x.shape
+    s = torch.empty((M,), dtype=torch.float32, device=x.device)
+    _lib.call("qi_b200_int8_row_scales", _ptr(x), _ptr(s), M, K, _stream(x.device))
+    return s
+
+
+def quantize_int8_rowwise_given(x: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """bf16 [M,K] -> int8 [M,K] with caller-provided per-row scales (fp32 [M])."""
+    _check(x, "x", torch.bfloat16, 2)
+    _check(scales, "scales", torch.float32, 1, x.device)
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    _lib.call("qi_b200_quantize_int8_rowwise_given", _ptr(x), _ptr(scales), _ptr(q), M, K, _stream(x.device))
+    return q
+
+
+def int8_epilogue(acc: torch.Tensor, act_scale: torch.Tensor, weight_scale: torch.Tensor,
+                  bias: torch.Tensor | None = None, gelu: bool = False) -> torch.Tensor:
+    """int32 [M,N] accumulators -> bf16 with the INT8 GEMM epilogue."""
+    _check(acc, "acc", torch.int32, 2)
+    M, N = acc.shape
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=acc.device)
+    _lib.call("qi_b200_int8_epilogue", _ptr(acc), _ptr(act_scale), _ptr(weight_scale), _ptr(bias), _ptr(out),
+              M, N, _lib.EPI_GELU if gelu else 0, _stream(acc.device))
+    return out
+
+
 def quantize_fp8_rowwise(x: torch.Tensor):
     """bf16 [M,K] -> (e4m3 codes uint8 [M,K], fp32 [M]) per-token scales."""
     _check(x, "x", torch.bfloat16, 2)

@@ -1,0 +1,171 @@
+"""GPU parity of the tensor-parallel pieces (through the C ABI).
+
+* The kernels that row-parallel INT8 adds: ``int8_row_scales``,
+  ``quantize_int8_rowwise_given`` and ``int8_epilogue``.  Each is checked
+  bit-exactly against the oracle and against the fused single-GPU path.
+* The row-parallel recipe with P ranks emulated on one GPU: per-slice scales,
+  then MAX, given-scale quantization, raw int32 GEMMs, SUM, then the
+  epilogue.  The result equals ``int8_linear`` on the whole row, bit for bit.
+* With two or more GPUs: NCCL column- and row-parallel ranks in child
+  processes, bit-exact against the single-GPU kernels.  NVLS is off, and
+  the process group has a short timeout.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import qi_oracle as O
+from qi_b200 import _lib, kernels as K
+from qi_b200.synthetic import make_small_case
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _device():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    _lib.load()
+    torch.cuda.set_device(0)
+    yield
+    torch.cuda.synchronize()
+    st = _lib.device_status(clear=True)
+    assert st[0] == 0, f"device status word reports a timed-out wait: {st}"
+
+
+def bits(t):
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def int8_weights(w):
+    qw, sw, _ = O.quantize_weight_rtn(w.float().numpy(), 8, -1, True)
+    return torch.from_numpy(qw).to(DEV), torch.from_numpy(sw.reshape(-1).astype(np.float32)).to(DEV), qw, sw
+
+
+@pytest.mark.parametrize("M,Kd", [(1, 64), (37, 512), (300, 3072), (5, 40)])
+def test_row_scales_and_given_quantizer(M, Kd):
+    x, _, _ = make_small_case(M, 8, Kd, seed=M * 7 + Kd, outlier_frac=0.01)
+    xd = x.to(DEV)
+    s = K.int8_row_scales(xd)
+    so = O.int8_row_scales(bits(x))
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), so.view(np.uint32))
+    q_ref, s_ref = K.quantize_int8_rowwise(xd)
+    np.testing.assert_array_equal(s.cpu().numpy(), s_ref.cpu().numpy())
+    q = K.quantize_int8_rowwise_given(xd, s)
+    np.testing.assert_array_equal(q.cpu().numpy(), q_ref.cpu().numpy())
+    # a larger given scale (as after a cross-rank MAX) quantizes like the oracle
+    s2 = s * 3.0
+    q2 = K.quantize_int8_rowwise_given(xd, s2)
+    np.testing.assert_array_equal(q2.cpu().numpy(), O.quantize_int8_rowwise_given(bits(x), s2.cpu().numpy()))
+
+
+@pytest.mark.parametrize("gelu", [False, True])
+@pytest.mark.parametrize("M,N,Kd", [(1, 64, 128), (130, 256, 512), (512, 384, 3072)])
+def test_int8_epilogue_matches_fused(M, N, Kd, gelu):
+    x, w, b = make_small_case(M, N, Kd, seed=N + Kd)
+    qw, sw, qw_np, sw_np = int8_weights(w)
+    xd, bd = x.to(DEV), b.to(DEV)
+    q, s = K.quantize_int8_rowwise(xd)
+    acc = K.gemm(_lib.KIND_INT8, q, qw, None, None, raw_acc=True)
+    y = K.int8_epilogue(acc, s, sw, bd, gelu=gelu)
+    y_fused = K.int8_linear(xd, qw, sw, bd, gelu=gelu)
+    np.testing.assert_array_equal(bits(y), bits(y_fused))
+    if not gelu:
+        yo = O.int8_epilogue(acc.cpu().numpy().astype(np.int64), s.cpu().numpy(), sw_np.reshape(-1), bits(b))
+        np.testing.assert_array_equal(bits(y), yo)
+
+
+@pytest.mark.parametrize("P", [2, 4, 8])
+@pytest.mark.parametrize("M,N,Kd", [(32, 1024, 4096), (3120, 3072, 14336)])
+def test_row_parallel_emulated_bit_exact(P, M, N, Kd):
+    """P K-slices on one GPU reproduce the whole-row INT8 linear bit for bit
+    (ffn.2 shape: K = 14336 split over P ranks)."""
+    x, w, b = make_small_case(M, N, Kd, seed=P + M, outlier_frac=0.001)
+    qw, sw, _, _ = int8_weights(w)
+    xd, bd = x.to(DEV), b.to(DEV)
+    kp = Kd // P
+    slices = [xd[:, r * kp:(r + 1) * kp].contiguous() for r in range(P)]
+    s = torch.stack([K.int8_row_scales(xs) for xs in slices]).amax(dim=0)
+    acc = None
+    for r, xs in enumerate(slices):
+        q = K.quantize_int8_rowwise_given(xs, s)
+        a = K.gemm(_lib.KIND_INT8, q, qw[:, r * kp:(r + 1) * kp].contiguous(), None, None, raw_acc=True)
+        acc = a if acc is None else acc + a
+    y = K.int8_epilogue(acc, s, sw, bd)
+    np.testing.assert_array_equal(bits(y), bits(K.int8_linear(xd, qw, sw, bd)))
+
+
+# ---------------------------------------------------------------------------
+# NCCL ranks (two or more GPUs)
+# ---------------------------------------------------------------------------
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_worker(rank, world, port, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+    import torch.nn as nn
+
+    from qi_b200 import sharding as S
+    from qi_b200.quantization import WeightActivationQuantConfig, WeightOnlyLinear
+    from qi_b200.quantization.backends import get_backend
+    from qi_b200.quantization.quantize import quantize_linear_weight
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        cfg = WeightActivationQuantConfig(enabled=True, quant_dtype="int", backend="b200",
+                                          activation_granularity="per_token", weight_granularity="per_channel")
+        M, D, F = 257, 1024, 4096
+        x, w_up, b_up = make_small_case(M, F, D, seed=11)
+        _, w_dn, b_dn = make_small_case(M, D, F, seed=12)
+
+        def layer(w, b, gelu):
+            lin = nn.Linear(w.shape[1], w.shape[0])
+            with torch.no_grad():
+                lin.weight.copy_(w.float())
+                lin.bias.copy_(b.float())
+            q = quantize_linear_weight(lin.weight.detach(), cfg)
+            ql = WeightOnlyLinear.from_linear(lin, q, cfg, get_backend("b200")).to(dev)
+            ql.bias = ql.bias.to(torch.bfloat16)
+            ql.fuse_gelu = gelu
+            return ql
+
+        up, dn = layer(w_up, b_up, True), layer(w_dn, b_dn, False)
+        xd = x.to(dev)
+        h_ref = up(xd)
+        y_ref = dn(h_ref)
+        h_full = S.ColumnShardedLinear(up, gather=S.GATHER_FULL)(xd)
+        y_tp = S.RowShardedInt8Linear(dn)(S.ColumnShardedLinear(up, gather=S.GATHER_NONE)(xd))
+        torch.cuda.synchronize()
+        ok = bool(torch.equal(h_full, h_ref)) and bool(torch.equal(y_tp, y_ref))
+        st = _lib.device_status()
+        with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
+            f.write(f"{int(ok)} {st[0]}\n")
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_nccl_tensor_parallel_bit_exact(tmp_path):
+    world = 2
+    mp.spawn(_nccl_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for r in range(world):
+        ok, st = (tmp_path / f"rank{r}.txt").read_text().split()
+        assert ok == "1" and st == "0", (r, ok, st)
