@@ -1,0 +1,517 @@
+"""The MoT DiT denoising step that drives the quantized linears.
+
+This is the BASELINE "DiT step" workload.  It has 30 blocks and two experts
+that share one joint self-attention.  Every block of every expert runs 10
+quantized Linears: self-attn q/k/v/o, cross-attn q/k/v/o, ffn.0 and ffn.2.
+
+Two forms, on the same weights:
+
+* ``MoTDiT`` follows the reference's module structure, with the same
+  names, so ``replace_linear_with_weight_only`` selects the same layers.
+  The block math restates ``src/qi/models/wan22/wan_video_dit.py:147-268``:
+  LayerNorm, modulate, RMSNorm of q/k over all heads, RoPE, SDPA,
+  gate-residual, and an FFN with GELU(tanh).  The joint MoT layer loop
+  restates ``src/qi/models/wan22/mot.py:465-574``: per-expert q/k/v, one
+  attention over the concatenated tokens under a boolean mask, then the
+  per-expert post block.  Each quantized Linear goes through
+  ``WeightOnlyLinear.forward`` -> ``B200Backend.linear``.
+* ``DiTStepRunner`` is the B200 execution plan of the same step:
+  - q, k and v of an expert share one activation.  Their INT8 weights are
+    concatenated, so one quantization and one GEMM (N = 3 x 3072) replace
+    three of each.  The context's cross-attn k and v are fused the same
+    way.  INT8 outputs are per-element, so this is bit-identical to
+    separate layers.
+  - The joint mask of ``fastwam.py:914-935`` ("first_frame_causal") has
+    block structure.  The runner runs it as three unmasked attention calls:
+    first-frame video queries over first-frame keys; the other video
+    queries over all video keys; action queries over first-frame video
+    keys plus action keys.  These give the same result as the masked
+    attention but can use the fused (flash) kernels.
+  - The whole step is captured once in a CUDA graph and replayed, so about
+    1,200 launches per step cost no host time.
+
+RoPE is computed in fp32 here.  The reference uses fp64 complex numbers
+(``wan_video_dit.py:55-61``).  Both round to bf16 at the end; fp32 keeps
+about 1e-7 relative error before that rounding.  Attention is bf16 SDPA
+(library code, not the quantized hot path).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+@dataclass(frozen=True)
+class ExpertSpec:
+    name: str
+    hidden: int
+    ffn: int
+    tokens: int
+
+
+@dataclass(frozen=True)
+class DiTConfig:
+    """BASELINE config 5.  The action expert uses 24 heads x 128.  The
+    reference MoT requires every expert to share ``num_heads`` and
+    ``attn_head_dim`` (``mot.py:43-51``, ``configs/model/fastwam.yaml:39-40``)."""
+
+    layers: int = 30
+    heads: int = 24
+    head_dim: int = 128
+    ctx_tokens: int = 128
+    tokens_per_frame: int = 120          # 12 x 10 latent patches per frame
+    eps: float = 1e-6
+    experts: tuple = field(default_factory=lambda: (ExpertSpec("video", 3072, 14336, 3120),
+                                                    ExpertSpec("action", 1024, 4096, 32)))
+
+    @property
+    def attn_dim(self) -> int:
+        return self.heads * self.head_dim
+
+    def linear_ops(self) -> float:
+        """2*M*N*K over the 10 Linears of every block and expert."""
+        a = self.attn_dim
+        tot = 0.0
+        for e in self.experts:
+            m, d, f, c = e.tokens, e.hidden, e.ffn, self.ctx_tokens
+            tot += 2 * m * d * a * 3 + 2 * m * a * d          # self q,k,v + o
+            tot += 2 * m * d * a + 2 * c * d * a * 2 + 2 * m * a * d   # cross q + k,v (context) + o
+            tot += 2 * m * d * f * 2                          # ffn.0 + ffn.2
+        return tot * self.layers
+
+
+CFG5 = DiTConfig()
+
+
+# ---------------------------------------------------------------------------
+# block modules (reference structure and names)
+# ---------------------------------------------------------------------------
+
+
+class RMSNorm(nn.Module):
+    """``wan_video_dit.py:147-158``: fp32 normalisation, cast back, times weight."""
+
+    def __init__(self, dim: int, eps: float):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + self.eps)).to(x.dtype) * self.weight
+
+
+class _Attn(nn.Module):
+    def __init__(self, hidden: int, heads: int, head_dim: int, eps: float):
+        super().__init__()
+        a = heads * head_dim
+        self.num_heads = heads
+        self.q = nn.Linear(hidden, a)
+        self.k = nn.Linear(hidden, a)
+        self.v = nn.Linear(hidden, a)
+        self.o = nn.Linear(a, hidden)
+        self.norm_q = RMSNorm(a, eps)
+        self.norm_k = RMSNorm(a, eps)
+
+
+class SelfAttention(_Attn):
+    pass
+
+
+class CrossAttention(_Attn):
+    def forward(self, x, ctx):
+        q = self.norm_q(self.q(x))
+        k = self.norm_k(self.k(ctx))
+        v = self.v(ctx)
+        return self.o(attention(q, k, v, self.num_heads))
+
+
+class DiTBlock(nn.Module):
+    def __init__(self, hidden: int, ffn: int, heads: int, head_dim: int, eps: float):
+        super().__init__()
+        self.num_heads = heads
+        self.self_attn = SelfAttention(hidden, heads, head_dim, eps)
+        self.cross_attn = CrossAttention(hidden, heads, head_dim, eps)
+        self.norm1 = nn.LayerNorm(hidden, eps=eps, elementwise_affine=False)
+        self.norm2 = nn.LayerNorm(hidden, eps=eps, elementwise_affine=False)
+        self.norm3 = nn.LayerNorm(hidden, eps=eps)
+        self.ffn = nn.Sequential(nn.Linear(hidden, ffn), nn.GELU(approximate="tanh"), nn.Linear(ffn, hidden))
+        self.modulation = nn.Parameter(torch.randn(1, 6, hidden) / hidden ** 0.5)
+
+
+class Expert(nn.Module):
+    def __init__(self, spec: ExpertSpec, cfg: DiTConfig):
+        super().__init__()
+        self.spec = spec
+        self.num_heads = cfg.heads
+        self.attn_head_dim = cfg.head_dim
+        self.blocks = nn.ModuleList()
+
+
+def attention(q, k, v, heads: int, mask=None):
+    """``wan_video_dit.py:14-23``: [B, S, H*D] -> SDPA over heads -> [B, S, H*D]."""
+    b, sq, hd = q.shape
+    d = hd // heads
+    qh = q.view(b, sq, heads, d).transpose(1, 2)
+    kh = k.view(b, k.shape[1], heads, d).transpose(1, 2)
+    vh = v.view(b, v.shape[1], heads, d).transpose(1, 2)
+    o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=mask)
+    return o.transpose(1, 2).reshape(b, sq, hd)
+
+
+def modulate(x, shift, scale):
+    return x * (1 + scale) + shift
+
+
+def rope_tables(cfg: DiTConfig, spec: ExpertSpec, device) -> torch.Tensor:
+    """[S, D/2, 2] fp32 (cos, sin).  Video tokens use the 3-D (frame, h, w)
+    split of ``precompute_freqs_cis_3d`` (``wan_video_dit.py:38-52``).  The
+    frame axis gets D - 2*(D//3) dims and h and w get D//3 each.  The grid
+    is frames x 12 x 10.  Action tokens use the 1-D table over the whole
+    head dimension."""
+    d = cfg.head_dim
+
+    def freqs(dim, pos):
+        inv = 1.0 / (10000.0 ** (torch.arange(0, dim, 2, dtype=torch.float64)[: dim // 2] / dim))
+        return torch.outer(pos.double(), inv)
+
+    s = spec.tokens
+    if spec.name == "video" and s % cfg.tokens_per_frame == 0:
+        hgt, wid = 12, cfg.tokens_per_frame // 12
+        t = torch.arange(s)
+        f_i, h_i, w_i = t // cfg.tokens_per_frame, (t % cfg.tokens_per_frame) // wid, t % wid
+        df = d - 2 * (d // 3)
+        ang = torch.cat([freqs(df, f_i), freqs(d // 3, h_i), freqs(d // 3, w_i)], dim=1)
+        assert hgt * wid == cfg.tokens_per_frame
+    else:
+        ang = freqs(d, torch.arange(s))
+    return torch.stack([torch.cos(ang), torch.sin(ang)], dim=-1).float().to(device)
+
+
+def rope_apply(x, table, heads: int):
+    """Rotate (even, odd) pairs of every head: the complex product of
+    ``wan_video_dit.py:55-61``, in fp32, rounded to x's dtype."""
+    b, s, hd = x.shape
+    xf = x.float().view(b, s, heads, -1, 2)
+    c, sn = table[None, :, None, :, 0], table[None, :, None, :, 1]
+    xe, xo = xf[..., 0], xf[..., 1]
+    out = torch.stack([xe * c - xo * sn, xe * sn + xo * c], dim=-1)
+    return out.view(b, s, hd).to(x.dtype)
+
+
+def first_frame_causal_mask(cfg: DiTConfig, sv: int, sa: int, device) -> torch.Tensor:
+    """The joint [video+action] bool mask of ``fastwam.py:914-935`` with the
+    ``first_frame_causal`` video mode (``wan_video_dit.py:501-505``)."""
+    t = min(cfg.tokens_per_frame, sv)
+    m = torch.zeros((sv + sa, sv + sa), dtype=torch.bool, device=device)
+    m[:sv, :sv] = True
+    m[:t, t:sv] = False
+    m[sv:, sv:] = True
+    m[sv:, :t] = True
+    return m
+
+
+def joint_attention_blocks(q: dict, k: dict, v: dict, cfg: DiTConfig, q_offset: int = 0) -> dict:
+    """Attention under the first_frame_causal joint mask, as unmasked calls
+    over the mask's blocks (same result as ``attention`` over the
+    concatenated tokens with ``first_frame_causal_mask``).
+
+    ``k``/``v`` hold every video token; ``q["video"]`` may be a contiguous
+    run of video queries starting at token ``q_offset`` (a token shard)."""
+    h = cfg.heads
+    qv, kv, vv = q["video"], k["video"], v["video"]
+    sv = kv.shape[1]
+    t = min(cfg.tokens_per_frame, sv)
+    nf = max(0, min(t - q_offset, qv.shape[1]))   # local queries inside the first frame
+    parts = []
+    if nf > 0:
+        parts.append(attention(qv[:, :nf], kv[:, :t], vv[:, :t], h))
+    if nf < qv.shape[1]:
+        parts.append(attention(qv[:, nf:], kv, vv, h))
+    out_v = parts[0] if len(parts) == 1 else torch.cat(parts, dim=1)
+    out_a = attention(q["action"], torch.cat([kv[:, :t], k["action"]], 1),
+                      torch.cat([vv[:, :t], v["action"]], 1), h)
+    return {"video": out_v, "action": out_a}
+
+
+class MoTDiT(nn.Module):
+    """Random-init MoT DiT blocks with the reference's module names
+    (``mixtures.<expert>.blocks.<i>.self_attn.q`` and so on)."""
+
+    def __init__(self, cfg: DiTConfig):
+        super().__init__()
+        self.cfg = cfg
+        self.mixtures = nn.ModuleDict({e.name: Expert(e, cfg) for e in cfg.experts})
+        self.expert_order = [e.name for e in cfg.experts]
+
+    def forward(self, tokens: dict, rope: dict, ctx: dict, t_mod: dict, mask: torch.Tensor | None = None) -> dict:
+        """``mot.py:465-574``, one call per Linear through the module API.
+        With ``mask`` the joint attention is one SDPA over the concatenated
+        tokens under that boolean mask (the reference's form); without it,
+        the block form of the first_frame_causal mask."""
+        cfg = self.cfg
+        h = cfg.heads
+        tokens = dict(tokens)
+        for li in range(cfg.layers):
+            q, k, v, post = {}, {}, {}, {}
+            for name in self.expert_order:
+                blk = self.mixtures[name].blocks[li]
+                x = tokens[name]
+                sm, cm, gm, s2, c2, g2 = (blk.modulation.to(t_mod[name].dtype) + t_mod[name]).chunk(6, dim=1)
+                a_in = modulate(blk.norm1(x), sm, cm)
+                sa = blk.self_attn
+                q[name] = rope_apply(sa.norm_q(sa.q(a_in)), rope[name], h)
+                k[name] = rope_apply(sa.norm_k(sa.k(a_in)), rope[name], h)
+                v[name] = sa.v(a_in)
+                post[name] = (blk, x, gm, s2, c2, g2)
+            if mask is None:
+                att = joint_attention_blocks(q, k, v, cfg)
+            else:
+                cat = [torch.cat([d[n] for n in self.expert_order], 1) for d in (q, k, v)]
+                mixed = attention(*cat, h, mask)
+                att, start = {}, 0
+                for name in self.expert_order:
+                    n = tokens[name].shape[1]
+                    att[name] = mixed[:, start:start + n]
+                    start += n
+            for name in self.expert_order:
+                blk, x, gm, s2, c2, g2 = post[name]
+                x = x + gm * blk.self_attn.o(att[name])
+                x = x + blk.cross_attn(blk.norm3(x), ctx[name])
+                x = x + g2 * blk.ffn(modulate(blk.norm2(x), s2, c2))
+                tokens[name] = x
+        return tokens
+
+
+# ---------------------------------------------------------------------------
+# construction (random init, quantized block by block)
+# ---------------------------------------------------------------------------
+
+
+INT8_DIT_CFG = dict(enabled=True, quant_dtype="int", backend="b200", activation_granularity="per_token",
+                    weight_granularity="per_channel")
+
+
+def _init_block(blk: DiTBlock, gen: torch.Generator):
+    with torch.no_grad():
+        for mod in blk.modules():
+            if isinstance(mod, nn.Linear):
+                mod.weight.normal_(0.0, 0.02, generator=gen)
+                mod.bias.normal_(0.0, 0.01, generator=gen)
+            elif isinstance(mod, nn.LayerNorm) and mod.weight is not None:
+                mod.weight.fill_(1.0)
+                mod.bias.zero_()
+        blk.modulation.normal_(0.0, 1.0, generator=gen).div_(blk.modulation.shape[-1] ** 0.5)
+
+
+def build_mot_dit(cfg: DiTConfig = CFG5, device="cuda", seed: int = 0, quantize: bool = True,
+                  dtype=torch.bfloat16) -> MoTDiT:
+    """Random-init MoT DiT (seeded) with every target Linear swapped for an
+    INT8 W8A8 ``WeightOnlyLinear`` as each block is built.  The fp32 weights
+    of one block at a time are resident, so peak memory is the INT8 model
+    plus one block."""
+    from .quantization import WeightActivationQuantConfig, fuse_ffn_gelu, replace_linear_with_weight_only
+
+    qcfg = WeightActivationQuantConfig(**INT8_DIT_CFG)
+    model = MoTDiT(cfg)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    for spec in cfg.experts:
+        ex = model.mixtures[spec.name]
+        for _ in range(cfg.layers):
+            blk = DiTBlock(spec.hidden, spec.ffn, cfg.heads, cfg.head_dim, cfg.eps).to(device)
+            _init_block(blk, gen)
+            if quantize:
+                replace_linear_with_weight_only(blk, qcfg)
+                fuse_ffn_gelu(blk)
+                for mod in blk.modules():
+                    if hasattr(mod, "qweight") and getattr(mod, "bias", None) is not None:
+                        mod.bias = mod.bias.to(dtype)
+            blk.to(dtype)
+            ex.blocks.append(blk)
+    return model
+
+
+def make_step_inputs(cfg: DiTConfig, device, seed: int = 0, dtype=torch.bfloat16):
+    """Seeded synthetic step inputs: tokens, context (already at each
+    expert's width), time modulation [1, 6, D], RoPE tables, joint mask."""
+    g = torch.Generator(device=device).manual_seed(seed + 1)
+    tokens, ctx, t_mod, rope = {}, {}, {}, {}
+    for e in cfg.experts:
+        tokens[e.name] = torch.randn(1, e.tokens, e.hidden, generator=g, device=device).to(dtype)
+        ctx[e.name] = torch.randn(1, cfg.ctx_tokens, e.hidden, generator=g, device=device).to(dtype)
+        t_mod[e.name] = (torch.randn(1, 6, e.hidden, generator=g, device=device) * 0.1).to(dtype)
+        rope[e.name] = rope_tables(cfg, e, device)
+    sv, sa = cfg.experts[0].tokens, cfg.experts[1].tokens
+    return tokens, rope, ctx, t_mod, first_frame_causal_mask(cfg, sv, sa, device)
+
+
+# ---------------------------------------------------------------------------
+# the B200 execution plan
+# ---------------------------------------------------------------------------
+
+
+def _cat_int8(layers):
+    """Concatenate INT8 W8A8 ``WeightOnlyLinear`` layers along N."""
+    w = torch.cat([l.qweight for l in layers], 0).contiguous()
+    s = torch.cat([l.scales.reshape(-1) for l in layers], 0).float().contiguous()
+    b = torch.cat([l.bias.reshape(-1) for l in layers], 0).to(torch.bfloat16).contiguous()
+    return w, s, b
+
+
+def _int8(layer):
+    return layer.qweight, layer.scales.reshape(-1).float().contiguous(), layer.bias.to(torch.bfloat16).contiguous()
+
+
+class _BlockPlan:
+    def __init__(self, blk: DiTBlock):
+        sa, ca = blk.self_attn, blk.cross_attn
+        self.qkv = _cat_int8([sa.q, sa.k, sa.v])
+        self.o = _int8(sa.o)
+        self.cq = _int8(ca.q)
+        self.ckv = _cat_int8([ca.k, ca.v])
+        self.co = _int8(ca.o)
+        self.f0 = _int8(blk.ffn[0])
+        self.f2 = _int8(blk.ffn[2])
+        self.nq, self.nk = sa.norm_q, sa.norm_k
+        self.cnq, self.cnk = ca.norm_q, ca.norm_k
+        self.norm1, self.norm2, self.norm3 = blk.norm1, blk.norm2, blk.norm3
+        self.modulation = blk.modulation
+
+
+class DiTStepRunner:
+    """One MoT DiT step on B200 (INT8 tcgen05 GEMMs, fused QKV, block-mask
+    attention), optionally captured as a CUDA graph.
+
+    With ``group`` (a process group of P ranks, one per GPU) the video
+    tokens are sharded by sequence.  Rank r owns tokens
+    ``[r*Sv/P, (r+1)*Sv/P)`` and runs all of their Linears locally with
+    replicated weights.  Per-token quantization makes those rows
+    bit-identical to one GPU.  The only exchange is one NCCL all-gather per
+    layer of the video K and V (``2*Sv*3072`` bf16), which the joint
+    attention needs.  The 32 action tokens are replicated: their GEMMs are
+    bound by weight bandwidth, so splitting them would not shorten the step.
+    """
+
+    def __init__(self, model: MoTDiT, group=None):
+        from . import kernels as K
+
+        self.K = K
+        self.cfg = model.cfg
+        self.names = model.expert_order
+        self.plans = {n: [_BlockPlan(b) for b in model.mixtures[n].blocks] for n in self.names}
+        self.graph = None
+        self.group = group
+        if group is not None:
+            import torch.distributed as dist
+
+            self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        else:
+            self.rank, self.world = 0, 1
+        sv = self.cfg.experts[0].tokens
+        if sv % self.world:
+            raise ValueError(f"{sv} video tokens do not split over {self.world} ranks.")
+        self.video_local = sv // self.world
+        self.video_offset = self.rank * self.video_local
+
+    def shard(self, tokens: dict, rope: dict):
+        """This rank's video tokens and RoPE rows (action replicated)."""
+        lo, hi = self.video_offset, self.video_offset + self.video_local
+        tok = {n: (x[:, lo:hi].contiguous() if n == "video" else x) for n, x in tokens.items()}
+        rp = {n: (r[lo:hi].contiguous() if n == "video" else r) for n, r in rope.items()}
+        return tok, rp
+
+    def _gather_video_kv(self, k, v):
+        import torch.distributed as dist
+
+        a = self.cfg.attn_dim
+        n = k.shape[1]
+        kv = torch.cat([k.reshape(n, a), v.reshape(n, a)], dim=1)
+        out = torch.empty((self.world * n, 2 * a), dtype=kv.dtype, device=kv.device)
+        dist.all_gather_into_tensor(out, kv, group=self.group)
+        return out[:, :a].unsqueeze(0), out[:, a:].unsqueeze(0)
+
+    def _lin(self, x, wsb, gelu=False):
+        w, s, b = wsb
+        x2 = x.reshape(-1, x.shape[-1])
+        y = self.K.int8_linear(x2, w, s, b, gelu=gelu)
+        return y.view(*x.shape[:-1], w.shape[0])
+
+    def _joint_attention(self, q, k, v):
+        if self.world > 1:
+            k, v = dict(k), dict(v)
+            k["video"], v["video"] = self._gather_video_kv(k["video"], v["video"])
+        return joint_attention_blocks(q, k, v, self.cfg, q_offset=self.video_offset)
+
+    @torch.no_grad()
+    def step(self, tokens: dict, rope: dict, ctx: dict, t_mod: dict) -> dict:
+        cfg, h = self.cfg, self.cfg.heads
+        a = cfg.attn_dim
+        x = dict(tokens)
+        for li in range(cfg.layers):
+            q, k, v, post = {}, {}, {}, {}
+            for n in self.names:
+                p = self.plans[n][li]
+                sm, cm, gm, s2, c2, g2 = (p.modulation + t_mod[n]).chunk(6, dim=1)
+                qkv = self._lin(modulate(p.norm1(x[n]), sm, cm), p.qkv)
+                q[n] = rope_apply(p.nq(qkv[..., :a]), rope[n], h)
+                k[n] = rope_apply(p.nk(qkv[..., a:2 * a]), rope[n], h)
+                v[n] = qkv[..., 2 * a:]
+                post[n] = (gm, s2, c2, g2)
+            att = self._joint_attention(q, k, v)
+            for n in self.names:
+                p = self.plans[n][li]
+                gm, s2, c2, g2 = post[n]
+                xn = x[n] + gm * self._lin(att[n], p.o)
+                cq = p.cnq(self._lin(p.norm3(xn), p.cq))
+                ckv = self._lin(ctx[n], p.ckv)
+                ck, cv = p.cnk(ckv[..., :a]), ckv[..., a:]
+                xn = xn + self._lin(attention(cq, ck, cv, h), p.co)
+                f = self._lin(modulate(p.norm2(xn), s2, c2), p.f0, gelu=True)
+                x[n] = xn + g2 * self._lin(f, p.f2)
+        return x
+
+    # -- CUDA graph ---------------------------------------------------------
+
+    def capture(self, tokens: dict, rope: dict, ctx: dict, t_mod: dict, warmup: int = 2):
+        """Capture one step on static input buffers; ``replay()`` reruns it."""
+        self.static_in = ({n: t.clone() for n, t in tokens.items()}, rope, ctx, t_mod)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.step(*self.static_in)
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.static_out = self.step(*self.static_in)
+        return self.static_out
+
+    def replay(self):
+        self.graph.replay()
+        return self.static_out
+
+
+def count_quantized_linears(model: nn.Module) -> int:
+    from .quantization import WeightOnlyLinear
+
+    return sum(isinstance(m, WeightOnlyLinear) for m in model.modules())
+
+
+def step_flops_attention(cfg: DiTConfig) -> float:
+    """bf16 attention FLOPs of one step under the first_frame_causal mask
+    (QK^T and PV, 4*Sq*Sk*H*D per pair of blocks)."""
+    sv, sa = cfg.experts[0].tokens, cfg.experts[1].tokens
+    t = min(cfg.tokens_per_frame, sv)
+    hd = cfg.attn_dim
+    pairs = t * t + (sv - t) * sv + sa * (t + sa)
+    cross = sum(e.tokens for e in cfg.experts) * cfg.ctx_tokens
+    return 4.0 * (pairs + cross) * hd * cfg.layers
+
+
+__all__ = ["CFG5", "DiTConfig", "DiTStepRunner", "ExpertSpec", "MoTDiT", "build_mot_dit", "count_quantized_linears",
+           "first_frame_causal_mask", "joint_attention_blocks", "make_step_inputs", "rope_tables",
+           "step_flops_attention"]

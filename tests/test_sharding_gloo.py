@@ -266,3 +266,57 @@ def test_shard_shape_errors():
     nv = WeightOnlyLinear.from_linear(lin, quantize_linear_weight(lin.weight.detach(), cfg), cfg, None)
     with pytest.raises(ValueError):
         S.column_shard_buffers(nv, 0, 2)  # 48 rows per rank: not whole 128-row scale atoms
+
+
+# ---------------------------------------------------------------------------
+# sequence-parallel DiT step (video tokens sharded, K/V all-gathered)
+# ---------------------------------------------------------------------------
+
+
+class OracleKernels:
+    """CPU stand-in for ``qi_b200.kernels`` in ``DiTStepRunner``."""
+
+    @staticmethod
+    def int8_linear(x2, w, s, b, gelu=False):
+        y, _, _, _ = O.int8_linear(bits(x2), w.numpy(), s.numpy(), bits(b))
+        if gelu:
+            y = O.f32_to_bf16(O.gelu_tanh(O.bf16_to_f32(y)))
+        return from_bits(y)
+
+
+def _dit_worker(rank, world, port, out_dir):
+    from qi_b200 import dit as D
+
+    _init(rank, world, port)
+    try:
+        cfg = D.DiTConfig(layers=2, heads=2, head_dim=24, ctx_tokens=8, tokens_per_frame=24,
+                          experts=(D.ExpertSpec("video", 32, 64, 96), D.ExpertSpec("action", 16, 32, 4)))
+        model = D.build_mot_dit(cfg, device="cpu", seed=3)
+        tokens, rope, ctx, t_mod, _ = D.make_step_inputs(cfg, "cpu", seed=3)
+        single = D.DiTStepRunner(model)
+        single.K = OracleKernels
+        ref = single.step(tokens, rope, ctx, t_mod)
+        tp = D.DiTStepRunner(model, group=dist.group.WORLD)
+        tp.K = OracleKernels
+        tok, rp = tp.shard(tokens, rope)
+        out = tp.step(tok, rp, ctx, t_mod)
+        lo, hi = tp.video_offset, tp.video_offset + tp.video_local
+        torch.save({"video": out["video"], "video_ref": ref["video"][:, lo:hi], "action": out["action"],
+                    "action_ref": ref["action"]}, os.path.join(out_dir, f"dit{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_dit_sequence_parallel_gloo(world, tmp_path):
+    """Each rank's video rows (and the replicated action rows) match the
+    single-process step.  Token shards cross the first-frame boundary at
+    world 4 (24 first-frame tokens, 24 tokens per rank)."""
+    mp.spawn(_dit_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for r in range(world):
+        d = torch.load(tmp_path / f"dit{r}.pt")
+        for n in ("video", "action"):
+            a, b = d[n].float(), d[n + "_ref"].float()
+            assert a.shape == b.shape
+            err = ((a - b).norm() / b.norm()).item()
+            assert err < 1e-2, (r, n, err)
