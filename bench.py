@@ -413,7 +413,7 @@ def run_dit(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
         group = dist.group.WORLD
-    cfg = D.CFG5
+    cfg = D.CFG5 if not args.layers else D.DiTConfig(layers=args.layers)
     model = D.build_mot_dit(cfg, device=device, seed=0)
     tokens, rope, ctx, t_mod, _ = D.make_step_inputs(cfg, device, seed=0)
     runner = D.DiTStepRunner(model, group=group)
@@ -426,7 +426,16 @@ def run_dit(args):
             dist.barrier()
         torch.cuda.synchronize(device)
 
-    runner.capture(tok_l, rope_l, ctx, t_mod, warmup=2)
+    if args.eager:  # launch-list profiling: every kernel launched from the host
+        runner.static_in = (tok_l, rope_l, ctx, t_mod)
+
+        def run_step():
+            runner.static_out = runner.step(*runner.static_in)
+            return runner.static_out
+        runner.replay = run_step
+        run_step()
+    else:
+        runner.capture(tok_l, rope_l, ctx, t_mod, warmup=2)
     for _ in range(args.warmup):
         runner.replay()
     barrier()
@@ -507,7 +516,7 @@ def run_dit(args):
                    "ctx_tokens": cfg.ctx_tokens, "attention": "bf16 SDPA, first_frame_causal mask in block form",
                    "parallelism": f"video tokens sharded x{world} + NCCL all_gather of K/V per layer"
                    if world > 1 else "single GPU",
-                   "launch": "cuda_graph", "linear_ops_per_step": cfg.linear_ops(),
+                   "launch": "eager" if args.eager else "cuda_graph", "linear_ops_per_step": cfg.linear_ops(),
                    "l2": "5.9 GB of INT8 weights streamed per step (> L2), no flush needed"},
         "e2e": {"value": round(e2e_ms, 4), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "qi_b200.dit.DiTStepRunner (graph replay) with pinned host tokens"},
@@ -696,6 +705,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="no CUDA graph for the timed steps")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="dit only: fewer layers than config 5's 30 (profiling captures; not a bench value)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

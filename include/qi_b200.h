@@ -91,6 +91,31 @@ int qi_b200_int8_row_scales(const void* x_bf16, float* scales, int rows, int col
 int qi_b200_int8_epilogue(const void* acc_int32, const float* act_scale, const float* weight_scale,
                           const void* bias, void* out_bf16, int M, int N, int flags, cudaStream_t stream);
 
+/* ---- Fused elementwise stages of the MoT DiT block (no counterpart in the
+ * reference's quantization package: they fuse the bf16 tensor ops of
+ * src/qi/models/wan22/wan_video_dit.py:147-268 and mot.py:100-122 that sit
+ * between the quantized Linears into one pass each). ----
+ *
+ * qi_b200_resid_ln_quant, one row of x [M, D] per CTA, every stage optional:
+ *   x  <- bf16(x + bf16(gate * y))  (y and gate given) or bf16(x + y) (y only)
+ *   n  <- bf16(LayerNorm(x, eps) [* ln_w + ln_b])
+ *   n  <- bf16(bf16(n * mod_scale1) + mod_shift)     mod_scale1 = bf16(1 + scale)
+ *   q_int8, scales <- per-token INT8 of n (quantize_int8.cu:7-59); xn_bf16 <- n
+ * With q_int8 and xn_bf16 both null only the residual update runs.
+ * D % 8 == 0, D <= 4096; bf16 pointers 16-byte aligned; y row stride ldy. */
+int qi_b200_resid_ln_quant(void* x_bf16, const void* y_bf16, long long ldy, const void* gate, const void* ln_w,
+                           const void* ln_b, const void* mod_scale1, const void* mod_shift, void* q_int8,
+                           float* scales, void* xn_bf16, int M, int D, float eps, cudaStream_t stream);
+
+/* qi_b200_rms_rope: for nparts (1 or 2) inputs of [M, A] (row stride ld_in):
+ *   out = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w)            (RMSNorm over all A)
+ *   then, with rope ([M, head_dim/2, 2] fp32 cos/sin per token), rotate each
+ *   (even, odd) pair of every head: (e c - o s, e s + o c) in fp32.
+ * A % 8 == 0, A <= 4096, head_dim % 8 == 0. */
+int qi_b200_rms_rope(const void* in0, const void* in1, long long ld_in, void* out0, void* out1, long long ld_out,
+                     const void* w0, const void* w1, const float* rope, int head_dim, int nparts, int M, int A,
+                     float eps, cudaStream_t stream);
+
 /* Per-token FP8: s = max(amax/448, 1e-12), q = e4m3_rn(clamp(x/s, +-448)).
  * Generalises backends/flashrt_fp8_ops.py:38-48 (per tensor) to per row. */
 int qi_b200_quantize_fp8_rowwise(const void* x_bf16, void* q_fp8, float* scales, int rows, int cols,
@@ -118,7 +143,7 @@ int qi_b200_int8_rowwise_bf16out_bias(const void* A, const void* B, const void* 
  * backends/flashrt_fp8_ops.py:68-89):
  *   D[m, n] (row stride ldd) = epi( acc[m,n] * a_scale[m*a_scale_stride] * b_scale[n*b_scale_stride] + bias[n] )
  * a_scale / b_scale / bias may be NULL; a stride of 0 broadcasts one scale.
- * tile_n = 0 picks the tile width; 64, 128 or 256 forces one. */
+ * tile_n = 0 picks the tile width; 64, 128, 192 or 256 forces one. */
 int qi_b200_gemm(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
                  const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd, int M, int N,
                  int K, int flags, int tile_n, cudaStream_t stream);

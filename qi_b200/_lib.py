@@ -34,6 +34,7 @@ class QiB200Error(RuntimeError):
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _LL = ctypes.c_longlong
+_F = ctypes.c_float
 
 # name -> argtypes (restype is int unless listed in _RESTYPES)
 SIGNATURES = {
@@ -44,6 +45,8 @@ SIGNATURES = {
     "qi_b200_quantize_int8_rowwise": [_P, _P, _P, _I, _I, _P],
     "qi_b200_quantize_int8_rowwise_given": [_P, _P, _P, _I, _I, _P],
     "qi_b200_int8_row_scales": [_P, _P, _I, _I, _P],
+    "qi_b200_resid_ln_quant": [_P, _P, _LL, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _P],
+    "qi_b200_rms_rope": [_P, _P, _LL, _P, _P, _LL, _P, _P, _P, _I, _I, _I, _I, _F, _P],
     "qi_b200_int8_epilogue": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
     "qi_b200_quantize_fp8_rowwise": [_P, _P, _P, _I, _I, _P],
     "qi_b200_quantize_fp8_static": [_P, _P, _P, _I, _I, _P],

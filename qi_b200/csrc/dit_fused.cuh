@@ -1,0 +1,511 @@
+// Fused elementwise kernels of the MoT DiT block, around the quantized
+// Linears.  Each replaces a chain of bf16 tensor ops of the reference block
+// (src/qi/models/wan22/wan_video_dit.py:147-268, mot.py:100-122) with one
+// pass over HBM.
+//
+// k_resid_ln_quant: one row per CTA, one 16-byte chunk per thread.  In order:
+//   x  <- bf16(x + bf16(gate * y))  or  bf16(x + y)   (GateModule / residual)
+//   n  <- bf16(LayerNorm(x) [* w + b])                 (norm1/norm2/norm3)
+//   n  <- bf16(bf16(n * scale1) + shift)               (modulate; scale1 = bf16(1+scale))
+//   q, s <- per-token INT8 quantization of n           (quantize_int8.cu:7-59)
+// Each stage is optional.  The bf16 rounding points are those of the
+// reference's tensor ops.  The row stays in registers between stages.
+//
+// k_rms_rope: RMSNorm over the whole attention width (all heads), times the
+// norm weight, then an optional rotary embedding of (even, odd) pairs.  Up to
+// two inputs (q and k) go through one launch, as blockIdx.y.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace qib {
+
+// One thread per 8-element chunk of a row: blockDim = D/8 rounded up to a
+// whole warp (D <= 4096 -> at most 512 threads, 16 warps).
+constexpr int kRowMaxThreads = 512;
+
+__host__ __device__ inline int row_threads(int d) { return ((d / 8 + 31) / 32) * 32; }
+
+struct ResLnParams {
+  __nv_bfloat16* x;                 // [M, D] residual stream; updated in place when y != nullptr
+  const __nv_bfloat16* y;           // [M, ldy] branch output, or nullptr
+  long long ldy;
+  const __nv_bfloat16* gate;        // [D] or nullptr (plain residual add)
+  const __nv_bfloat16* ln_w;        // [D] or nullptr (no affine)
+  const __nv_bfloat16* ln_b;        // [D] or nullptr
+  const __nv_bfloat16* mod_scale1;  // [D] = bf16(1 + scale), or nullptr (no modulate)
+  const __nv_bfloat16* mod_shift;   // [D] (with mod_scale1)
+  int8_t* q;                        // [M, D] INT8 codes, or nullptr (residual update only)
+  float* s;                         // [M] per-token scales (with q)
+  __nv_bfloat16* xn;                // [M, D] bf16 normalized/modulated row, or nullptr
+  int M, D;
+  float eps;
+};
+
+// Block-wide sums / maxima of R values at once (one shared-memory round for
+// all R rows of a CTA).  red holds [R][kRowMaxThreads/32] floats.
+template <int R, bool MAX>
+__device__ __forceinline__ void block_reduce(float (&v)[R], float* red) {
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float u = __shfl_xor_sync(0xffffffffu, v[r], o);
+      v[r] = MAX ? fmaxf(v[r], u) : v[r] + u;
+    }
+  }
+  const int nw = blockDim.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) red[r * (kRowMaxThreads / 32) + (threadIdx.x >> 5)] = v[r];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    float t = 0.f;
+    for (int w = 0; w < nw; ++w) {
+      const float u = red[r * (kRowMaxThreads / 32) + w];
+      t = MAX ? fmaxf(t, u) : t + u;
+    }
+    v[r] = t;
+  }
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return u;
+}
+
+__device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// Round 8 fp32 values to bf16 (kept as fp32), two per conversion instruction.
+__device__ __forceinline__ void round8(float (&v)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(__floats2bfloat162_rn(v[2 * i], v[2 * i + 1]));
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// Pack 8 values that are already exactly bf16 (upper halves of their fp32 bits).
+__device__ __forceinline__ uint4 pack8_exact(const float (&v)[8]) {
+  uint4 u;
+  u.x = __byte_perm(__float_as_uint(v[0]), __float_as_uint(v[1]), 0x7632);
+  u.y = __byte_perm(__float_as_uint(v[2]), __float_as_uint(v[3]), 0x7632);
+  u.z = __byte_perm(__float_as_uint(v[4]), __float_as_uint(v[5]), 0x7632);
+  u.w = __byte_perm(__float_as_uint(v[6]), __float_as_uint(v[7]), 0x7632);
+  return u;
+}
+
+// INT8 codes clamp(rint(v * inv), -127, 127) of 8 values.  rint is done by
+// adding 1.5 * 2^23 in the FP32 adder (round-to-nearest-even, exact for the
+// pre-clamped |t| <= 128), which equals cvt.rni without the conversion unit.
+__device__ __forceinline__ uint2 quant8(const float (&v)[8], float inv) {
+  uint32_t b[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float t = fminf(fmaxf(__fmul_rn(v[e], inv), -128.0f), 128.0f);
+    int qi = static_cast<int>(__float_as_uint(__fadd_rn(t, 12582912.0f))) - 0x4B400000;
+    qi = max(-127, min(127, qi));
+    b[e] = static_cast<uint32_t>(qi) & 0xFFu;
+  }
+  return make_uint2(b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24), b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24));
+}
+
+// R rows per CTA: their loads are all issued before the first reduction and
+// the three block reductions (sum, sum of squares, max) serve all R rows, so
+// a CTA keeps R times the bytes in flight per synchronization.
+template <int R>
+__global__ void __launch_bounds__(kRowMaxThreads) k_resid_ln_quant(ResLnParams p) {
+  __shared__ float red[R * (kRowMaxThreads / 32)];
+  const int row0 = blockIdx.x * R;
+  const int j = threadIdx.x;                 // this thread's 8-element chunk of each row
+  const bool act_col = j < (p.D >> 3);
+  float v[R][8];
+  bool act[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    act[r] = act_col && (row0 + r) < p.M;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[r][e] = 0.f;
+  }
+
+  // residual update (all R rows' loads first)
+  uint4 xu[R], yu[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if (!act[r]) continue;
+    const long long rr = row0 + r;
+    xu[r] = reinterpret_cast<const uint4*>(p.x + rr * p.D)[j];
+    if (p.y != nullptr) yu[r] = reinterpret_cast<const uint4*>(p.y + rr * p.ldy)[j];
+  }
+  float g[8];
+  if (p.gate != nullptr && act_col) unpack8(reinterpret_cast<const uint4*>(p.gate)[j], g);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if (!act[r]) continue;
+    unpack8(xu[r], v[r]);
+    if (p.y != nullptr) {
+      float yv[8];
+      unpack8(yu[r], yv);
+      if (p.gate != nullptr) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) yv[e] = __fmul_rn(g[e], yv[e]);
+        round8(yv);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[r][e] = __fadd_rn(v[r][e], yv[e]);
+      round8(v[r]);
+      reinterpret_cast<uint4*>(p.x + static_cast<long long>(row0 + r) * p.D)[j] = pack8_exact(v[r]);
+    }
+  }
+  if (p.q == nullptr && p.xn == nullptr) return;
+
+  // LayerNorm statistics (two passes over registers)
+  float st[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    st[r] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) st[r] += v[r][e];
+  }
+  block_reduce<R, false>(st, red);
+  float mean[R], rstd[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    mean[r] = st[r] / static_cast<float>(p.D);
+    st[r] = 0.f;
+    if (act[r]) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = v[r][e] - mean[r];
+        st[r] = fmaf(d, d, st[r]);
+      }
+    }
+  }
+  block_reduce<R, false>(st, red);
+#pragma unroll
+  for (int r = 0; r < R; ++r) rstd[r] = rsqrtf(st[r] / static_cast<float>(p.D) + p.eps);
+
+  // normalize, affine, modulate (bf16 after each reference tensor op)
+  float w[8], b[8], s1[8], sh[8];
+  if (act_col) {
+    if (p.ln_w != nullptr) {
+      unpack8(reinterpret_cast<const uint4*>(p.ln_w)[j], w);
+      unpack8(reinterpret_cast<const uint4*>(p.ln_b)[j], b);
+    }
+    if (p.mod_scale1 != nullptr) {
+      unpack8(reinterpret_cast<const uint4*>(p.mod_scale1)[j], s1);
+      unpack8(reinterpret_cast<const uint4*>(p.mod_shift)[j], sh);
+    }
+  }
+  float amax[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    amax[r] = 0.f;
+    if (!act[r]) continue;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float n = (v[r][e] - mean[r]) * rstd[r];
+      if (p.ln_w != nullptr) n = fmaf(n, w[e], b[e]);
+      v[r][e] = n;
+    }
+    round8(v[r]);
+    if (p.mod_scale1 != nullptr) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[r][e] = __fmul_rn(v[r][e], s1[e]);
+      round8(v[r]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[r][e] = __fadd_rn(v[r][e], sh[e]);
+      round8(v[r]);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax[r] = fmaxf(amax[r], fabsf(v[r][e]));
+    if (p.xn != nullptr)
+      reinterpret_cast<uint4*>(p.xn + static_cast<long long>(row0 + r) * p.D)[j] = pack8_exact(v[r]);
+  }
+  if (p.q == nullptr) return;
+
+  // per-token INT8: s = max(amax/127, 1e-10), q = clamp(rint(n * (1/s)), +-127)
+  block_reduce<R, true>(amax, red);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if (row0 + r >= p.M) continue;
+    const float s = fmaxf(__fdiv_rn(amax[r], 127.0f), 1e-10f);
+    const float inv = __frcp_rn(s);
+    if (j == 0) p.s[row0 + r] = s;
+    if (!act[r]) continue;
+    reinterpret_cast<uint2*>(p.q + static_cast<long long>(row0 + r) * p.D)[j] = quant8(v[r], inv);
+  }
+}
+
+struct RmsRopeParams {
+  const __nv_bfloat16* in[2];  // [M, ld_in] rows (q and k), A used columns
+  long long ld_in;
+  __nv_bfloat16* out[2];       // [M, ld_out]
+  long long ld_out;
+  const __nv_bfloat16* w[2];   // [A] RMSNorm weights
+  const float* rope;           // [M, head_dim/2, 2] fp32 (cos, sin) per token and pair within a head, or nullptr
+  int pairs_per_head;          // head_dim / 2
+  int M, A;
+  float eps;
+};
+
+// One row of one part per CTA.  RMSNorm: bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w)
+// (wan_video_dit.py:147-158); RoPE on (even, odd) pairs within each head:
+// (e c - o s, e s + o c) in fp32 (wan_video_dit.py:55-61).
+template <int R>
+__global__ void __launch_bounds__(kRowMaxThreads) k_rms_rope(RmsRopeParams p) {
+  __shared__ float red[R * (kRowMaxThreads / 32)];
+  const int row0 = blockIdx.x * R;
+  const int part = blockIdx.y;
+  const int j = threadIdx.x;
+  const bool act_col = j < (p.A >> 3);
+  const __nv_bfloat16* in = part ? p.in[1] : p.in[0];
+  __nv_bfloat16* out = part ? p.out[1] : p.out[0];
+  const __nv_bfloat16* wp = part ? p.w[1] : p.w[0];
+  float v[R][8];
+  float sq[R];
+  uint4 u[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+    if (act_col && row0 + r < p.M) u[r] = reinterpret_cast<const uint4*>(in + static_cast<long long>(row0 + r) * p.ld_in)[j];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    sq[r] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[r][e] = 0.f;
+    if (act_col && row0 + r < p.M) {
+      unpack8(u[r], v[r]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sq[r] = fmaf(v[r][e], v[r][e], sq[r]);
+    }
+  }
+  block_reduce<R, false>(sq, red);
+  if (!act_col) return;
+  float w[8];
+  unpack8(reinterpret_cast<const uint4*>(wp)[j], w);
+  const int pair0 = (j * 4) % p.pairs_per_head;  // chunk j holds pairs 4j..4j+3; index within the head
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int row = row0 + r;
+    if (row >= p.M) continue;
+    const float rr = rsqrtf(sq[r] / static_cast<float>(p.A) + p.eps);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[r][e] = __fmul_rn(v[r][e], rr);
+    round8(v[r]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[r][e] = __fmul_rn(v[r][e], w[e]);
+    round8(v[r]);
+    if (p.rope != nullptr) {
+      const float4* tab = reinterpret_cast<const float4*>(
+          p.rope + (static_cast<long long>(row) * p.pairs_per_head + pair0) * 2);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float4 cs = tab[i];  // (cos, sin) of two consecutive pairs
+        const float e0 = v[r][4 * i], o0 = v[r][4 * i + 1], e1 = v[r][4 * i + 2], o1 = v[r][4 * i + 3];
+        v[r][4 * i] = __fsub_rn(__fmul_rn(e0, cs.x), __fmul_rn(o0, cs.y));
+        v[r][4 * i + 1] = __fadd_rn(__fmul_rn(e0, cs.y), __fmul_rn(o0, cs.x));
+        v[r][4 * i + 2] = __fsub_rn(__fmul_rn(e1, cs.z), __fmul_rn(o1, cs.w));
+        v[r][4 * i + 3] = __fadd_rn(__fmul_rn(e1, cs.w), __fmul_rn(o1, cs.z));
+      }
+    }
+    reinterpret_cast<uint4*>(out + static_cast<long long>(row) * p.ld_out)[j] = pack8(v[r]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Warp-per-row variants for D % 256 == 0 (C = D/256 16-byte chunks per lane).
+// A row lives in registers as packed bf16 (4C registers); reductions are warp
+// shuffles only, so the 4 warps of a CTA work on 4 rows with no block barrier and
+// many rows' loads are in flight per SM.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+constexpr int kWarpRowThreads = 128;
+
+template <int C>
+__global__ void __launch_bounds__(kWarpRowThreads) k_resid_ln_quant_warp(ResLnParams p) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (kWarpRowThreads / 32) + (threadIdx.x >> 5);
+  if (row >= p.M) return;
+  uint4* xr = reinterpret_cast<uint4*>(p.x + static_cast<long long>(row) * p.D);
+  uint4 xu[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) xu[c] = xr[c * 32 + lane];
+  if (p.y != nullptr) {
+    const uint4* yr = reinterpret_cast<const uint4*>(p.y + static_cast<long long>(row) * p.ldy);
+    uint4 yu[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) yu[c] = yr[c * 32 + lane];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      float v[8], yv[8];
+      unpack8(xu[c], v);
+      unpack8(yu[c], yv);
+      if (p.gate != nullptr) {
+        float g[8];
+        unpack8(reinterpret_cast<const uint4*>(p.gate)[c * 32 + lane], g);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) yv[e] = __fmul_rn(g[e], yv[e]);
+        round8(yv);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], yv[e]);
+      xu[c] = pack8(v);
+      xr[c * 32 + lane] = xu[c];
+    }
+  }
+  if (p.q == nullptr && p.xn == nullptr) return;
+
+  float sum = 0.f;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    float v[8];
+    unpack8(xu[c], v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sum += v[e];
+  }
+  const float mean = warp_sum(sum) / static_cast<float>(p.D);
+  float sq = 0.f;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    float v[8];
+    unpack8(xu[c], v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float d = v[e] - mean;
+      sq = fmaf(d, d, sq);
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(sq) / static_cast<float>(p.D) + p.eps);
+
+  float amax = 0.f;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int j = c * 32 + lane;
+    float v[8];
+    unpack8(xu[c], v);
+    float w[8], b[8], s1[8], sh[8];
+    if (p.ln_w != nullptr) {
+      unpack8(reinterpret_cast<const uint4*>(p.ln_w)[j], w);
+      unpack8(reinterpret_cast<const uint4*>(p.ln_b)[j], b);
+    }
+    if (p.mod_scale1 != nullptr) {
+      unpack8(reinterpret_cast<const uint4*>(p.mod_scale1)[j], s1);
+      unpack8(reinterpret_cast<const uint4*>(p.mod_shift)[j], sh);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float n = (v[e] - mean) * rstd;
+      if (p.ln_w != nullptr) n = fmaf(n, w[e], b[e]);
+      v[e] = n;
+    }
+    round8(v);
+    if (p.mod_scale1 != nullptr) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], s1[e]);
+      round8(v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], sh[e]);
+      round8(v);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[e]));
+    xu[c] = pack8_exact(v);
+    if (p.xn != nullptr) reinterpret_cast<uint4*>(p.xn + static_cast<long long>(row) * p.D)[j] = xu[c];
+  }
+  if (p.q == nullptr) return;
+  amax = warp_max(amax);
+  const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-10f);
+  const float inv = __frcp_rn(s);
+  if (lane == 0) p.s[row] = s;
+  uint2* qr = reinterpret_cast<uint2*>(p.q + static_cast<long long>(row) * p.D);
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    float v[8];
+    unpack8(xu[c], v);
+    qr[c * 32 + lane] = quant8(v, inv);
+  }
+}
+
+template <int C>
+__global__ void __launch_bounds__(kWarpRowThreads) k_rms_rope_warp(RmsRopeParams p) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (kWarpRowThreads / 32) + (threadIdx.x >> 5);
+  const int part = blockIdx.y;
+  if (row >= p.M) return;
+  const uint4* ir = reinterpret_cast<const uint4*>((part ? p.in[1] : p.in[0]) + static_cast<long long>(row) * p.ld_in);
+  uint4* orow = reinterpret_cast<uint4*>((part ? p.out[1] : p.out[0]) + static_cast<long long>(row) * p.ld_out);
+  const uint4* wp = reinterpret_cast<const uint4*>(part ? p.w[1] : p.w[0]);
+  uint4 u[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) u[c] = ir[c * 32 + lane];
+  float sq = 0.f;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    float v[8];
+    unpack8(u[c], v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sq = fmaf(v[e], v[e], sq);
+  }
+  const float r = rsqrtf(warp_sum(sq) / static_cast<float>(p.A) + p.eps);
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int j = c * 32 + lane;
+    float v[8], w[8];
+    unpack8(u[c], v);
+    unpack8(wp[j], w);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], r);
+    round8(v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], w[e]);
+    round8(v);
+    if (p.rope != nullptr) {
+      const int pair0 = (j * 4) % p.pairs_per_head;
+      const float4* tab = reinterpret_cast<const float4*>(
+          p.rope + (static_cast<long long>(row) * p.pairs_per_head + pair0) * 2);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float4 cs = tab[i];
+        const float e0 = v[4 * i], o0 = v[4 * i + 1], e1 = v[4 * i + 2], o1 = v[4 * i + 3];
+        v[4 * i] = __fsub_rn(__fmul_rn(e0, cs.x), __fmul_rn(o0, cs.y));
+        v[4 * i + 1] = __fadd_rn(__fmul_rn(e0, cs.y), __fmul_rn(o0, cs.x));
+        v[4 * i + 2] = __fsub_rn(__fmul_rn(e1, cs.z), __fmul_rn(o1, cs.w));
+        v[4 * i + 3] = __fadd_rn(__fmul_rn(e1, cs.w), __fmul_rn(o1, cs.z));
+      }
+    }
+    orow[j] = pack8(v);
+  }
+}
+
+}  // namespace qib

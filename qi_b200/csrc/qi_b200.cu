@@ -16,6 +16,7 @@
 #include <algorithm>
 #include <mutex>
 
+#include "dit_fused.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_w4a16.cuh"
 #include "quantize_act.cuh"
@@ -139,7 +140,7 @@ static int pick_bn(int M, int N, int num_sms) {
   const int mt = (M + 127) / 128;
   int best_bn = 256;
   long best = -1;
-  for (int bn : {256, 128, 64}) {
+  for (int bn : {256, 192, 128, 64}) {
     const long tiles = (long)mt * ((N + bn - 1) / bn);
     const long waves = (tiles + num_sms - 1) / num_sms;
     const long cost = waves * (bn + 64);
@@ -162,6 +163,7 @@ static int launch_gemm(const void* A, const void* B, const EpiParams& p, cudaStr
     const int bn = force_bn > 0 ? force_bn : pick_bn(p.M, p.N, di->num_sms);
     switch (bn) {
       case 256: return launch_gemm_cfg<KIND, 256, 4>(A, B, p, di->num_sms, stream);
+      case 192: return launch_gemm_cfg<KIND, 192, 5>(A, B, p, di->num_sms, stream);
       case 128: return launch_gemm_cfg<KIND, 128, 6>(A, B, p, di->num_sms, stream);
       case 64: return launch_gemm_cfg<KIND, 64, 8>(A, B, p, di->num_sms, stream);
       default: return QI_B200_EINVAL;
@@ -454,6 +456,87 @@ int qi_b200_quantize_int8_rowwise_given(const void* x_bf16, const float* scales,
   if (x_bf16 == nullptr || q_int8 == nullptr || scales == nullptr) return QI_B200_EINVAL;
   return quant_status(
       launch_rowquant<QuantInt8Given>(x_bf16, q_int8, const_cast<float*>(scales), nullptr, rows, cols, stream));
+}
+
+int qi_b200_resid_ln_quant(void* x_bf16, const void* y_bf16, long long ldy, const void* gate, const void* ln_w,
+                           const void* ln_b, const void* mod_scale1, const void* mod_shift, void* q_int8,
+                           float* scales, void* xn_bf16, int M, int D, float eps, cudaStream_t stream) {
+  if (M < 0 || D <= 0) return QI_B200_ESHAPE;
+  if (M == 0) return QI_B200_OK;
+  if (x_bf16 == nullptr) return QI_B200_EINVAL;
+  if (D % 8 != 0 || D > kRowMaxThreads * 8) return QI_B200_ESHAPE;
+  if ((ln_w == nullptr) != (ln_b == nullptr) || (mod_scale1 == nullptr) != (mod_shift == nullptr) ||
+      (q_int8 != nullptr && scales == nullptr) || (y_bf16 == nullptr && gate != nullptr))
+    return QI_B200_EINVAL;
+  if (y_bf16 != nullptr && (ldy < D || ldy % 8 != 0)) return QI_B200_ESHAPE;
+  const void* ptrs[] = {x_bf16, y_bf16, gate, ln_w, ln_b, mod_scale1, mod_shift, xn_bf16};
+  for (const void* ptr : ptrs)
+    if (ptr != nullptr && !aligned16(ptr)) return QI_B200_EALIGN;
+  if (q_int8 != nullptr && (reinterpret_cast<uintptr_t>(q_int8) & 7u) != 0) return QI_B200_EALIGN;
+  ResLnParams p;
+  p.x = static_cast<__nv_bfloat16*>(x_bf16);
+  p.y = static_cast<const __nv_bfloat16*>(y_bf16);
+  p.ldy = ldy;
+  p.gate = static_cast<const __nv_bfloat16*>(gate);
+  p.ln_w = static_cast<const __nv_bfloat16*>(ln_w);
+  p.ln_b = static_cast<const __nv_bfloat16*>(ln_b);
+  p.mod_scale1 = static_cast<const __nv_bfloat16*>(mod_scale1);
+  p.mod_shift = static_cast<const __nv_bfloat16*>(mod_shift);
+  p.q = static_cast<int8_t*>(q_int8);
+  p.s = scales;
+  p.xn = static_cast<__nv_bfloat16*>(xn_bf16);
+  p.M = M;
+  p.D = D;
+  p.eps = eps;
+  const int wgrid = (M + kWarpRowThreads / 32 - 1) / (kWarpRowThreads / 32);
+  switch (D) {  // warp per row where the row splits into whole 256-element slices
+    case 1024: k_resid_ln_quant_warp<4><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
+    case 2048: k_resid_ln_quant_warp<8><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
+    case 3072: k_resid_ln_quant_warp<12><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
+    case 4096: k_resid_ln_quant_warp<16><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
+    default: k_resid_ln_quant<1><<<M, row_threads(D), 0, stream>>>(p);
+  }
+  return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+int qi_b200_rms_rope(const void* in0, const void* in1, long long ld_in, void* out0, void* out1, long long ld_out,
+                     const void* w0, const void* w1, const float* rope, int head_dim, int nparts, int M, int A,
+                     float eps, cudaStream_t stream) {
+  if (M < 0 || A <= 0 || nparts < 1 || nparts > 2) return QI_B200_ESHAPE;
+  if (M == 0) return QI_B200_OK;
+  if (A % 8 != 0 || A > kRowMaxThreads * 8 || ld_in < A || ld_out < A || ld_in % 8 || ld_out % 8)
+    return QI_B200_ESHAPE;
+  if (rope != nullptr && (head_dim <= 0 || head_dim % 8 != 0 || A % head_dim != 0)) return QI_B200_ESHAPE;
+  const void* ins[2] = {in0, in1};
+  void* outs[2] = {out0, out1};
+  const void* ws[2] = {w0, w1};
+  RmsRopeParams p;
+  for (int i = 0; i < nparts; ++i) {
+    if (ins[i] == nullptr || outs[i] == nullptr || ws[i] == nullptr) return QI_B200_EINVAL;
+    if (!aligned16(ins[i]) || !aligned16(outs[i]) || !aligned16(ws[i])) return QI_B200_EALIGN;
+  }
+  if (rope != nullptr && !aligned16(rope)) return QI_B200_EALIGN;
+  for (int i = 0; i < 2; ++i) {
+    p.in[i] = static_cast<const __nv_bfloat16*>(ins[i < nparts ? i : 0]);
+    p.out[i] = static_cast<__nv_bfloat16*>(outs[i < nparts ? i : 0]);
+    p.w[i] = static_cast<const __nv_bfloat16*>(ws[i < nparts ? i : 0]);
+  }
+  p.ld_in = ld_in;
+  p.ld_out = ld_out;
+  p.rope = rope;
+  p.pairs_per_head = rope != nullptr ? head_dim / 2 : 1;
+  p.M = M;
+  p.A = A;
+  p.eps = eps;
+  const dim3 wgrid((M + kWarpRowThreads / 32 - 1) / (kWarpRowThreads / 32), nparts);
+  switch (A) {
+    case 1024: k_rms_rope_warp<4><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
+    case 2048: k_rms_rope_warp<8><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
+    case 3072: k_rms_rope_warp<12><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
+    case 4096: k_rms_rope_warp<16><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
+    default: k_rms_rope<1><<<dim3(M, nparts), row_threads(A), 0, stream>>>(p);
+  }
+  return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
 int qi_b200_int8_row_scales(const void* x_bf16, float* scales, int rows, int cols, cudaStream_t stream) {

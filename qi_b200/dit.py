@@ -396,13 +396,18 @@ class DiTStepRunner:
     bound by weight bandwidth, so splitting them would not shorten the step.
     """
 
-    def __init__(self, model: MoTDiT, group=None):
+    def __init__(self, model: MoTDiT, group=None, fused: bool = True):
+        from . import _lib
         from . import kernels as K
 
         self.K = K
+        self.kind_int8 = _lib.KIND_INT8
         self.cfg = model.cfg
         self.names = model.expert_order
         self.plans = {n: [_BlockPlan(b) for b in model.mixtures[n].blocks] for n in self.names}
+        # all layers' modulation tables of an expert, [L, 6, D]: one add per step
+        self.mod_tables = {n: torch.cat([p.modulation for p in self.plans[n]], 0).contiguous() for n in self.names}
+        self.fused = fused
         self.graph = None
         self.group = group
         if group is not None:
@@ -448,6 +453,110 @@ class DiTStepRunner:
 
     @torch.no_grad()
     def step(self, tokens: dict, rope: dict, ctx: dict, t_mod: dict) -> dict:
+        if self.fused:
+            return self._step_fused(tokens, rope, ctx, t_mod)
+        return self._step_unfused(tokens, rope, ctx, t_mod)
+
+    def _gemm(self, q8, s8, wsb, gelu=False):
+        w, sw, b = wsb
+        return self.K.gemm(self.kind_int8, q8, w, s8, sw, b, gelu=gelu)
+
+    def _pre(self, n, li, x, y_ffn, mods, sc1, rope):
+        """Residual + norm1 + modulate + INT8 -> fused QKV GEMM -> RMSNorm+RoPE."""
+        K, cfg = self.K, self.cfg
+        a, hd, eps = cfg.attn_dim, cfg.head_dim, cfg.eps
+        p, m = self.plans[n][li], mods[n][li]
+        if li == 0:
+            q8, s8 = K.resid_ln_quant(x[n], mod_scale1=sc1[n][li, 0], mod_shift=m[0], eps=eps)
+        else:
+            q8, s8 = K.resid_ln_quant(x[n], y_ffn[n], gate=mods[n][li - 1][5], mod_scale1=sc1[n][li, 0],
+                                      mod_shift=m[0], eps=eps)
+        qkv = self._gemm(q8, s8, p.qkv)
+        qn, kn = K.rms_rope([qkv[:, :a], qkv[:, a:2 * a]], [p.nq.weight, p.nk.weight], rope[n], hd, eps)
+        return qn.unsqueeze(0), kn.unsqueeze(0), qkv[:, 2 * a:].unsqueeze(0), qkv
+
+    def _post(self, n, li, att, x, y_ffn, mods, sc1, ctxq):
+        """o GEMM + gate-residual + norm3 -> cross-attention -> norm2 + FFN."""
+        K, cfg = self.K, self.cfg
+        h, a, hd, eps = cfg.heads, cfg.attn_dim, cfg.head_dim, cfg.eps
+        p, m = self.plans[n][li], mods[n][li]
+        y_o = K.int8_linear(att.reshape(-1, a), *p.o)
+        q8, s8 = K.resid_ln_quant(x[n], y_o, gate=m[2], ln_w=p.norm3.weight, ln_b=p.norm3.bias, eps=eps)
+        cq = K.rms_rope([self._gemm(q8, s8, p.cq)], [p.cnq.weight], None, hd, eps)[0]
+        ckv = self._gemm(*ctxq[n], p.ckv)
+        ck = K.rms_rope([ckv[:, :a]], [p.cnk.weight], None, hd, eps)[0]
+        ca = attention(cq.unsqueeze(0), ck.unsqueeze(0), ckv[:, a:].unsqueeze(0), h)
+        y_co = K.int8_linear(ca.reshape(-1, a), *p.co)
+        q8, s8 = K.resid_ln_quant(x[n], y_co, mod_scale1=sc1[n][li, 1], mod_shift=m[3], eps=eps)
+        f = self._gemm(q8, s8, p.f0, gelu=True)
+        y_ffn[n] = K.int8_linear(f, *p.f2)
+
+    def _video_attention(self, q, k, v):
+        """Video queries of this rank under the first_frame_causal mask: all
+        video keys, except first-frame queries, which see first-frame keys
+        only (recomputed for those rows and written over them, so the bulk
+        attention output needs no concatenation)."""
+        h = self.cfg.heads
+        sv = k.shape[1]
+        t = min(self.cfg.tokens_per_frame, sv)
+        nf = max(0, min(t - self.video_offset, q.shape[1]))
+        out = attention(q, k, v, h)
+        if nf > 0 and sv > t:
+            out[:, :nf] = attention(q[:, :nf], k[:, :t], v[:, :t], h)
+        return out
+
+    def _step_fused(self, tokens, rope, ctx, t_mod):
+        """The step with the elementwise chains fused into row kernels:
+        ``resid_ln_quant`` (gate-residual + LayerNorm + modulate + INT8
+        quantization, feeding the next GEMM directly) and ``rms_rope``.
+        Per expert and layer: 3 row kernels, 3 RMSNorm(+RoPE) kernels, 7
+        GEMMs, 3 activation quantizers (attention outputs, FFN hidden).
+
+        The action expert runs on a second stream.  It joins the video
+        stream once per layer, after the video K/V exist, because action
+        queries attend first-frame video keys; video never attends action
+        tokens.  Its small launches then overlap the video GEMMs."""
+        K, cfg = self.K, self.cfg
+        x = {n: t.reshape(-1, t.shape[-1]).clone() for n, t in tokens.items()}
+        mods, sc1, ctxq = {}, {}, {}
+        for n in self.names:
+            mods[n] = self.mod_tables[n] + t_mod[n]              # [L, 6, D] bf16 (mot.py:56-75)
+            sc1[n] = 1 + mods[n][:, 1::3]                        # bf16(1 + scale) for msa / mlp
+            ctxq[n] = K.quantize_int8_rowwise(ctx[n].reshape(-1, ctx[n].shape[-1]).contiguous())
+        main = torch.cuda.current_stream()
+        side = self._side_stream()
+        side.wait_stream(main)
+        t = min(cfg.tokens_per_frame, cfg.experts[0].tokens)
+        y_ffn = {}
+        for li in range(cfg.layers):
+            qv, kv, vv, qkv_v = self._pre("video", li, x, y_ffn, mods, sc1, rope)
+            if self.world > 1:
+                kv, vv = self._gather_video_kv(kv, vv)
+            kf, vf = kv[:, :t].contiguous(), vv[:, :t].contiguous()   # first-frame keys for the action queries
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                qa, ka, va, _ = self._pre("action", li, x, y_ffn, mods, sc1, rope)
+                att_a = attention(qa, torch.cat([kf, ka], 1), torch.cat([vf, va], 1), cfg.heads)
+                self._post("action", li, att_a, x, y_ffn, mods, sc1, ctxq)
+            kf.record_stream(side)
+            vf.record_stream(side)
+            att_v = self._video_attention(qv, kv, vv)
+            self._post("video", li, att_v, x, y_ffn, mods, sc1, ctxq)
+        with torch.cuda.stream(side):
+            K.resid_ln_quant(x["action"], y_ffn["action"], gate=mods["action"][cfg.layers - 1][5], quant=False)
+        K.resid_ln_quant(x["video"], y_ffn["video"], gate=mods["video"][cfg.layers - 1][5], quant=False)
+        main.wait_stream(side)
+        for n in self.names:
+            x[n].record_stream(side)
+        return {n: x[n].view(tokens[n].shape) for n in self.names}
+
+    def _side_stream(self):
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream()
+        return self._side
+
+    def _step_unfused(self, tokens, rope, ctx, t_mod):
+        """The step as the reference's tensor-op chain (fused QKV GEMM only)."""
         cfg, h = self.cfg, self.cfg.heads
         a = cfg.attn_dim
         x = dict(tokens)

@@ -84,6 +84,60 @@ def int8_epilogue(acc: torch.Tensor, act_scale: torch.Tensor, weight_scale: torc
     return out
 
 
+def resid_ln_quant(x: torch.Tensor, y: torch.Tensor | None = None, gate: torch.Tensor | None = None,
+                   ln_w: torch.Tensor | None = None, ln_b: torch.Tensor | None = None,
+                   mod_scale1: torch.Tensor | None = None, mod_shift: torch.Tensor | None = None,
+                   eps: float = 1e-6, quant: bool = True, q: torch.Tensor | None = None,
+                   s: torch.Tensor | None = None, xn: torch.Tensor | None = None):
+    """Fused residual update / LayerNorm / modulate / INT8 quantization of
+    the rows of ``x`` [M, D] bf16 (``x`` is updated in place when ``y`` is
+    given).  Returns (q int8 [M, D], s fp32 [M]) or (None, None)."""
+    _check(x, "x", torch.bfloat16, 2)
+    M, D = x.shape
+    dev = x.device
+    if y is not None:
+        _check(y, "y", torch.bfloat16, 2, dev) if y.is_contiguous() else None
+        if y.shape[0] != M or y.stride(1) != 1 or y.shape[1] != D:
+            raise ValueError("y must be [M, D] with unit column stride.")
+    for t, nm in ((gate, "gate"), (ln_w, "ln_w"), (ln_b, "ln_b"), (mod_scale1, "mod_scale1"),
+                  (mod_shift, "mod_shift")):
+        if t is not None:
+            _check(t, nm, torch.bfloat16, device=dev)
+            if t.numel() != D:
+                raise ValueError(f"{nm} must have {D} values.")
+    if quant:
+        q = q if q is not None else torch.empty((M, D), dtype=torch.int8, device=dev)
+        s = s if s is not None else torch.empty((M,), dtype=torch.float32, device=dev)
+    _lib.call("qi_b200_resid_ln_quant", _ptr(x), _ptr(y), 0 if y is None else y.stride(0), _ptr(gate), _ptr(ln_w),
+              _ptr(ln_b), _ptr(mod_scale1), _ptr(mod_shift), _ptr(q) if quant else None,
+              _ptr(s) if quant else None, _ptr(xn), M, D, float(eps), _stream(dev))
+    return (q, s) if quant else (None, None)
+
+
+def rms_rope(inputs, weights, rope: torch.Tensor | None, head_dim: int, eps: float = 1e-6, outs=None):
+    """RMSNorm (+ RoPE) of one or two [M, A] bf16 row blocks (row stride may
+    exceed A, e.g. column slices of a fused QKV output).  Returns the
+    normalized contiguous [M, A] tensors."""
+    n = len(inputs)
+    x0 = inputs[0]
+    M, A = x0.shape
+    dev = x0.device
+    for t in inputs:
+        if t.dtype != torch.bfloat16 or t.stride(1) != 1 or t.shape != (M, A) or t.stride(0) != x0.stride(0):
+            raise ValueError("rms_rope inputs must be bf16 [M, A] with a shared row stride and unit column stride.")
+    for w in weights:
+        _check(w, "weight", torch.bfloat16, device=dev)
+    if rope is not None:
+        _check(rope, "rope", torch.float32, device=dev)
+        if rope.numel() != M * head_dim:
+            raise ValueError("rope must be [M, head_dim/2, 2] fp32.")
+    outs = outs if outs is not None else [torch.empty((M, A), dtype=torch.bfloat16, device=dev) for _ in range(n)]
+    _lib.call("qi_b200_rms_rope", _ptr(inputs[0]), _ptr(inputs[-1]), x0.stride(0), _ptr(outs[0]), _ptr(outs[-1]),
+              outs[0].stride(0), _ptr(weights[0]), _ptr(weights[-1]), _ptr(rope), int(head_dim), n, M, A,
+              float(eps), _stream(dev))
+    return outs
+
+
 def quantize_fp8_rowwise(x: torch.Tensor):
     """bf16 [M,K] -> (e4m3 codes uint8 [M,K], fp32 [M]) per-token scales."""
     _check(x, "x", torch.bfloat16, 2)

@@ -48,13 +48,80 @@ def test_runner_matches_module_forward(cfg):
     tokens, rope, ctx, t_mod, mask = D.make_step_inputs(cfg, DEV, seed=0)
     with torch.no_grad():
         ref = model(tokens, rope, ctx, t_mod)
-        runner = D.DiTStepRunner(model)
-        out = runner.step(tokens, rope, ctx, t_mod)
+        out = D.DiTStepRunner(model, fused=False).step(tokens, rope, ctx, t_mod)
         for n in ref:
             assert torch.equal(out[n], ref[n]), (n, rel(out[n], ref[n]))
+        # fused row kernels: LayerNorm / RMSNorm reductions in another order
+        # (an occasional 1-ulp bf16 difference, then INT8 re-quantization)
+        fused = D.DiTStepRunner(model).step(tokens, rope, ctx, t_mod)
+        for n in ref:
+            assert rel(fused[n], ref[n]) < 2e-2, (n, rel(fused[n], ref[n]))
         masked = model(tokens, rope, ctx, t_mod, mask)
         for n in ref:
             assert rel(masked[n], ref[n]) < 2e-2, (n, rel(masked[n], ref[n]))
+
+
+def _bf16_chain(x, y, gate, ln_w, ln_b, s1, sh, eps):
+    """The reference's bf16 tensor ops (GateModule, LayerNorm, modulate)."""
+    if y is not None:
+        x = x + (gate * y if gate is not None else y)
+    n = torch.nn.functional.layer_norm(x, (x.shape[-1],), ln_w, ln_b, eps)
+    if s1 is not None:
+        n = n * s1 + sh
+    return x, n
+
+
+@pytest.mark.parametrize("D_,gated,affine,mod", [(3072, True, False, True), (3072, False, True, False),
+                                                 (1024, False, False, True), (4096, True, True, True)])
+def test_resid_ln_quant_matches_tensor_ops(D_, gated, affine, mod):
+    from qi_b200 import kernels as K
+
+    g = torch.Generator(device=DEV).manual_seed(D_)
+    M = 257
+    bf = torch.bfloat16
+    x = (torch.randn(M, D_, generator=g, device=DEV) * 2).to(bf)
+    y = torch.randn(M, D_, generator=g, device=DEV).to(bf)
+    gate = (torch.randn(D_, generator=g, device=DEV) * 0.5).to(bf) if gated else None
+    w = (1 + 0.1 * torch.randn(D_, generator=g, device=DEV)).to(bf) if affine else None
+    b = (0.1 * torch.randn(D_, generator=g, device=DEV)).to(bf) if affine else None
+    s1 = (1 + 0.2 * torch.randn(D_, generator=g, device=DEV)).to(bf) if mod else None
+    sh = (0.2 * torch.randn(D_, generator=g, device=DEV)).to(bf) if mod else None
+    x_ref, n_ref = _bf16_chain(x, y, gate, w, b, s1, sh, 1e-6)
+    xk = x.clone()
+    xn = torch.empty_like(x)
+    q, s = K.resid_ln_quant(xk, y, gate=gate, ln_w=w, ln_b=b, mod_scale1=s1, mod_shift=sh, xn=xn)
+    assert torch.equal(xk, x_ref)                        # residual update: elementwise, bit-exact
+    # LayerNorm statistics reduce in another order: a few elements differ by
+    # an ulp or two of bf16 (after modulate, relative to the operands' size)
+    diff = (xn.float() - n_ref.float()).abs()
+    assert (diff <= n_ref.float().abs() * 2 ** -6 + 2 ** -8).all()
+    assert (diff > 0).float().mean() < 0.02
+    q_ref, s_ref = K.quantize_int8_rowwise(xn)        # codes from the kernel's own bf16 row
+    assert torch.equal(q, q_ref) and torch.equal(s, s_ref)
+
+
+def test_rms_rope_matches_tensor_ops():
+    from qi_b200 import kernels as K
+
+    cfg = D.CFG5
+    spec = cfg.experts[0]
+    g = torch.Generator(device=DEV).manual_seed(5)
+    M, a = spec.tokens, cfg.attn_dim
+    qkv = torch.randn(M, 3 * a, generator=g, device=DEV).to(torch.bfloat16)
+    wq = (1 + 0.1 * torch.randn(a, generator=g, device=DEV)).to(torch.bfloat16)
+    wk = (1 + 0.1 * torch.randn(a, generator=g, device=DEV)).to(torch.bfloat16)
+    rope = D.rope_tables(cfg, spec, DEV)
+    qn, kn = K.rms_rope([qkv[:, :a], qkv[:, a:2 * a]], [wq, wk], rope, cfg.head_dim, cfg.eps)
+    for got, src, w in ((qn, qkv[:, :a], wq), (kn, qkv[:, a:2 * a], wk)):
+        norm = D.RMSNorm(a, cfg.eps).to(DEV)
+        norm.weight.data = w
+        ref = D.rope_apply(norm(src.unsqueeze(0)), rope, cfg.heads)[0]
+        # the RMS reduction runs in another order: an occasional 1-ulp bf16
+        # difference before RoPE, which the rotation mixes into both outputs
+        # of the pair (absolute bound, outputs are O(1) after the norm)
+        diff = (got.float() - ref.float()).abs()
+        assert diff.max().item() <= 2 ** -5, diff.max().item()
+        assert (diff > 0).float().mean().item() < 0.05
 
 
 def test_graph_replay_bit_exact():

@@ -78,8 +78,8 @@ def test_quantize_fp8_rowwise_and_static_bit_exact(M, Kd):
 SHAPES = [(1, 64, 128), (17, 192, 256), (128, 256, 512), (129, 136, 272), (300, 520, 1024), (512, 3072, 3072)]
 
 
-@pytest.mark.parametrize("M,N,Kd", SHAPES)
-@pytest.mark.parametrize("tile_n", [0, 64, 128, 256])
+@pytest.mark.parametrize("M,N,Kd", SHAPES + [(3120, 3072, 1024)])
+@pytest.mark.parametrize("tile_n", [0, 64, 128, 192, 256])
 def test_int8_gemm_int32_accumulators_bit_exact(M, N, Kd, tile_n):
     g = torch.Generator().manual_seed(M * 7 + N + Kd)
     a = torch.randint(-127, 128, (M, Kd), generator=g, dtype=torch.int8)
@@ -180,6 +180,20 @@ def test_fp8_config2_full_size_sampled_rows():
 # --------------------------------------------------------------------------
 # BF16 GEMM (mainloop of the W4A16 path)
 # --------------------------------------------------------------------------
+
+@pytest.mark.parametrize("tile_n", [0, 192])
+@pytest.mark.parametrize("M,N,Kd", [(1, 64, 128), (300, 520, 512), (3120, 3072, 1024)])
+def test_fp8_gemm_accumulators_vs_fp64(M, N, Kd, tile_n):
+    """FP8 E4M3 raw fp32 accumulators against the exact (fp64) sum of the
+    decoded operands, including the 192-column tile."""
+    g = torch.Generator().manual_seed(M + N + tile_n)
+    a = (torch.randn(M, Kd, generator=g) * 4).to(torch.float8_e4m3fn)
+    b = (torch.randn(N, Kd, generator=g) * 4).to(torch.float8_e4m3fn)
+    acc = K.gemm(_lib.KIND_FP8_E4M3, a.to(DEV), b.to(DEV), None, None, raw_acc=True, tile_n=tile_n)
+    ref = a.double() @ b.double().T
+    err = ((acc.cpu().double() - ref).norm() / ref.norm()).item()
+    assert err < 1e-6, err
+
 
 @pytest.mark.parametrize("M,N,Kd", [(1, 64, 64), (100, 192, 320), (256, 512, 1024)])
 def test_bf16_gemm_vs_fp64(M, N, Kd):
