@@ -293,10 +293,11 @@ def _dit_worker(rank, world, port, out_dir):
                           experts=(D.ExpertSpec("video", 32, 64, 96), D.ExpertSpec("action", 16, 32, 4)))
         model = D.build_mot_dit(cfg, device="cpu", seed=3)
         tokens, rope, ctx, t_mod, _ = D.make_step_inputs(cfg, "cpu", seed=3)
-        single = D.DiTStepRunner(model)
+        # the tensor-op form of the step (the fused form needs CUDA streams)
+        single = D.DiTStepRunner(model, fused=False)
         single.K = OracleKernels
         ref = single.step(tokens, rope, ctx, t_mod)
-        tp = D.DiTStepRunner(model, group=dist.group.WORLD)
+        tp = D.DiTStepRunner(model, group=dist.group.WORLD, fused=False)
         tp.K = OracleKernels
         tok, rp = tp.shard(tokens, rope)
         out = tp.step(tok, rp, ctx, t_mod)
