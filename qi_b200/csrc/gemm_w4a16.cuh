@@ -17,9 +17,10 @@
 //   f = 1 + q/16 (built from the nibble's bits), w = fma(f, 16 s, -(16 + z) s);
 //   both products are exact in fp32, so the only rounding is the final bf16.
 //
-// CTA (512 threads): warp 0 TMA (activation tiles, 128-byte swizzled), warp 1
-// TMEM allocation + MMA issue, warps 4-7 epilogue, warps 8-15 dequant (warp
-// w owns TMEM lanes 32*(w%4).. and K half (w-8)/4 of every 64-element stage).
+// CTA (768 threads): warp 0 TMA (activation tiles, 128-byte swizzled), warp 1
+// TMEM allocation + MMA issue, warps 4-7 epilogue, warps 8-23 dequant (warp
+// w owns TMEM lanes 32*(w%4).. and K quarter (w-8)/4 of every 64-element
+// stage, i.e. 16 consecutive K elements = 2 packed words per thread).
 #pragma once
 
 #include <cuda.h>
