@@ -180,8 +180,6 @@ def run_ours(args):
     from qi_b200 import _lib, kernels as K
 
     world, rank, local = dist_env()
-    if world > 1:
-        print(f"[bench] rank {rank}/{world} local {local} start", file=sys.stderr, flush=True)
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
@@ -226,8 +224,25 @@ def run_ours(args):
     quant = K.quantize_fp8_rowwise if c["kind"] == "fp8" else K.quantize_int8_rowwise
     # kernels per step: w4a16 1; nvfp4 3 (amax, quantize, GEMM; plus a 4-byte memset); int8/fp8 2
     launches_per_step = {"w4a16": 1, "nvfp4": 3}.get(c["kind"], 2)
+    # N > 1, INT8/FP8: the all-gather fused into the GEMM epilogue (peer stores over NVLink)
+    peer = world > 1 and args.gather == "peer" and c["kind"] in ("fp8", "int8")
+    peer_api = None
+    if peer:
+        from qi_b200.sharding import PeerGatherLinear
+        peer_api = PeerGatherLinear(layer, max_tokens=M, shard=False)
+        launches_per_step = 3 + len(peer_api._plan(M))  # quantizer, 2 barriers, one GEMM per row block
+
+    def step_peer(i, ev=None):
+        cur = torch.cuda.current_stream(device)
+        if ev is not None:
+            ev[0].record(cur)
+        peer_api(xs[i % ncopy])
+        if ev is not None:
+            ev[1].record(cur)
 
     def step(i, ev=None):
+        if peer:
+            return step_peer(i, ev)
         x, w = xs[i % ncopy], wqs[i % ncopy]
         cur = torch.cuda.current_stream(device)  # the capture stream inside torch.cuda.graph
         if c["kind"] == "w4a16":
@@ -262,7 +277,7 @@ def run_ours(args):
     # does not leak into the device time of small configs; per-step events
     # around the GEMM are event-record nodes inside the graph.  Multi-GPU:
     # eager steps (the all-gather dominates; NCCL stays outside capture).
-    use_graph = world == 1 and not args.eager
+    use_graph = (world == 1 or peer) and not args.eager
     for i in range(args.warmup):
         step(i)
     barrier()
@@ -310,7 +325,9 @@ def run_ours(args):
     out_shape = (world, M, Nl) if world > 1 else (M, N)
     y_host = torch.empty(out_shape, dtype=torch.bfloat16).pin_memory()
     api_layer = layer
-    if world > 1:
+    if peer:
+        api_layer = peer_api  # returns the rank-major [P, M, N/P] view
+    elif world > 1:
         from qi_b200.sharding import GATHER_RANK_MAJOR, ColumnShardedLinear
         api_layer = ColumnShardedLinear.from_shard(layer, N, gather=GATHER_RANK_MAJOR)
 
@@ -345,7 +362,21 @@ def run_ours(args):
     else:
         alg_bytes = wq.numel() + Nl * 8 + M * Kd + M * 4 + M * Nl * 2
         hbm_bound = False
-    if hbm_bound:
+    if peer:
+        # fused compute + collective: the target time is the slower of the
+        # tensor-core time and the NVLink time of the bytes this rank sends
+        # (M x N/P bf16 to each of P-1 peers at the measured 770 GB/s per direction)
+        link_bytes = M * Nl * 2 * (world - 1)
+        t_tensor = gemm_flops_launch / (2 * bf16_tf * 1e12)
+        t_link = link_bytes / 770e9
+        target = max(t_tensor, t_link)
+        roofline = {"bound": "nvlink" if t_link > t_tensor else "tensor",
+                    "achieved": round(gemm_flops_launch / (gemm_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                    "peak": round(gemm_flops_launch / target / 1e12, 1), "frac": round(target / (gemm_ms * 1e-3), 4),
+                    "traffic": traffic, "algorithmic_bytes": alg_bytes, "nvlink_bytes_sent": link_bytes,
+                    "peak_source": f"max(flops / 2 x bf16 measured dense, NVLink bytes / 770 GB/s measured peer copy)"
+                                   f" = {target * 1e6:.1f} us; {src}"}
+    elif hbm_bound:
         achieved = alg_bytes / (gemm_ms * 1e-3) / 1e9
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_gbs, "unit": "GB/s",
                     "frac": round(achieved / hbm_gbs, 4), "traffic": traffic, "algorithmic_bytes": alg_bytes,
@@ -358,7 +389,9 @@ def run_ours(args):
         roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                     "frac": round(achieved / peak, 4), "traffic": traffic, "algorithmic_bytes": alg_bytes,
                     "peak_source": f"{mult:g} x bf16 dense, " + src}
-    roofline.update({"kernel": "k_gemm_w4a16" if c["kind"] == "w4a16" else f"k_gemm_tc<{c['kind']}>",
+    roofline.update({"kernel": "k_gemm_w4a16" if c["kind"] == "w4a16" else
+                     (f"k_gemm_tc<{c['kind']}> row blocks + copy-engine NVLink copies + 2 barriers "
+                      "(activation quantizer included)" if peer else f"k_gemm_tc<{c['kind']}>"),
                      "kernel_ms": round(gemm_ms, 5), "kernel_timing": gemm_src})
 
     result = {
@@ -370,25 +403,29 @@ def run_ours(args):
                                  "nvfp4": "nvfp4 block16, dynamic per-tensor global scale"}.get(c["kind"], "per_token"),
                    "weight_quant": {"w4a16": "int4 asym g128 packed",
                                     "nvfp4": "nvfp4 block16 + per-tensor global scale"}.get(c["kind"], "per_channel"),
-                   "parallelism": f"N-shard x{world} + NCCL all_gather" if world > 1 else "single GPU",
+                   "parallelism": (f"N-shard x{world}, all-gather overlapped with the GEMM row blocks "
+                                   "(copy-engine NVLink copies into IPC-mapped peer buffers)"
+                                   if peer else f"N-shard x{world} + NCCL all_gather") if world > 1 else "single GPU",
                    "launch": "cuda_graph" if use_graph else "eager",
                    "l2": f"{ncopy} rotating input copies ({ncopy * per_copy / 2**20:.0f} MiB > L2)"},
         "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
                 "api": "qi_b200.quantization.WeightOnlyLinear.forward" if world == 1
-                       else "qi_b200.sharding.ColumnShardedLinear.forward"},
+                       else ("qi_b200.sharding.PeerGatherLinear.forward" if peer
+                             else "qi_b200.sharding.ColumnShardedLinear.forward")},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": roofline,
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args.config, samples=3)
+    graph = None
+    if peer:
+        peer_api.close()
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
-    if world > 1:
-        print(f"[bench] rank {rank} done", file=sys.stderr, flush=True)
     if rank == 0:
         print(json.dumps(result), flush=True)
 
@@ -705,6 +742,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="no CUDA graph for the timed steps")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="N > 1, INT8/FP8: all-gather overlapped with the GEMM on copy engines (peer) "
+                         "or a separate NCCL call")
     ap.add_argument("--layers", type=int, default=0,
                     help="dit only: fewer layers than config 5's 30 (profiling captures; not a bench value)")
     args = ap.parse_args()

@@ -22,6 +22,7 @@
 #define QI_B200_H_
 
 #include <cuda_runtime_api.h>
+#include <stddef.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -90,6 +91,39 @@ int qi_b200_int8_row_scales(const void* x_bf16, float* scales, int rows, int col
  * cross-rank int32 sum of K-sharded partial accumulators. */
 int qi_b200_int8_epilogue(const void* acc_int32, const float* act_scale, const float* weight_scale,
                           const void* bias, void* out_bf16, int M, int N, int flags, cudaStream_t stream);
+
+/* ---- Peer memory for the column-parallel linear with an overlapped all-gather
+ * (no counterpart in the reference, which runs on one GPU).  One process per
+ * GPU; buffers are plain device allocations shared over CUDA IPC (no NVLink
+ * multicast object).  The host exchanges the IPC handles (e.g. with
+ * torch.distributed.all_gather_object) and opens the peers' handles. ---- */
+#define QI_B200_IPC_HANDLE_BYTES 64
+#define QI_B200_MAX_PEERS 8
+
+/* cudaMalloc(bytes), zero it, and export its IPC handle (64 bytes). */
+int qi_b200_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+/* Map a peer's buffer (cudaIpcOpenMemHandle, lazy peer access). */
+int qi_b200_peer_open(const void* ipc_handle, void** ptr);
+int qi_b200_peer_close(void* ptr);
+int qi_b200_peer_free(void* ptr);
+
+/* Cross-GPU barrier on the stream.  flags[i] is rank i's flag block
+ * (QI_B200_PEER_FLAG_BYTES, zero-initialized): word j is written by rank j,
+ * word QI_B200_MAX_PEERS is rank i's own barrier counter.  The kernel
+ * advances this rank's counter (so CUDA-graph replays advance it too),
+ * writes it into word `rank` of every block (release, system scope) and
+ * waits until every rank has written the same value into its own block
+ * (acquire).  All ranks must run the same sequence of barriers.  The wait is
+ * bounded (2 s): on timeout the device status word records tag 0x300 and the
+ * kernel returns. */
+#define QI_B200_PEER_FLAG_BYTES 256
+int qi_b200_peer_barrier(void* const* flags, int P, int rank, cudaStream_t stream);
+
+/* cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, stream): moves a
+ * finished row block of this rank's output into a peer's buffer (mapped with
+ * qi_b200_peer_open) on a copy engine, so the NVLink transfer runs beside
+ * the GEMM of the next row block without taking SMs. */
+int qi_b200_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream);
 
 /* ---- Fused elementwise stages of the MoT DiT block (no counterpart in the
  * reference's quantization package: they fuse the bf16 tensor ops of

@@ -57,6 +57,7 @@ struct EpiParams {
   const uint8_t* sfb;
   int sf_ka;
 };
+constexpr int kMaxPeers = 8;
 
 template <MmaKind KIND, int BN_, int STAGES_>
 struct GemmCfg {

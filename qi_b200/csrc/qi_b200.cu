@@ -13,6 +13,7 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <cstring>
 #include <algorithm>
 #include <mutex>
 
@@ -193,7 +194,7 @@ static int gemm_dispatch(int kind, const void* A, const void* B, const float* sa
                          int force_bn, cudaStream_t stream) {
   int rc = check_gemm_args(kind, A, B, sa, sa_stride, sb, sb_stride, bias, D, ldd, M, N, K, flags);
   if (rc) return rc;
-  EpiParams p;
+  EpiParams p{};
   p.sa = sa;
   p.sa_stride = sa_stride;
   p.sb = sb;
@@ -213,6 +214,107 @@ static int gemm_dispatch(int kind, const void* A, const void* B, const float* sa
 }
 
 static int quant_status(cudaError_t e) { return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA; }
+
+// ---------------------------------------------------------------------------
+// Peer memory for the column-parallel all-gather overlapped with the GEMM:
+// buffers shared over CUDA IPC (plain device allocations, no multicast
+// object), a bounded cross-GPU barrier on per-rank flag words, and an
+// asynchronous copy (copy engine over NVLink) into a peer's buffer.
+// ---------------------------------------------------------------------------
+
+struct PeerFlags {
+  unsigned int* flag[kMaxPeers];  // rank i's flag block: word j written by rank j; word kMaxPeers = i's counter
+  int P, rank;
+};
+
+// One warp.  This rank's barrier counter (in its own flag block, so a CUDA
+// graph replay advances it too) gives the epoch.  Lane i < P publishes the
+// epoch in rank i's block (release, system scope), then waits (acquire,
+// bounded by the 2 s budget) until rank i has published the same epoch in
+// this rank's block.  Every rank runs the same sequence of barriers.
+__global__ void k_peer_barrier(PeerFlags f) {
+  const int lane = threadIdx.x;
+  unsigned int epoch = 0;
+  if (lane == 0) {
+    unsigned int* ctr = f.flag[f.rank] + kMaxPeers;
+    epoch = *ctr + 1u;
+    *ctr = epoch;
+  }
+  epoch = __shfl_sync(0xffffffffu, epoch, 0);
+  if (lane < f.P) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f.flag[lane] + f.rank), "r"(epoch) : "memory");
+    const unsigned int* mine = f.flag[f.rank] + lane;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+      unsigned int v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if (static_cast<int>(v - epoch) >= 0) break;
+      if (globaltimer_ns() - t0 > QI_WAIT_TIMEOUT_NS) {
+        record_error(kDevWaitTimeout, 0x300u, static_cast<unsigned int>(lane));
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncwarp();
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) <= QI_B200_IPC_HANDLE_BYTES, "IPC handle size");
+
+extern "C" int qi_b200_peer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  if (ptr == nullptr || ipc_handle == nullptr || bytes == 0) return QI_B200_EINVAL;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return QI_B200_ECUDA;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+    cudaFree(p);
+    return QI_B200_ECUDA;
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return QI_B200_ECUDA;
+  }
+  std::memset(ipc_handle, 0, QI_B200_IPC_HANDLE_BYTES);
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return QI_B200_OK;
+}
+
+extern "C" int qi_b200_peer_open(const void* ipc_handle, void** ptr) {
+  if (ptr == nullptr || ipc_handle == nullptr) return QI_B200_EINVAL;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+extern "C" int qi_b200_peer_close(void* ptr) {
+  if (ptr == nullptr) return QI_B200_EINVAL;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+extern "C" int qi_b200_peer_free(void* ptr) {
+  if (ptr == nullptr) return QI_B200_EINVAL;
+  return cudaFree(ptr) == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+extern "C" int qi_b200_peer_barrier(void* const* flags, int P, int rank, cudaStream_t stream) {
+  if (flags == nullptr || P < 1 || P > kMaxPeers || rank < 0 || rank >= P) return QI_B200_EINVAL;
+  PeerFlags f{};
+  for (int i = 0; i < P; ++i) {
+    if (flags[i] == nullptr || (reinterpret_cast<uintptr_t>(flags[i]) & 3u) != 0) return QI_B200_EALIGN;
+    f.flag[i] = static_cast<unsigned int*>(flags[i]);
+  }
+  f.P = P;
+  f.rank = rank;
+  k_peer_barrier<<<1, 32, 0, stream>>>(f);
+  return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+extern "C" int qi_b200_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
+  if (bytes == 0) return QI_B200_OK;
+  if (dst == nullptr || src == nullptr) return QI_B200_EINVAL;
+  return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, stream) == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
 
 // ---------------------------------------------------------------------------
 // NVFP4

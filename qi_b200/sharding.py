@@ -38,6 +38,8 @@ tests pass an oracle-backed stand-in and run the same exchange logic on
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 import torch.nn as nn
@@ -180,6 +182,191 @@ class ColumnShardedLinear(nn.Module):
         if self.gather == GATHER_RANK_MAJOR:
             return buf
         return buf.permute(1, 0, 2).reshape(*lead, self.world * n_loc)
+
+
+# ---------------------------------------------------------------------------
+# peer memory: the all-gather fused into the GEMM epilogue
+# ---------------------------------------------------------------------------
+
+
+class _CudaArray:
+    """A raw device range as a torch tensor (``__cuda_array_interface__``)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerBuffer:
+    """``nbytes`` of device memory on every rank of ``group``, each rank's
+    buffer mapped into every other rank over CUDA IPC, with a block of
+    barrier flags in front (``QI_B200_PEER_FLAG_BYTES``).
+
+    The allocations are plain ``cudaMalloc`` ranges.  No NVLink multicast
+    object is bound to them, so a rank that leaves takes no other GPU's
+    mapping with it.  Collective: every rank constructs it, with the same
+    ``nbytes``, at the same point of the program."""
+
+    FLAG_BYTES = 256
+
+    def __init__(self, nbytes: int, group=None):
+        from . import _lib
+
+        self._lib = _lib
+        self.group = group
+        self.rank, self.world = _group_info(group)
+        if self.world > 8:
+            raise ValueError("peer buffers support at most 8 ranks (one node).")
+        self.nbytes = int(nbytes)
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        _lib.call("qi_b200_peer_alloc", ctypes.c_size_t(self.FLAG_BYTES + self.nbytes), ctypes.byref(ptr), handle)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.ptrs, self._opened = [], []
+        for i, h in enumerate(handles):
+            if i == self.rank:
+                self.ptrs.append(ptr.value)
+                continue
+            peer = ctypes.c_void_p()
+            hb = (ctypes.c_char * 64).from_buffer_copy(h)
+            _lib.call("qi_b200_peer_open", hb, ctypes.byref(peer))
+            self.ptrs.append(peer.value)
+            self._opened.append(peer.value)
+        self._own = ptr.value
+        self._flags = (ctypes.c_void_p * self.world)(*self.ptrs)
+        self.data = [p + self.FLAG_BYTES for p in self.ptrs]
+
+    def local(self, shape, dtype=torch.bfloat16) -> torch.Tensor:
+        """This rank's data region as a tensor (no copy)."""
+        code = {torch.bfloat16: "<i2", torch.float16: "<i2", torch.float32: "<f4", torch.int8: "|i1"}[dtype]
+        n = 1
+        for d in shape:
+            n *= d
+        if n * torch.empty((), dtype=dtype).element_size() > self.nbytes:
+            raise ValueError("view exceeds the peer buffer.")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        t = torch.as_tensor(_CudaArray(self.data[self.rank], shape, code), device=dev)
+        return t.view(dtype) if dtype in (torch.bfloat16, torch.float16) else t
+
+    def barrier(self, stream=None):
+        """Bounded cross-GPU barrier on ``stream`` (default: torch's current)."""
+        st = stream if stream is not None else torch.cuda.current_stream()
+        self._lib.call("qi_b200_peer_barrier", self._flags, self.world, self.rank, st.cuda_stream)
+
+    def close(self):
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            self._lib.call("qi_b200_peer_close", ctypes.c_void_p(p))
+        dist.barrier(group=self.group)
+        self._lib.call("qi_b200_peer_free", ctypes.c_void_p(self._own))
+        self._own = None
+
+
+class PeerGatherLinear(nn.Module):
+    """Column-parallel INT8 / FP8 W8A8 linear whose all-gather overlaps the
+    GEMM, row block by row block, on the copy engines.
+
+    Rank r writes its [M, N/P] output into block r of a rank-major
+    [P, M, N/P] buffer that every rank has mapped (``PeerBuffer``).  The
+    GEMM runs in ``chunks`` row blocks on the current stream.  As each block
+    finishes, a side stream copies it into block r of every peer's buffer
+    with ``cudaMemcpyAsync`` over NVLink.  So the transfer of block i runs
+    beside the GEMM of block i+1, and no SM time goes to the collective.
+
+    Per call:
+
+    1. a barrier (every rank has finished reading the previous output);
+    2. the activation quantizer;
+    3. the pipelined GEMM and copies;
+    4. a barrier (all blocks have landed).
+
+    Both barriers are bounded.  Every column is computed by one rank with
+    the single-GPU kernel, so the gathered result is bit-identical to one
+    GPU.
+
+    ``forward`` returns the rank-major [P, M, N/P] view of the buffer (the
+    layout of ``ColumnShardedLinear(gather="rank")``).  It stays valid until
+    the layer's next call."""
+
+    def __init__(self, layer: WeightOnlyLinear, max_tokens: int, group=None, shard: bool = True, chunks: int = 0):
+        super().__init__()
+        from . import _lib
+        from . import kernels as K
+
+        self._lib, self.K = _lib, K
+        self.group = group
+        self.rank, self.world = _group_info(group)
+        self.local = column_shard_buffers(layer, self.rank, self.world) if shard else layer
+        self.n_local = self.local.out_features
+        self.out_features = self.n_local * self.world
+        self.in_features = self.local.in_features
+        loc = self.local
+        if loc.weight_fp8 is not None:
+            self.kind = _lib.KIND_FP8_E4M3
+            self.w = loc.weight_fp8.contiguous()
+            self.ws = loc.weight_scale.reshape(-1).float().contiguous()
+        elif loc.qweight is not None and loc.qweight.dtype == torch.int8 and loc.activation_granularity == "per_token":
+            self.kind = _lib.KIND_INT8
+            self.w = loc.qweight.contiguous()
+            self.ws = loc.scales.reshape(-1).float().contiguous()
+        else:
+            raise ValueError("PeerGatherLinear serves INT8 and FP8 W8A8 layers.")
+        self.static_act = None if self.kind == _lib.KIND_INT8 or loc.activation_granularity == "per_token" \
+            else loc.activation_scale.float().reshape(1).contiguous()
+        self.bias = None if loc.bias is None else loc.bias.to(torch.bfloat16).contiguous()
+        self.gelu = bool(loc.fuse_gelu)
+        self.max_tokens = int(max_tokens)
+        self.chunks = int(chunks)
+        self.buf = PeerBuffer(self.world * self.max_tokens * self.n_local * 2, group)
+        self._side = torch.cuda.Stream()
+
+    def _plan(self, m: int) -> list:
+        c = self.chunks if self.chunks > 0 else (4 if m >= 2048 else (2 if m >= 512 else 1))
+        step = -(-m // c)
+        step = -(-step // 128) * 128  # whole 128-row GEMM tiles per block
+        return [(r0, min(m, r0 + step)) for r0 in range(0, m, step)]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        K, L = self.K, self._lib
+        x2 = x.reshape(-1, x.shape[-1]).to(torch.bfloat16).contiguous()
+        m = x2.shape[0]
+        if m > self.max_tokens:
+            raise ValueError(f"{m} tokens exceed this layer's peer buffer ({self.max_tokens}).")
+        if self.kind == L.KIND_INT8:
+            q, s = K.quantize_int8_rowwise(x2)
+        elif self.static_act is None:
+            q, s = K.quantize_fp8_rowwise(x2)
+        else:
+            q, s = K.quantize_fp8_static(x2, self.static_act), self.static_act
+        main = torch.cuda.current_stream()
+        side = self._side
+        nl, P, r = self.n_local, self.world, self.rank
+        blk = self.max_tokens * nl * 2                     # bytes of one rank block
+        out = self.buf.local((P, self.max_tokens, nl))     # rank-major, this GPU's copy
+        self.buf.barrier(main)  # every rank has finished reading the previous output
+        side.wait_stream(main)
+        for r0, r1 in self._plan(m):
+            s_blk = s if s.numel() == 1 else s[r0:r1]
+            K.gemm(self.kind, q[r0:r1], self.w, s_blk, self.ws, self.bias, gelu=self.gelu, out=out[r, r0:r1])
+            ev = torch.cuda.Event()
+            ev.record(main)
+            side.wait_event(ev)
+            off = r * blk + r0 * nl * 2
+            nbytes = (r1 - r0) * nl * 2
+            for j in range(1, P):
+                peer = (r + j) % P
+                L.call("qi_b200_copy_async", self.buf.data[peer] + off, self.buf.data[r] + off, nbytes,
+                       side.cuda_stream)
+        main.wait_stream(side)
+        self.buf.barrier(main)  # every rank's blocks have landed here
+        return out[:, :m]
+
+    def close(self):
+        self.buf.close()
 
 
 # ---------------------------------------------------------------------------

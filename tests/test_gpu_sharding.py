@@ -154,6 +154,30 @@ def _nccl_worker(rank, world, port, out_dir):
         y_tp = S.RowShardedInt8Linear(dn)(S.ColumnShardedLinear(up, gather=S.GATHER_NONE)(xd))
         torch.cuda.synchronize()
         ok = bool(torch.equal(h_full, h_ref)) and bool(torch.equal(y_tp, y_ref))
+        # all-gather overlapped with the GEMM (copy-engine copies into IPC-mapped
+        # peer buffers + bounded barriers), twice in a row on the same peer
+        # buffer, INT8 (+GELU) and FP8; output is rank-major [P, M, N/P]
+        def rank_major(y):
+            return y.view(y.shape[0], world, -1).permute(1, 0, 2)
+
+        pg = S.PeerGatherLinear(up, max_tokens=M, chunks=3)
+        ok = ok and bool(torch.equal(pg(xd), rank_major(h_ref)))
+        x2 = (xd.float() * 0.5).to(torch.bfloat16)
+        ok = ok and bool(torch.equal(pg(x2[:100]), rank_major(up(x2[:100]))))
+        fcfg = WeightActivationQuantConfig(enabled=True, quant_dtype="fp8", backend="b200",
+                                           activation_granularity="per_token", weight_granularity="per_channel")
+        lin = nn.Linear(D, F)
+        with torch.no_grad():
+            lin.weight.copy_(w_up.float())
+            lin.bias.copy_(b_up.float())
+        f8 = WeightOnlyLinear.from_linear(lin, quantize_linear_weight(lin.weight.detach(), fcfg), fcfg,
+                                          get_backend("b200")).to(dev)
+        f8.bias = f8.bias.to(torch.bfloat16)
+        pf = S.PeerGatherLinear(f8, max_tokens=M)
+        ok = ok and bool(torch.equal(pf(xd), rank_major(f8(xd))))
+        torch.cuda.synchronize()
+        pg.close()
+        pf.close()
         st = _lib.device_status()
         with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
             f.write(f"{int(ok)} {st[0]}\n")
