@@ -292,7 +292,8 @@ class PeerGatherLinear(nn.Module):
     layout of ``ColumnShardedLinear(gather="rank")``).  It stays valid until
     the layer's next call."""
 
-    def __init__(self, layer: WeightOnlyLinear, max_tokens: int, group=None, shard: bool = True, chunks: int = 0):
+    def __init__(self, layer: WeightOnlyLinear, max_tokens: int, group=None, shard: bool = True, chunks: int = 0,
+                 copy_streams: int = 1):
         super().__init__()
         from . import _lib
         from . import kernels as K
@@ -322,7 +323,8 @@ class PeerGatherLinear(nn.Module):
         self.max_tokens = int(max_tokens)
         self.chunks = int(chunks)
         self.buf = PeerBuffer(self.world * self.max_tokens * self.n_local * 2, group)
-        self._side = torch.cuda.Stream()
+        # each row block's copy is split over several streams (several copy engines share NVLink)
+        self._side = [torch.cuda.Stream() for _ in range(max(1, int(copy_streams)))]
 
     def _plan(self, m: int) -> list:
         c = self.chunks if self.chunks > 0 else (4 if m >= 2048 else (2 if m >= 512 else 1))
@@ -343,25 +345,31 @@ class PeerGatherLinear(nn.Module):
         else:
             q, s = K.quantize_fp8_static(x2, self.static_act), self.static_act
         main = torch.cuda.current_stream()
-        side = self._side
         nl, P, r = self.n_local, self.world, self.rank
         blk = self.max_tokens * nl * 2                     # bytes of one rank block
         out = self.buf.local((P, self.max_tokens, nl))     # rank-major, this GPU's copy
         self.buf.barrier(main)  # every rank has finished reading the previous output
-        side.wait_stream(main)
+        for sd in self._side:
+            sd.wait_stream(main)
+        ns = len(self._side)
         for r0, r1 in self._plan(m):
             s_blk = s if s.numel() == 1 else s[r0:r1]
             K.gemm(self.kind, q[r0:r1], self.w, s_blk, self.ws, self.bias, gelu=self.gelu, out=out[r, r0:r1])
             ev = torch.cuda.Event()
             ev.record(main)
-            side.wait_event(ev)
-            off = r * blk + r0 * nl * 2
-            nbytes = (r1 - r0) * nl * 2
-            for j in range(1, P):
-                peer = (r + j) % P
-                L.call("qi_b200_copy_async", self.buf.data[peer] + off, self.buf.data[r] + off, nbytes,
-                       side.cuda_stream)
-        main.wait_stream(side)
+            rows = -(-(r1 - r0) // ns)
+            for i, sd in enumerate(self._side):
+                a0, a1 = r0 + i * rows, min(r1, r0 + (i + 1) * rows)
+                if a0 >= a1:
+                    continue
+                sd.wait_event(ev)
+                off = r * blk + a0 * nl * 2
+                for j in range(1, P):
+                    peer = (r + j) % P
+                    L.call("qi_b200_copy_async", self.buf.data[peer] + off, self.buf.data[r] + off,
+                           (a1 - a0) * nl * 2, sd.cuda_stream)
+        for sd in self._side:
+            main.wait_stream(sd)
         self.buf.barrier(main)  # every rank's blocks have landed here
         return out[:, :m]
 
