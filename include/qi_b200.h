@@ -60,8 +60,9 @@ int qi_b200_device_status(unsigned int* out4, int clear);
 
 /* Launch plan of the calling thread's most recent GEMM launch, for
  * diagnostics: out6 = {kernel (1 int8, 2 fp8, 3 bf16, 4 nvfp4, 5 w4a16 tiles,
- * 6 w4a16 split-K clusters), grid, cluster size, tile N (or padded M for
- * kernel 6), pipeline stages, dynamic shared memory bytes}. */
+ * 6 w4a16 split-K clusters, 7 w4a16 small-M weight streaming, 8/9/10 int8 /
+ * fp8 / bf16 CTA-pair tiles), grid, cluster size, tile N (or padded M for
+ * kernel 6, M for kernel 7), pipeline stages, dynamic shared memory bytes}. */
 int qi_b200_last_launch(int* out6);
 
 /* ---- activation quantizers --------------------------------------------
@@ -177,7 +178,9 @@ int qi_b200_int8_rowwise_bf16out_bias(const void* A, const void* B, const void* 
  * backends/flashrt_fp8_ops.py:68-89):
  *   D[m, n] (row stride ldd) = epi( acc[m,n] * a_scale[m*a_scale_stride] * b_scale[n*b_scale_stride] + bias[n] )
  * a_scale / b_scale / bias may be NULL; a stride of 0 broadcasts one scale.
- * tile_n = 0 picks the tile width; 64, 128, 192 or 256 forces one. */
+ * tile_n = 0 picks the kernel and tile width; 64, 128, 192 or 256 forces a
+ * single-CTA tile of that width; -128, -192 or -256 forces the CTA-pair
+ * kernel (tcgen05 cta_group::2, 256-row tiles over two SMs) of that width. */
 int qi_b200_gemm(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
                  const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd, int M, int N,
                  int K, int flags, int tile_n, cudaStream_t stream);

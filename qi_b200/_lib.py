@@ -115,7 +115,8 @@ def last_launch() -> dict:
     """Plan of this thread's most recent GEMM launch (see qi_b200_last_launch)."""
     buf = (ctypes.c_int * 6)()
     check("qi_b200_last_launch", load().qi_b200_last_launch(ctypes.cast(buf, _P)))
-    names = {1: "gemm_int8", 2: "gemm_fp8", 3: "gemm_bf16", 4: "gemm_nvfp4", 5: "w4a16_tiles", 6: "w4a16_splitk"}
+    names = {1: "gemm_int8", 2: "gemm_fp8", 3: "gemm_bf16", 4: "gemm_nvfp4", 5: "w4a16_tiles", 6: "w4a16_splitk",
+             7: "w4a16_small", 8: "gemm_int8_pair", 9: "gemm_fp8_pair", 10: "gemm_bf16_pair"}
     v = list(buf)
     return {"kernel": names.get(v[0], "none"), "grid": v[1], "cluster": v[2], "tile_n": v[3], "stages": v[4],
             "smem": v[5]}

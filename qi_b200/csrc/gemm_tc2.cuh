@@ -1,0 +1,241 @@
+// CTA-pair tcgen05 GEMM (cta_group::2): D[M,N] = epilogue(A[M,K] . B[N,K]^T)
+// with one 256 x BN MMA tile spread over the tensor cores of two SMs.
+//
+// Why: with one CTA per 128 x 256 tile, every SM streams 16 KB of A plus
+// 32 KB of B from L2 per 128-byte K slice, about 96 B per clock at the
+// 8-bit MMA rate.  That is more than an SM's share of L2 bandwidth, so the
+// single-CTA kernel plateaus near 70 % of the tensor peak.  A CTA pair
+// computes a 256 x BN tile.  Each CTA loads its own 128 rows of A and half
+// of B, and the even CTA's MMA reads B's halves from both shared memories.
+// The L2 -> SMEM traffic per MMA drops by a third (BN = 256: 32 KB per SM
+// per K slice).
+//
+// Roles per CTA (384 threads, one CTA per SM, clusters of 2):
+//   warp 0      TMA producer: this CTA's A rows (128) and B rows (BN/2) of
+//               every K slice; completion is counted on the EVEN CTA's
+//               `full` barrier (the even CTA's producer posts the expected
+//               bytes of both CTAs)
+//   warp 1      both CTAs allocate TMEM together (cta_group::2); the even
+//               CTA's lane 0 issues tcgen05.mma.cta_group::2 (M = 256) and
+//               commits to `empty` / `tfull` of both CTAs (multicast commit)
+//   warps 4-11  epilogue of this CTA's 128 accumulator rows, as in the
+//               single-CTA kernel; each warp arrives on the even CTA's
+//               `tempty` when its TMEM columns have been read
+// Loads have one destination CTA each (no TMA multicast), so the kernel is
+// safe in processes whose peers map this GPU's memory.
+#pragma once
+
+#include "gemm_tc.cuh"
+
+namespace qib {
+
+template <MmaKind KIND, int BN_, int STAGES_>
+struct Gemm2Cfg {
+  static constexpr int BM = 128;  // rows per CTA; a pair covers 256
+  static constexpr int BN = BN_;  // output columns of a pair tile
+  static constexpr int STAGES = STAGES_;
+  static constexpr int ELEM = (KIND == MmaKind::BF16) ? 2 : 1;
+  static constexpr int BK = 128 / ELEM;
+  static constexpr int UMMA_K = (KIND == MmaKind::BF16) ? 16 : 32;
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = (BN / 2) * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int ACC_COLS = BN;
+  static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
+  static constexpr int COLPARAM_BYTES = 2 * BN * (4 + 2);
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + COLPARAM_BYTES + BAR_BYTES + 1024;
+  static constexpr uint32_t IDESC = (KIND == MmaKind::I8)   ? make_idesc(kDS32, kFmtS8, kFmtS8, 256, BN)
+                                    : (KIND == MmaKind::F8) ? make_idesc(kDF32, kFmtE4M3, kFmtE4M3, 256, BN)
+                                                            : make_idesc(kDF32, kFmtBF16, kFmtBF16, 256, BN);
+  static_assert(KIND != MmaKind::NVF4, "block-scaled pairs are not built");
+  static_assert(BN % 64 == 0 && BN >= 128 && BN <= 256, "BN");
+  static_assert(2 * BN <= 512, "TMEM");
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
+};
+
+template <MmaKind KIND, int BN, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const EpiParams p) {
+  using C = Gemm2Cfg<KIND, BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  float* col_scale = reinterpret_cast<float*>(sB + STAGES * C::B_BYTES);
+  __nv_bfloat16* col_bias = reinterpret_cast<__nv_bfloat16*>(col_scale + 2 * BN);
+  uint64_t* full = reinterpret_cast<uint64_t*>(col_bias + 2 * BN);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint64_t* epi_sync = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_sync + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = the CTA that issues the MMAs
+  const bool leader = rank == 0;
+  constexpr unsigned int kTag = 0x200u + static_cast<unsigned int>(KIND) * 16u;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * kEpiWarps);  // one arrive per epilogue warp of both CTAs
+      mbar_init(&epi_sync[b], kEpiThreads);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&tmA);
+    tma_prefetch_map(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any remote arrive / complete_tx
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int m_tiles = (p.M + 255) / 256;
+  const int n_tiles = (p.N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (p.K + C::BK - 1) / C::BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs) ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        const int mb = tile % m_tiles, nb = tile / m_tiles;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kTag, 1)) { ok = false; break; }
+          const uint32_t lfull = map_shared_rank(smem_u32(&full[stage]), 0);
+          if (leader) mbar_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+          tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, lfull, kb * C::BK, mb * 256 + rank * C::BM);
+          tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, lfull, kb * C::BK, nb * BN + rank * (BN / 2));
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok && leader) {
+        // the pair's copies complete on the even CTA's barriers: wait (bounded)
+        // until the stages in flight have landed before the pair exits
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          if (--s < 0) { s = STAGES - 1; ph ^= 1u; }
+          mbar_wait_drain(&full[s], ph);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (even CTA) ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++local) {
+        const int buf = local & 1;
+        const uint32_t tph = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[buf], tph ^ 1u, abort_flag, kTag, 2)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * C::ACC_COLS);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, kTag, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk)
+            mma_pair<static_cast<int>(KIND)>(d_tmem, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32),
+                                             C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+          tc_commit_pair_mc(&empty[stage], 0x3);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) tc_commit_pair_mc(&tfull[buf], 0x3);
+      }
+      if (!ok) {
+        tc_commit_pair_mc(drain, 0x1);
+        mbar_wait_drain(drain, 0);
+      }
+    }
+  } else if (warp >= kFirstEpiWarp) {
+    // ---------------- epilogue (8 warps, this CTA's 128 rows) ----------------
+    const int et = threadIdx.x - kFirstEpiWarp * 32;
+    const int wq = warp & 3;
+    const int half = (warp - kFirstEpiWarp) >> 2;
+    constexpr int COLS = BN / 2;
+    int local = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
+      const int mb = tile % m_tiles, nb = tile / m_tiles;
+      const int buf = local & 1;
+      const uint32_t tph = (local >> 1) & 1;
+      float* sb_t = col_scale + buf * BN;
+      __nv_bfloat16* bias_t = col_bias + buf * BN;
+      for (int j = et; j < BN; j += kEpiThreads) {
+        const int n = nb * BN + j;
+        float sv = 1.0f;
+        if (p.sb != nullptr) sv = (n < p.N) ? __ldg(p.sb + static_cast<long long>(n) * p.sb_stride) : 0.0f;
+        sb_t[j] = sv;
+        bias_t[j] = (p.bias != nullptr && n < p.N) ? p.bias[n] : __float2bfloat16_rn(0.0f);
+      }
+      const int row = wq * 32 + lane;
+      const int m = mb * 256 + static_cast<int>(rank) * C::BM + row;
+      float sa = 1.0f;
+      if (p.sa != nullptr && m < p.M) sa = __ldg(p.sa + static_cast<long long>(m) * p.sa_stride);
+      mbar_arrive(&epi_sync[buf]);
+      if (!mbar_wait(&epi_sync[buf], tph, abort_flag, kTag, 5)) break;
+      if (!mbar_wait(&tfull[buf], tph, abort_flag, kTag, 4)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) +
+                             static_cast<uint32_t>(buf * C::ACC_COLS + half * COLS);
+#pragma unroll 1
+      for (int c = 0; c < COLS; c += 64) {
+        const int n0 = nb * BN + half * COLS + c;
+        if (n0 >= p.N) break;  // warp-uniform
+        uint32_t r0[32], r1[32];
+        const bool two = (COLS - c) >= 64;
+        tmem_ld_32x32b_x32(taddr + c, r0);
+        if (two) tmem_ld_32x32b_x32(taddr + c + 32, r1);
+        tmem_ld_wait();
+        if (m < p.M) {
+          const int j0 = half * COLS + c;
+          epilogue_chunk<KIND>(r0, p, m, n0, sa, sb_t + j0, bias_t + j0);
+          if (two && n0 + 32 < p.N) epilogue_chunk<KIND>(r1, p, m, n0 + 32, sa, sb_t + j0 + 32, bias_t + j0 + 32);
+        }
+      }
+      // this warp's TMEM columns are read: tell the MMA issuer (even CTA)
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_shared_rank(smem_u32(&tempty[buf]), 0));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no MMA of the pair still targets either CTA's TMEM or smem
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace qib

@@ -506,4 +506,183 @@ k_gemm_w4a16_skinny(const __grid_constant__ CUtensorMap tmX, const EpiParams p, 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Small M (<= 8 tokens): weight-bandwidth-bound streaming kernel.
+//
+// At small M the GEMM reads 0.5 byte of packed weight per 2*M flops, so HBM
+// bounds it.  There, the 128-row TMEM staging of the tile kernel above adds
+// a serial dequant -> tcgen05.st -> MMA chain per 64-K stage.  This kernel
+// instead streams the packed words with 16-byte loads issued several chunks
+// ahead, dequantizes them in registers straight into the B fragments of a
+// warp-level bf16 MMA (m16n8k16, the tokens as the 16-row A operand, read
+// from shared memory with ldmatrix), and never stages weights in shared
+// memory.
+//
+// CTA: 8 warps over 16 weight rows (two 8-column MMA tiles); warp w owns K
+// range [w*K/8, (w+1)*K/8) in 128-element chunks.  Lane (g = lane/4,
+// t = lane%4) loads words 4t..4t+3 of each chunk for rows n0+g and n0+8+g; a
+// k16 step needs words 2s, 2s+1, fetched by shuffle from lane 4g + s/2.  The
+// eight warps' fp32 partials are summed in shared memory in warp order, then
+// bias is added and bf16 is stored.  Dequantization is the exact
+// bf16((q - z) * s) of the tile kernel.
+// ---------------------------------------------------------------------------
+
+namespace w4s {
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kRows = 16;          // weight rows (output columns) per CTA
+constexpr int kChunk = 128;        // K elements per chunk (16 words per row)
+constexpr int kDepth = 4;          // chunks in flight per lane
+constexpr int kMaxM = 8;
+}  // namespace w4s
+
+// Shared memory of k_gemm_w4a16_small: the M token rows plus one zero row
+// (rows >= M of the 16-row A fragment read it), each padded by 16 bytes.
+inline int w4s_smem_bytes(int M, int K) { return (M + 1) * (K + 8) * 2; }
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&a)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+               : "r"(addr));
+}
+
+// two nibbles (elements 2t, 2t+1 of word w) -> packed bf16x2 of (q - z) * s
+__device__ __forceinline__ uint32_t dequant_pair(uint32_t w, int t, float s16x, float c) {
+  const uint32_t n0 = (w >> (8 * t)) & 0xFu, n1 = (w >> (8 * t + 4)) & 0xFu;
+  const float f0 = fmaf(__uint_as_float(0x3F800000u | (n0 << 19)), s16x, c);
+  const float f1 = fmaf(__uint_as_float(0x3F800000u | (n1 << 19)), s16x, c);
+  return pack_bf16x2(f0, f1);
+}
+
+__global__ void __launch_bounds__(w4s::kThreads)
+k_gemm_w4a16_small(const __nv_bfloat16* __restrict__ X, EpiParams p, W4Params q) {
+  __shared__ float red[w4s::kWarps][32][8];
+  extern __shared__ __align__(16) uint8_t xs_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ldx = p.K + 8;  // padded row stride of the staged tokens (elements)
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(xs_raw);
+  const int g = lane >> 2, t = lane & 3;
+  const int n0 = blockIdx.x * w4s::kRows;
+  const int kr = p.K / w4s::kWarps;                 // K range of this warp
+  const int k_begin = warp * kr;
+  const int nchunks = kr / w4s::kChunk;
+  const long long row0 = n0 + g, row1 = n0 + 8 + g;
+  const bool ok0 = row0 < p.N, ok1 = row1 < p.N;
+  const uint4* w0p = reinterpret_cast<const uint4*>(q.wq + row0 * q.kw + k_begin / 8) + t;
+  const uint4* w1p = reinterpret_cast<const uint4*>(q.wq + row1 * q.kw + k_begin / 8) + t;
+
+  uint4 buf0[w4s::kDepth], buf1[w4s::kDepth];
+#pragma unroll
+  for (int i = 0; i < w4s::kDepth; ++i) {
+    if (i < nchunks) {
+      buf0[i] = ok0 ? __ldg(w0p + i * 4) : make_uint4(0, 0, 0, 0);
+      buf1[i] = ok1 ? __ldg(w1p + i * 4) : make_uint4(0, 0, 0, 0);
+    }
+  }
+  // stage the M token rows (and a zero row) in shared memory, 16-byte moves,
+  // while this thread's first weight chunks are in flight
+  {
+    const int vpr = p.K / 8;  // uint4 per row
+    for (int i = threadIdx.x; i < (p.M + 1) * vpr; i += w4s::kThreads) {
+      const int r = i / vpr, c = i - r * vpr;
+      const uint4 v = r < p.M ? __ldg(reinterpret_cast<const uint4*>(X + static_cast<long long>(r) * p.K) + c)
+                              : make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(xs + r * ldx + c * 8) = v;
+    }
+  }
+  __syncthreads();
+  // ldmatrix row address of this lane: matrices (rows 0-7 | 8-15) x (k 0-7 | 8-15)
+  const int a_row = (lane & 7) + ((lane >> 3) & 1) * 8;
+  const uint32_t a_base = smem_u32(xs + (a_row < p.M ? a_row : p.M) * ldx + (lane >> 4) * 8);
+
+  float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+  int cur_group = -1;
+  float s16x0 = 0.f, c0 = 0.f, s16x1 = 0.f, c1 = 0.f;
+  for (int cb = 0; cb < nchunks; cb += w4s::kDepth) {
+#pragma unroll
+  for (int slot = 0; slot < w4s::kDepth; ++slot) {  // register slots stay compile-time
+    const int ci = cb + slot;
+    if (ci >= nchunks) break;
+    const uint4 u0 = buf0[slot], u1 = buf1[slot];
+    if (ci + w4s::kDepth < nchunks) {
+      buf0[slot] = ok0 ? __ldg(w0p + (ci + w4s::kDepth) * 4) : make_uint4(0, 0, 0, 0);
+      buf1[slot] = ok1 ? __ldg(w1p + (ci + w4s::kDepth) * 4) : make_uint4(0, 0, 0, 0);
+    }
+    const int kc = k_begin + ci * w4s::kChunk;
+#pragma unroll
+    for (int st = 0; st < w4s::kChunk / 16; ++st) {
+      const int k0 = kc + st * 16;
+      const int grp = q.group_shift >= 0 ? (k0 >> q.group_shift) : (k0 / q.group);
+      if (grp != cur_group) {
+        cur_group = grp;
+        float sa = 0.f, sb = 0.f;
+        uint32_t za = 0, zb = 0;
+        if (ok0) {
+          sa = __half2float(q.scales[row0 * q.G + grp]);
+          za = (static_cast<uint32_t>(__ldg(q.zeros + row0 * q.zw + (grp >> 3))) >> (4 * (grp & 7))) & 0xFu;
+        }
+        if (ok1) {
+          sb = __half2float(q.scales[row1 * q.G + grp]);
+          zb = (static_cast<uint32_t>(__ldg(q.zeros + row1 * q.zw + (grp >> 3))) >> (4 * (grp & 7))) & 0xFu;
+        }
+        s16x0 = sa * 16.0f;
+        c0 = -(16.0f + static_cast<float>(za)) * sa;
+        s16x1 = sb * 16.0f;
+        c1 = -(16.0f + static_cast<float>(zb)) * sb;
+      }
+      // words 2st, 2st+1 of this chunk live in lane 4g + st/2, at index (2st)%4
+      const int src = (lane & ~3) | (st >> 1);
+      const uint32_t wa0 = __shfl_sync(0xffffffffu, (st & 1) ? u0.z : u0.x, src);
+      const uint32_t wa1 = __shfl_sync(0xffffffffu, (st & 1) ? u0.w : u0.y, src);
+      const uint32_t wb0 = __shfl_sync(0xffffffffu, (st & 1) ? u1.z : u1.x, src);
+      const uint32_t wb1 = __shfl_sync(0xffffffffu, (st & 1) ? u1.w : u1.y, src);
+      uint32_t a[4];
+      ldmatrix_x4(a, a_base + static_cast<uint32_t>(k0) * 2u);
+      mma_bf16_16816(d0, a, dequant_pair(wa0, t, s16x0, c0), dequant_pair(wa1, t, s16x0, c0));
+      mma_bf16_16816(d1, a, dequant_pair(wb0, t, s16x1, c1), dequant_pair(wb1, t, s16x1, c1));
+    }
+  }
+  }
+  // K-split reduction in warp order, then the epilogue (bias, bf16)
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    red[warp][lane][i] = d0[i];
+    red[warp][lane][4 + i] = d1[i];
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float v = red[0][lane][i];
+    for (int w = 1; w < w4s::kWarps; ++w) v += red[w][lane][i];
+    acc[i] = v;
+  }
+  // D fragment: acc[0..1] token g, cols 2t,2t+1 of tile 0; acc[2..3] token g+8; acc[4..7] tile 1
+#pragma unroll
+  for (int tile = 0; tile < 2; ++tile) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int m = g + 8 * h;
+      const int n = n0 + 8 * tile + 2 * t;
+      if (m >= p.M || n >= p.N) continue;
+      float y0 = acc[4 * tile + 2 * h], y1 = acc[4 * tile + 2 * h + 1];
+      if (p.bias != nullptr) {
+        y0 = __fadd_rn(y0, __bfloat162float(p.bias[n]));
+        y1 = __fadd_rn(y1, __bfloat162float(p.bias[n + 1]));
+      }
+      *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(p.D) + static_cast<long long>(m) * p.ldd + n) =
+          pack_bf16x2(y0, y1);
+    }
+  }
+}
+
 }  // namespace qib

@@ -19,6 +19,7 @@
 
 #include "dit_fused.cuh"
 #include "gemm_tc.cuh"
+#include "gemm_tc2.cuh"
 #include "gemm_w4a16.cuh"
 #include "quantize_act.cuh"
 #include "quantize_nvfp4.cuh"
@@ -104,7 +105,8 @@ struct LaunchPlan {
 };
 static thread_local LaunchPlan g_last_plan = {0, 0, 0, 0, 0, 0};
 enum PlanKernel { kPlanGemmI8 = 1, kPlanGemmF8 = 2, kPlanGemmBF16 = 3, kPlanGemmNVF4 = 4, kPlanW4Tile = 5,
-                  kPlanW4Skinny = 6 };
+                  kPlanW4Skinny = 6, kPlanW4Small = 7,
+                  kPlanGemmPair = 8 /* + kind: 8 int8, 9 fp8, 10 bf16 */ };
 
 // ---------------------------------------------------------------------------
 // GEMM launch
@@ -136,6 +138,46 @@ static int launch_gemm_cfg(const void* A, const void* B, const EpiParams& p, int
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
+// CTA-pair kernel (cta_group::2): 256 x BN tiles over clusters of 2 CTAs.
+template <MmaKind KIND, int BN, int STAGES>
+static int launch_gemm2_cfg(const void* A, const void* B, const EpiParams& p, int num_sms, cudaStream_t stream) {
+  using C = Gemm2Cfg<KIND, BN, STAGES>;
+  const CUtensorMapDataType dt =
+      (KIND == MmaKind::BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const uint64_t ku = (uint64_t)p.K;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A, dt, ku, (uint64_t)p.M, ku * C::ELEM, C::BK, C::BM);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, B, dt, ku, (uint64_t)p.N, ku * C::ELEM, C::BK, BN / 2);
+  if (rc) return rc;
+  static bool attr_done[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev]) {
+    if (cudaFuncSetAttribute(k_gemm_tc2<KIND, BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::SMEM_BYTES) != cudaSuccess)
+      return QI_B200_ECUDA;
+    attr_done[dev] = true;
+  }
+  const int tiles = ((p.M + 255) / 256) * ((p.N + BN - 1) / BN);
+  const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  g_last_plan = {kPlanGemmPair + static_cast<int>(KIND), 2 * pairs, 2, BN, STAGES, C::SMEM_BYTES};
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_tc2<KIND, BN, STAGES>, ta, tb, p);
+  return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
 // Column-tile width: minimise (tiles per CTA) x (BN + fixed per-tile cost).
 static int pick_bn(int M, int N, int num_sms) {
   const int mt = (M + 127) / 128;
@@ -161,7 +203,22 @@ static int launch_gemm(const void* A, const void* B, const EpiParams& p, cudaStr
   if constexpr (KIND == MmaKind::NVF4) {
     return launch_gemm_cfg<KIND, 128, 6>(A, B, p, di->num_sms, stream);
   } else {
+    if (force_bn < 0) {  // the CTA-pair kernel with tile width -force_bn
+      switch (-force_bn) {
+        case 256: return launch_gemm2_cfg<KIND, 256, 6>(A, B, p, di->num_sms, stream);
+        case 192: return launch_gemm2_cfg<KIND, 192, 7>(A, B, p, di->num_sms, stream);
+        case 128: return launch_gemm2_cfg<KIND, 128, 8>(A, B, p, di->num_sms, stream);
+        default: return QI_B200_EINVAL;
+      }
+    }
     const int bn = force_bn > 0 ? force_bn : pick_bn(p.M, p.N, di->num_sms);
+    // Large problems on 256-wide tiles run as CTA pairs (256 x 256 tiles on two
+    // SMs): a third less L2 -> SMEM traffic per MMA.  Measured on B200: FP8
+    // 4096x14336x3072 72 -> 78 %, INT8 3120x14336x3072 74 -> 81 %, BF16
+    // 4096^3 77 -> 85 % of peak; small M stays on single-CTA tiles.
+    if (force_bn == 0 && bn == 256 && p.M >= 1024 &&
+        (long long)((p.M + 255) / 256) * ((p.N + 255) / 256) >= di->num_sms / 2)
+      return launch_gemm2_cfg<KIND, 256, 6>(A, B, p, di->num_sms, stream);
     switch (bn) {
       case 256: return launch_gemm_cfg<KIND, 256, 4>(A, B, p, di->num_sms, stream);
       case 192: return launch_gemm_cfg<KIND, 192, 5>(A, B, p, di->num_sms, stream);
@@ -473,6 +530,24 @@ static int launch_w4a16(const void* X, const void* wq, const void* scales, const
   q.zeros = static_cast<const int32_t*>(zeros);
   q.wq = static_cast<const int32_t*>(wq);
   q.kw = K / 8;
+  if (M <= w4s::kMaxM && K % (w4s::kWarps * w4s::kChunk) == 0 && group % 16 == 0 &&
+      w4s_smem_bytes(M, K) <= 200 * 1024) {
+    // weight-streaming kernel: 16 weight rows per CTA, 8 warps splitting K
+    static bool attr_small[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_small[dev]) {
+      if (cudaFuncSetAttribute(k_gemm_w4a16_small, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+          cudaSuccess)
+        return QI_B200_ECUDA;
+      attr_small[dev] = true;
+    }
+    const int grid = (N + w4s::kRows - 1) / w4s::kRows;
+    const int smem = w4s_smem_bytes(M, K);
+    g_last_plan = {kPlanW4Small, grid, 1, M, 0, smem};
+    k_gemm_w4a16_small<<<grid, w4s::kThreads, smem, stream>>>(static_cast<const __nv_bfloat16*>(X), p, q);
+    return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+  }
   if (M <= 16) return launch_w4_skinny<16>(X, p, q, di->num_sms, stream);
   if (M <= 32) return launch_w4_skinny<32>(X, p, q, di->num_sms, stream);
   if (M <= 64) return launch_w4_skinny<64>(X, p, q, di->num_sms, stream);

@@ -79,14 +79,30 @@ SHAPES = [(1, 64, 128), (17, 192, 256), (128, 256, 512), (129, 136, 272), (300, 
 
 
 @pytest.mark.parametrize("M,N,Kd", SHAPES + [(3120, 3072, 1024)])
-@pytest.mark.parametrize("tile_n", [0, 64, 128, 192, 256])
+@pytest.mark.parametrize("tile_n", [0, 64, 128, 192, 256, -128, -192, -256])
 def test_int8_gemm_int32_accumulators_bit_exact(M, N, Kd, tile_n):
+    """tile_n < 0: the CTA-pair kernel (cta_group::2, 256-row tiles over two SMs)."""
     g = torch.Generator().manual_seed(M * 7 + N + Kd)
     a = torch.randint(-127, 128, (M, Kd), generator=g, dtype=torch.int8)
     b = torch.randint(-127, 128, (N, Kd), generator=g, dtype=torch.int8)
     acc = K.gemm(_lib.KIND_INT8, a.to(DEV), b.to(DEV), None, None, raw_acc=True, tile_n=tile_n)
     ref = O.int8_gemm_acc(a.numpy(), b.numpy())
     np.testing.assert_array_equal(acc.cpu().numpy().astype(np.int64), ref)
+
+
+@pytest.mark.parametrize("gelu", [False, True])
+@pytest.mark.parametrize("tile_n", [-256, -192, -128])
+def test_pair_kernel_epilogue_matches_single_cta(tile_n, gelu):
+    """The CTA-pair kernel's epilogue (per-token x per-channel scales, bias,
+    GELU) gives the same bytes as the single-CTA kernel."""
+    x, w, b = make_small_case(3120, 3072, 1024, seed=7, outlier_frac=0.002)
+    qw, sw, _ = O.quantize_weight_rtn(w.numpy(), 8, -1, True)
+    qa, sa = K.quantize_int8_rowwise(x.to(DEV))
+    args = (_lib.KIND_INT8, qa, torch.from_numpy(qw).to(DEV), sa, torch.from_numpy(sw[:, 0]).to(DEV), b.to(DEV))
+    y1 = K.gemm(*args, gelu=gelu, tile_n=256)
+    y2 = K.gemm(*args, gelu=gelu, tile_n=tile_n)
+    assert _lib.last_launch()["kernel"] == "gemm_int8_pair"
+    assert torch.equal(y1, y2)
 
 
 @pytest.mark.parametrize("M,N,Kd", SHAPES)
@@ -181,7 +197,7 @@ def test_fp8_config2_full_size_sampled_rows():
 # BF16 GEMM (mainloop of the W4A16 path)
 # --------------------------------------------------------------------------
 
-@pytest.mark.parametrize("tile_n", [0, 192])
+@pytest.mark.parametrize("tile_n", [0, 192, -256, -192, -128])
 @pytest.mark.parametrize("M,N,Kd", [(1, 64, 128), (300, 520, 512), (3120, 3072, 1024)])
 def test_fp8_gemm_accumulators_vs_fp64(M, N, Kd, tile_n):
     """FP8 E4M3 raw fp32 accumulators against the exact (fp64) sum of the
@@ -195,12 +211,13 @@ def test_fp8_gemm_accumulators_vs_fp64(M, N, Kd, tile_n):
     assert err < 1e-6, err
 
 
-@pytest.mark.parametrize("M,N,Kd", [(1, 64, 64), (100, 192, 320), (256, 512, 1024)])
-def test_bf16_gemm_vs_fp64(M, N, Kd):
+@pytest.mark.parametrize("tile_n", [0, -256, -128])
+@pytest.mark.parametrize("M,N,Kd", [(1, 64, 64), (100, 192, 320), (256, 512, 1024), (700, 1024, 512)])
+def test_bf16_gemm_vs_fp64(M, N, Kd, tile_n):
     g = torch.Generator().manual_seed(M + N)
     a = torch.randn(M, Kd, generator=g).bfloat16()
     b = (torch.randn(N, Kd, generator=g) * 0.02).bfloat16()
-    y = K.gemm(_lib.KIND_BF16, a.to(DEV), b.to(DEV), None, None)
+    y = K.gemm(_lib.KIND_BF16, a.to(DEV), b.to(DEV), None, None, tile_n=tile_n)
     ref = a.double() @ b.double().T
     assert O.rel_fro(y.float().cpu().numpy(), ref.numpy()) <= 5e-3
 

@@ -5,7 +5,7 @@
   ``bf16((q - z) * s)`` (reference quantize.py:110-117 on the packed layout).
 * Outputs: relative Frobenius <= 2e-3 vs the oracle (fp32 accumulation
   order), <= 5e-3 vs the reference's own output (golden fixture).
-* Both kernels: the split-K cluster kernel (M <= 256) and the 256x128 tile
+* The kernels: weight streaming (M <= 8, K % 1024 == 0), the split-K cluster kernel (M <= 256) and the 256x128 tile
   kernel (M > 256); BASELINE config 3 (N=K=3072, g=128, M in 1/16/256/4096).
 """
 
@@ -68,6 +68,29 @@ def test_w4a16_dequant_bit_exact_one_hot(N, Kd, group, M):
     y = K.w4a16_linear(xt, qp_d, s_d, zp_d, group)
     wb = O.w4a16_dequant_bf16(qp, s16, zp, Kd, group)
     np.testing.assert_array_equal(bits(y), wb[:, np.arange(M) % Kd].T)
+
+
+@pytest.mark.parametrize("N,Kd,group", [(128, 1024, 128), (136, 2048, 64), (64, 3072, 32), (256, 1024, 96)])
+@pytest.mark.parametrize("M", [1, 5, 8])
+def test_w4a16_small_m_kernel(N, Kd, group, M):
+    """M <= 8 with K % 1024 == 0 runs the weight-streaming kernel (plan 7):
+    dequantization bit-exact (one-hot rows) and outputs vs the oracle."""
+    g = torch.Generator().manual_seed(N + Kd + M)
+    w = (torch.randn(N, Kd, generator=g) * 0.02).numpy()
+    qp, s16, zp = packed(w, group, symmetric=(M == 5))
+    qp_d, zp_d = dev(qp, zp)
+    s_d = torch.from_numpy(s16).to(DEV)
+    x = np.zeros((M, Kd), np.float32)
+    x[np.arange(M), (np.arange(M) * 97) % Kd] = 1.0
+    xt = torch.from_numpy(O.f32_to_bf16(x).view(np.int16)).view(torch.bfloat16).to(DEV)
+    y = K.w4a16_linear(xt, qp_d, s_d, zp_d, group)
+    assert _lib.last_launch()["kernel"] == "w4a16_small"
+    wb = O.w4a16_dequant_bf16(qp, s16, zp, Kd, group)
+    np.testing.assert_array_equal(bits(y), wb[:, (np.arange(M) * 97) % Kd].T)
+    xr, _, b = make_small_case(M, N, Kd, seed=M + Kd)
+    y = K.w4a16_linear(xr.to(DEV), qp_d, s_d, zp_d, group, b.to(DEV))
+    yo = O.w4a16_linear(bits(xr), qp, s16, zp, group, bits(b))
+    assert O.rel_fro(O.bf16_to_f32(bits(y)), O.bf16_to_f32(yo)) <= 2e-3
 
 
 @pytest.mark.parametrize("M", [1, 3, 16, 17, 64, 100, 256, 257, 512])
