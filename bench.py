@@ -230,7 +230,7 @@ def run_ours(args):
     if peer:
         from qi_b200.sharding import PeerGatherLinear
         peer_api = PeerGatherLinear(layer, max_tokens=M, shard=False)
-        launches_per_step = 3 + len(peer_api._plan(M))  # quantizer, 2 barriers, one GEMM per row block
+        launches_per_step = 4  # quantizer, barrier, GEMM with the fused gather, barrier
 
     def step_peer(i, ev=None):
         cur = torch.cuda.current_stream(device)
@@ -390,8 +390,9 @@ def run_ours(args):
                     "frac": round(achieved / peak, 4), "traffic": traffic, "algorithmic_bytes": alg_bytes,
                     "peak_source": f"{mult:g} x bf16 dense, " + src}
     roofline.update({"kernel": "k_gemm_w4a16" if c["kind"] == "w4a16" else
-                     (f"k_gemm_tc<{c['kind']}> row blocks + copy-engine NVLink copies + 2 barriers "
-                      "(activation quantizer included)" if peer else f"k_gemm_tc<{c['kind']}>"),
+                     (f"k_gemm_tc2<{c['kind']}> with the all-gather fused into its epilogue (TMA stores to "
+                      "every rank) + 2 barriers (activation quantizer included)" if peer
+                      else f"k_gemm_tc<{c['kind']}>"),
                      "kernel_ms": round(gemm_ms, 5), "kernel_timing": gemm_src})
 
     result = {
@@ -403,8 +404,8 @@ def run_ours(args):
                                  "nvfp4": "nvfp4 block16, dynamic per-tensor global scale"}.get(c["kind"], "per_token"),
                    "weight_quant": {"w4a16": "int4 asym g128 packed",
                                     "nvfp4": "nvfp4 block16 + per-tensor global scale"}.get(c["kind"], "per_channel"),
-                   "parallelism": (f"N-shard x{world}, all-gather overlapped with the GEMM row blocks "
-                                   "(copy-engine NVLink copies into IPC-mapped peer buffers)"
+                   "parallelism": (f"N-shard x{world}, all-gather fused into the GEMM epilogue (TMA stores "
+                                   "into IPC-mapped peer buffers over NVLink)"
                                    if peer else f"N-shard x{world} + NCCL all_gather") if world > 1 else "single GPU",
                    "launch": "cuda_graph" if use_graph else "eager",
                    "l2": f"{ncopy} rotating input copies ({ncopy * per_copy / 2**20:.0f} MiB > L2)"},
@@ -743,8 +744,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="no CUDA graph for the timed steps")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
-                    help="N > 1, INT8/FP8: all-gather overlapped with the GEMM on copy engines (peer) "
-                         "or a separate NCCL call")
+                    help="N > 1, INT8/FP8: all-gather fused into the GEMM epilogue (peer) or a separate "
+                         "NCCL call")
     ap.add_argument("--layers", type=int, default=0,
                     help="dit only: fewer layers than config 5's 30 (profiling captures; not a bench value)")
     args = ap.parse_args()

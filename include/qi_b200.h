@@ -120,6 +120,18 @@ int qi_b200_peer_free(void* ptr);
 #define QI_B200_PEER_FLAG_BYTES 256
 int qi_b200_peer_barrier(void* const* flags, int P, int rank, cudaStream_t stream);
 
+/* qi_b200_gemm (INT8 / FP8 / BF16, bf16 out, optional GELU) on the CTA-pair
+ * kernel with the column-parallel all-gather fused into its epilogue: every
+ * finished 32 x 64 output box is written by TMA into each of the ndst [M, N]
+ * blocks dst[i] (row pitch ldd elements): this rank's block of its own
+ * output buffer and of its peers' buffers, mapped with qi_b200_peer_open.
+ * The NVLink transfer of a tile overlaps the MMAs of the next tiles.  When
+ * the kernel retires, its stores have completed; follow with
+ * qi_b200_peer_barrier before any rank reads.  ndst <= 8; N % 8 == 0. */
+int qi_b200_gemm_gather(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
+                        const float* b_scale, int b_scale_stride, const void* bias, void* const* dst, int ndst,
+                        long long ldd, int M, int N, int K, int flags, cudaStream_t stream);
+
 /* cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, stream): moves a
  * finished row block of this rank's output into a peer's buffer (mapped with
  * qi_b200_peer_open) on a copy engine, so the NVLink transfer runs beside

@@ -51,6 +51,7 @@ SIGNATURES = {
     "qi_b200_peer_free": [_P],
     "qi_b200_peer_barrier": [_P, _I, _I, _P],
     "qi_b200_copy_async": [_P, _P, ctypes.c_size_t, _P],
+    "qi_b200_gemm_gather": [_I, _P, _P, _P, _I, _P, _I, _P, _P, _I, _LL, _I, _I, _I, _I, _P],
     "qi_b200_resid_ln_quant": [_P, _P, _LL, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _P],
     "qi_b200_rms_rope": [_P, _P, _LL, _P, _P, _LL, _P, _P, _P, _I, _I, _I, _I, _F, _P],
     "qi_b200_int8_epilogue": [_P, _P, _P, _P, _P, _I, _I, _I, _P],

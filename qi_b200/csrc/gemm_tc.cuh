@@ -142,7 +142,8 @@ __device__ __forceinline__ void mma_issue(uint32_t d, uint64_t a, uint64_t b, ui
 // indexed from the chunk's first column); the row scale is in a register.
 template <MmaKind KIND>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], const EpiParams& p, int m, int n0,
-                                               float sa, const float* sb_s, const __nv_bfloat16* bias_s) {
+                                               float sa, const float* sb_s, const __nv_bfloat16* bias_s,
+                                               uint32_t* packed_out = nullptr) {
   const int n_valid = p.N - n0;  // >= 1; a multiple of 8 when < 32 (N % 8 == 0)
   if (p.flags & kEpiRawAcc) {
     uint32_t* drow = static_cast<uint32_t*>(p.D) + static_cast<long long>(m) * p.ldd;
@@ -194,6 +195,11 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], const Ep
       const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&packed[j]));
       packed[j] = pack_bf16x2(gelu_tanh_fast(f.x), gelu_tanh_fast(f.y));
     }
+  }
+  if (packed_out != nullptr) {  // the caller stores the bf16 row chunk itself
+#pragma unroll
+    for (int j = 0; j < 16; ++j) packed_out[j] = packed[j];
+    return;
   }
   __nv_bfloat16* drow = static_cast<__nv_bfloat16*>(p.D) + static_cast<long long>(m) * p.ldd;
 #pragma unroll

@@ -29,7 +29,16 @@
 
 namespace qib {
 
-template <MmaKind KIND, int BN_, int STAGES_>
+// Output tensor maps for the column-parallel all-gather fused into the
+// epilogue: map[i] describes the [M, N] bf16 block this rank owns in
+// destination i (this GPU's output buffer or a peer's, mapped over NVLink).
+// Every 32 x 64 output box is written with one TMA store per destination.
+struct OutMaps {
+  CUtensorMap map[kMaxPeers];
+  int n;  // 0: plain stores to EpiParams::D
+};
+
+template <MmaKind KIND, int BN_, int STAGES_, bool GATHER_ = false>
 struct Gemm2Cfg {
   static constexpr int BM = 128;  // rows per CTA; a pair covers 256
   static constexpr int BN = BN_;  // output columns of a pair tile
@@ -44,7 +53,11 @@ struct Gemm2Cfg {
   static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
   static constexpr int COLPARAM_BYTES = 2 * BN * (4 + 2);
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + COLPARAM_BYTES + BAR_BYTES + 1024;
+  // fused gather: one 32-row x 64-column bf16 box (128-byte rows) per epilogue
+  // warp (measured on 2 GPUs: 64-column boxes with 5 stages beat 32-column
+  // boxes by 25 % and 128-column boxes with 4 stages by 10 %)
+  static constexpr int STAGING_BYTES = GATHER_ ? kEpiWarps * 32 * 64 * 2 : 0;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + COLPARAM_BYTES + BAR_BYTES + STAGING_BYTES + 1024;
   static constexpr uint32_t IDESC = (KIND == MmaKind::I8)   ? make_idesc(kDS32, kFmtS8, kFmtS8, 256, BN)
                                     : (KIND == MmaKind::F8) ? make_idesc(kDF32, kFmtE4M3, kFmtE4M3, 256, BN)
                                                             : make_idesc(kDF32, kFmtBF16, kFmtBF16, 256, BN);
@@ -52,17 +65,20 @@ struct Gemm2Cfg {
   static_assert(BN % 64 == 0 && BN >= 128 && BN <= 256, "BN");
   static_assert(2 * BN <= 512, "TMEM");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
+  static_assert(!GATHER_ || BN % 128 == 0, "gather boxes are 64 columns per epilogue warp");
 };
 
-template <MmaKind KIND, int BN, int STAGES>
+template <MmaKind KIND, int BN, int STAGES, bool GATHER = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const EpiParams p) {
-  using C = Gemm2Cfg<KIND, BN, STAGES>;
+k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const EpiParams p,
+           const __grid_constant__ OutMaps om) {
+  using C = Gemm2Cfg<KIND, BN, STAGES, GATHER>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * C::A_BYTES;
-  float* col_scale = reinterpret_cast<float*>(sB + STAGES * C::B_BYTES);
+  uint8_t* staging = sB + STAGES * C::B_BYTES;  // 1024-byte aligned: 8 boxes of 32 x 64 bf16 (GATHER)
+  float* col_scale = reinterpret_cast<float*>(staging + C::STAGING_BYTES);
   __nv_bfloat16* col_bias = reinterpret_cast<__nv_bfloat16*>(col_scale + 2 * BN);
   uint64_t* full = reinterpret_cast<uint64_t*>(col_bias + 2 * BN);
   uint64_t* empty = full + STAGES;
@@ -215,10 +231,32 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
         tmem_ld_32x32b_x32(taddr + c, r0);
         if (two) tmem_ld_32x32b_x32(taddr + c + 32, r1);
         tmem_ld_wait();
-        if (m < p.M) {
-          const int j0 = half * COLS + c;
-          epilogue_chunk<KIND>(r0, p, m, n0, sa, sb_t + j0, bias_t + j0);
-          if (two && n0 + 32 < p.N) epilogue_chunk<KIND>(r1, p, m, n0 + 32, sa, sb_t + j0 + 32, bias_t + j0 + 32);
+        const int j0 = half * COLS + c;
+        if constexpr (!GATHER) {
+          if (m < p.M) {
+            epilogue_chunk<KIND>(r0, p, m, n0, sa, sb_t + j0, bias_t + j0);
+            if (two && n0 + 32 < p.N) epilogue_chunk<KIND>(r1, p, m, n0 + 32, sa, sb_t + j0 + 32, bias_t + j0 + 32);
+          }
+        } else {
+          // fused all-gather: stage this warp's 32 x 64 box (one 128-byte row
+          // per lane), then one TMA store per destination (clipped to [M, N]
+          // by the tensor maps)
+          uint8_t* box = staging + (warp - kFirstEpiWarp) * (32 * 64 * 2);
+          const int row_base = mb * 256 + static_cast<int>(rank) * C::BM + wq * 32;
+          uint32_t pk[32];
+          epilogue_chunk<KIND>(r0, p, m, n0, sa, sb_t + j0, bias_t + j0, pk);
+          if (two) epilogue_chunk<KIND>(r1, p, m, n0 + 32, sa, sb_t + j0 + 32, bias_t + j0 + 32, pk + 16);
+          if (lane == 0) bulk_wait_read_all();  // the previous box has left shared memory
+          __syncwarp();
+          uint4* dst = reinterpret_cast<uint4*>(box + lane * 128);
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4) dst[q4] = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            for (int d = 0; d < om.n; ++d) tma_store_2d(&om.map[d], box, n0, row_base);
+            bulk_commit_group();
+          }
         }
       }
       // this warp's TMEM columns are read: tell the MMA issuer (even CTA)
@@ -228,6 +266,13 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
     }
   }
 
+  if (GATHER && warp >= kFirstEpiWarp && lane == 0) {
+    // the fused gather's stores have reached every destination before the
+    // kernel retires (the cross-GPU barrier that follows publishes them)
+    bulk_wait_all();
+    fence_proxy_async_global();
+    __threadfence_system();
+  }
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // no MMA of the pair still targets either CTA's TMEM or smem

@@ -139,9 +139,12 @@ static int launch_gemm_cfg(const void* A, const void* B, const EpiParams& p, int
 }
 
 // CTA-pair kernel (cta_group::2): 256 x BN tiles over clusters of 2 CTAs.
-template <MmaKind KIND, int BN, int STAGES>
-static int launch_gemm2_cfg(const void* A, const void* B, const EpiParams& p, int num_sms, cudaStream_t stream) {
-  using C = Gemm2Cfg<KIND, BN, STAGES>;
+template <MmaKind KIND, int BN, int STAGES, bool GATHER = false>
+static int launch_gemm2_cfg(const void* A, const void* B, const EpiParams& p, int num_sms, cudaStream_t stream,
+                            const OutMaps* om_in = nullptr) {
+  using C = Gemm2Cfg<KIND, BN, STAGES, GATHER>;
+  static OutMaps kNoMaps = {};  // n = 0: plain epilogue stores
+  const OutMaps& om = om_in != nullptr ? *om_in : kNoMaps;
   const CUtensorMapDataType dt =
       (KIND == MmaKind::BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const uint64_t ku = (uint64_t)p.K;
@@ -154,7 +157,7 @@ static int launch_gemm2_cfg(const void* A, const void* B, const EpiParams& p, in
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_done[dev]) {
-    if (cudaFuncSetAttribute(k_gemm_tc2<KIND, BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(k_gemm_tc2<KIND, BN, STAGES, GATHER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::SMEM_BYTES) != cudaSuccess)
       return QI_B200_ECUDA;
     attr_done[dev] = true;
@@ -174,7 +177,7 @@ static int launch_gemm2_cfg(const void* A, const void* B, const EpiParams& p, in
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   g_last_plan = {kPlanGemmPair + static_cast<int>(KIND), 2 * pairs, 2, BN, STAGES, C::SMEM_BYTES};
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_tc2<KIND, BN, STAGES>, ta, tb, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_tc2<KIND, BN, STAGES, GATHER>, ta, tb, p, om);
   return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
@@ -365,6 +368,47 @@ extern "C" int qi_b200_peer_barrier(void* const* flags, int P, int rank, cudaStr
   f.rank = rank;
   k_peer_barrier<<<1, 32, 0, stream>>>(f);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+extern "C" int qi_b200_gemm_gather(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
+                                   const float* b_scale, int b_scale_stride, const void* bias, void* const* dst,
+                                   int ndst, long long ldd, int M, int N, int K, int flags, cudaStream_t stream) {
+  if (dst == nullptr || ndst < 1 || ndst > kMaxPeers) return QI_B200_EINVAL;
+  if (kind != QI_B200_KIND_INT8 && kind != QI_B200_KIND_FP8_E4M3 && kind != QI_B200_KIND_BF16) return QI_B200_EINVAL;
+  if (flags & ~kEpiGelu) return QI_B200_EINVAL;  // bf16 outputs only
+  for (int i = 0; i < ndst; ++i)
+    if (dst[i] == nullptr || !aligned16(dst[i])) return QI_B200_EALIGN;
+  int rc = check_gemm_args(kind, A, B, a_scale, a_scale_stride, b_scale, b_scale_stride, bias, dst[0], ldd, M, N, K,
+                           flags);
+  if (rc) return rc;
+  DeviceInfo* di = nullptr;
+  rc = device_info(&di);
+  if (rc) return rc;
+  OutMaps om = {};
+  om.n = ndst;
+  for (int i = 0; i < ndst; ++i) {
+    rc = make_tmap_2d(&om.map[i], dst[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)N, (uint64_t)M,
+                      (uint64_t)ldd * 2, 64, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  EpiParams p{};
+  p.sa = a_scale;
+  p.sa_stride = a_scale_stride;
+  p.sb = b_scale;
+  p.sb_stride = b_scale_stride;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.D = dst[0];
+  p.ldd = ldd;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.flags = flags;
+  switch (kind) {
+    case QI_B200_KIND_INT8: return launch_gemm2_cfg<MmaKind::I8, 256, 5, true>(A, B, p, di->num_sms, stream, &om);
+    case QI_B200_KIND_FP8_E4M3:
+      return launch_gemm2_cfg<MmaKind::F8, 256, 5, true>(A, B, p, di->num_sms, stream, &om);
+    default: return launch_gemm2_cfg<MmaKind::BF16, 256, 5, true>(A, B, p, di->num_sms, stream, &om);
+  }
 }
 
 extern "C" int qi_b200_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream) {

@@ -106,6 +106,30 @@ def test_row_parallel_emulated_bit_exact(P, M, N, Kd):
 # ---------------------------------------------------------------------------
 
 
+@pytest.mark.parametrize("ndst", [1, 3])
+@pytest.mark.parametrize("M,N,Kd,gelu", [(300, 520, 512, False), (2048, 1536, 1024, True)])
+def test_gemm_gather_epilogue_one_gpu(M, N, Kd, gelu, ndst):
+    """The TMA-store epilogue of qi_b200_gemm_gather, with every destination
+    on this GPU: each destination block holds the bytes of the plain GEMM."""
+    x, w, b = make_small_case(M, N, Kd, seed=M + ndst, outlier_frac=0.002)
+    qw, sw, _, _ = int8_weights(w)
+    qa, sa = K.quantize_int8_rowwise(x.to(DEV))
+    bd = b.to(DEV)
+    ref = K.gemm(_lib.KIND_INT8, qa, qw, sa, sw, bd, gelu=gelu)
+    ld = N + 64  # blocks inside wider buffers (row pitch != N)
+    bufs = [torch.full((M + 5, ld), 7.0, dtype=torch.bfloat16, device=DEV) for _ in range(ndst)]
+    import ctypes
+    dst = (ctypes.c_void_p * ndst)(*[t.data_ptr() for t in bufs])
+    _lib.call("qi_b200_gemm_gather", _lib.KIND_INT8, qa.data_ptr(), qw.data_ptr(), sa.data_ptr(), 1,
+              sw.data_ptr(), 1, bd.data_ptr(), dst, ndst, ld, M, N, Kd, _lib.EPI_GELU if gelu else 0,
+              torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert _lib.last_launch()["kernel"] == "gemm_int8_pair"
+    for t in bufs:
+        assert torch.equal(t[:M, :N], ref)
+        assert bool((t[:M, N:] == 7.0).all()) and bool((t[M:] == 7.0).all())  # nothing written outside
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -154,16 +178,19 @@ def _nccl_worker(rank, world, port, out_dir):
         y_tp = S.RowShardedInt8Linear(dn)(S.ColumnShardedLinear(up, gather=S.GATHER_NONE)(xd))
         torch.cuda.synchronize()
         ok = bool(torch.equal(h_full, h_ref)) and bool(torch.equal(y_tp, y_ref))
-        # all-gather overlapped with the GEMM (copy-engine copies into IPC-mapped
-        # peer buffers + bounded barriers), twice in a row on the same peer
+        # all-gather fused into the GEMM epilogue (TMA stores into IPC-mapped peer
+        # buffers) and the copy-engine form, each twice in a row on the same peer
         # buffer, INT8 (+GELU) and FP8; output is rank-major [P, M, N/P]
         def rank_major(y):
             return y.view(y.shape[0], world, -1).permute(1, 0, 2)
 
-        pg = S.PeerGatherLinear(up, max_tokens=M, chunks=3)
-        ok = ok and bool(torch.equal(pg(xd), rank_major(h_ref)))
         x2 = (xd.float() * 0.5).to(torch.bfloat16)
-        ok = ok and bool(torch.equal(pg(x2[:100]), rank_major(up(x2[:100]))))
+        for mode in ("fused", "copy"):
+            pg = S.PeerGatherLinear(up, max_tokens=M, chunks=3, mode=mode)
+            ok = ok and bool(torch.equal(pg(xd), rank_major(h_ref)))
+            ok = ok and bool(torch.equal(pg(x2[:100]), rank_major(up(x2[:100]))))
+            if mode == "copy":
+                pg.close()
         fcfg = WeightActivationQuantConfig(enabled=True, quant_dtype="fp8", backend="b200",
                                            activation_granularity="per_token", weight_granularity="per_channel")
         lin = nn.Linear(D, F)
