@@ -225,7 +225,10 @@ def run_ours(args):
     # kernels per step: w4a16 1; nvfp4 3 (amax, quantize, GEMM; plus a 4-byte memset); int8/fp8 2
     launches_per_step = {"w4a16": 1, "nvfp4": 3}.get(c["kind"], 2)
     # N > 1, INT8/FP8: the all-gather fused into the GEMM epilogue (peer stores over NVLink)
-    peer = world > 1 and args.gather == "peer" and c["kind"] in ("fp8", "int8")
+    # auto: the fused gather where it has been validated on the GPU (2 ranks);
+    # NCCL's all-gather beyond that
+    gather = args.gather if args.gather != "auto" else ("peer" if world == 2 else "nccl")
+    peer = world > 1 and gather == "peer" and c["kind"] in ("fp8", "int8")
     peer_api = None
     if peer:
         from qi_b200.sharding import PeerGatherLinear
@@ -743,9 +746,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="no CUDA graph for the timed steps")
-    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
-                    help="N > 1, INT8/FP8: all-gather fused into the GEMM epilogue (peer) or a separate "
-                         "NCCL call")
+    ap.add_argument("--gather", default="auto", choices=["auto", "peer", "nccl"],
+                    help="N > 1, INT8/FP8: all-gather fused into the GEMM epilogue (peer), a separate "
+                         "NCCL call (nccl), or auto (peer at 2 ranks, NCCL beyond)")
     ap.add_argument("--layers", type=int, default=0,
                     help="dit only: fewer layers than config 5's 30 (profiling captures; not a bench value)")
     args = ap.parse_args()
