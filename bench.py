@@ -288,6 +288,7 @@ def run_ours(args):
             torch.cuda.Event(enable_timing=True, external=use_graph)) for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     graph = None
+    launches0 = _lib.launch_count()  # this library's kernels in the K timed steps (graph: counted at capture)
     if use_graph:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
@@ -305,6 +306,10 @@ def run_ours(args):
                 step(i, evs[i])
         t1.record(stream)
         barrier()
+    gpu_launches = _lib.launch_count() - launches0
+    if gpu_launches != launches_per_step * args.steps:
+        print(f"warning: {gpu_launches} library launches, expected {launches_per_step} x {args.steps}",
+              file=sys.stderr)
     ms_total = max_over_ranks(t0.elapsed_time(t1), world, device)
     try:
         gemm_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
@@ -417,7 +422,7 @@ def run_ours(args):
                 "api": "qi_b200.quantization.WeightOnlyLinear.forward" if world == 1
                        else ("qi_b200.sharding.PeerGatherLinear.forward" if peer
                              else "qi_b200.sharding.ColumnShardedLinear.forward")},
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": gpu_launches,
         "roofline": roofline,
         "clocks": clk.summary(),
     }
@@ -475,12 +480,16 @@ def run_dit(args):
             return runner.static_out
         runner.replay = run_step
         run_step()
+        per_step_launches = None
     else:
-        runner.capture(tok_l, rope_l, ctx, t_mod, warmup=2)
+        c0 = _lib.launch_count()
+        runner.capture(tok_l, rope_l, ctx, t_mod, warmup=2)  # 2 eager warm-up steps + the captured one
+        per_step_launches = (_lib.launch_count() - c0) // 3
     for _ in range(args.warmup):
         runner.replay()
     barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0 = _lib.launch_count()
     with ClockSampler(local) as clk:
         barrier()
         t0.record(stream)
@@ -488,6 +497,9 @@ def run_dit(args):
             runner.replay()
         t1.record(stream)
         barrier()
+    # this library's kernels in the timed steps (graph replays: as captured)
+    gpu_launches = (_lib.launch_count() - c0 if per_step_launches is None
+                    else per_step_launches * args.steps)
     ms_step = max_over_ranks(t0.elapsed_time(t1), world, device) / args.steps
     st = _lib.device_status()
     if st[0] != 0:
@@ -546,7 +558,6 @@ def run_dit(args):
                 "peak_source": "2 x bf16 dense, " + src, "kernel": "k_gemm_tc<int8> (video ffn.0 + GELU)",
                 "kernel_ms": round(gemm_ms, 5), "kernel_timing": "cuda events over 20 graph-captured launches",
                 "step_linear_tops": round(cfg.linear_ops() / world / (ms_step * 1e-3) / 1e12, 1)}
-    per_layer = 14 * len(cfg.experts)  # 7 GEMMs + 7 activation quantizers per expert
     result = {
         "metric": "dit_step_latency_ms", "value": round(ms_step, 4), "unit": "ms", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": False,
@@ -561,7 +572,7 @@ def run_dit(args):
                    "l2": "5.9 GB of INT8 weights streamed per step (> L2), no flush needed"},
         "e2e": {"value": round(e2e_ms, 4), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "qi_b200.dit.DiTStepRunner (graph replay) with pinned host tokens"},
-        "gpu_launches": per_layer * cfg.layers * args.steps,
+        "gpu_launches": gpu_launches,
         "roofline": roofline,
         "clocks": clk.summary(),
     }

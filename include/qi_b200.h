@@ -61,9 +61,14 @@ int qi_b200_device_status(unsigned int* out4, int clear);
 /* Launch plan of the calling thread's most recent GEMM launch, for
  * diagnostics: out6 = {kernel (1 int8, 2 fp8, 3 bf16, 4 nvfp4, 5 w4a16 tiles,
  * 6 w4a16 split-K clusters, 7 w4a16 small-M weight streaming, 8/9/10 int8 /
- * fp8 / bf16 CTA-pair tiles), grid, cluster size, tile N (or padded M for
- * kernel 6, M for kernel 7), pipeline stages, dynamic shared memory bytes}. */
+ * fp8 / bf16 CTA-pair tiles), grid, cluster size (K splits for kernels 1-3
+ * under qi_b200_gemm_splitk), tile N (or padded M for kernel 6, M for kernel
+ * 7), pipeline stages, dynamic shared memory bytes}. */
 int qi_b200_last_launch(int* out6);
+
+/* Number of kernels this library has launched in this process, counting
+ * launches recorded into a CUDA graph under capture once (at capture). */
+int qi_b200_launch_count(unsigned long long* out);
 
 /* ---- activation quantizers --------------------------------------------
  * Replaces qi_quantize_int8_rowwise (csrc/int8_w8a8/quantize_int8.cuh:7-13,
@@ -92,6 +97,25 @@ int qi_b200_int8_row_scales(const void* x_bf16, float* scales, int rows, int col
  * cross-rank int32 sum of K-sharded partial accumulators. */
 int qi_b200_int8_epilogue(const void* acc_int32, const float* act_scale, const float* weight_scale,
                           const void* bias, void* out_bf16, int M, int N, int flags, cudaStream_t stream);
+
+/* qi_b200_gemm split over K for problems whose 128 x 256 tiles cannot fill
+ * the GPU (small M: the reference's INT8 config 1 at M = 512 has 48 tiles for
+ * 148 SMs; the DiT action expert's M = 32 linears fewer still).  `splits`
+ * CTAs share each output tile, each over a contiguous range of K; their raw
+ * accumulators go to `workspace` (splits x M x N x 4 bytes, caller-owned),
+ * and a second kernel sums them (int32 exactly for INT8, so INT8 outputs are
+ * bit-identical to qi_b200_gemm) and applies the epilogue.  bf16 output only
+ * (flags: QI_B200_EPI_GELU).  qi_b200_gemm_splitk_plan gives the split count
+ * at which 128 x 256 tiles fill the SMs (1 = they already do) and the
+ * workspace it needs.  qi_b200_gemm never splits on its own: measured on a
+ * B200, writing and re-reading the partials cost more than the idle SMs at
+ * the reference's shapes (M = 512, N = K = 3072: 21.2 us at 2 splits against
+ * 13.6 us unsplit). */
+int qi_b200_gemm_splitk_plan(int kind, int M, int N, int K, int* splits, size_t* workspace_bytes);
+int qi_b200_gemm_splitk(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
+                        const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd, int M,
+                        int N, int K, int flags, int splits, void* workspace, size_t workspace_bytes,
+                        cudaStream_t stream);
 
 /* ---- Peer memory for the column-parallel linear with an overlapped all-gather
  * (no counterpart in the reference, which runs on one GPU).  One process per

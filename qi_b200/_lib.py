@@ -42,6 +42,7 @@ SIGNATURES = {
     "qi_b200_error_string": [_I],
     "qi_b200_device_status": [_P, _I],
     "qi_b200_last_launch": [_P],
+    "qi_b200_launch_count": [_P],
     "qi_b200_quantize_int8_rowwise": [_P, _P, _P, _I, _I, _P],
     "qi_b200_quantize_int8_rowwise_given": [_P, _P, _P, _I, _I, _P],
     "qi_b200_int8_row_scales": [_P, _P, _I, _I, _P],
@@ -51,6 +52,8 @@ SIGNATURES = {
     "qi_b200_peer_free": [_P],
     "qi_b200_peer_barrier": [_P, _I, _I, _P],
     "qi_b200_copy_async": [_P, _P, ctypes.c_size_t, _P],
+    "qi_b200_gemm_splitk_plan": [_I, _I, _I, _I, _P, _P],
+    "qi_b200_gemm_splitk": [_I, _P, _P, _P, _I, _P, _I, _P, _P, _LL, _I, _I, _I, _I, _I, _P, ctypes.c_size_t, _P],
     "qi_b200_gemm_gather": [_I, _P, _P, _P, _I, _P, _I, _P, _P, _I, _LL, _I, _I, _I, _I, _P],
     "qi_b200_resid_ln_quant": [_P, _P, _LL, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _P],
     "qi_b200_rms_rope": [_P, _P, _LL, _P, _P, _LL, _P, _P, _P, _I, _I, _I, _I, _F, _P],
@@ -110,6 +113,13 @@ def check(fn_name: str, rc: int) -> None:
 def call(fn_name: str, *args) -> None:
     """Call a C-ABI entry point and raise on a non-zero status."""
     check(fn_name, getattr(load(), fn_name)(*args))
+
+
+def launch_count() -> int:
+    """Kernels this library has launched in this process (graph captures count once)."""
+    n = ctypes.c_ulonglong(0)
+    check("qi_b200_launch_count", load().qi_b200_launch_count(ctypes.byref(n)))
+    return n.value
 
 
 def last_launch() -> dict:

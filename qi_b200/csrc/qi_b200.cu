@@ -18,6 +18,7 @@
 #include <mutex>
 
 #include "dit_fused.cuh"
+#include "launch_count.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
 #include "gemm_w4a16.cuh"
@@ -131,10 +132,11 @@ static int launch_gemm_cfg(const void* A, const void* B, const EpiParams& p, int
       return QI_B200_ECUDA;
     attr_done[dev] = true;
   }
-  const int tiles = ((p.M + C::BM - 1) / C::BM) * ((p.N + BN - 1) / BN);
+  const int tiles = ((p.M + C::BM - 1) / C::BM) * ((p.N + BN - 1) / BN) * (p.ksplit > 1 ? p.ksplit : 1);
   const int grid = tiles < num_sms ? tiles : num_sms;
-  g_last_plan = {1 + static_cast<int>(KIND), grid, 1, BN, STAGES, C::SMEM_BYTES};
+  g_last_plan = {1 + static_cast<int>(KIND), grid, p.ksplit > 1 ? p.ksplit : 1, BN, STAGES, C::SMEM_BYTES};
   k_gemm_tc<KIND, BN, STAGES><<<grid, kGemmThreads, C::SMEM_BYTES, stream>>>(ta, tb, p);
+  count_launches(1);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
@@ -178,6 +180,7 @@ static int launch_gemm2_cfg(const void* A, const void* B, const EpiParams& p, in
   cfg.numAttrs = 1;
   g_last_plan = {kPlanGemmPair + static_cast<int>(KIND), 2 * pairs, 2, BN, STAGES, C::SMEM_BYTES};
   const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_tc2<KIND, BN, STAGES, GATHER>, ta, tb, p, om);
+  count_launches(1);
   return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
@@ -367,6 +370,7 @@ extern "C" int qi_b200_peer_barrier(void* const* flags, int P, int rank, cudaStr
   f.P = P;
   f.rank = rank;
   k_peer_barrier<<<1, 32, 0, stream>>>(f);
+  count_launches(1);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
@@ -411,6 +415,81 @@ extern "C" int qi_b200_gemm_gather(int kind, const void* A, const void* B, const
   }
 }
 
+// Split-K plan for problems too small to fill the GPU with 128 x 256 tiles:
+// splits so that tiles x splits ~ #SMs, at least 4 K blocks per split (a
+// shorter main loop does not pay for the second kernel).
+static int splitk_splits(int kind, int M, int N, int K, int num_sms) {
+  if (kind < 0 || kind > 2 || M <= 0 || N <= 0 || K <= 0) return 1;
+  const int bk = kind == QI_B200_KIND_BF16 ? 64 : 128;
+  const int k_blocks = (K + bk - 1) / bk;
+  const long long tiles = (long long)((M + 127) / 128) * ((N + 255) / 256);
+  if (tiles * 2 > num_sms) return 1;
+  int sp = static_cast<int>(num_sms / tiles);
+  sp = std::min(sp, k_blocks / 4);
+  sp = std::min(sp, 16);
+  if (sp < 2) return 1;
+  const int kbp = (k_blocks + sp - 1) / sp;
+  return (k_blocks + kbp - 1) / kbp;  // every split gets a non-empty K range
+}
+
+extern "C" int qi_b200_gemm_splitk_plan(int kind, int M, int N, int K, int* splits, size_t* workspace_bytes) {
+  if (splits == nullptr || workspace_bytes == nullptr) return QI_B200_EINVAL;
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  *splits = splitk_splits(kind, M, N, K, di->num_sms);
+  *workspace_bytes = *splits > 1 ? static_cast<size_t>(*splits) * M * N * 4 : 0;
+  return QI_B200_OK;
+}
+
+extern "C" int qi_b200_gemm_splitk(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
+                                   const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd,
+                                   int M, int N, int K, int flags, int splits, void* workspace,
+                                   size_t workspace_bytes, cudaStream_t stream) {
+  if (flags & ~kEpiGelu) return QI_B200_EINVAL;  // bf16 outputs
+  if (kind < 0 || kind > 2 || splits < 2 || splits > 16) return QI_B200_EINVAL;
+  int rc = check_gemm_args(kind, A, B, a_scale, a_scale_stride, b_scale, b_scale_stride, bias, D, ldd, M, N, K,
+                           flags);
+  if (rc) return rc;
+  const int bk = kind == QI_B200_KIND_BF16 ? 64 : 128;
+  const int k_blocks = (K + bk - 1) / bk;
+  const int kbp = (k_blocks + splits - 1) / splits;
+  if ((long long)kbp * (splits - 1) >= k_blocks) return QI_B200_ESHAPE;  // a split with no K blocks
+  if (workspace == nullptr || !aligned16(workspace) || workspace_bytes < static_cast<size_t>(splits) * M * N * 4)
+    return QI_B200_EINVAL;
+  DeviceInfo* di = nullptr;
+  rc = device_info(&di);
+  if (rc) return rc;
+  EpiParams p{};
+  p.D = workspace;
+  p.ldd = N;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.flags = kEpiRawAcc;
+  p.ksplit = splits;
+  p.split_stride = (long long)M * N;
+  switch (kind) {
+    case QI_B200_KIND_INT8: rc = launch_gemm_cfg<MmaKind::I8, 256, 4>(A, B, p, di->num_sms, stream); break;
+    case QI_B200_KIND_FP8_E4M3: rc = launch_gemm_cfg<MmaKind::F8, 256, 4>(A, B, p, di->num_sms, stream); break;
+    default: rc = launch_gemm_cfg<MmaKind::BF16, 256, 4>(A, B, p, di->num_sms, stream); break;
+  }
+  if (rc) return rc;
+  const long long vec = (long long)M * (N / 8);
+  const int grid = (int)std::min<long long>((vec + 255) / 256, (long long)di->num_sms * 8);
+  const auto* bsp = static_cast<const __nv_bfloat16*>(bias);
+  auto* out = static_cast<__nv_bfloat16*>(D);
+  const int gelu = flags & kEpiGelu;
+  if (kind == QI_B200_KIND_INT8)
+    k_splitk_epilogue<true><<<grid, 256, 0, stream>>>(workspace, splits, p.split_stride, a_scale, a_scale_stride,
+                                                       b_scale, b_scale_stride, bsp, out, ldd, M, N, gelu);
+  else
+    k_splitk_epilogue<false><<<grid, 256, 0, stream>>>(workspace, splits, p.split_stride, a_scale, a_scale_stride,
+                                                        b_scale, b_scale_stride, bsp, out, ldd, M, N, gelu);
+  count_launches(1);
+  return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
 extern "C" int qi_b200_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
   if (bytes == 0) return QI_B200_OK;
   if (dst == nullptr || src == nullptr) return QI_B200_EINVAL;
@@ -446,11 +525,14 @@ static int nvfp4_quantize(const void* x, int rows, int cols, int g_mode, const f
     const int g2 = (int)std::min<long long>((n / 8 + 255) / 256 + 1, (long long)di->num_sms * 8);
     k_amax_bf16<<<g2, 256, 0, stream>>>(xb, n, ws_amax);
     k_quant_nvfp4<1><<<grid_flat, 256, 0, stream>>>(xb, rows, cols, nullptr, ws_amax, g_out, qb, sb, ka);
+    count_launches(2);
   } else if (g_mode == 0) {
     k_quant_nvfp4<0><<<grid_flat, 256, 0, stream>>>(xb, rows, cols, g_in, nullptr, nullptr, qb, sb, ka);
+    count_launches(1);
   } else {
     const int g3 = std::min(rows_pad, di->num_sms * 8);
     k_quant_nvfp4<2><<<g3, 256, 0, stream>>>(xb, rows, cols, nullptr, nullptr, g_out, qb, sb, ka);
+    count_launches(1);
   }
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
@@ -544,6 +626,7 @@ static int launch_w4_skinny(const void* X, const EpiParams& p, const W4Params& q
   attr[0].val.clusterDim.x = ks;
   g_last_plan = {kPlanW4Skinny, n_tiles * ks, ks, MP, C::STAGES, C::SMEM_BYTES};
   cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_w4a16_skinny<MP>, tx, p, q, kbc);
+  count_launches(1);
   return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
@@ -590,6 +673,7 @@ static int launch_w4a16(const void* X, const void* wq, const void* scales, const
     const int smem = w4s_smem_bytes(M, K);
     g_last_plan = {kPlanW4Small, grid, 1, M, 0, smem};
     k_gemm_w4a16_small<<<grid, w4s::kThreads, smem, stream>>>(static_cast<const __nv_bfloat16*>(X), p, q);
+    count_launches(1);
     return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
   }
   if (M <= 16) return launch_w4_skinny<16>(X, p, q, di->num_sms, stream);
@@ -614,6 +698,7 @@ static int launch_w4a16(const void* X, const void* wq, const void* scales, const
   const int grid = tiles < di->num_sms ? tiles : di->num_sms;
   g_last_plan = {kPlanW4Tile, grid, 1, 256, W4Cfg<256>::STAGES, W4Cfg<256>::SMEM_BYTES};
   k_gemm_w4a16<<<grid, w4::kThreads, W4Cfg<256>::SMEM_BYTES, stream>>>(tx, p, q);
+  count_launches(1);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
@@ -640,6 +725,12 @@ const char* qi_b200_error_string(int code) {
     case QI_B200_ETOOBIG: return "size exceeds the entry point's fixed maximum";
     default: return "unknown status";
   }
+}
+
+int qi_b200_launch_count(unsigned long long* out) {
+  if (out == nullptr) return QI_B200_EINVAL;
+  *out = launch_counter().load(std::memory_order_relaxed);
+  return QI_B200_OK;
 }
 
 int qi_b200_last_launch(int* out6) {
@@ -717,6 +808,7 @@ int qi_b200_resid_ln_quant(void* x_bf16, const void* y_bf16, long long ldy, cons
     case 4096: k_resid_ln_quant_warp<16><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
     default: k_resid_ln_quant<1><<<M, row_threads(D), 0, stream>>>(p);
   }
+  count_launches(1);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
@@ -757,6 +849,7 @@ int qi_b200_rms_rope(const void* in0, const void* in1, long long ld_in, void* ou
     case 4096: k_rms_rope_warp<16><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
     default: k_rms_rope<1><<<dim3(M, nparts), row_threads(A), 0, stream>>>(p);
   }
+  count_launches(1);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
@@ -782,6 +875,7 @@ int qi_b200_int8_epilogue(const void* acc_int32, const float* act_scale, const f
   k_int8_epilogue<<<grid, 256, 0, stream>>>(static_cast<const int32_t*>(acc_int32), act_scale, weight_scale,
                                              static_cast<const __nv_bfloat16*>(bias),
                                              static_cast<__nv_bfloat16*>(out_bf16), M, N, flags & kEpiGelu);
+  count_launches(1);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 

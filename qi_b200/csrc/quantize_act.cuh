@@ -14,6 +14,7 @@
 //   fp8 static (flashrt_fp8_ops.py:207-216): q = e4m3_rn(clamp(x/s_static, +-448)).
 #pragma once
 
+#include "launch_count.cuh"
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
@@ -206,6 +207,7 @@ inline cudaError_t launch_rowquant(const void* x, void* q, float* scales, const 
     k_rowquant_scalar<Op><<<(rows + 7) / 8, kQuantThreads, 0, stream>>>(xb, qb, scales, static_scale, rows,
                                                                         cols);
   }
+  count_launches(1);
   return cudaGetLastError();
 }
 

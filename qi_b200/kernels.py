@@ -163,14 +163,31 @@ def quantize_fp8_static(x: torch.Tensor, scale: torch.Tensor):
 # ---------------------------------------------------------------------------
 
 
+_SPLITK_PLANS: dict = {}
+
+
+def splitk_plan(kind: int, M: int, N: int, K: int) -> tuple:
+    """(splits, workspace bytes) that fill the SMs with 128 x 256 tiles; 1 = the tiles already do."""
+    key = (kind, M, N, K, torch.cuda.current_device())
+    plan = _SPLITK_PLANS.get(key)
+    if plan is None:
+        import ctypes
+        sp, wb = ctypes.c_int(0), ctypes.c_size_t(0)
+        _lib.call("qi_b200_gemm_splitk_plan", kind, M, N, K, ctypes.byref(sp), ctypes.byref(wb))
+        plan = _SPLITK_PLANS[key] = (sp.value, wb.value)
+    return plan
+
+
 def gemm(kind: int, a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor | None,
          b_scale: torch.Tensor | None, bias: torch.Tensor | None = None, *, gelu: bool = False,
-         raw_acc: bool = False, out: torch.Tensor | None = None, tile_n: int = 0) -> torch.Tensor:
+         raw_acc: bool = False, out: torch.Tensor | None = None, tile_n: int = 0,
+         splits: int = 1) -> torch.Tensor:
     """D = epi(A[M,K] . B[N,K]^T); see ``qi_b200_gemm`` in include/qi_b200.h.
 
     Scales of one element broadcast (per tensor); otherwise a_scale is [M]
     and b_scale is [N].  ``raw_acc`` returns the 32-bit accumulators (int32
-    for INT8, fp32 otherwise) instead of bf16.
+    for INT8, fp32 otherwise) instead of bf16.  ``splits > 1`` splits K over
+    that many CTAs per output tile (``qi_b200_gemm_splitk``).
     """
     dt = {_lib.KIND_INT8: (torch.int8,), _lib.KIND_FP8_E4M3: (torch.uint8, torch.float8_e4m3fn),
           _lib.KIND_BF16: (torch.bfloat16,)}[kind]
@@ -201,6 +218,15 @@ def gemm(kind: int, a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor | No
         odt = (torch.int32 if kind == _lib.KIND_INT8 else torch.float32) if raw_acc else torch.bfloat16
         out = torch.empty((M, N), dtype=odt, device=a.device)
     flags = (_lib.EPI_GELU if gelu else 0) | (_lib.EPI_RAW_ACC if raw_acc else 0)
+    if splits > 1:  # split K over several CTAs per tile, sum the partials in a second kernel
+        if raw_acc or tile_n != 0:
+            raise ValueError("splits > 1 takes bf16 outputs and the library's tile choice")
+        ws_bytes = splits * M * N * 4
+        ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=a.device)
+        _lib.call("qi_b200_gemm_splitk", kind, _ptr(a), _ptr(b), _ptr(sa), sa_stride, _ptr(sb), sb_stride,
+                  _ptr(bias), _ptr(out), out.stride(0), M, N, K, flags, splits, _ptr(ws), ws_bytes,
+                  _stream(a.device))
+        return out
     _lib.call("qi_b200_gemm", kind, _ptr(a), _ptr(b), _ptr(sa), sa_stride, _ptr(sb), sb_stride,
               _ptr(bias), _ptr(out), out.stride(0), M, N, K, flags, tile_n, _stream(a.device))
     return out

@@ -105,6 +105,33 @@ def test_pair_kernel_epilogue_matches_single_cta(tile_n, gelu):
     assert torch.equal(y1, y2)
 
 
+@pytest.mark.parametrize("gelu", [False, True])
+@pytest.mark.parametrize("M,N,Kd", [(512, 3072, 3072), (32, 9216, 1024), (1, 1024, 4096), (100, 520, 2048)])
+def test_splitk_matches_unsplit(M, N, Kd, gelu):
+    """Small problems split K over several CTAs (qi_b200_gemm_splitk): INT8
+    outputs are bit-identical to the unsplit kernel (int32 partial sums are
+    exact); FP8 agrees to fp32 summation order."""
+    x, w, b = make_small_case(M, N, Kd, seed=M + N, outlier_frac=0.002)
+    qw, sw, _ = O.quantize_weight_rtn(w.numpy(), 8, -1, True)
+    qa, sa = K.quantize_int8_rowwise(x.to(DEV))
+    qwd, swd, bd = torch.from_numpy(qw).to(DEV), torch.from_numpy(sw[:, 0]).to(DEV), b.to(DEV)
+    splits, _ = K.splitk_plan(_lib.KIND_INT8, M, N, Kd)
+    assert splits > 1, splits
+    y_split = K.gemm(_lib.KIND_INT8, qa, qwd, sa, swd, bd, gelu=gelu, splits=splits)
+    assert _lib.last_launch()["cluster"] == splits
+    y_ref = K.gemm(_lib.KIND_INT8, qa, qwd, sa, swd, bd, gelu=gelu, tile_n=128)
+    assert torch.equal(y_split, y_ref)
+    if not gelu:  # and the whole linear against the oracle
+        yo, _, _, _ = O.int8_linear(bits(x), qw, sw[:, 0], bits(b))
+        np.testing.assert_array_equal(bits(y_split), yo)
+    qf, sf = K.quantize_fp8_rowwise(x.to(DEV))
+    wf = (w * 20).to(torch.float8_e4m3fn).view(torch.uint8).to(DEV)
+    wsf = torch.full((N,), 0.05, device=DEV)
+    f_split = K.gemm(_lib.KIND_FP8_E4M3, qf, wf, sf, wsf, bd, gelu=gelu, splits=splits)
+    f_ref = K.gemm(_lib.KIND_FP8_E4M3, qf, wf, sf, wsf, bd, gelu=gelu, tile_n=128)
+    assert O.rel_fro(f_split.float().cpu().numpy(), f_ref.float().cpu().numpy()) <= 2e-3
+
+
 @pytest.mark.parametrize("M,N,Kd", SHAPES)
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_int8_linear_bf16_bit_exact(M, N, Kd, with_bias):
