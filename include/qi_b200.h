@@ -48,6 +48,11 @@ extern "C" {
 /* epilogue flags for qi_b200_gemm / qi_b200_fp8_linear */
 #define QI_B200_EPI_GELU 1    /* GELU(tanh) of the bf16-rounded linear output */
 #define QI_B200_EPI_RAW_ACC 2 /* store raw 32-bit accumulators instead of bf16 (debug) */
+/* NVFP4 GEMM tile choice in flags bits 8-9: 0 = the library's choice (CTA
+ * pairs with 256 x 256 tiles for M >= 1024 when they fill half the SMs, else
+ * single-CTA 128 x 128), 1 = single-CTA 128 x 128, 2 = CTA pair 256 x 128,
+ * 3 = CTA pair 256 x 256. */
+#define QI_B200_NVFP4_TILE_SHIFT 8
 
 int qi_b200_abi_version(void);
 const char* qi_b200_error_string(int code);
@@ -60,8 +65,8 @@ int qi_b200_device_status(unsigned int* out4, int clear);
 
 /* Launch plan of the calling thread's most recent GEMM launch, for
  * diagnostics: out6 = {kernel (1 int8, 2 fp8, 3 bf16, 4 nvfp4, 5 w4a16 tiles,
- * 6 w4a16 split-K clusters, 7 w4a16 small-M weight streaming, 8/9/10 int8 /
- * fp8 / bf16 CTA-pair tiles), grid, cluster size (K splits for kernels 1-3
+ * 6 w4a16 split-K clusters, 7 w4a16 small-M weight streaming, 8/9/10/11
+ * int8 / fp8 / bf16 / nvfp4 CTA-pair tiles), grid, cluster size (K splits for kernels 1-3
  * under qi_b200_gemm_splitk), tile N (or padded M for kernel 6, M for kernel
  * 7), pipeline stages, dynamic shared memory bytes}. */
 int qi_b200_last_launch(int* out6);
@@ -250,7 +255,9 @@ int qi_b200_w4a16_linear(const void* x_bf16, const void* qweight_packed, const v
 int qi_b200_quantize_nvfp4(const void* x_bf16, int rows, int cols, int g_mode, const float* g_in,
                            unsigned int* ws_amax, float* g_out, void* q_packed, void* sf_atoms, cudaStream_t stream);
 /* D = bf16( (acc * a_g[m or 0]) * b_g[0] + bias ), acc = sum over 16-blocks of
- * (q_a q_b) sf_a sf_b on tcgen05 kind::mxf4nvf4 (block16).  K % 256 == 0. */
+ * (q_a q_b) sf_a sf_b on tcgen05 kind::mxf4nvf4 (block16).  K % 256 == 0.
+ * flags: QI_B200_EPI_GELU, QI_B200_EPI_RAW_ACC, tile choice (see
+ * QI_B200_NVFP4_TILE_SHIFT). */
 int qi_b200_nvfp4_gemm(const void* A_packed, const void* A_sf, const void* B_packed, const void* B_sf,
                        const float* a_global_scale, int a_scale_per_row, const float* b_global_scale,
                        const void* bias, void* D, long long ldd, int M, int N, int K, int flags, cudaStream_t stream);

@@ -17,6 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libqi_b200.so"
 OK, EINVAL, ESHAPE, EALIGN, ECUDA, ETMAP, EARCH, ETOOBIG = range(8)
 KIND_INT8, KIND_FP8_E4M3, KIND_BF16 = 0, 1, 2
 EPI_GELU, EPI_RAW_ACC = 1, 2
+NVFP4_TILE_SHIFT = 8  # flags bits 8-9: 0 auto, 1 single-CTA 128x128, 2 pair 256x128, 3 pair 256x256
 
 
 class QiB200Unavailable(RuntimeError):
@@ -127,7 +128,8 @@ def last_launch() -> dict:
     buf = (ctypes.c_int * 6)()
     check("qi_b200_last_launch", load().qi_b200_last_launch(ctypes.cast(buf, _P)))
     names = {1: "gemm_int8", 2: "gemm_fp8", 3: "gemm_bf16", 4: "gemm_nvfp4", 5: "w4a16_tiles", 6: "w4a16_splitk",
-             7: "w4a16_small", 8: "gemm_int8_pair", 9: "gemm_fp8_pair", 10: "gemm_bf16_pair"}
+             7: "w4a16_small", 8: "gemm_int8_pair", 9: "gemm_fp8_pair", 10: "gemm_bf16_pair",
+             11: "gemm_nvfp4_pair"}
     v = list(buf)
     return {"kernel": names.get(v[0], "none"), "grid": v[1], "cluster": v[2], "tile_n": v[3], "stages": v[4],
             "smem": v[5]}

@@ -23,6 +23,18 @@
 //               `tempty` when its TMEM columns have been read
 // Loads have one destination CTA each (no TMA multicast), so the kernel is
 // safe in processes whose peers map this GPU's memory.
+//
+// NVFP4 (kind::mxf4nvf4, block16 UE4M3 scales): each CTA also loads (plain
+// TMA, its own barrier) the scale-factor atoms of its own 128 A rows and of
+// ALL BN columns of B, since the pair's MMA reads each CTA's scales from that
+// CTA's TMEM.  Four more warps (one per TMEM lane quadrant) move the atoms
+// from shared memory into a ring of TMEM scale slots with tcgen05.st, then
+// arrive on the even CTA's `sf_ready`.  Measured on B200: tcgen05.cp of the
+// 12 atoms of a K slice from the MMA thread costs 82 clocks per 128-clock MMA
+// (serialised with the MMAs, even from another warp), while tcgen05.st from
+// other warps runs concurrently with them.  Roles: warp 0 TMA, warp 1 MMA,
+// warps 4-7 scale slots, warps 8-15 epilogue (512 threads).  At BN = 256 the
+// accumulator is single-buffered (256 + 4 slots x 48 columns of 512).
 #pragma once
 
 #include "gemm_tc.cuh"
@@ -40,44 +52,62 @@ struct OutMaps {
 
 template <MmaKind KIND, int BN_, int STAGES_, bool GATHER_ = false>
 struct Gemm2Cfg {
+  static constexpr bool NVF4 = (KIND == MmaKind::NVF4);
   static constexpr int BM = 128;  // rows per CTA; a pair covers 256
   static constexpr int BN = BN_;  // output columns of a pair tile
   static constexpr int STAGES = STAGES_;
   static constexpr int ELEM = (KIND == MmaKind::BF16) ? 2 : 1;
-  static constexpr int BK = 128 / ELEM;
-  static constexpr int UMMA_K = (KIND == MmaKind::BF16) ? 16 : 32;
+  static constexpr int BK = 128 / ELEM;  // TMA elements per 128-byte K slice (NVF4: packed bytes, 256 values)
+  static constexpr int UMMA_K = (KIND == MmaKind::BF16) ? 16 : 32;  // TMA elements per MMA
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = (BN / 2) * 128;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SFA_BYTES = NVF4 ? 4 * 512 : 0;               // this CTA's 128 rows, 4 K atoms
+  static constexpr int SFB_BYTES = NVF4 ? 4 * 512 * (BN / 128) : 0;  // every column of the pair tile
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  static constexpr int ACC_BUFS = (NVF4 && BN == 256) ? 1 : 2;
   static constexpr int ACC_COLS = BN;
-  static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
+  static constexpr int SF_COLS = NVF4 ? 4 * 4 + 4 * (BN / 32) : 0;  // per K slice: A 4 x 4, B 4 x BN/32 columns
+  static constexpr int SF_SLOTS = NVF4 ? (BN == 256 ? 5 : 8) : 0;  // TMEM scale slots in flight
+  static constexpr int SF_COL0 = ACC_BUFS * BN;                     // first scale column
+  static constexpr int TMEM_COLS = (SF_COL0 + SF_SLOTS * SF_COLS <= 256) ? 256 : 512;
+  // warp roles: 0 TMA, 1 MMA, [4, 4 + 4) scale slots (NVFP4), then 8 epilogue warps
+  static constexpr int SF_WARP0 = 4;
+  static constexpr int EPI_WARP0 = NVF4 ? 8 : kFirstEpiWarp;
+  static constexpr int THREADS = (EPI_WARP0 + kEpiWarps) * 32;
   static constexpr int COLPARAM_BYTES = 2 * BN * (4 + 2);
-  static constexpr int BAR_BYTES = 256;
+  static constexpr int BAR_BYTES = 512;
   // fused gather: one 32-row x 64-column bf16 box (128-byte rows) per epilogue
   // warp (measured on 2 GPUs: 64-column boxes with 5 stages beat 32-column
   // boxes by 25 % and 128-column boxes with 4 stages by 10 %)
   static constexpr int STAGING_BYTES = GATHER_ ? kEpiWarps * 32 * 64 * 2 : 0;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + COLPARAM_BYTES + BAR_BYTES + STAGING_BYTES + 1024;
-  static constexpr uint32_t IDESC = (KIND == MmaKind::I8)   ? make_idesc(kDS32, kFmtS8, kFmtS8, 256, BN)
-                                    : (KIND == MmaKind::F8) ? make_idesc(kDF32, kFmtE4M3, kFmtE4M3, 256, BN)
-                                                            : make_idesc(kDF32, kFmtBF16, kFmtBF16, 256, BN);
-  static_assert(KIND != MmaKind::NVF4, "block-scaled pairs are not built");
+  static constexpr uint32_t IDESC = (KIND == MmaKind::I8)     ? make_idesc(kDS32, kFmtS8, kFmtS8, 256, BN)
+                                    : (KIND == MmaKind::F8)   ? make_idesc(kDF32, kFmtE4M3, kFmtE4M3, 256, BN)
+                                    : (KIND == MmaKind::NVF4) ? make_idesc_nvf4(256, BN)
+                                                              : make_idesc(kDF32, kFmtBF16, kFmtBF16, 256, BN);
+  static_assert(!NVF4 || BN == 128 || BN == 256, "NVFP4 pair tiles: whole 128-column scale atoms");
+  static_assert(!NVF4 || !GATHER_, "NVFP4 with the fused gather is not built");
   static_assert(BN % 64 == 0 && BN >= 128 && BN <= 256, "BN");
-  static_assert(2 * BN <= 512, "TMEM");
+  static_assert(SF_COL0 + SF_SLOTS * SF_COLS <= 512, "TMEM");
+  static_assert(SF_COLS % 16 == 0, "scale slots are written 16 columns at a time");
+  static_assert(BAR_BYTES >= 8 * (3 * STAGES + 2 * SF_SLOTS + 7) + 8, "barrier region");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
   static_assert(!GATHER_ || BN % 128 == 0, "gather boxes are 64 columns per epilogue warp");
 };
 
 template <MmaKind KIND, int BN, int STAGES, bool GATHER = false>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const EpiParams p,
+__global__ void __launch_bounds__(Gemm2Cfg<KIND, BN, STAGES, GATHER>::THREADS, 1)
+k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+           const __grid_constant__ CUtensorMap tmSFA, const __grid_constant__ CUtensorMap tmSFB, const EpiParams p,
            const __grid_constant__ OutMaps om) {
   using C = Gemm2Cfg<KIND, BN, STAGES, GATHER>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * C::A_BYTES;
-  uint8_t* staging = sB + STAGES * C::B_BYTES;  // 1024-byte aligned: 8 boxes of 32 x 64 bf16 (GATHER)
+  uint8_t* sSFA = sB + STAGES * C::B_BYTES;      // NVFP4 only
+  uint8_t* sSFB = sSFA + STAGES * C::SFA_BYTES;  // NVFP4 only
+  uint8_t* staging = sSFB + STAGES * C::SFB_BYTES;  // 1024-byte aligned: 8 boxes of 32 x 64 bf16 (GATHER)
   float* col_scale = reinterpret_cast<float*>(staging + C::STAGING_BYTES);
   __nv_bfloat16* col_bias = reinterpret_cast<__nv_bfloat16*>(col_scale + 2 * BN);
   uint64_t* full = reinterpret_cast<uint64_t*>(col_bias + 2 * BN);
@@ -86,8 +116,12 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint64_t* epi_sync = drain + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_sync + 2);
+  uint64_t* sf_full = epi_sync + 2;          // [STAGES] this CTA's scale atoms landed (NVFP4)
+  uint64_t* sf_ready = sf_full + STAGES;     // [SF_SLOTS] even CTA: both CTAs' slot written
+  uint64_t* sf_free = sf_ready + C::SF_SLOTS;  // [SF_SLOTS] the MMAs reading the slot are done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_free + C::SF_SLOTS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  constexpr int kFirstEpi = C::EPI_WARP0;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -105,6 +139,13 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
       mbar_init(&tempty[b], 2 * kEpiWarps);  // one arrive per epilogue warp of both CTAs
       mbar_init(&epi_sync[b], kEpiThreads);
     }
+    if constexpr (C::NVF4) {
+      for (int s = 0; s < STAGES; ++s) mbar_init(&sf_full[s], 1);
+      for (int s = 0; s < C::SF_SLOTS; ++s) {
+        mbar_init(&sf_ready[s], 2 * 4);  // one arrive per scale warp of both CTAs
+        mbar_init(&sf_free[s], 1);
+      }
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -112,6 +153,10 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
   if (warp == 0 && lane == 0) {
     tma_prefetch_map(&tmA);
     tma_prefetch_map(&tmB);
+    if constexpr (C::NVF4) {
+      tma_prefetch_map(&tmSFA);
+      tma_prefetch_map(&tmSFB);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
@@ -128,7 +173,8 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
   const int m_tiles = (p.M + 255) / 256;
   const int n_tiles = (p.N + BN - 1) / BN;
   const int num_tiles = m_tiles * n_tiles;
-  const int k_blocks = (p.K + C::BK - 1) / C::BK;
+  const int k_units = C::NVF4 ? p.K / 2 : p.K;  // K in TMA elements
+  const int k_blocks = (k_units + C::BK - 1) / C::BK;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -142,9 +188,20 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kTag, 1)) { ok = false; break; }
           const uint32_t lfull = map_shared_rank(smem_u32(&full[stage]), 0);
-          if (leader) mbar_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+          if (leader) mbar_expect_tx(&full[stage], 2 * (C::A_BYTES + C::B_BYTES));
           tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, lfull, kb * C::BK, mb * 256 + rank * C::BM);
           tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, lfull, kb * C::BK, nb * BN + rank * (BN / 2));
+          if constexpr (C::NVF4) {
+            // scale atoms (this CTA's barrier): rows are [128-row block][K atom of 64
+            // values]; 4 atoms per K slice
+            mbar_expect_tx(&sf_full[stage], C::SFA_BYTES + C::SFB_BYTES);
+            tma_load_2d(sSFA + stage * C::SFA_BYTES, &tmSFA, &sf_full[stage], 0,
+                        (2 * mb + static_cast<int>(rank)) * p.sf_ka + kb * 4);
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              tma_load_2d(sSFB + stage * C::SFB_BYTES + j * 2048, &tmSFB, &sf_full[stage], 0,
+                          (nb * (BN / 128) + j) * p.sf_ka + kb * 4);
+          }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -159,6 +216,15 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
           mbar_wait_drain(&full[s], ph);
         }
       }
+      if (!ok && C::NVF4) {
+        // this CTA's scale loads complete on its own barriers
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          if (--s < 0) { s = STAGES - 1; ph ^= 1u; }
+          mbar_wait_drain(&sf_full[s], ph);
+        }
+      }
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
@@ -166,10 +232,11 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
+      int g = 0;  // K slices issued so far (scale slot ring)
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++local) {
-        const int buf = local & 1;
-        const uint32_t tph = (local >> 1) & 1;
+        const int buf = local % C::ACC_BUFS;
+        const uint32_t tph = (local / C::ACC_BUFS) & 1;
         if (!mbar_wait(&tempty[buf], tph ^ 1u, abort_flag, kTag, 2)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * C::ACC_COLS);
@@ -178,10 +245,25 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
           const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
+          if constexpr (C::NVF4) {
+            // both CTAs' scale slot for this K slice is in TMEM
+            const int slot = g % C::SF_SLOTS;
+            if (!mbar_wait(&sf_ready[slot], (g / C::SF_SLOTS) & 1, abort_flag, kTag, 6)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t tsfa = tmem_base + static_cast<uint32_t>(C::SF_COL0 + slot * C::SF_COLS);
+            const uint32_t tsfb = tsfa + 16;
 #pragma unroll
-          for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk)
-            mma_pair<static_cast<int>(KIND)>(d_tmem, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32),
-                                             C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk)
+              mma_nvf4_pair(d_tmem, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32), C::IDESC,
+                            tsfa + 4 * kk, tsfb + (BN / 32) * kk, (kb | kk) != 0 ? 1u : 0u);
+            tc_commit_pair_mc(&sf_free[slot], 0x3);
+            ++g;
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk)
+              mma_pair<static_cast<int>(KIND)>(d_tmem, sw128_kmajor_desc(a0 + kk * 32),
+                                               sw128_kmajor_desc(b0 + kk * 32), C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+          }
           tc_commit_pair_mc(&empty[stage], 0x3);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -192,17 +274,61 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
         mbar_wait_drain(drain, 0);
       }
     }
-  } else if (warp >= kFirstEpiWarp) {
+  } else if (C::NVF4 && warp >= C::SF_WARP0 && warp < C::SF_WARP0 + 4) {
+    // ---------------- scale slots (NVFP4): shared-memory atoms -> TMEM ----------------
+    // Atom layout: row r (0..31) holds 16 bytes, the 4 K scales of rows r, r+32,
+    // r+64, r+96; each lane quadrant of TMEM gets the same 32 rows (the layout
+    // a 32x128b.warpx4 copy produces): lane l, column 4a + c of atom a = bytes
+    // [4c, 4c + 4) of row l % 32.  Slot columns: A atoms kk at 4kk, B atoms
+    // (kk, j) at 16 + (BN/32) kk + 4j.
+    if constexpr (C::NVF4) {
+    const uint32_t tq = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    int stage = 0;
+    uint32_t phase = 0;
+    int g = 0;
+    bool ok = true;
+    for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+      for (int kb = 0; kb < k_blocks; ++kb, ++g) {
+        const int slot = g % C::SF_SLOTS;
+        if (!mbar_wait(&sf_free[slot], ((g / C::SF_SLOTS) & 1) ^ 1u, abort_flag, kTag, 7)) { ok = false; break; }
+        if (!mbar_wait(&sf_full[stage], phase, abort_flag, kTag, 8)) { ok = false; break; }
+        const uint4* fa = reinterpret_cast<const uint4*>(sSFA + stage * C::SFA_BYTES) + lane;
+        const uint4* fb = reinterpret_cast<const uint4*>(sSFB + stage * C::SFB_BYTES) + lane;
+        uint32_t r[C::SF_COLS];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint4 v = fa[kk * 32];
+          r[4 * kk] = v.x; r[4 * kk + 1] = v.y; r[4 * kk + 2] = v.z; r[4 * kk + 3] = v.w;
+#pragma unroll
+          for (int j = 0; j < BN / 128; ++j) {
+            const uint4 u = fb[j * 128 + kk * 32];
+            const int c = 16 + (BN / 32) * kk + 4 * j;
+            r[c] = u.x; r[c + 1] = u.y; r[c + 2] = u.z; r[c + 3] = u.w;
+          }
+        }
+        const uint32_t taddr = tq + static_cast<uint32_t>(C::SF_COL0 + slot * C::SF_COLS);
+#pragma unroll
+        for (int c = 0; c < C::SF_COLS; c += 16)
+          tmem_st_32x32b_x16(taddr + c, *reinterpret_cast<const uint32_t(*)[16]>(&r[c]));
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster_relaxed(map_shared_rank(smem_u32(&sf_ready[slot]), 0));
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+    }
+    }
+  } else if (warp >= kFirstEpi) {
     // ---------------- epilogue (8 warps, this CTA's 128 rows) ----------------
-    const int et = threadIdx.x - kFirstEpiWarp * 32;
+    const int et = threadIdx.x - kFirstEpi * 32;
     const int wq = warp & 3;
-    const int half = (warp - kFirstEpiWarp) >> 2;
+    const int half = (warp - kFirstEpi) >> 2;
     constexpr int COLS = BN / 2;
     int local = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
       const int mb = tile % m_tiles, nb = tile / m_tiles;
-      const int buf = local & 1;
-      const uint32_t tph = (local >> 1) & 1;
+      const int buf = local % C::ACC_BUFS;
+      const uint32_t tph = (local / C::ACC_BUFS) & 1;
       float* sb_t = col_scale + buf * BN;
       __nv_bfloat16* bias_t = col_bias + buf * BN;
       for (int j = et; j < BN; j += kEpiThreads) {
@@ -241,7 +367,7 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
           // fused all-gather: stage this warp's 32 x 64 box (one 128-byte row
           // per lane), then one TMA store per destination (clipped to [M, N]
           // by the tensor maps)
-          uint8_t* box = staging + (warp - kFirstEpiWarp) * (32 * 64 * 2);
+          uint8_t* box = staging + (warp - kFirstEpi) * (32 * 64 * 2);
           const int row_base = mb * 256 + static_cast<int>(rank) * C::BM + wq * 32;
           uint32_t pk[32];
           epilogue_chunk<KIND>(r0, p, m, n0, sa, sb_t + j0, bias_t + j0, pk);
@@ -266,7 +392,7 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
     }
   }
 
-  if (GATHER && warp >= kFirstEpiWarp && lane == 0) {
+  if (GATHER && warp >= kFirstEpi && lane == 0) {
     // the fused gather's stores have reached every destination before the
     // kernel retires (the cross-GPU barrier that follows publishes them)
     bulk_wait_all();

@@ -149,12 +149,23 @@ static int launch_gemm2_cfg(const void* A, const void* B, const EpiParams& p, in
   const OutMaps& om = om_in != nullptr ? *om_in : kNoMaps;
   const CUtensorMapDataType dt =
       (KIND == MmaKind::BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  const uint64_t ku = (uint64_t)p.K;
-  CUtensorMap ta, tb;
+  const uint64_t ku = C::NVF4 ? (uint64_t)p.K / 2 : (uint64_t)p.K;  // K in TMA elements (fp4: packed bytes)
+  CUtensorMap ta, tb, tsa = {}, tsb = {};
   int rc = make_tmap_2d(&ta, A, dt, ku, (uint64_t)p.M, ku * C::ELEM, C::BK, C::BM);
   if (rc) return rc;
   rc = make_tmap_2d(&tb, B, dt, ku, (uint64_t)p.N, ku * C::ELEM, C::BK, BN / 2);
   if (rc) return rc;
+  if constexpr (C::NVF4) {
+    // scale atoms as rows of 512 bytes (128 x u32): [128-row block][K atom]; 4 atoms per box
+    const uint64_t rows_a = (uint64_t)((p.M + 127) / 128) * p.sf_ka;
+    const uint64_t rows_b = (uint64_t)((p.N + 127) / 128) * p.sf_ka;
+    rc = make_tmap_2d(&tsa, p.sfa, CU_TENSOR_MAP_DATA_TYPE_UINT32, 128, rows_a, 512, 128, 4,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = make_tmap_2d(&tsb, p.sfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, 128, rows_b, 512, 128, 4,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
   static bool attr_done[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -173,13 +184,13 @@ static int launch_gemm2_cfg(const void* A, const void* B, const EpiParams& p, in
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.blockDim = dim3(C::THREADS, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   g_last_plan = {kPlanGemmPair + static_cast<int>(KIND), 2 * pairs, 2, BN, STAGES, C::SMEM_BYTES};
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_tc2<KIND, BN, STAGES, GATHER>, ta, tb, p, om);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_tc2<KIND, BN, STAGES, GATHER>, ta, tb, tsa, tsb, p, om);
   count_launches(1);
   return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
@@ -207,6 +218,14 @@ static int launch_gemm(const void* A, const void* B, const EpiParams& p, cudaStr
   int rc = device_info(&di);
   if (rc) return rc;
   if constexpr (KIND == MmaKind::NVF4) {
+    // 128 x 128 single-CTA tiles, or CTA pairs: 256 x 128 (double-buffered
+    // accumulator) or 256 x 256 (single-buffered: the scale factors take TMEM
+    // columns too)
+    if (force_bn == -256) return launch_gemm2_cfg<KIND, 256, 5>(A, B, p, di->num_sms, stream);
+    if (force_bn == -128) return launch_gemm2_cfg<KIND, 128, 7>(A, B, p, di->num_sms, stream);
+    if (force_bn == 0 && p.M >= 1024 &&
+        (long long)((p.M + 255) / 256) * ((p.N + 255) / 256) >= di->num_sms / 2)
+      return launch_gemm2_cfg<KIND, 256, 5>(A, B, p, di->num_sms, stream);
     return launch_gemm_cfg<KIND, 128, 6>(A, B, p, di->num_sms, stream);
   } else {
     if (force_bn < 0) {  // the CTA-pair kernel with tile width -force_bn
@@ -544,6 +563,8 @@ static int nvfp4_gemm(const void* A, const void* SFA, const void* B, const void*
   if (M <= 0 || N <= 0 || K <= 0) return QI_B200_ESHAPE;
   if (K % 256 != 0 || N % 8 != 0 || ldd < N || ldd % 8 != 0) return QI_B200_ESHAPE;
   if (!aligned16(A) || !aligned16(B) || !aligned16(D) || !aligned16(SFA) || !aligned16(SFB)) return QI_B200_EALIGN;
+  const int tile = (flags >> QI_B200_NVFP4_TILE_SHIFT) & 3;
+  flags &= ~(3 << QI_B200_NVFP4_TILE_SHIFT);
   if (flags & ~(kEpiGelu | kEpiRawAcc)) return QI_B200_EINVAL;
   EpiParams p = {};
   p.sa = a_g;
@@ -560,7 +581,8 @@ static int nvfp4_gemm(const void* A, const void* SFA, const void* B, const void*
   p.sfa = static_cast<const uint8_t*>(SFA);
   p.sfb = static_cast<const uint8_t*>(SFB);
   p.sf_ka = K / 64;
-  return launch_gemm<MmaKind::NVF4>(A, B, p, stream, 128);
+  static const int kTileForce[4] = {0, 128, -128, -256};
+  return launch_gemm<MmaKind::NVF4>(A, B, p, stream, kTileForce[tile]);
 }
 
 // ---------------------------------------------------------------------------

@@ -85,6 +85,32 @@ def test_nvfp4_gemm_accumulators(M, N, Kd):
     assert err < 1e-5, err
 
 
+@pytest.mark.parametrize("M,N,Kd", [(256, 256, 256), (300, 384, 1024), (1100, 640, 512), (1024, 1024, 2048)])
+@pytest.mark.parametrize("tile", [2, 3])
+def test_nvfp4_pair_tiles(M, N, Kd, tile):
+    """CTA-pair NVFP4 tiles (256 x 128 and 256 x 256, scale atoms copied into
+    both CTAs' TMEM): accumulators within 1e-5 of the exact block-scaled sum
+    and bf16 outputs identical to the single-CTA 128 x 128 kernel.  The
+    shapes leave whole CTAs of a pair, and whole scale atoms, past M and N."""
+    x, w, b = make_small_case(M, N, Kd, seed=3 * M + N)
+    wq, wsf, wg, wq_np, wsf_np, wg_f = weights(w)
+    qa, sfa, ga = K.quantize_nvfp4(x.to(DEV), K.NVFP4_DYNAMIC_TENSOR)
+    one = torch.ones(1, dtype=torch.float32, device=DEV)
+    acc = K.nvfp4_gemm(qa, sfa, wq, wsf, one, one, raw_acc=True, tile=tile)
+    assert _lib.last_launch()["kernel"] == "gemm_nvfp4_pair" and _lib.last_launch()["tile_n"] == 128 * (tile - 1)
+    a_nib = O.unpack_fp4(qa.cpu().numpy())
+    a_sf = O.sf_from_atom_layout(sfa.cpu().numpy(), M, Kd // 16)
+    ref = O.nvfp4_dequant(a_nib, a_sf, 1.0) @ O.nvfp4_dequant(O.unpack_fp4(wq_np), wsf_np, 1.0).T
+    got = acc.cpu().numpy().astype(np.float64)
+    err = np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30)
+    assert err < 1e-5, err
+    bd = b.to(DEV)
+    y_pair = K.nvfp4_gemm(qa, sfa, wq, wsf, ga, wg, bd, tile=tile)
+    y_one = K.nvfp4_gemm(qa, sfa, wq, wsf, ga, wg, bd, tile=1)
+    assert _lib.last_launch()["kernel"] == "gemm_nvfp4"
+    assert torch.equal(y_pair, y_one)
+
+
 @pytest.mark.parametrize("M,N,Kd", [(1, 128, 256), (33, 256, 512), (300, 128, 768)])
 @pytest.mark.parametrize("per_row", [False, True])
 def test_nvfp4_linear_vs_oracle(M, N, Kd, per_row):
