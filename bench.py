@@ -235,39 +235,38 @@ def run_ours(args):
         peer_api = PeerGatherLinear(layer, max_tokens=M, shard=False)
         launches_per_step = 4  # quantizer, barrier, GEMM with the fused gather, barrier
 
-    def step_peer(i, ev=None):
-        cur = torch.cuda.current_stream(device)
-        if ev is not None:
-            ev[0].record(cur)
-        peer_api(xs[i % ncopy])
-        if ev is not None:
-            ev[1].record(cur)
-
-    def step(i, ev=None):
+    def step(i):
         if peer:
-            return step_peer(i, ev)
+            return peer_api(xs[i % ncopy])
         x, w = xs[i % ncopy], wqs[i % ncopy]
-        cur = torch.cuda.current_stream(device)  # the capture stream inside torch.cuda.graph
         if c["kind"] == "w4a16":
-            if ev is not None:
-                ev[0].record(cur)
             y = K.w4a16_linear(x, w, layer.scale_factors, layer.zeros, c["group"], bias)
         elif c["kind"] == "nvfp4":
             qa, sfa, ga = K.quantize_nvfp4(x, K.NVFP4_DYNAMIC_TENSOR)
-            if ev is not None:
-                ev[0].record(cur)
             y = K.nvfp4_gemm(qa, sfa, w, layer.scale_factors, ga, ws, bias)
         else:
             q, s = quant(x)
-            if ev is not None:
-                ev[0].record(cur)
             y = K.gemm(kind, q, w, s, ws, bias, gelu=c["gelu"])
-        if ev is not None:
-            ev[1].record(cur)
         if world > 1:
             import torch.distributed as dist
             dist.all_gather_into_tensor(gathered, y)
         return y
+
+    # the dominant kernel alone (activations quantized beforehand): its
+    # duration is timed over a graph of back-to-back launches below
+    pre = None
+    if not peer and c["kind"] in ("nvfp4", "int8", "fp8"):
+        pre = [K.quantize_nvfp4(x, K.NVFP4_DYNAMIC_TENSOR) if c["kind"] == "nvfp4" else quant(x) for x in xs]
+
+    def gemm_only(i):
+        if peer or pre is None:
+            return step(i) if peer else K.w4a16_linear(xs[i % ncopy], wqs[i % ncopy], layer.scale_factors,
+                                                       layer.zeros, c["group"], bias)
+        if c["kind"] == "nvfp4":
+            qa, sfa, ga = pre[i % ncopy]
+            return K.nvfp4_gemm(qa, sfa, wqs[i % ncopy], layer.scale_factors, ga, ws, bias)
+        q, s = pre[i % ncopy]
+        return K.gemm(kind, q, wqs[i % ncopy], s, ws, bias, gelu=c["gelu"])
 
     def barrier():
         if world > 1:
@@ -277,15 +276,14 @@ def run_ours(args):
 
     # Single GPU: the K timed steps are captured once in a CUDA graph (the
     # reference deploys its DiT under CUDA graphs too) so host launch latency
-    # does not leak into the device time of small configs; per-step events
-    # around the GEMM are event-record nodes inside the graph.  Multi-GPU:
-    # eager steps (the all-gather dominates; NCCL stays outside capture).
+    # does not leak into the device time of small configs.  Multi-GPU: eager
+    # steps (the all-gather dominates; NCCL stays outside capture), except the
+    # fused peer gather, which is graph-safe.
     use_graph = (world == 1 or peer) and not args.eager
     for i in range(args.warmup):
         step(i)
+        gemm_only(i)
     barrier()
-    evs = [(torch.cuda.Event(enable_timing=True, external=use_graph),
-            torch.cuda.Event(enable_timing=True, external=use_graph)) for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     graph = None
     launches0 = _lib.launch_count()  # this library's kernels in the K timed steps (graph: counted at capture)
@@ -293,7 +291,7 @@ def run_ours(args):
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             for i in range(args.steps):
-                step(i, evs[i])
+                step(i)
         graph.replay()  # untimed: uploads the graph
         barrier()
     with ClockSampler(local) as clk:
@@ -303,7 +301,7 @@ def run_ours(args):
             graph.replay()
         else:
             for i in range(args.steps):
-                step(i, evs[i])
+                step(i)
         t1.record(stream)
         barrier()
     gpu_launches = _lib.launch_count() - launches0
@@ -311,12 +309,23 @@ def run_ours(args):
         print(f"warning: {gpu_launches} library launches, expected {launches_per_step} x {args.steps}",
               file=sys.stderr)
     ms_total = max_over_ranks(t0.elapsed_time(t1), world, device)
-    try:
-        gemm_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
-        gemm_src = "cuda events around each GEMM launch in the timed region"
-    except Exception:
-        # event-record nodes not timeable: time K back-to-back GEMM launches instead
-        gemm_ms, gemm_src = time_gemm_alone(step, args.steps, stream), "cuda events, GEMM-only graph"
+    # dominant kernel: CUDA events around a graph of K back-to-back launches
+    # on the same rotating inputs (no event nodes between launches, which
+    # would add a launch gap to every small kernel); eager launches for the
+    # multi-rank NCCL path
+    barrier()
+    if use_graph:
+        gemm_ms = time_gemm_alone(gemm_only, args.steps, stream)
+        gemm_src = f"cuda events around a graph of {args.steps} back-to-back launches (same rotating inputs)"
+    else:
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for i in range(args.steps):
+            gemm_only(i)
+        g1.record(stream)
+        torch.cuda.synchronize(device)
+        gemm_ms = g0.elapsed_time(g1) / args.steps
+        gemm_src = f"cuda events around {args.steps} back-to-back eager launches"
     gemm_ms = max_over_ranks(gemm_ms, world, device)
     st = _lib.device_status()
     if st[0] != 0:

@@ -530,15 +530,32 @@ k_gemm_w4a16_skinny(const __grid_constant__ CUtensorMap tmX, const EpiParams p, 
 namespace w4s {
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kRows = 16;          // weight rows (output columns) per CTA
-constexpr int kChunk = 128;        // K elements per chunk (16 words per row)
-constexpr int kDepth = 4;          // chunks in flight per lane
-constexpr int kMaxM = 8;
+constexpr int kRowPad = 16;  // bytes after each staged weight row (spreads the rows over banks)
+constexpr int kMaxM = 16;    // one m16 MMA row block
 }  // namespace w4s
 
-// Shared memory of k_gemm_w4a16_small: the M token rows plus one zero row
-// (rows >= M of the 16-row A fragment read it), each padded by 16 bytes.
-inline int w4s_smem_bytes(int M, int K) { return (M + 1) * (K + 8) * 2; }
+// Shared-memory layout of k_gemm_w4a16_small<NT, KS> (byte offsets, all
+// 16-aligned): mbarrier | RB = 8 NT weight rows of this CTA's K range (KC/2
+// bytes + pad) | RB x G fp16 scales | RB x zw zero words | M token rows of the
+// K range (KC + 8 bf16, K-permuted) | token sums [M][KC / group] fp32 |
+// warp partials | CTA partials (read by the cluster's rank 0).
+struct W4sLayout {
+  int w_off, w_stride, s_off, z_off, x_off, xsum_off, red_off, part_off, total;
+};
+__host__ __device__ inline W4sLayout w4s_layout(int NT, int KS, int M, int K, int G, int zw, int group) {
+  const int RB = 8 * NT, KC = K / KS;
+  W4sLayout L;
+  L.w_off = 16;
+  L.w_stride = KC / 2 + w4s::kRowPad;
+  L.s_off = L.w_off + RB * L.w_stride;
+  L.z_off = L.s_off + ((RB * G * 2 + 15) & ~15);
+  L.x_off = L.z_off + ((RB * zw * 4 + 15) & ~15);
+  L.xsum_off = L.x_off + M * (KC + 8) * 2;
+  L.red_off = L.xsum_off + ((M * (KC / group) * 4 + 15) & ~15);
+  L.part_off = L.red_off + w4s::kWarps * 32 * 4 * 4;
+  L.total = L.part_off + NT * 32 * 4 * 4;
+  return L;
+}
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -554,127 +571,158 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t (&a)[4], uint32_t addr) {
                : "r"(addr));
 }
 
-// two nibbles (elements 2t, 2t+1 of word w) -> packed bf16x2 of (q - z) * s
-__device__ __forceinline__ uint32_t dequant_pair(uint32_t w, int t, float s16x, float c) {
-  const uint32_t n0 = (w >> (8 * t)) & 0xFu, n1 = (w >> (8 * t + 4)) & 0xFu;
-  const float f0 = fmaf(__uint_as_float(0x3F800000u | (n0 << 19)), s16x, c);
-  const float f1 = fmaf(__uint_as_float(0x3F800000u | (n1 << 19)), s16x, c);
-  return pack_bf16x2(f0, f1);
+// Elements t and t + 4 of a packed word as bf16x2 (128 + q_t, 128 + q_{t+4}):
+// the nibble lands in the low mantissa bits of bf16 128.0 (exact).
+__device__ __forceinline__ uint32_t nibbles_bf16x2(uint32_t w, int t4) {
+  return ((w >> t4) & 0x000F000Fu) | 0x43004300u;
 }
 
+// W4A16 for M <= 16 tokens.  A CTA covers RB = 8 NT weight rows and 1/KS of K
+// (KS CTAs of a cluster split K).  Thread 0 brings the CTA's weight row
+// slices, scales and zeros into shared memory with bulk copies; the token
+// slice is staged meanwhile with K permuted inside every 8-element chunk, so
+// that lane t's MMA B fragment is one shift and one LOP of a packed word
+// (elements t, t+4 -> logical k 2t, 2t+1).  The MMAs multiply the tokens by
+// 128 + q exactly; per quantization group the fp32 partial D is turned into
+// s (D - (128 + z) sum_k x_k), the group's exact contribution
+// sum_k x_k (q_k - z) s.  With one-hot token rows this is bf16((q - z) s),
+// the reference's dequantized weight, bit for bit; in general it skips the
+// reference's bf16 rounding of each weight (relative difference ~1e-3).
+// Warps: n-tile warp % NT, K part warp / NT.  Partials are added in K order:
+// warps in the CTA, then the cluster's CTAs by rank (distributed shared memory).
+template <int NT, int KS>
 __global__ void __launch_bounds__(w4s::kThreads)
 k_gemm_w4a16_small(const __nv_bfloat16* __restrict__ X, EpiParams p, W4Params q) {
-  __shared__ float red[w4s::kWarps][32][8];
-  extern __shared__ __align__(16) uint8_t xs_raw[];
+  constexpr int RB = 8 * NT, KP = w4s::kWarps / NT;
+  extern __shared__ __align__(128) uint8_t sm[];
+  const W4sLayout L = w4s_layout(NT, KS, p.M, p.K, q.G, q.zw, q.group);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ldx = p.K + 8;  // padded row stride of the staged tokens (elements)
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(xs_raw);
-  const int g = lane >> 2, t = lane & 3;
-  const int n0 = blockIdx.x * w4s::kRows;
-  const int kr = p.K / w4s::kWarps;                 // K range of this warp
-  const int k_begin = warp * kr;
-  const int nchunks = kr / w4s::kChunk;
-  const long long row0 = n0 + g, row1 = n0 + 8 + g;
-  const bool ok0 = row0 < p.N, ok1 = row1 < p.N;
-  const uint4* w0p = reinterpret_cast<const uint4*>(q.wq + row0 * q.kw + k_begin / 8) + t;
-  const uint4* w1p = reinterpret_cast<const uint4*>(q.wq + row1 * q.kw + k_begin / 8) + t;
-
-  uint4 buf0[w4s::kDepth], buf1[w4s::kDepth];
-#pragma unroll
-  for (int i = 0; i < w4s::kDepth; ++i) {
-    if (i < nchunks) {
-      buf0[i] = ok0 ? __ldg(w0p + i * 4) : make_uint4(0, 0, 0, 0);
-      buf1[i] = ok1 ? __ldg(w1p + i * 4) : make_uint4(0, 0, 0, 0);
-    }
+  const int cr = KS > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int n0 = (blockIdx.x / KS) * RB;
+  const int rows = min(RB, p.N - n0);
+  const int KC = p.K / KS, kc0 = cr * KC;
+  const int GC = KC / q.group;
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    mbar_expect_tx(bar, static_cast<uint32_t>(rows * (KC / 2 + q.G * 2 + q.zw * 4)));
+#pragma unroll 1
+    for (int r = 0; r < rows; ++r)
+      bulk_load(sm + L.w_off + r * L.w_stride, q.wq + static_cast<long long>(n0 + r) * q.kw + kc0 / 8, KC / 2, bar);
+    bulk_load(sm + L.s_off, q.scales + static_cast<long long>(n0) * q.G, rows * q.G * 2, bar);
+    bulk_load(sm + L.z_off, q.zeros + static_cast<long long>(n0) * q.zw, rows * q.zw * 4, bar);
   }
-  // stage the M token rows (and a zero row) in shared memory, 16-byte moves,
-  // while this thread's first weight chunks are in flight
+  // token slice -> shared memory, each 8-element chunk reordered (0,4,1,5,2,6,3,7),
+  // and the token sums per quantization group: the group's group/8 chunks sit
+  // in consecutive lanes, each lane adds its 8 elements, then a butterfly over
+  // those lanes (fixed order) gives the group sum
+  const int ldx = KC + 8;
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(sm + L.x_off);
+  float* xsum = reinterpret_cast<float*>(sm + L.xsum_off);
   {
-    const int vpr = p.K / 8;  // uint4 per row
-    for (int i = threadIdx.x; i < (p.M + 1) * vpr; i += w4s::kThreads) {
-      const int r = i / vpr, c = i - r * vpr;
-      const uint4 v = r < p.M ? __ldg(reinterpret_cast<const uint4*>(X + static_cast<long long>(r) * p.K) + c)
-                              : make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(xs + r * ldx + c * 8) = v;
-    }
-  }
-  __syncthreads();
-  // ldmatrix row address of this lane: matrices (rows 0-7 | 8-15) x (k 0-7 | 8-15)
-  const int a_row = (lane & 7) + ((lane >> 3) & 1) * 8;
-  const uint32_t a_base = smem_u32(xs + (a_row < p.M ? a_row : p.M) * ldx + (lane >> 4) * 8);
-
-  float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-  int cur_group = -1;
-  float s16x0 = 0.f, c0 = 0.f, s16x1 = 0.f, c1 = 0.f;
-  for (int cb = 0; cb < nchunks; cb += w4s::kDepth) {
+    const int vpr = KC / 8, cpg = q.group / 8;  // chunks per row, per group (a power of two <= 32)
+    const int total = p.M * vpr;
+    for (int base = warp * 32; base < total; base += w4s::kThreads) {
+      const int i = base + lane;
+      const bool on = i < total;  // the group's lanes are all on or all off
+      const int r = on ? i / vpr : 0, c = on ? i - r * vpr : 0;
+      float v = 0.f;
+      if (on) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(X + static_cast<long long>(r) * p.K + kc0) + c);
+        *reinterpret_cast<uint4*>(xs + r * ldx + c * 8) =
+            make_uint4(__byte_perm(u.x, u.z, 0x5410), __byte_perm(u.x, u.z, 0x7632),
+                       __byte_perm(u.y, u.w, 0x5410), __byte_perm(u.y, u.w, 0x7632));
+        const uint32_t e[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-  for (int slot = 0; slot < w4s::kDepth; ++slot) {  // register slots stay compile-time
-    const int ci = cb + slot;
-    if (ci >= nchunks) break;
-    const uint4 u0 = buf0[slot], u1 = buf1[slot];
-    if (ci + w4s::kDepth < nchunks) {
-      buf0[slot] = ok0 ? __ldg(w0p + (ci + w4s::kDepth) * 4) : make_uint4(0, 0, 0, 0);
-      buf1[slot] = ok1 ? __ldg(w1p + (ci + w4s::kDepth) * 4) : make_uint4(0, 0, 0, 0);
-    }
-    const int kc = k_begin + ci * w4s::kChunk;
-#pragma unroll
-    for (int st = 0; st < w4s::kChunk / 16; ++st) {
-      const int k0 = kc + st * 16;
-      const int grp = q.group_shift >= 0 ? (k0 >> q.group_shift) : (k0 / q.group);
-      if (grp != cur_group) {
-        cur_group = grp;
-        float sa = 0.f, sb = 0.f;
-        uint32_t za = 0, zb = 0;
-        if (ok0) {
-          sa = __half2float(q.scales[row0 * q.G + grp]);
-          za = (static_cast<uint32_t>(__ldg(q.zeros + row0 * q.zw + (grp >> 3))) >> (4 * (grp & 7))) & 0xFu;
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&e[j]));
+          v += f.x;
+          v += f.y;
         }
-        if (ok1) {
-          sb = __half2float(q.scales[row1 * q.G + grp]);
-          zb = (static_cast<uint32_t>(__ldg(q.zeros + row1 * q.zw + (grp >> 3))) >> (4 * (grp & 7))) & 0xFu;
-        }
-        s16x0 = sa * 16.0f;
-        c0 = -(16.0f + static_cast<float>(za)) * sa;
-        s16x1 = sb * 16.0f;
-        c1 = -(16.0f + static_cast<float>(zb)) * sb;
       }
-      // words 2st, 2st+1 of this chunk live in lane 4g + st/2, at index (2st)%4
-      const int src = (lane & ~3) | (st >> 1);
-      const uint32_t wa0 = __shfl_sync(0xffffffffu, (st & 1) ? u0.z : u0.x, src);
-      const uint32_t wa1 = __shfl_sync(0xffffffffu, (st & 1) ? u0.w : u0.y, src);
-      const uint32_t wb0 = __shfl_sync(0xffffffffu, (st & 1) ? u1.z : u1.x, src);
-      const uint32_t wb1 = __shfl_sync(0xffffffffu, (st & 1) ? u1.w : u1.y, src);
-      uint32_t a[4];
-      ldmatrix_x4(a, a_base + static_cast<uint32_t>(k0) * 2u);
-      mma_bf16_16816(d0, a, dequant_pair(wa0, t, s16x0, c0), dequant_pair(wa1, t, s16x0, c0));
-      mma_bf16_16816(d1, a, dequant_pair(wb0, t, s16x1, c1), dequant_pair(wb1, t, s16x1, c1));
+      for (int off = cpg >> 1; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (on && (c & (cpg - 1)) == 0) xsum[r * GC + c / cpg] = v;
     }
   }
-  }
-  // K-split reduction in warp order, then the epilogue (bias, bf16)
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    red[warp][lane][i] = d0[i];
-    red[warp][lane][4 + i] = d1[i];
-  }
   __syncthreads();
-  if (warp != 0) return;
-  float acc[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    float v = red[0][lane][i];
-    for (int w = 1; w < w4s::kWarps; ++w) v += red[w][lane][i];
-    acc[i] = v;
+  bool ok = mbar_wait_drain(bar, 0);  // bounded; a bulk copy of valid memory completes
+  if (!ok && threadIdx.x == 0) record_error(kDevWaitTimeout, 0x300u, 1);
+
+  const int g = lane >> 2, t = lane & 3;
+  const int nt = warp % NT, kp = warp / NT;
+  const int KW = KC / KP;  // this warp's K range (whole groups)
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (ok) {
+    const uint8_t* wrow = sm + L.w_off + (nt * 8 + g) * L.w_stride + kp * KW / 2;
+    // scale / zero of the two weight rows of this lane's D columns
+    const int r0 = nt * 8 + 2 * t;
+    const __half* s0p = reinterpret_cast<const __half*>(sm + L.s_off) + r0 * q.G;
+    const uint32_t* z0p = reinterpret_cast<const uint32_t*>(sm + L.z_off) + r0 * q.zw;
+    const int a_row = (lane & 7) + ((lane >> 3) & 1) * 8;
+    const uint32_t a_base =
+        smem_u32(xs + (a_row < p.M ? a_row : 0) * ldx + kp * KW + (lane >> 4) * 8);
+    const int m0 = g < p.M ? g : 0, m1 = g + 8 < p.M ? g + 8 : 0;
+    const int t4 = 4 * t;
+#pragma unroll 1
+    for (int gl = 0; gl < KW / q.group; ++gl) {
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      const int kg = gl * q.group;
+#pragma unroll 4
+      for (int k = kg; k < kg + q.group; k += 32) {
+        const uint4 w = *reinterpret_cast<const uint4*>(wrow + k / 2);  // elements k .. k + 31 of row g
+        uint32_t a[4];
+        ldmatrix_x4(a, a_base + static_cast<uint32_t>(k) * 2u);
+        mma_bf16_16816(d, a, nibbles_bf16x2(w.x, t4), nibbles_bf16x2(w.y, t4));
+        ldmatrix_x4(a, a_base + static_cast<uint32_t>(k + 16) * 2u);
+        mma_bf16_16816(d, a, nibbles_bf16x2(w.z, t4), nibbles_bf16x2(w.w, t4));
+      }
+      // the group's contribution: s (D - (128 + z) sum x), columns r0, r0 + 1
+      const int grp = (kc0 + kp * KW) / q.group + gl;
+      const int glc = kp * KW / q.group + gl;  // group index within this CTA's token sums
+      const float sa = __half2float(s0p[grp]), sb = __half2float(s0p[q.G + grp]);
+      const float za = 128.0f + static_cast<float>((z0p[grp >> 3] >> (4 * (grp & 7))) & 0xFu);
+      const float zb = 128.0f + static_cast<float>((z0p[q.zw + (grp >> 3)] >> (4 * (grp & 7))) & 0xFu);
+      const float x0 = xsum[m0 * GC + glc], x1 = xsum[m1 * GC + glc];
+      acc[0] = fmaf(sa, fmaf(-za, x0, d[0]), acc[0]);
+      acc[1] = fmaf(sb, fmaf(-zb, x0, d[1]), acc[1]);
+      acc[2] = fmaf(sa, fmaf(-za, x1, d[2]), acc[2]);
+      acc[3] = fmaf(sb, fmaf(-zb, x1, d[3]), acc[3]);
+    }
   }
-  // D fragment: acc[0..1] token g, cols 2t,2t+1 of tile 0; acc[2..3] token g+8; acc[4..7] tile 1
+  // warps of one n-tile add their K parts in order
+  float* red = reinterpret_cast<float*>(sm + L.red_off);
+  float* part = reinterpret_cast<float*>(sm + L.part_off);
 #pragma unroll
-  for (int tile = 0; tile < 2; ++tile) {
+  for (int i = 0; i < 4; ++i) red[(warp * 32 + lane) * 4 + i] = acc[i];
+  __syncthreads();
+  if (warp < NT) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float v = red[(warp * 32 + lane) * 4 + i];
+      for (int k = 1; k < KP; ++k) v += red[((k * NT + warp) * 32 + lane) * 4 + i];
+      part[(warp * 32 + lane) * 4 + i] = v;
+    }
+  }
+  if constexpr (KS > 1) cluster_sync_all();  // every CTA's partials are in its shared memory
+  if (cr == 0 && warp < NT) {
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = part[(warp * 32 + lane) * 4 + i];
+    if constexpr (KS > 1) {
+      for (int r = 1; r < KS; ++r) {
+        const uint32_t base = map_shared_rank(smem_u32(part + (warp * 32 + lane) * 4), static_cast<uint32_t>(r));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] += ld_shared_cluster_f32(base + 4 * i);
+      }
+    }
+    // D fragment: v[0..1] token g, weight rows n0 + 8 warp + 2t, +1; v[2..3] token g + 8
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int m = g + 8 * h;
-      const int n = n0 + 8 * tile + 2 * t;
+      const int n = n0 + warp * 8 + 2 * t;
       if (m >= p.M || n >= p.N) continue;
-      float y0 = acc[4 * tile + 2 * h], y1 = acc[4 * tile + 2 * h + 1];
+      float y0 = v[2 * h], y1 = v[2 * h + 1];
       if (p.bias != nullptr) {
         y0 = __fadd_rn(y0, __bfloat162float(p.bias[n]));
         y1 = __fadd_rn(y1, __bfloat162float(p.bias[n + 1]));
@@ -683,6 +731,7 @@ k_gemm_w4a16_small(const __nv_bfloat16* __restrict__ X, EpiParams p, W4Params q)
           pack_bf16x2(y0, y1);
     }
   }
+  if constexpr (KS > 1) cluster_sync_all();  // rank 0 has read the peers' partials
 }
 
 }  // namespace qib

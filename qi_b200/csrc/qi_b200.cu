@@ -652,6 +652,39 @@ static int launch_w4_skinny(const void* X, const EpiParams& p, const W4Params& q
   return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
+template <int NT, int KS>
+static int launch_w4_small(const void* X, const EpiParams& p, const W4Params& q, cudaStream_t stream) {
+  const W4sLayout L = w4s_layout(NT, KS, p.M, p.K, q.G, q.zw, q.group);
+  if (L.total > 200 * 1024) return QI_B200_ESHAPE;
+  static bool attr_done[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev]) {
+    if (cudaFuncSetAttribute(k_gemm_w4a16_small<NT, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             200 * 1024) != cudaSuccess)
+      return QI_B200_ECUDA;
+    attr_done[dev] = true;
+  }
+  const int blocks = (p.N + 8 * NT - 1) / (8 * NT);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = KS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(blocks * KS, 1, 1);
+  cfg.blockDim = dim3(w4s::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L.total;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  g_last_plan = {kPlanW4Small, blocks * KS, KS, p.M, 0, L.total};
+  const cudaError_t e =
+      cudaLaunchKernelEx(&cfg, k_gemm_w4a16_small<NT, KS>, static_cast<const __nv_bfloat16*>(X), p, q);
+  count_launches(1);
+  return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
 static int launch_w4a16(const void* X, const void* wq, const void* scales, const void* zeros, int group,
                         const void* bias, void* D, long long ldd, int M, int N, int K, cudaStream_t stream) {
   if (X == nullptr || wq == nullptr || scales == nullptr || zeros == nullptr || D == nullptr) return QI_B200_EINVAL;
@@ -679,24 +712,14 @@ static int launch_w4a16(const void* X, const void* wq, const void* scales, const
   q.zeros = static_cast<const int32_t*>(zeros);
   q.wq = static_cast<const int32_t*>(wq);
   q.kw = K / 8;
-  if (M <= w4s::kMaxM && K % (w4s::kWarps * w4s::kChunk) == 0 && group % 16 == 0 &&
-      w4s_smem_bytes(M, K) <= 200 * 1024) {
-    // weight-streaming kernel: 16 weight rows per CTA, 8 warps splitting K
-    static bool attr_small[kMaxDevices] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!attr_small[dev]) {
-      if (cudaFuncSetAttribute(k_gemm_w4a16_small, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
-          cudaSuccess)
-        return QI_B200_ECUDA;
-      attr_small[dev] = true;
-    }
-    const int grid = (N + w4s::kRows - 1) / w4s::kRows;
-    const int smem = w4s_smem_bytes(M, K);
-    g_last_plan = {kPlanW4Small, grid, 1, M, 0, smem};
-    k_gemm_w4a16_small<<<grid, w4s::kThreads, smem, stream>>>(static_cast<const __nv_bfloat16*>(X), p, q);
-    count_launches(1);
-    return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+  if (M <= w4s::kMaxM && group >= 32 && group <= 256 && (group & (group - 1)) == 0 && K % (8 * group) == 0 &&
+      aligned16(scales) && aligned16(zeros)) {
+    // small M: rows per CTA and the cluster's K split grow with M, so that
+    // each CTA stages at most 4 token rows x K of activations
+    if (M <= 4) rc = launch_w4_small<1, 1>(X, p, q, stream);
+    else if (M <= 8) rc = launch_w4_small<2, 2>(X, p, q, stream);
+    else rc = launch_w4_small<4, 4>(X, p, q, stream);
+    if (rc != QI_B200_ESHAPE) return rc;  // ESHAPE: shared memory too small, use the split-K kernel
   }
   if (M <= 16) return launch_w4_skinny<16>(X, p, q, di->num_sms, stream);
   if (M <= 32) return launch_w4_skinny<32>(X, p, q, di->num_sms, stream);

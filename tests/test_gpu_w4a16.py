@@ -4,9 +4,11 @@
   is exactly bf16(W) (+0 bias), compared bitwise with the oracle's
   ``bf16((q - z) * s)`` (reference quantize.py:110-117 on the packed layout).
 * Outputs: relative Frobenius <= 2e-3 vs the oracle (fp32 accumulation
-  order), <= 5e-3 vs the reference's own output (golden fixture).
-* The kernels: weight streaming (M <= 8, K % 1024 == 0), the split-K cluster kernel (M <= 256) and the 256x128 tile
-  kernel (M > 256); BASELINE config 3 (N=K=3072, g=128, M in 1/16/256/4096).
+  order; 5e-3 for the small-M kernel, which scales fp32 group partials
+  instead of rounding each weight to bf16), <= 5e-3 vs the reference's own
+  output (golden fixture).
+* The kernels: small M (M <= 16, K % 256 == 0; weight rows brought in by bulk copies), the split-K cluster
+  kernel (M <= 256) and the 256x128 tile kernel (M > 256); BASELINE config 3 (N=K=3072, g=128, M in 1/16/256/4096).
 """
 
 from pathlib import Path
@@ -40,6 +42,17 @@ def bits(t):
     return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
 
 
+def tol(M: int, Kd: int, group: int) -> float:
+    """Relative Frobenius bound vs the oracle.  The small-M kernel (M <= 16,
+    K % (8 group) == 0) applies each group's scale to fp32 partial sums of
+    x (128 + q) instead of rounding every dequantized weight to bf16 first,
+    so it differs from dequantize-then-matmul by that rounding (~1e-3, plus
+    the bf16 output rounding of both sides): the north-star INT4 bound
+    5e-3.  The other kernels dequantize to bf16 exactly as the reference: 2e-3."""
+    small = M <= 16 and 32 <= group <= 256 and group & (group - 1) == 0 and Kd % (8 * group) == 0
+    return 5e-3 if small else 2e-3
+
+
 def packed(w: np.ndarray, group: int, symmetric: bool = False):
     q, s, z = O.quantize_weight_rtn(w, 4, group, symmetric)
     if symmetric:
@@ -70,11 +83,14 @@ def test_w4a16_dequant_bit_exact_one_hot(N, Kd, group, M):
     np.testing.assert_array_equal(bits(y), wb[:, np.arange(M) % Kd].T)
 
 
-@pytest.mark.parametrize("N,Kd,group", [(128, 1024, 128), (136, 2048, 64), (64, 3072, 32), (256, 1024, 96)])
-@pytest.mark.parametrize("M", [1, 5, 8])
+@pytest.mark.parametrize("N,Kd,group", [(128, 1024, 128), (136, 2048, 64), (64, 3072, 32), (256, 2048, 256),
+                                         (24, 1024, 128), (3072, 3072, 128)])
+@pytest.mark.parametrize("M", [1, 3, 5, 8, 11, 16])
 def test_w4a16_small_m_kernel(N, Kd, group, M):
-    """M <= 8 with K % 1024 == 0 runs the weight-streaming kernel (plan 7):
-    dequantization bit-exact (one-hot rows) and outputs vs the oracle."""
+    """M <= 16, a power-of-two group in [32, 256] and K % (8 group) == 0 run the small-M kernel (plan 7: weight
+    rows brought into shared memory by bulk copies, K split over a cluster
+    for M > 4, group scales applied to fp32 partials): dequantization
+    bit-exact (one-hot rows) and outputs vs the oracle."""
     g = torch.Generator().manual_seed(N + Kd + M)
     w = (torch.randn(N, Kd, generator=g) * 0.02).numpy()
     qp, s16, zp = packed(w, group, symmetric=(M == 5))
@@ -90,7 +106,7 @@ def test_w4a16_small_m_kernel(N, Kd, group, M):
     xr, _, b = make_small_case(M, N, Kd, seed=M + Kd)
     y = K.w4a16_linear(xr.to(DEV), qp_d, s_d, zp_d, group, b.to(DEV))
     yo = O.w4a16_linear(bits(xr), qp, s16, zp, group, bits(b))
-    assert O.rel_fro(O.bf16_to_f32(bits(y)), O.bf16_to_f32(yo)) <= 2e-3
+    assert O.rel_fro(O.bf16_to_f32(bits(y)), O.bf16_to_f32(yo)) <= tol(M, Kd, group)
 
 
 @pytest.mark.parametrize("M", [1, 3, 16, 17, 64, 100, 256, 257, 512])
@@ -102,7 +118,7 @@ def test_w4a16_linear_vs_oracle(M, N, Kd, group):
     y = K.w4a16_linear(x.to(DEV), qp_d, torch.from_numpy(s16).to(DEV), zp_d, group, b.to(DEV))
     yo = O.w4a16_linear(bits(x), qp, s16, zp, group, bits(b))
     e = O.rel_fro(O.bf16_to_f32(bits(y)), O.bf16_to_f32(yo))
-    assert e <= 2e-3, e
+    assert e <= tol(M, Kd, group), e
 
 
 def test_w4a16_vs_reference_fixture():
@@ -126,4 +142,4 @@ def test_w4a16_config3_full_size(M):
     rows = np.arange(M) if M <= 256 else np.r_[0:64, 2048:2080, 4064:4096]
     yo = O.w4a16_linear(bits(x)[rows], qp, s16, zp, 128, bits(b))
     e = O.rel_fro(O.bf16_to_f32(bits(y)[rows]), O.bf16_to_f32(yo))
-    assert e <= 2e-3, e
+    assert e <= tol(M, 3072, 128), e
