@@ -251,7 +251,8 @@ int qi_b200_w4a16_linear(const void* x_bf16, const void* qweight_packed, const v
  *   q = e2m1(clamp(x / (sf g), +-6)).
  * Activation quantization, g_mode: 0 = static per-tensor g (g_in), 1 =
  * dynamic per-tensor (two passes; ws_amax is one uint32 of scratch; g_out[0]),
- * 2 = dynamic per-row (g_out[rows]).  cols % 64 == 0. */
+ * 2 = dynamic per-row (g_out[rows]).  cols % 64 == 0; x and sf_atoms
+ * 16-byte aligned, q_packed 8-byte aligned. */
 int qi_b200_quantize_nvfp4(const void* x_bf16, int rows, int cols, int g_mode, const float* g_in,
                            unsigned int* ws_amax, float* g_out, void* q_packed, void* sf_atoms, cudaStream_t stream);
 /* D = bf16( (acc * a_g[m or 0]) * b_g[0] + bias ), acc = sum over 16-blocks of

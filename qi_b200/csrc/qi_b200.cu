@@ -523,11 +523,12 @@ static int nvfp4_quantize(const void* x, int rows, int cols, int g_mode, const f
   if (rows <= 0 || cols <= 0) return QI_B200_ESHAPE;
   if (cols % 64 != 0) return QI_B200_ESHAPE;
   if (x == nullptr || q == nullptr || sf == nullptr) return QI_B200_EINVAL;
-  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u)) return QI_B200_EALIGN;
+  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u) || !aligned16(sf)) return QI_B200_EALIGN;
   if (g_mode == 0 && g_in == nullptr) return QI_B200_EINVAL;
   if (g_mode == 1 && (ws_amax == nullptr || g_out == nullptr)) return QI_B200_EINVAL;
   if (g_mode == 2 && g_out == nullptr) return QI_B200_EINVAL;
   if (g_mode < 0 || g_mode > 2) return QI_B200_EINVAL;
+  if ((long long)((rows + 127) & ~127) * (cols / 16) >= (1ll << 31)) return QI_B200_ESHAPE;
   DeviceInfo* di = nullptr;
   int rc = device_info(&di);
   if (rc) return rc;
@@ -543,10 +544,10 @@ static int nvfp4_quantize(const void* x, int rows, int cols, int g_mode, const f
     const long long n = (long long)rows * cols;
     const int g2 = (int)std::min<long long>((n / 8 + 255) / 256 + 1, (long long)di->num_sms * 8);
     k_amax_bf16<<<g2, 256, 0, stream>>>(xb, n, ws_amax);
-    k_quant_nvfp4<1><<<grid_flat, 256, 0, stream>>>(xb, rows, cols, nullptr, ws_amax, g_out, qb, sb, ka);
+    k_quant_nvfp4_tensor<1><<<grid_flat, 256, 0, stream>>>(xb, rows, cols, nullptr, ws_amax, g_out, qb, sb, ka);
     count_launches(2);
   } else if (g_mode == 0) {
-    k_quant_nvfp4<0><<<grid_flat, 256, 0, stream>>>(xb, rows, cols, g_in, nullptr, nullptr, qb, sb, ka);
+    k_quant_nvfp4_tensor<0><<<grid_flat, 256, 0, stream>>>(xb, rows, cols, g_in, nullptr, nullptr, qb, sb, ka);
     count_launches(1);
   } else {
     const int g3 = std::min(rows_pad, di->num_sms * 8);

@@ -104,6 +104,101 @@ __device__ __forceinline__ uint2 nvfp4_block(const uint4& v0, const uint4& v1, f
   return make_uint2(lo, hi);
 }
 
+__device__ __forceinline__ float rcp_approx(float v) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+  return r;
+}
+__device__ __forceinline__ uint32_t e4m3_code(float v) {
+  return static_cast<uint32_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+}
+
+// nvfp4_block with divisions only where they decide the result, for a
+// per-tensor g.  Each quotient the recipe rounds (bm / fl(6 g) for the block
+// scale, x / fl(sf g) for the codes) is bracketed by two products with a
+// reciprocal widened by +-2^-20 (8 ulp, more than the approximate
+// reciprocal's and the products' rounding): the exact quotient and its fp32
+// rounding both lie inside the bracket, and E4M3 / E2M1 rounding is
+// monotonic, so when both ends convert to the same code that code is the
+// recipe's.  Where they differ (a quotient within a few ulp of a rounding
+// boundary; exact ties occur, e.g. when sf carries a factor that cancels
+// against g's), that scale or that pair of codes is recomputed with
+// correctly rounded divisions.  rg = the bracket ends of 1 / fl(6 g).
+// Saturating conversions are the recipe's clamps (448, +-6).
+__device__ __forceinline__ uint2 nvfp4_block_fast(const uint4& v0, const uint4& v1, float g, float g6, float2 rg,
+                                                  uint8_t& sfc) {
+  const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+  __nv_bfloat162 m2 = __habs2(*reinterpret_cast<const __nv_bfloat162*>(&w[0]));
+#pragma unroll
+  for (int k = 1; k < 8; ++k) m2 = __hmax2(m2, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&w[k])));
+  const float bm = fmaxf(__low2float(m2), __high2float(m2));  // exact: max of the same values
+  uint32_t c = e4m3_code(__fmul_rn(bm, rg.x));
+  if (c != e4m3_code(__fmul_rn(bm, rg.y))) c = e4m3_code(fminf(__fdiv_rn(bm, g6), 448.0f));
+  sfc = static_cast<uint8_t>(c);
+  __half_raw hr = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(sfc), __NV_E4M3);
+  const float denom = __fmul_rn(__half2float(__half(hr)), g);
+  const float inv = denom > 0.f ? rcp_approx(denom) : 0.f;
+  const float il = inv * (1.0f - 0x1p-20f), ih = inv * (1.0f + 0x1p-20f);
+  const float2 il2 = make_float2(il, il), ih2 = make_float2(ih, ih);
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+    const float2 a = __fmul2_rn(f, il2), b = __fmul2_rn(f, ih2);
+    uint32_t byte = e2m1x2(a.x, a.y);
+    if (byte != e2m1x2(b.x, b.y))
+      byte = e2m1x2(fminf(fmaxf(__fdiv_rn(f.x, denom), -6.f), 6.f), fminf(fmaxf(__fdiv_rn(f.y, denom), -6.f), 6.f));
+    if (k < 4) lo |= byte << (8 * k);
+    else hi |= byte << (8 * (k - 4));
+  }
+  return make_uint2(lo, hi);
+}
+
+// Per-tensor g (GMODE 0: *g_in, 1: from *amax_bits, g written to g_out[0]).
+// One thread per 16-element block; a warp covers 32 consecutive blocks, and
+// warps walk the tensor from its END, so the part of x that the amax pass
+// read last (still in L2) is read first.  Four lanes' block scales (one 4-byte
+// word of an atom row) are stored together.  rows_pad * bpr % 32 == 0.
+template <int GMODE>
+__global__ void __launch_bounds__(256)
+k_quant_nvfp4_tensor(const __nv_bfloat16* __restrict__ x, int rows, int cols, const float* __restrict__ g_in,
+                     const unsigned int* __restrict__ amax_bits, float* __restrict__ g_out, uint8_t* __restrict__ q,
+                     uint8_t* __restrict__ sf, int ka_per_rowblock) {
+  const int bpr = cols >> 4;
+  const int rows_pad = (rows + 127) & ~127;
+  float g;
+  if (GMODE == 0) {
+    g = __ldg(g_in);
+  } else {
+    g = nvfp4_g_from_amax(__uint_as_float(*amax_bits));
+    if (blockIdx.x == 0 && threadIdx.x == 0) g_out[0] = g;
+  }
+  const int lane = threadIdx.x & 31;
+  const float g6 = __fmul_rn(6.0f, g);
+  const float rg0 = rcp_approx(g6);
+  const float2 rg = make_float2(rg0 * (1.0f - 0x1p-20f), rg0 * (1.0f + 0x1p-20f));
+  const int chunks = rows_pad * bpr / 32;  // the host keeps rows_pad * bpr < 2^31
+  for (int ch = (blockIdx.x * 256 + threadIdx.x) / 32; ch < chunks; ch += 256 * gridDim.x / 32) {
+    const int t = (chunks - 1 - ch) * 32 + lane;
+    const int row = t / bpr;
+    const int b = t - row * bpr;
+    uint8_t sfc = 0;
+    if (row < rows) {
+      const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<long long>(row) * cols + b * 16);
+      const uint4 v0 = __ldg(p), v1 = __ldg(p + 1);
+      const uint2 packed = nvfp4_block_fast(v0, v1, g, g6, rg, sfc);
+      *reinterpret_cast<uint2*>(q + static_cast<long long>(row) * (cols >> 1) + b * 8) = packed;
+    }
+    // blocks b .. b+3 (b % 4 == 0) of one row share a 4-byte word of the atom row
+    const uint32_t s0 = sfc;
+    const uint32_t s1 = __shfl_down_sync(0xffffffffu, s0, 1);
+    const uint32_t s2 = __shfl_down_sync(0xffffffffu, s0, 2);
+    const uint32_t s3 = __shfl_down_sync(0xffffffffu, s0, 3);
+    if ((b & 3) == 0)
+      *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(row, b, ka_per_rowblock)) = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
+  }
+}
+
 // One thread per 16-element block.  GMODE: 0 = per-tensor g from *g_in,
 // 1 = per-tensor g from *amax_bits (g written to g_out[0]), 2 = per-row g
 // (the row's amax is reduced here first; g written to g_out[row]).
@@ -142,10 +237,13 @@ k_quant_nvfp4(const __nv_bfloat16* __restrict__ x, int rows, int cols, const flo
       }
       __syncthreads();
       const float g = g_sh;
+      const float g6 = __fmul_rn(6.0f, g);
+      const float rg0 = rcp_approx(g6);
+      const float2 rg = make_float2(rg0 * (1.0f - 0x1p-20f), rg0 * (1.0f + 0x1p-20f));
       for (int b = threadIdx.x; b < bpr; b += 256) {
         const uint4* p = reinterpret_cast<const uint4*>(xr + b * 16);
         uint8_t sfc;
-        const uint2 packed = nvfp4_block(__ldg(p), __ldg(p + 1), g, sfc);
+        const uint2 packed = nvfp4_block_fast(__ldg(p), __ldg(p + 1), g, g6, rg, sfc);
         *reinterpret_cast<uint2*>(q + static_cast<long long>(row) * (cols >> 1) + b * 8) = packed;
         sf[sf_atom_offset(row, b, ka_per_rowblock)] = sfc;
       }
