@@ -224,6 +224,9 @@ def run_ours(args):
     quant = K.quantize_fp8_rowwise if c["kind"] == "fp8" else K.quantize_int8_rowwise
     # kernels per step: w4a16 1; nvfp4 3 (amax, quantize, GEMM; plus a 4-byte memset); int8/fp8 2
     launches_per_step = {"w4a16": 1, "nvfp4": 3}.get(c["kind"], 2)
+    w4_dequant = c["kind"] == "w4a16" and M >= _lib.W4A16_DEQUANT_MIN_M
+    if w4_dequant:
+        launches_per_step = 2  # weights dequantized once into a workspace, then the bf16 GEMM
     # N > 1, INT8/FP8: the all-gather fused into the GEMM epilogue (peer stores over NVLink)
     # auto: the fused gather where it has been validated on the GPU (2 ranks);
     # NCCL's all-gather beyond that
@@ -406,7 +409,8 @@ def run_ours(args):
         roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                     "frac": round(achieved / peak, 4), "traffic": traffic, "algorithmic_bytes": alg_bytes,
                     "peak_source": f"{mult:g} x bf16 dense, " + src}
-    roofline.update({"kernel": "k_gemm_w4a16" if c["kind"] == "w4a16" else
+    roofline.update({"kernel": ("k_w4a16_dequant + bf16 GEMM (k_gemm_tc2<bf16>), timed together" if w4_dequant
+                                else "k_gemm_w4a16") if c["kind"] == "w4a16" else
                      (f"k_gemm_tc2<{c['kind']}> with the all-gather fused into its epilogue (TMA stores to "
                       "every rank) + 2 barriers (activation quantizer included)" if peer
                       else f"k_gemm_tc<{c['kind']}>"),

@@ -240,6 +240,21 @@ int qi_b200_w4a16_linear(const void* x_bf16, const void* qweight_packed, const v
                          const void* zeros_packed, int group_size, const void* bias, void* out_bf16, int M, int N,
                          int K, cudaStream_t stream);
 
+/* Packed INT4 weights -> bf16 [N, K] (qweight and out_bf16 16-byte aligned),
+ * exactly the reference's dequantization.  group_size % 32 == 0, K % 32 == 0. */
+int qi_b200_w4a16_dequant(const void* qweight_packed, const void* scales_fp16, const void* zeros_packed,
+                          int group_size, void* out_bf16, int N, int K, cudaStream_t stream);
+
+/* qi_b200_w4a16_linear with a caller-owned workspace of at least N * K * 2
+ * bytes (16-byte aligned): for M >= QI_B200_W4A16_DEQUANT_MIN_M the weights
+ * are dequantized once into it and multiplied with the bf16 tcgen05 GEMM (the
+ * fused kernels would rebuild each dequantized tile for every M tile); below
+ * that, or without a workspace, it is qi_b200_w4a16_linear. */
+#define QI_B200_W4A16_DEQUANT_MIN_M 257
+int qi_b200_w4a16_linear_ws(const void* x_bf16, const void* qweight_packed, const void* scales_fp16,
+                            const void* zeros_packed, int group_size, const void* bias, void* out_bf16, int M, int N,
+                            int K, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* ---- NVFP4 W4A4 (no counterpart in the reference, which only names the
  * buffers qweight_packed / scale_factors / weight_global_scale at
  * src/qi/quantization/modules.py:21-23) ------------------------------------

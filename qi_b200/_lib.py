@@ -17,6 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libqi_b200.so"
 OK, EINVAL, ESHAPE, EALIGN, ECUDA, ETMAP, EARCH, ETOOBIG = range(8)
 KIND_INT8, KIND_FP8_E4M3, KIND_BF16 = 0, 1, 2
 EPI_GELU, EPI_RAW_ACC = 1, 2
+W4A16_DEQUANT_MIN_M = 257  # QI_B200_W4A16_DEQUANT_MIN_M (measured crossover: M=512 26 us vs 43 us fused)
 NVFP4_TILE_SHIFT = 8  # flags bits 8-9: 0 auto, 1 single-CTA 128x128, 2 pair 256x128, 3 pair 256x256
 
 
@@ -44,6 +45,8 @@ SIGNATURES = {
     "qi_b200_device_status": [_P, _I],
     "qi_b200_last_launch": [_P],
     "qi_b200_launch_count": [_P],
+    "qi_b200_w4a16_dequant": [_P, _P, _P, _I, _P, _I, _I, _P],
+    "qi_b200_w4a16_linear_ws": [_P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _P, ctypes.c_size_t, _P],
     "qi_b200_quantize_int8_rowwise": [_P, _P, _P, _I, _I, _P],
     "qi_b200_quantize_int8_rowwise_given": [_P, _P, _P, _I, _I, _P],
     "qi_b200_int8_row_scales": [_P, _P, _I, _I, _P],

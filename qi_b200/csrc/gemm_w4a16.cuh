@@ -527,6 +527,42 @@ k_gemm_w4a16_skinny(const __grid_constant__ CUtensorMap tmX, const EpiParams p, 
 // bf16((q - z) * s) of the tile kernel.
 // ---------------------------------------------------------------------------
 
+// two nibbles (elements 2t, 2t+1 of word w) -> packed bf16x2 of (q - z) * s:
+// 1 + q/16 is exact in fp32 (exponent 0, q in the top mantissa bits), and
+// fma(1 + q/16, 16 s, -(16 + z) s) rounds the exact (q - z) s once.
+__device__ __forceinline__ uint32_t dequant_pair(uint32_t w, int t, float s16x, float c) {
+  const uint32_t b = w >> (8 * t);
+  const float f0 = fmaf(__uint_as_float(0x3F800000u | ((b << 19) & 0x00780000u)), s16x, c);
+  const float f1 = fmaf(__uint_as_float(0x3F800000u | ((b << 15) & 0x00780000u)), s16x, c);
+  return pack_bf16x2(f0, f1);
+}
+
+// Dequantize packed INT4 weights to bf16 [N, K] (the reference's
+// bf16((q - z) s), exact), four packed words (32 elements) per thread.
+// HBM-bound: K/2 + 2K bytes per row (+ scales).  group % 32 == 0, K % 32 == 0.
+__global__ void __launch_bounds__(256)
+k_w4a16_dequant(W4Params q, __nv_bfloat16* __restrict__ out, int N, int K) {
+  const int qpr = q.kw / 4;  // word quads per row
+  const int quads = N * qpr;  // the host keeps N * K / 32 < 2^31
+  for (int i = blockIdx.x * 256 + threadIdx.x; i < quads; i += 256 * gridDim.x) {
+    const int n = i / qpr;
+    const int w0 = (i - n * qpr) * 4;
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(q.wq + static_cast<long long>(n) * q.kw + w0));
+    const int k0 = w0 * 8;
+    const int grp = q.group_shift >= 0 ? (k0 >> q.group_shift) : (k0 / q.group);  // 32 elements: one group
+    const float sc = __half2float(__ldg(q.scales + static_cast<long long>(n) * q.G + grp));
+    const uint32_t z = (static_cast<uint32_t>(__ldg(q.zeros + static_cast<long long>(n) * q.zw + (grp >> 3))) >>
+                        (4 * (grp & 7))) & 0xFu;
+    const float s16x = sc * 16.0f, c = -(16.0f + static_cast<float>(z)) * sc;
+    const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint4* dst = reinterpret_cast<uint4*>(out + static_cast<long long>(n) * K + k0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      dst[j] = make_uint4(dequant_pair(wd[j], 0, s16x, c), dequant_pair(wd[j], 1, s16x, c),
+                          dequant_pair(wd[j], 2, s16x, c), dequant_pair(wd[j], 3, s16x, c));
+  }
+}
+
 namespace w4s {
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;

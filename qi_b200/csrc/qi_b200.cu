@@ -968,6 +968,50 @@ int qi_b200_w4a16_linear(const void* x_bf16, const void* qweight_packed, const v
                       stream);
 }
 
+int qi_b200_w4a16_dequant(const void* qweight_packed, const void* scales_fp16, const void* zeros_packed,
+                          int group_size, void* out_bf16, int N, int K, cudaStream_t stream) {
+  if (qweight_packed == nullptr || scales_fp16 == nullptr || zeros_packed == nullptr || out_bf16 == nullptr)
+    return QI_B200_EINVAL;
+  if (N <= 0 || K <= 0) return QI_B200_ESHAPE;
+  int group = group_size;
+  if (group <= 0 || group > K) group = K;
+  if (K % 32 != 0 || group % 32 != 0 || (long long)N * (K / 32) >= (1ll << 31)) return QI_B200_ESHAPE;
+  if (!aligned16(out_bf16) || !aligned16(qweight_packed)) return QI_B200_EALIGN;
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  W4Params q;
+  q.G = (K + group - 1) / group;
+  q.zw = (q.G + 7) / 8;
+  q.group = group;
+  q.group_shift = ((group & (group - 1)) == 0) ? __builtin_ctz(static_cast<unsigned>(group)) : -1;
+  q.scales = static_cast<const __half*>(scales_fp16);
+  q.zeros = static_cast<const int32_t*>(zeros_packed);
+  q.wq = static_cast<const int32_t*>(qweight_packed);
+  q.kw = K / 8;
+  const long long quads = (long long)N * (K / 32);
+  const int grid = (int)std::min<long long>((quads + 255) / 256, (long long)di->num_sms * 16);
+  k_w4a16_dequant<<<grid, 256, 0, stream>>>(q, static_cast<__nv_bfloat16*>(out_bf16), N, K);
+  count_launches(1);
+  return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+int qi_b200_w4a16_linear_ws(const void* x_bf16, const void* qweight_packed, const void* scales_fp16,
+                            const void* zeros_packed, int group_size, const void* bias, void* out_bf16, int M, int N,
+                            int K, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (M == 0) return QI_B200_OK;
+  if (M < QI_B200_W4A16_DEQUANT_MIN_M || workspace == nullptr || workspace_bytes < (size_t)N * K * 2)
+    return launch_w4a16(x_bf16, qweight_packed, scales_fp16, zeros_packed, group_size, bias, out_bf16, N, M, N, K,
+                        stream);
+  // large M: the weights are dequantized once into the workspace, then a bf16
+  // tcgen05 GEMM (the dequantized tile would otherwise be rebuilt for every
+  // M tile)
+  int rc = qi_b200_w4a16_dequant(qweight_packed, scales_fp16, zeros_packed, group_size, workspace, N, K, stream);
+  if (rc) return rc;
+  return gemm_dispatch(QI_B200_KIND_BF16, x_bf16, workspace, nullptr, 0, nullptr, 0, bias, out_bf16, N, M, N, K, 0,
+                       0, stream);
+}
+
 int qi_b200_quantize_nvfp4(const void* x_bf16, int rows, int cols, int g_mode, const float* g_in,
                            unsigned int* ws_amax, float* g_out, void* q_packed, void* sf_atoms, cudaStream_t stream) {
   if (rows == 0) return QI_B200_OK;

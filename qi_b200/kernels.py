@@ -289,8 +289,25 @@ def w4a16_linear(x_bf16_2d: torch.Tensor, qweight_packed: torch.Tensor, scales_f
         if bias.numel() != N:
             raise ValueError(f"bias must have {N} values.")
     out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    if M >= _lib.W4A16_DEQUANT_MIN_M:  # dequantize once into a workspace, then the bf16 GEMM
+        ws = torch.empty((N * K * 2,), dtype=torch.uint8, device=dev)
+        _lib.call("qi_b200_w4a16_linear_ws", _ptr(x_bf16_2d), _ptr(qweight_packed), _ptr(scales_fp16),
+                  _ptr(zeros_packed), int(g), _ptr(bias), _ptr(out), M, N, K, _ptr(ws), ws.numel(), _stream(dev))
+        return out
     _lib.call("qi_b200_w4a16_linear", _ptr(x_bf16_2d), _ptr(qweight_packed), _ptr(scales_fp16),
               _ptr(zeros_packed), int(g), _ptr(bias), _ptr(out), M, N, K, _stream(dev))
+    return out
+
+
+def w4a16_dequant(qweight_packed: torch.Tensor, scales_fp16: torch.Tensor, zeros_packed: torch.Tensor,
+                  group_size: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Packed INT4 weights -> bf16 [N, K], exactly bf16((q - z) s) (``qi_b200_w4a16_dequant``)."""
+    N = qweight_packed.shape[0]
+    K = qweight_packed.shape[1] * 8
+    if out is None:
+        out = torch.empty((N, K), dtype=torch.bfloat16, device=qweight_packed.device)
+    _lib.call("qi_b200_w4a16_dequant", _ptr(qweight_packed), _ptr(scales_fp16), _ptr(zeros_packed),
+              int(group_size), _ptr(out), N, K, _stream(qweight_packed.device))
     return out
 
 

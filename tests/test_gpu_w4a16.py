@@ -143,3 +143,37 @@ def test_w4a16_config3_full_size(M):
     yo = O.w4a16_linear(bits(x)[rows], qp, s16, zp, 128, bits(b))
     e = O.rel_fro(O.bf16_to_f32(bits(y)[rows]), O.bf16_to_f32(yo))
     assert e <= tol(M, 3072, 128), e
+
+
+@pytest.mark.parametrize("N,Kd,group", [(128, 256, 128), (136, 384, 32), (3072, 3072, 128), (64, 1024, -1)])
+def test_w4a16_dequant_kernel_bit_exact(N, Kd, group):
+    """qi_b200_w4a16_dequant: bf16 weights equal the oracle's bf16((q - z) s) bit for bit."""
+    g = torch.Generator().manual_seed(N * 7 + Kd)
+    w = (torch.randn(N, Kd, generator=g) * 0.02).numpy()
+    qp, s16, zp = packed(w, group if group > 0 else Kd)
+    qp_d, zp_d = dev(qp, zp)
+    wb = K.w4a16_dequant(qp_d, torch.from_numpy(s16).to(DEV), zp_d, group)
+    np.testing.assert_array_equal(bits(wb), O.w4a16_dequant_bf16(qp, s16, zp, Kd, group if group > 0 else Kd))
+
+
+@pytest.mark.parametrize("M", [64, 256, 300, 600])
+def test_w4a16_fused_kernels_large_m(M):
+    """The fused kernels (split-K cluster for M <= 256, 256 x 128 tiles above)
+    stay reachable through qi_b200_w4a16_linear without a workspace; from
+    M = 257 the module path dequantizes once and runs the bf16 GEMM."""
+    N, Kd, group = 256, 1024, 128
+    x, w, b = make_small_case(M, N, Kd, seed=M + 11)
+    qp, s16, zp = packed(w.numpy(), group)
+    qp_d, zp_d = dev(qp, zp)
+    s_d = torch.from_numpy(s16).to(DEV)
+    xd, bd = x.to(DEV), b.to(DEV)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=DEV)
+    _lib.call("qi_b200_w4a16_linear", xd.data_ptr(), qp_d.data_ptr(), s_d.data_ptr(), zp_d.data_ptr(), group,
+              bd.data_ptr(), y.data_ptr(), M, N, Kd, torch.cuda.current_stream().cuda_stream)
+    assert _lib.last_launch()["kernel"] == ("w4a16_splitk" if M <= 256 else "w4a16_tiles")
+    yo = O.w4a16_linear(bits(x), qp, s16, zp, group, bits(b))
+    assert O.rel_fro(O.bf16_to_f32(bits(y)), O.bf16_to_f32(yo)) <= 2e-3
+    y2 = K.w4a16_linear(xd, qp_d, s_d, zp_d, group, bd)
+    if M >= _lib.W4A16_DEQUANT_MIN_M:
+        assert _lib.last_launch()["kernel"] in ("gemm_bf16", "gemm_bf16_pair")
+    assert O.rel_fro(O.bf16_to_f32(bits(y2)), O.bf16_to_f32(yo)) <= 2e-3
