@@ -449,7 +449,7 @@ def run_ours(args):
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(result), flush=True)
+        emit(result)
 
 
 # --------------------------------------------------------------------------
@@ -598,7 +598,7 @@ def run_dit(args):
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(result), flush=True)
+        emit(result)
 
 
 def _dit_cpu_layer_sample():
@@ -731,7 +731,7 @@ def run_reference(args):
         for _ in range(args.steps):
             fn()
         ms = (time.perf_counter() - t) / args.steps * 1e3 * cfg.layers
-        print(json.dumps({
+        emit({
             "impl": "reference", "metric": "dit_step_latency_ms", "value": round(ms, 1), "unit": "ms",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 1),
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": CONFIGS["dit"]["dtype"],
@@ -739,7 +739,7 @@ def run_reference(args):
             "cpu_baseline": {"value": round(ms, 1), "unit": "ms", "cores": torch.get_num_threads(), "kind": "port",
                              "sample": "20 INT8 Linears of 1 of 30 layers per step, scaled x30"},
             "e2e": {"value": round(ms, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        }), flush=True)
+        })
         return
     fn, rows, case, desc = _cpu_sample(args.config)
     for _ in range(args.warmup):
@@ -749,7 +749,7 @@ def run_reference(args):
         fn()
     dt = (time.perf_counter() - t) / args.steps
     value = 2.0 * rows * case.N * case.K / dt / 1e12
-    print(json.dumps({
+    emit({
         "impl": "reference", "metric": "quantized_gemm_tops", "value": round(value, 5), "unit": "TOPS",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": CONFIGS[args.config]["dtype"],
@@ -758,10 +758,29 @@ def run_reference(args):
         "cpu_baseline": {"value": round(value, 5), "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
                          "sample": desc},
         "e2e": {"value": round(value, 5), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    })
+
+
+# The JSON result line goes to the process's original stdout; everything
+# else that would reach fd 1 (library banners such as NCCL's version line,
+# stray prints) is sent to stderr, so stdout carries exactly one line.
+_RESULT_FD = None
+
+
+def emit(obj) -> None:
+    line = (json.dumps(obj) + "\n").encode()
+    if _RESULT_FD is None:
+        sys.stdout.write(line.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_RESULT_FD, line)
 
 
 def main():
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
