@@ -352,15 +352,32 @@ __device__ __forceinline__ float warp_max(float v) {
 
 constexpr int kWarpRowThreads = 128;
 
+// The per-column vectors (gate, LayerNorm affine, modulation) are staged in
+// shared memory once per CTA, so the per-chunk loops read them without an L2
+// round trip each (the loops would otherwise wait on C dependent loads).
+// Dynamic shared memory: 5 * D bf16.
 template <int C>
 __global__ void __launch_bounds__(kWarpRowThreads) k_resid_ln_quant_warp(ResLnParams p) {
+  extern __shared__ __align__(16) uint4 vecs[];  // [5][C * 32]: gate, ln_w, ln_b, scale1, shift
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (kWarpRowThreads / 32) + (threadIdx.x >> 5);
+  {
+    const __nv_bfloat16* src[5] = {p.gate, p.ln_w, p.ln_b, p.mod_scale1, p.mod_shift};
+#pragma unroll
+    for (int v = 0; v < 5; ++v)
+      if (src[v] != nullptr)
+        for (int i = threadIdx.x; i < C * 32; i += kWarpRowThreads)
+          vecs[v * C * 32 + i] = __ldg(reinterpret_cast<const uint4*>(src[v]) + i);
+  }
+  uint4 xu[C];
+  if (row < p.M) {
+    const uint4* xr0 = reinterpret_cast<const uint4*>(p.x + static_cast<long long>(row) * p.D);
+#pragma unroll
+    for (int c = 0; c < C; ++c) xu[c] = xr0[c * 32 + lane];
+  }
+  __syncthreads();
   if (row >= p.M) return;
   uint4* xr = reinterpret_cast<uint4*>(p.x + static_cast<long long>(row) * p.D);
-  uint4 xu[C];
-#pragma unroll
-  for (int c = 0; c < C; ++c) xu[c] = xr[c * 32 + lane];
   if (p.y != nullptr) {
     const uint4* yr = reinterpret_cast<const uint4*>(p.y + static_cast<long long>(row) * p.ldy);
     uint4 yu[C];
@@ -373,7 +390,7 @@ __global__ void __launch_bounds__(kWarpRowThreads) k_resid_ln_quant_warp(ResLnPa
       unpack8(yu[c], yv);
       if (p.gate != nullptr) {
         float g[8];
-        unpack8(reinterpret_cast<const uint4*>(p.gate)[c * 32 + lane], g);
+        unpack8(vecs[c * 32 + lane], g);
 #pragma unroll
         for (int e = 0; e < 8; ++e) yv[e] = __fmul_rn(g[e], yv[e]);
         round8(yv);
@@ -416,12 +433,12 @@ __global__ void __launch_bounds__(kWarpRowThreads) k_resid_ln_quant_warp(ResLnPa
     unpack8(xu[c], v);
     float w[8], b[8], s1[8], sh[8];
     if (p.ln_w != nullptr) {
-      unpack8(reinterpret_cast<const uint4*>(p.ln_w)[j], w);
-      unpack8(reinterpret_cast<const uint4*>(p.ln_b)[j], b);
+      unpack8(vecs[1 * C * 32 + j], w);
+      unpack8(vecs[2 * C * 32 + j], b);
     }
     if (p.mod_scale1 != nullptr) {
-      unpack8(reinterpret_cast<const uint4*>(p.mod_scale1)[j], s1);
-      unpack8(reinterpret_cast<const uint4*>(p.mod_shift)[j], sh);
+      unpack8(vecs[3 * C * 32 + j], s1);
+      unpack8(vecs[4 * C * 32 + j], sh);
     }
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -457,18 +474,38 @@ __global__ void __launch_bounds__(kWarpRowThreads) k_resid_ln_quant_warp(ResLnPa
   }
 }
 
+// The RMSNorm weight is staged in shared memory once per CTA; when a head's
+// pair count divides 128 every chunk of a lane covers the same pairs of its
+// head, so the row's (cos, sin) for them are loaded once.  Dynamic shared
+// memory: A bf16.
 template <int C>
 __global__ void __launch_bounds__(kWarpRowThreads) k_rms_rope_warp(RmsRopeParams p) {
+  extern __shared__ __align__(16) uint4 wsm[];  // [C * 32] RMSNorm weight of this part
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (kWarpRowThreads / 32) + (threadIdx.x >> 5);
   const int part = blockIdx.y;
-  if (row >= p.M) return;
-  const uint4* ir = reinterpret_cast<const uint4*>((part ? p.in[1] : p.in[0]) + static_cast<long long>(row) * p.ld_in);
-  uint4* orow = reinterpret_cast<uint4*>((part ? p.out[1] : p.out[0]) + static_cast<long long>(row) * p.ld_out);
-  const uint4* wp = reinterpret_cast<const uint4*>(part ? p.w[1] : p.w[0]);
+  {
+    const uint4* wsrc = reinterpret_cast<const uint4*>(part ? p.w[1] : p.w[0]);
+    for (int i = threadIdx.x; i < C * 32; i += kWarpRowThreads) wsm[i] = __ldg(wsrc + i);
+  }
   uint4 u[C];
+  const bool rope_fixed = p.rope != nullptr && (128 % p.pairs_per_head) == 0;
+  float4 cs_fixed[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  if (row < p.M) {
+    const uint4* ir = reinterpret_cast<const uint4*>((part ? p.in[1] : p.in[0]) + static_cast<long long>(row) * p.ld_in);
 #pragma unroll
-  for (int c = 0; c < C; ++c) u[c] = ir[c * 32 + lane];
+    for (int c = 0; c < C; ++c) u[c] = ir[c * 32 + lane];
+    if (rope_fixed) {
+      const float4* tab = reinterpret_cast<const float4*>(
+          p.rope + (static_cast<long long>(row) * p.pairs_per_head + (lane * 4) % p.pairs_per_head) * 2);
+      cs_fixed[0] = tab[0];
+      cs_fixed[1] = tab[1];
+    }
+  }
+  __syncthreads();
+  if (row >= p.M) return;
+  uint4* orow = reinterpret_cast<uint4*>((part ? p.out[1] : p.out[0]) + static_cast<long long>(row) * p.ld_out);
+  const uint4* wp = wsm;
   float sq = 0.f;
 #pragma unroll
   for (int c = 0; c < C; ++c) {
@@ -496,7 +533,7 @@ __global__ void __launch_bounds__(kWarpRowThreads) k_rms_rope_warp(RmsRopeParams
           p.rope + (static_cast<long long>(row) * p.pairs_per_head + pair0) * 2);
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        const float4 cs = tab[i];
+        const float4 cs = rope_fixed ? cs_fixed[i] : tab[i];
         const float e0 = v[4 * i], o0 = v[4 * i + 1], e1 = v[4 * i + 2], o1 = v[4 * i + 3];
         v[4 * i] = __fsub_rn(__fmul_rn(e0, cs.x), __fmul_rn(o0, cs.y));
         v[4 * i + 1] = __fadd_rn(__fmul_rn(e0, cs.y), __fmul_rn(o0, cs.x));

@@ -848,10 +848,10 @@ int qi_b200_resid_ln_quant(void* x_bf16, const void* y_bf16, long long ldy, cons
   p.eps = eps;
   const int wgrid = (M + kWarpRowThreads / 32 - 1) / (kWarpRowThreads / 32);
   switch (D) {  // warp per row where the row splits into whole 256-element slices
-    case 1024: k_resid_ln_quant_warp<4><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
-    case 2048: k_resid_ln_quant_warp<8><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
-    case 3072: k_resid_ln_quant_warp<12><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
-    case 4096: k_resid_ln_quant_warp<16><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
+    case 1024: k_resid_ln_quant_warp<4><<<wgrid, kWarpRowThreads, 5 * 1024 * 2, stream>>>(p); break;
+    case 2048: k_resid_ln_quant_warp<8><<<wgrid, kWarpRowThreads, 5 * 2048 * 2, stream>>>(p); break;
+    case 3072: k_resid_ln_quant_warp<12><<<wgrid, kWarpRowThreads, 5 * 3072 * 2, stream>>>(p); break;
+    case 4096: k_resid_ln_quant_warp<16><<<wgrid, kWarpRowThreads, 5 * 4096 * 2, stream>>>(p); break;
     default: k_resid_ln_quant<1><<<M, row_threads(D), 0, stream>>>(p);
   }
   count_launches(1);
@@ -889,10 +889,10 @@ int qi_b200_rms_rope(const void* in0, const void* in1, long long ld_in, void* ou
   p.eps = eps;
   const dim3 wgrid((M + kWarpRowThreads / 32 - 1) / (kWarpRowThreads / 32), nparts);
   switch (A) {
-    case 1024: k_rms_rope_warp<4><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
-    case 2048: k_rms_rope_warp<8><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
-    case 3072: k_rms_rope_warp<12><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
-    case 4096: k_rms_rope_warp<16><<<wgrid, kWarpRowThreads, 0, stream>>>(p); break;
+    case 1024: k_rms_rope_warp<4><<<wgrid, kWarpRowThreads, 1024 * 2, stream>>>(p); break;
+    case 2048: k_rms_rope_warp<8><<<wgrid, kWarpRowThreads, 2048 * 2, stream>>>(p); break;
+    case 3072: k_rms_rope_warp<12><<<wgrid, kWarpRowThreads, 3072 * 2, stream>>>(p); break;
+    case 4096: k_rms_rope_warp<16><<<wgrid, kWarpRowThreads, 4096 * 2, stream>>>(p); break;
     default: k_rms_rope<1><<<dim3(M, nparts), row_threads(A), 0, stream>>>(p);
   }
   count_launches(1);
