@@ -65,10 +65,11 @@ int qi_b200_device_status(unsigned int* out4, int clear);
 
 /* Launch plan of the calling thread's most recent GEMM launch, for
  * diagnostics: out6 = {kernel (1 int8, 2 fp8, 3 bf16, 4 nvfp4, 5 w4a16 tiles,
- * 6 w4a16 split-K clusters, 7 w4a16 small-M weight streaming, 8/9/10/11
- * int8 / fp8 / bf16 / nvfp4 CTA-pair tiles), grid, cluster size (K splits for kernels 1-3
- * under qi_b200_gemm_splitk), tile N (or padded M for kernel 6, M for kernel
- * 7), pipeline stages, dynamic shared memory bytes}. */
+ * 6 w4a16 split-K clusters, 7 w4a16 small-M, 8/9/10/11 int8 / fp8 / bf16 /
+ * nvfp4 CTA-pair tiles, 12/13/14 int8 / fp8 / bf16 cluster split-K), grid,
+ * cluster size (K splits for kernels 1-3 under qi_b200_gemm_splitk), tile N
+ * (or padded M for kernel 6, M for kernel 7), pipeline stages, dynamic shared
+ * memory bytes}. */
 int qi_b200_last_launch(int* out6);
 
 /* Number of kernels this library has launched in this process, counting
@@ -117,6 +118,18 @@ int qi_b200_int8_epilogue(const void* acc_int32, const float* act_scale, const f
  * the reference's shapes (M = 512, N = K = 3072: 21.2 us at 2 splits against
  * 13.6 us unsplit). */
 int qi_b200_gemm_splitk_plan(int kind, int M, int N, int K, int* splits, size_t* workspace_bytes);
+
+/* qi_b200_gemm split over K inside a thread-block cluster: `splits` (2..8)
+ * CTAs share one 128 x tile_n output tile (tile_n 128, 192 or 256), each
+ * over a contiguous range of K; the partial tiles are added in rank order
+ * through distributed shared memory (int32 exactly for INT8, so INT8 outputs
+ * are bit-identical to qi_b200_gemm) and each rank runs the fused epilogue on
+ * a share of the tile's columns.  No workspace.  tile_n = 0 / splits = 0 pick
+ * the plan that puts the most CTAs to work (QI_B200_ESHAPE when the tiles
+ * already fill half the SMs). */
+int qi_b200_gemm_csk(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
+                     const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd, int M, int N,
+                     int K, int flags, int tile_n, int splits, cudaStream_t stream);
 int qi_b200_gemm_splitk(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
                         const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd, int M,
                         int N, int K, int flags, int splits, void* workspace, size_t workspace_bytes,

@@ -57,6 +57,7 @@ SIGNATURES = {
     "qi_b200_peer_barrier": [_P, _I, _I, _P],
     "qi_b200_copy_async": [_P, _P, ctypes.c_size_t, _P],
     "qi_b200_gemm_splitk_plan": [_I, _I, _I, _I, _P, _P],
+    "qi_b200_gemm_csk": [_I, _P, _P, _P, _I, _P, _I, _P, _P, _LL, _I, _I, _I, _I, _I, _I, _P],
     "qi_b200_gemm_splitk": [_I, _P, _P, _P, _I, _P, _I, _P, _P, _LL, _I, _I, _I, _I, _I, _P, ctypes.c_size_t, _P],
     "qi_b200_gemm_gather": [_I, _P, _P, _P, _I, _P, _I, _P, _P, _I, _LL, _I, _I, _I, _I, _P],
     "qi_b200_resid_ln_quant": [_P, _P, _LL, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _P],
@@ -132,7 +133,7 @@ def last_launch() -> dict:
     check("qi_b200_last_launch", load().qi_b200_last_launch(ctypes.cast(buf, _P)))
     names = {1: "gemm_int8", 2: "gemm_fp8", 3: "gemm_bf16", 4: "gemm_nvfp4", 5: "w4a16_tiles", 6: "w4a16_splitk",
              7: "w4a16_small", 8: "gemm_int8_pair", 9: "gemm_fp8_pair", 10: "gemm_bf16_pair",
-             11: "gemm_nvfp4_pair"}
+             11: "gemm_nvfp4_pair", 12: "gemm_int8_csk", 13: "gemm_fp8_csk", 14: "gemm_bf16_csk"}
     v = list(buf)
     return {"kernel": names.get(v[0], "none"), "grid": v[1], "cluster": v[2], "tile_n": v[3], "stages": v[4],
             "smem": v[5]}

@@ -20,6 +20,8 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 
+#include "launch_count.cuh"
+
 namespace qib {
 
 // One thread per 8-element chunk of a row: blockDim = D/8 rounded up to a
@@ -134,6 +136,8 @@ __device__ __forceinline__ uint2 quant8(const float (&v)[8], float inv) {
 // a CTA keeps R times the bytes in flight per synchronization.
 template <int R>
 __global__ void __launch_bounds__(kRowMaxThreads) k_resid_ln_quant(ResLnParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float red[R * (kRowMaxThreads / 32)];
   const int row0 = blockIdx.x * R;
   const int j = threadIdx.x;                 // this thread's 8-element chunk of each row
@@ -273,6 +277,8 @@ struct RmsRopeParams {
 // (e c - o s, e s + o c) in fp32 (wan_video_dit.py:55-61).
 template <int R>
 __global__ void __launch_bounds__(kRowMaxThreads) k_rms_rope(RmsRopeParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float red[R * (kRowMaxThreads / 32)];
   const int row0 = blockIdx.x * R;
   const int part = blockIdx.y;
@@ -358,6 +364,8 @@ constexpr int kWarpRowThreads = 128;
 // Dynamic shared memory: 5 * D bf16.
 template <int C>
 __global__ void __launch_bounds__(kWarpRowThreads) k_resid_ln_quant_warp(ResLnParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
   extern __shared__ __align__(16) uint4 vecs[];  // [5][C * 32]: gate, ln_w, ln_b, scale1, shift
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (kWarpRowThreads / 32) + (threadIdx.x >> 5);
@@ -480,6 +488,8 @@ __global__ void __launch_bounds__(kWarpRowThreads) k_resid_ln_quant_warp(ResLnPa
 // memory: A bf16.
 template <int C>
 __global__ void __launch_bounds__(kWarpRowThreads) k_rms_rope_warp(RmsRopeParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
   extern __shared__ __align__(16) uint4 wsm[];  // [C * 32] RMSNorm weight of this part
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (kWarpRowThreads / 32) + (threadIdx.x >> 5);

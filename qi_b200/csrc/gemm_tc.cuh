@@ -330,6 +330,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
 
   const int m_tiles = (p.M + C::BM - 1) / C::BM;
   const int n_tiles = (p.N + BN - 1) / BN;
@@ -492,6 +494,195 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
   if (warp == 1) {
     __syncwarp();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Split-K over a thread-block cluster, for problems whose output tiles cannot
+// fill the SMs (48 tiles of 128 x 256 for 148 SMs).  The S
+// CTAs of a cluster share one output tile and split its K blocks.  Each
+// CTA's MMAs accumulate its K range in TMEM; the epilogue warps copy the raw
+// accumulator into shared memory (the pipeline stages are free by then);
+// after a cluster barrier each CTA finishes the 32-column chunks j with
+// j % S == its rank: it adds the S partial chunks in rank order (its own
+// from shared memory, the others over distributed shared memory; int32
+// exactly for INT8) and runs the fused epilogue on the sum.  A second cluster
+// barrier keeps every CTA's buffer alive until all ranks have read it.
+// One tile per cluster: grid = tiles x S.
+// ---------------------------------------------------------------------------
+template <MmaKind KIND, int BN, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+k_gemm_csk(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const EpiParams p) {
+  using C = GemmCfg<KIND, BN, STAGES>;
+  static_assert(!C::NVF4, "block-scaled split-K is not built");
+  constexpr int RED_LD = BN + 4;  // 32-bit words per staged row (16-byte pad: conflict-free row accesses)
+  static_assert(128 * RED_LD * 4 <= STAGES * C::STAGE_BYTES, "reduction buffer fits in the pipeline stages");
+  constexpr int TMEM_COLS = BN <= 128 ? 128 : 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint32_t* red = reinterpret_cast<uint32_t*>(smem);  // after the tile's MMAs: [128][RED_LD] raw accumulators
+  float* col_scale = reinterpret_cast<float*>(sB + STAGES * C::B_BYTES);
+  __nv_bfloat16* col_bias = reinterpret_cast<__nv_bfloat16*>(col_scale + BN);
+  uint64_t* full = reinterpret_cast<uint64_t*>(col_bias + BN);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* drain = tfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  constexpr unsigned int kTag = 0x400u + static_cast<unsigned int>(KIND) * 16u;
+  const int S = static_cast<int>(cluster_nctarank());
+  const int sk = static_cast<int>(cluster_ctarank());
+  const int m_tiles = (p.M + C::BM - 1) / C::BM;
+  const int tile = blockIdx.x / S;
+  const int mb = tile % m_tiles, nb = tile / m_tiles;
+  const int k_blocks = (p.K + C::BK - 1) / C::BK;
+  const int kb_per = (k_blocks + S - 1) / S;
+  const int kb0 = sk * kb_per, kb1 = min(k_blocks, kb0 + kb_per);  // the host makes every range non-empty
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&tmA);
+    tma_prefetch_map(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer: this CTA's K blocks ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kTag, 1)) { ok = false; break; }
+        mbar_expect_tx(&full[stage], C::STAGE_BYTES);
+        tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * C::BK, mb * C::BM);
+        tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * C::BK, nb * BN);
+        ++issued;
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok) {
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          if (--s < 0) { s = STAGES - 1; ph ^= 1u; }
+          mbar_wait_drain(&full[s], ph);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag, kTag, 3)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
+        const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk)
+          mma_issue<KIND>(tmem_base, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32), C::IDESC,
+                          (kb != kb0 || kk != 0) ? 1u : 0u);
+        tc_commit(&empty[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+      if (ok) tc_commit(tfull);
+      else {
+        tc_commit(drain);
+        mbar_wait_drain(drain, 0);
+      }
+    }
+  }
+  const int et = threadIdx.x - kFirstEpiWarp * 32;
+  const int wq = warp & 3;
+  const int half = (warp - kFirstEpiWarp) >> 2;
+  constexpr int COLS = BN / 2;
+  const int row = wq * 32 + lane;
+  const int m = mb * C::BM + row;
+  float sa = 1.0f;
+  if (warp >= kFirstEpiWarp) {
+    // column scales / bias of the tile; raw accumulators -> shared memory
+    for (int j = et; j < BN; j += kEpiThreads) {
+      const int n = nb * BN + j;
+      float sv = 1.0f;
+      if (p.sb != nullptr) sv = (n < p.N) ? __ldg(p.sb + static_cast<long long>(n) * p.sb_stride) : 0.0f;
+      col_scale[j] = sv;
+      col_bias[j] = (p.bias != nullptr && n < p.N) ? p.bias[n] : __float2bfloat16_rn(0.0f);
+    }
+    if (p.sa != nullptr && m < p.M) sa = __ldg(p.sa + static_cast<long long>(m) * p.sa_stride);
+    ok = mbar_wait(tfull, 0, abort_flag, kTag, 4);
+    tc_fence_after();
+    if (ok) {
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + static_cast<uint32_t>(half * COLS);
+#pragma unroll 1
+      for (int c = 0; c < COLS; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c, r);
+        tmem_ld_wait();
+        uint4* dst = reinterpret_cast<uint4*>(red + row * RED_LD + half * COLS + c);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) dst[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();  // every CTA's partial tile is in its shared memory; column parameters staged
+  if (warp >= kFirstEpiWarp) {
+#pragma unroll 1
+    for (int c = 0; c < COLS; c += 32) {
+      const int j0 = half * COLS + c;  // column of the tile
+      if (((j0 >> 5) % S) != sk) continue;
+      const int n0 = nb * BN + j0;
+      if (n0 >= p.N || m >= p.M) continue;
+      uint32_t acc[32];
+      const uint32_t loc = smem_u32(red + row * RED_LD + j0);
+#pragma unroll 1
+      for (int r = 0; r < S; ++r) {
+        const uint32_t base = map_shared_rank(loc, static_cast<uint32_t>(r));
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint4 v = ld_shared_cluster_v4(base + 16u * q);
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (r == 0) acc[4 * q + e] = w[e];
+            else if constexpr (KIND == MmaKind::I8)
+              acc[4 * q + e] = static_cast<uint32_t>(static_cast<int>(acc[4 * q + e]) + static_cast<int>(w[e]));
+            else
+              acc[4 * q + e] = __float_as_uint(__fadd_rn(__uint_as_float(acc[4 * q + e]), __uint_as_float(w[e])));
+          }
+        }
+      }
+      epilogue_chunk<KIND>(acc, p, m, n0, sa, col_scale + j0, col_bias + j0);
+    }
+  }
+  cluster_sync_all();  // no CTA frees its buffer while another rank may still read it
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 

@@ -167,6 +167,8 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
   cluster_sync_all();  // both CTAs' barriers exist before any remote arrive / complete_tx
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
 
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;

@@ -542,6 +542,8 @@ __device__ __forceinline__ uint32_t dequant_pair(uint32_t w, int t, float s16x, 
 // HBM-bound: K/2 + 2K bytes per row (+ scales).  group % 32 == 0, K % 32 == 0.
 __global__ void __launch_bounds__(256)
 k_w4a16_dequant(W4Params q, __nv_bfloat16* __restrict__ out, int N, int K) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int qpr = q.kw / 4;  // word quads per row
   const int quads = N * qpr;  // the host keeps N * K / 32 < 2^31
   for (int i = blockIdx.x * 256 + threadIdx.x; i < quads; i += 256 * gridDim.x) {
@@ -630,6 +632,8 @@ template <int NT, int KS>
 __global__ void __launch_bounds__(w4s::kThreads)
 k_gemm_w4a16_small(const __nv_bfloat16* __restrict__ X, EpiParams p, W4Params q) {
   constexpr int RB = 8 * NT, KP = w4s::kWarps / NT;
+  griddep_wait();
+  griddep_launch_dependents();
   extern __shared__ __align__(128) uint8_t sm[];
   const W4sLayout L = w4s_layout(NT, KS, p.M, p.K, q.G, q.zw, q.group);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm);

@@ -107,7 +107,8 @@ struct LaunchPlan {
 static thread_local LaunchPlan g_last_plan = {0, 0, 0, 0, 0, 0};
 enum PlanKernel { kPlanGemmI8 = 1, kPlanGemmF8 = 2, kPlanGemmBF16 = 3, kPlanGemmNVF4 = 4, kPlanW4Tile = 5,
                   kPlanW4Skinny = 6, kPlanW4Small = 7,
-                  kPlanGemmPair = 8 /* + kind: 8 int8, 9 fp8, 10 bf16 */ };
+                  kPlanGemmPair = 8 /* + kind: 8 int8, 9 fp8, 10 bf16, 11 nvfp4 */,
+                  kPlanGemmCsk = 12 /* + kind: 12 int8, 13 fp8, 14 bf16 */ };
 
 // ---------------------------------------------------------------------------
 // GEMM launch
@@ -135,9 +136,10 @@ static int launch_gemm_cfg(const void* A, const void* B, const EpiParams& p, int
   const int tiles = ((p.M + C::BM - 1) / C::BM) * ((p.N + BN - 1) / BN) * (p.ksplit > 1 ? p.ksplit : 1);
   const int grid = tiles < num_sms ? tiles : num_sms;
   g_last_plan = {1 + static_cast<int>(KIND), grid, p.ksplit > 1 ? p.ksplit : 1, BN, STAGES, C::SMEM_BYTES};
-  k_gemm_tc<KIND, BN, STAGES><<<grid, kGemmThreads, C::SMEM_BYTES, stream>>>(ta, tb, p);
+  const cudaError_t e =
+      launch_pdl(k_gemm_tc<KIND, BN, STAGES>, dim3(grid), dim3(kGemmThreads), C::SMEM_BYTES, stream, 1, ta, tb, p);
   count_launches(1);
-  return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+  return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
 // CTA-pair kernel (cta_group::2): 256 x BN tiles over clusters of 2 CTAs.
@@ -177,22 +179,90 @@ static int launch_gemm2_cfg(const void* A, const void* B, const EpiParams& p, in
   }
   const int tiles = ((p.M + 255) / 256) * ((p.N + BN - 1) / BN);
   const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
+  g_last_plan = {kPlanGemmPair + static_cast<int>(KIND), 2 * pairs, 2, BN, STAGES, C::SMEM_BYTES};
+  const cudaError_t e = launch_pdl(k_gemm_tc2<KIND, BN, STAGES, GATHER>, dim3(2 * pairs), dim3(C::THREADS),
+                                   C::SMEM_BYTES, stream, 2, ta, tb, tsa, tsb, p, om);
+  count_launches(1);
+  return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+// Cluster split-K (k_gemm_csk): S CTAs of a cluster share one 128 x BN tile.
+template <MmaKind KIND, int BN, int STAGES>
+static int launch_gemm_csk_cfg(const void* A, const void* B, const EpiParams& p, int S, cudaStream_t stream) {
+  using C = GemmCfg<KIND, BN, STAGES>;
+  const CUtensorMapDataType dt =
+      (KIND == MmaKind::BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const uint64_t ku = (uint64_t)p.K;
+  const int k_blocks = (p.K + C::BK - 1) / C::BK;
+  const int kbp = (k_blocks + S - 1) / S;
+  if (S < 2 || S > 8 || (long long)kbp * (S - 1) >= k_blocks) return QI_B200_ESHAPE;  // a rank without K blocks
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A, dt, ku, (uint64_t)p.M, ku * C::ELEM, C::BK, C::BM);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, B, dt, ku, (uint64_t)p.N, ku * C::ELEM, C::BK, BN);
+  if (rc) return rc;
+  static bool attr_done[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev]) {
+    if (cudaFuncSetAttribute(k_gemm_csk<KIND, BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::SMEM_BYTES) != cudaSuccess)
+      return QI_B200_ECUDA;
+    attr_done[dev] = true;
+  }
+  const int tiles = ((p.M + C::BM - 1) / C::BM) * ((p.N + BN - 1) / BN);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.x = S;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(C::THREADS, 1, 1);
+  cfg.gridDim = dim3(tiles * S, 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  g_last_plan = {kPlanGemmPair + static_cast<int>(KIND), 2 * pairs, 2, BN, STAGES, C::SMEM_BYTES};
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_tc2<KIND, BN, STAGES, GATHER>, ta, tb, tsa, tsb, p, om);
+  g_last_plan = {kPlanGemmCsk + static_cast<int>(KIND), tiles * S, S, BN, STAGES, C::SMEM_BYTES};
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_csk<KIND, BN, STAGES>, ta, tb, p);
   count_launches(1);
   return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+template <MmaKind KIND>
+static int launch_gemm_csk(const void* A, const void* B, const EpiParams& p, int bn, int S, cudaStream_t stream) {
+  switch (bn) {
+    case 256: return launch_gemm_csk_cfg<KIND, 256, 4>(A, B, p, S, stream);
+    case 192: return launch_gemm_csk_cfg<KIND, 192, 5>(A, B, p, S, stream);
+    case 128: return launch_gemm_csk_cfg<KIND, 128, 6>(A, B, p, S, stream);
+    default: return QI_B200_EINVAL;
+  }
+}
+
+// The cluster split-K plan for a problem whose tiles leave most SMs idle:
+// the tile width and cluster size (2..4, >= 4 K blocks per rank) that put the
+// most CTAs to work; {0, 1} when the tiles already fill half the SMs.
+static void csk_plan(int kind, int M, int N, int K, int num_sms, int* bn_out, int* s_out) {
+  *bn_out = 0;
+  *s_out = 1;
+  if (kind < 0 || kind > 2) return;
+  const int bk = kind == QI_B200_KIND_BF16 ? 64 : 128;
+  const int k_blocks = (K + bk - 1) / bk;
+  int best = 0;
+  for (int bn : {256, 192, 128}) {
+    const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+    if (tiles * 2 > num_sms) continue;
+    int S = std::min(4, std::min(num_sms / tiles, k_blocks / 4));
+    if (S < 2) continue;
+    const int kbp = (k_blocks + S - 1) / S;
+    S = (k_blocks + kbp - 1) / kbp;  // every rank gets >= 1 K block
+    if (S < 2) continue;
+    if (tiles * S > best) {
+      best = tiles * S;
+      *bn_out = bn;
+      *s_out = S;
+    }
+  }
 }
 
 // Column-tile width: minimise (tiles per CTA) x (BN + fixed per-tile cost).
@@ -234,6 +304,18 @@ static int launch_gemm(const void* A, const void* B, const EpiParams& p, cudaStr
         case 192: return launch_gemm2_cfg<KIND, 192, 7>(A, B, p, di->num_sms, stream);
         case 128: return launch_gemm2_cfg<KIND, 128, 8>(A, B, p, di->num_sms, stream);
         default: return QI_B200_EINVAL;
+      }
+    }
+    if (force_bn == 0 && p.ksplit <= 1) {
+      // very few tiles over a long K (e.g. the DiT action expert's FFN-down,
+      // M = 32, N = 1024, K = 4096: 12.5 -> 8.8 us): split K inside clusters
+      const int bk = KIND == MmaKind::BF16 ? 64 : 128;
+      const int k_blocks = (p.K + bk - 1) / bk;
+      const int tiles128 = ((p.M + 127) / 128) * ((p.N + 127) / 128);
+      if (tiles128 <= 16 && k_blocks >= 32) {
+        int cbn, cs;
+        csk_plan(static_cast<int>(KIND), p.M, p.N, p.K, di->num_sms, &cbn, &cs);
+        if (cbn != 0) return launch_gemm_csk<KIND>(A, B, p, cbn, cs, stream);
       }
     }
     const int bn = force_bn > 0 ? force_bn : pick_bn(p.M, p.N, di->num_sms);
@@ -509,6 +591,41 @@ extern "C" int qi_b200_gemm_splitk(int kind, const void* A, const void* B, const
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
+extern "C" int qi_b200_gemm_csk(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
+                                const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd,
+                                int M, int N, int K, int flags, int tile_n, int splits, cudaStream_t stream) {
+  int rc = check_gemm_args(kind, A, B, a_scale, a_scale_stride, b_scale, b_scale_stride, bias, D, ldd, M, N, K,
+                           flags);
+  if (rc) return rc;
+  DeviceInfo* di = nullptr;
+  rc = device_info(&di);
+  if (rc) return rc;
+  if (tile_n == 0 || splits == 0) {
+    int bn, S;
+    csk_plan(kind, M, N, K, di->num_sms, &bn, &S);
+    if (bn == 0) return QI_B200_ESHAPE;
+    if (tile_n == 0) tile_n = bn;
+    if (splits == 0) splits = S;
+  }
+  EpiParams p{};
+  p.sa = a_scale;
+  p.sa_stride = a_scale_stride;
+  p.sb = b_scale;
+  p.sb_stride = b_scale_stride;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.D = D;
+  p.ldd = ldd;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.flags = flags;
+  switch (kind) {
+    case QI_B200_KIND_INT8: return launch_gemm_csk<MmaKind::I8>(A, B, p, tile_n, splits, stream);
+    case QI_B200_KIND_FP8_E4M3: return launch_gemm_csk<MmaKind::F8>(A, B, p, tile_n, splits, stream);
+    default: return launch_gemm_csk<MmaKind::BF16>(A, B, p, tile_n, splits, stream);
+  }
+}
+
 extern "C" int qi_b200_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
   if (bytes == 0) return QI_B200_OK;
   if (dst == nullptr || src == nullptr) return QI_B200_EINVAL;
@@ -543,15 +660,18 @@ static int nvfp4_quantize(const void* x, int rows, int cols, int g_mode, const f
     if (cudaMemsetAsync(ws_amax, 0, sizeof(unsigned int), stream) != cudaSuccess) return QI_B200_ECUDA;
     const long long n = (long long)rows * cols;
     const int g2 = (int)std::min<long long>((n / 8 + 255) / 256 + 1, (long long)di->num_sms * 8);
-    k_amax_bf16<<<g2, 256, 0, stream>>>(xb, n, ws_amax);
-    k_quant_nvfp4_tensor<1><<<grid_flat, 256, 0, stream>>>(xb, rows, cols, nullptr, ws_amax, g_out, qb, sb, ka);
+    launch_pdl(k_amax_bf16, dim3(g2), dim3(256), 0, stream, 1, xb, n, ws_amax);
+    launch_pdl(k_quant_nvfp4_tensor<1>, dim3(grid_flat), dim3(256), 0, stream, 1, xb, rows, cols,
+               static_cast<const float*>(nullptr), static_cast<const unsigned int*>(ws_amax), g_out, qb, sb, ka);
     count_launches(2);
   } else if (g_mode == 0) {
-    k_quant_nvfp4_tensor<0><<<grid_flat, 256, 0, stream>>>(xb, rows, cols, g_in, nullptr, nullptr, qb, sb, ka);
+    launch_pdl(k_quant_nvfp4_tensor<0>, dim3(grid_flat), dim3(256), 0, stream, 1, xb, rows, cols, g_in,
+               static_cast<const unsigned int*>(nullptr), static_cast<float*>(nullptr), qb, sb, ka);
     count_launches(1);
   } else {
     const int g3 = std::min(rows_pad, di->num_sms * 8);
-    k_quant_nvfp4<2><<<g3, 256, 0, stream>>>(xb, rows, cols, nullptr, nullptr, g_out, qb, sb, ka);
+    launch_pdl(k_quant_nvfp4<2>, dim3(g3), dim3(256), 0, stream, 1, xb, rows, cols, static_cast<const float*>(nullptr),
+               static_cast<const unsigned int*>(nullptr), g_out, qb, sb, ka);
     count_launches(1);
   }
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
@@ -667,21 +787,9 @@ static int launch_w4_small(const void* X, const EpiParams& p, const W4Params& q,
     attr_done[dev] = true;
   }
   const int blocks = (p.N + 8 * NT - 1) / (8 * NT);
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = KS;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(blocks * KS, 1, 1);
-  cfg.blockDim = dim3(w4s::kThreads, 1, 1);
-  cfg.dynamicSmemBytes = L.total;
-  cfg.stream = stream;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   g_last_plan = {kPlanW4Small, blocks * KS, KS, p.M, 0, L.total};
-  const cudaError_t e =
-      cudaLaunchKernelEx(&cfg, k_gemm_w4a16_small<NT, KS>, static_cast<const __nv_bfloat16*>(X), p, q);
+  const cudaError_t e = launch_pdl(k_gemm_w4a16_small<NT, KS>, dim3(blocks * KS), dim3(w4s::kThreads), L.total,
+                                   stream, KS, static_cast<const __nv_bfloat16*>(X), p, q);
   count_launches(1);
   return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
@@ -848,11 +956,11 @@ int qi_b200_resid_ln_quant(void* x_bf16, const void* y_bf16, long long ldy, cons
   p.eps = eps;
   const int wgrid = (M + kWarpRowThreads / 32 - 1) / (kWarpRowThreads / 32);
   switch (D) {  // warp per row where the row splits into whole 256-element slices
-    case 1024: k_resid_ln_quant_warp<4><<<wgrid, kWarpRowThreads, 5 * 1024 * 2, stream>>>(p); break;
-    case 2048: k_resid_ln_quant_warp<8><<<wgrid, kWarpRowThreads, 5 * 2048 * 2, stream>>>(p); break;
-    case 3072: k_resid_ln_quant_warp<12><<<wgrid, kWarpRowThreads, 5 * 3072 * 2, stream>>>(p); break;
-    case 4096: k_resid_ln_quant_warp<16><<<wgrid, kWarpRowThreads, 5 * 4096 * 2, stream>>>(p); break;
-    default: k_resid_ln_quant<1><<<M, row_threads(D), 0, stream>>>(p);
+    case 1024: launch_pdl(k_resid_ln_quant_warp<4>, dim3(wgrid), dim3(kWarpRowThreads), 5 * 1024 * 2, stream, 1, p); break;
+    case 2048: launch_pdl(k_resid_ln_quant_warp<8>, dim3(wgrid), dim3(kWarpRowThreads), 5 * 2048 * 2, stream, 1, p); break;
+    case 3072: launch_pdl(k_resid_ln_quant_warp<12>, dim3(wgrid), dim3(kWarpRowThreads), 5 * 3072 * 2, stream, 1, p); break;
+    case 4096: launch_pdl(k_resid_ln_quant_warp<16>, dim3(wgrid), dim3(kWarpRowThreads), 5 * 4096 * 2, stream, 1, p); break;
+    default: launch_pdl(k_resid_ln_quant<1>, dim3(M), dim3(row_threads(D)), 0, stream, 1, p);
   }
   count_launches(1);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
@@ -889,11 +997,11 @@ int qi_b200_rms_rope(const void* in0, const void* in1, long long ld_in, void* ou
   p.eps = eps;
   const dim3 wgrid((M + kWarpRowThreads / 32 - 1) / (kWarpRowThreads / 32), nparts);
   switch (A) {
-    case 1024: k_rms_rope_warp<4><<<wgrid, kWarpRowThreads, 1024 * 2, stream>>>(p); break;
-    case 2048: k_rms_rope_warp<8><<<wgrid, kWarpRowThreads, 2048 * 2, stream>>>(p); break;
-    case 3072: k_rms_rope_warp<12><<<wgrid, kWarpRowThreads, 3072 * 2, stream>>>(p); break;
-    case 4096: k_rms_rope_warp<16><<<wgrid, kWarpRowThreads, 4096 * 2, stream>>>(p); break;
-    default: k_rms_rope<1><<<dim3(M, nparts), row_threads(A), 0, stream>>>(p);
+    case 1024: launch_pdl(k_rms_rope_warp<4>, wgrid, dim3(kWarpRowThreads), 1024 * 2, stream, 1, p); break;
+    case 2048: launch_pdl(k_rms_rope_warp<8>, wgrid, dim3(kWarpRowThreads), 2048 * 2, stream, 1, p); break;
+    case 3072: launch_pdl(k_rms_rope_warp<12>, wgrid, dim3(kWarpRowThreads), 3072 * 2, stream, 1, p); break;
+    case 4096: launch_pdl(k_rms_rope_warp<16>, wgrid, dim3(kWarpRowThreads), 4096 * 2, stream, 1, p); break;
+    default: launch_pdl(k_rms_rope<1>, dim3(M, nparts), dim3(row_threads(A)), 0, stream, 1, p);
   }
   count_launches(1);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
@@ -991,7 +1099,7 @@ int qi_b200_w4a16_dequant(const void* qweight_packed, const void* scales_fp16, c
   q.kw = K / 8;
   const long long quads = (long long)N * (K / 32);
   const int grid = (int)std::min<long long>((quads + 255) / 256, (long long)di->num_sms * 16);
-  k_w4a16_dequant<<<grid, 256, 0, stream>>>(q, static_cast<__nv_bfloat16*>(out_bf16), N, K);
+  launch_pdl(k_w4a16_dequant, dim3(grid), dim3(256), 0, stream, 1, q, static_cast<__nv_bfloat16*>(out_bf16), N, K);
   count_launches(1);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }

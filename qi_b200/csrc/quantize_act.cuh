@@ -101,6 +101,8 @@ template <class Op, int TPR>
 __global__ void __launch_bounds__(kQuantThreads)
 k_rowquant_vec(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, float* __restrict__ scales,
                const float* __restrict__ static_scale, int rows, int cols) {
+  griddep_wait();
+  griddep_launch_dependents();
   constexpr int RPB = kQuantThreads / TPR;
   constexpr int WPR = TPR / 32;
   __shared__ float red[RPB][WPR];
@@ -153,6 +155,8 @@ template <class Op>
 __global__ void __launch_bounds__(kQuantThreads)
 k_rowquant_scalar(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, float* __restrict__ scales,
                   const float* __restrict__ static_scale, int rows, int cols) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int row = blockIdx.x * (kQuantThreads / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -183,29 +187,30 @@ inline cudaError_t launch_rowquant(const void* x, void* q, float* scales, const 
   const bool aligned = (cols % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(q) % 8 == 0);
   const int nvec = cols / 8;
+  const dim3 blk(kQuantThreads);
   if (aligned) {
     auto fits = [&](int tpr) { return (nvec + tpr - 1) / tpr <= kQuantMaxChunks; };
     if (fits(32)) {
       constexpr int RPB = kQuantThreads / 32;
-      k_rowquant_vec<Op, 32><<<(rows + RPB - 1) / RPB, kQuantThreads, 0, stream>>>(xb, qb, scales, static_scale,
-                                                                                     rows, cols);
+      launch_pdl(k_rowquant_vec<Op, 32>, dim3((rows + RPB - 1) / RPB), blk, 0, stream, 1, xb, qb, scales,
+                 static_scale, rows, cols);
     } else if (fits(64)) {
       constexpr int RPB = kQuantThreads / 64;
-      k_rowquant_vec<Op, 64><<<(rows + RPB - 1) / RPB, kQuantThreads, 0, stream>>>(xb, qb, scales, static_scale,
-                                                                                     rows, cols);
+      launch_pdl(k_rowquant_vec<Op, 64>, dim3((rows + RPB - 1) / RPB), blk, 0, stream, 1, xb, qb, scales,
+                 static_scale, rows, cols);
     } else if (fits(128)) {
       constexpr int RPB = kQuantThreads / 128;
-      k_rowquant_vec<Op, 128><<<(rows + RPB - 1) / RPB, kQuantThreads, 0, stream>>>(xb, qb, scales,
-                                                                                       static_scale, rows, cols);
+      launch_pdl(k_rowquant_vec<Op, 128>, dim3((rows + RPB - 1) / RPB), blk, 0, stream, 1, xb, qb, scales,
+                 static_scale, rows, cols);
     } else if (fits(256)) {
-      k_rowquant_vec<Op, 256><<<rows, kQuantThreads, 0, stream>>>(xb, qb, scales, static_scale, rows, cols);
+      launch_pdl(k_rowquant_vec<Op, 256>, dim3(rows), blk, 0, stream, 1, xb, qb, scales, static_scale, rows, cols);
     } else {
-      k_rowquant_scalar<Op><<<(rows + 7) / 8, kQuantThreads, 0, stream>>>(xb, qb, scales, static_scale, rows,
-                                                                          cols);
+      launch_pdl(k_rowquant_scalar<Op>, dim3((rows + 7) / 8), blk, 0, stream, 1, xb, qb, scales, static_scale, rows,
+                 cols);
     }
   } else {
-    k_rowquant_scalar<Op><<<(rows + 7) / 8, kQuantThreads, 0, stream>>>(xb, qb, scales, static_scale, rows,
-                                                                        cols);
+    launch_pdl(k_rowquant_scalar<Op>, dim3((rows + 7) / 8), blk, 0, stream, 1, xb, qb, scales, static_scale, rows,
+               cols);
   }
   count_launches(1);
   return cudaGetLastError();

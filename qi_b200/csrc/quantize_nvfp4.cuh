@@ -45,6 +45,8 @@ __device__ __forceinline__ long long sf_atom_offset(int row, int blk, int ka_per
 // amax of a whole bf16 tensor into *amax_bits (float bits; must start at 0)
 __global__ void __launch_bounds__(256)
 k_amax_bf16(const __nv_bfloat16* __restrict__ x, long long n, unsigned int* __restrict__ amax_bits) {
+  griddep_wait();
+  griddep_launch_dependents();
   float m = 0.f;
   const long long nvec = n / 8;
   const uint4* xv = reinterpret_cast<const uint4*>(x);
@@ -164,6 +166,8 @@ __global__ void __launch_bounds__(256)
 k_quant_nvfp4_tensor(const __nv_bfloat16* __restrict__ x, int rows, int cols, const float* __restrict__ g_in,
                      const unsigned int* __restrict__ amax_bits, float* __restrict__ g_out, uint8_t* __restrict__ q,
                      uint8_t* __restrict__ sf, int ka_per_rowblock) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int bpr = cols >> 4;
   const int rows_pad = (rows + 127) & ~127;
   float g;
@@ -209,6 +213,8 @@ __global__ void __launch_bounds__(256)
 k_quant_nvfp4(const __nv_bfloat16* __restrict__ x, int rows, int cols, const float* __restrict__ g_in,
               const unsigned int* __restrict__ amax_bits, float* __restrict__ g_out, uint8_t* __restrict__ q,
               uint8_t* __restrict__ sf, int ka_per_rowblock) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int bpr = cols >> 4;  // blocks per row
   const int rows_pad = (rows + 127) & ~127;
   if (GMODE == 2) {

@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 
+#include "launch_count.cuh"
+
 #ifndef QI_WAIT_TIMEOUT_NS
 #define QI_WAIT_TIMEOUT_NS 2000000000ull  // 2 s
 #endif
@@ -290,6 +292,14 @@ __device__ __forceinline__ uint32_t map_shared_rank(uint32_t addr, uint32_t rank
 __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 ld_shared_cluster_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
   return v;
 }
 // Every thread of every CTA in the cluster must execute this (all code paths

@@ -275,3 +275,58 @@ def test_linears_capture_in_cuda_graph_and_replay():
     np.testing.assert_array_equal(bits(y8), O.int8_linear(bits(x2), qw, sw[:, 0], bits(b))[0])
     qa, sa = O.quantize_fp8_rowwise(O.bf16_to_f32(bits(x2)))
     assert O.rel_fro(O.bf16_to_f32(bits(yf)), O.bf16_to_f32(O.fp8_linear(qa, sa, fq, fs, bits(b), gelu=True))) <= 2e-3
+
+
+@pytest.mark.parametrize("M,N,Kd,tile_n,splits", [(512, 3072, 3072, 0, 0), (512, 3072, 3072, 256, 2),
+                                                   (100, 520, 2048, 128, 4), (32, 9216, 1024, 0, 0),
+                                                   (390, 3072, 3072, 192, 2), (1, 256, 4096, 256, 3)])
+@pytest.mark.parametrize("gelu", [False, True])
+def test_cluster_splitk_matches_unsplit(M, N, Kd, tile_n, splits, gelu):
+    """qi_b200_gemm_csk: S CTAs of a cluster split K and add their partial
+    tiles through distributed shared memory.  INT8 outputs are bit-identical
+    to the unsplit kernel (int32 sums); FP8 agrees to fp32 summation order."""
+    x, w, b = make_small_case(M, N, Kd, seed=M + 3 * N, outlier_frac=0.002)
+    qw, sw, _ = O.quantize_weight_rtn(w.numpy(), 8, -1, True)
+    qa, sa = K.quantize_int8_rowwise(x.to(DEV))
+    qwd, swd, bd = torch.from_numpy(qw).to(DEV), torch.from_numpy(sw[:, 0]).to(DEV), b.to(DEV)
+    st = torch.cuda.current_stream().cuda_stream
+    flags = _lib.EPI_GELU if gelu else 0
+
+    def csk(kind, a, bw, s_a, s_b):
+        y = torch.empty((M, N), dtype=torch.bfloat16, device=DEV)
+        _lib.call("qi_b200_gemm_csk", kind, a.data_ptr(), bw.data_ptr(), s_a.data_ptr(), 1, s_b.data_ptr(), 1,
+                  bd.data_ptr(), y.data_ptr(), N, M, N, Kd, flags, tile_n, splits, st)
+        return y
+
+    y = csk(_lib.KIND_INT8, qa, qwd, sa, swd)
+    plan = _lib.last_launch()
+    assert plan["kernel"] == "gemm_int8_csk" and plan["cluster"] >= 2, plan
+    y_ref = K.gemm(_lib.KIND_INT8, qa, qwd, sa, swd, bd, gelu=gelu, tile_n=128)
+    assert torch.equal(y, y_ref)
+    if not gelu:
+        yo, _, _, _ = O.int8_linear(bits(x), qw, sw[:, 0], bits(b))
+        np.testing.assert_array_equal(bits(y), yo)
+    qf, sf = K.quantize_fp8_rowwise(x.to(DEV))
+    wf = (w * 20).to(torch.float8_e4m3fn).view(torch.uint8).to(DEV)
+    wsf = torch.full((N,), 0.05, device=DEV)
+    f = csk(_lib.KIND_FP8_E4M3, qf, wf, sf, wsf)
+    f_ref = K.gemm(_lib.KIND_FP8_E4M3, qf, wf, sf, wsf, bd, gelu=gelu, tile_n=128)
+    assert O.rel_fro(f.float().cpu().numpy(), f_ref.float().cpu().numpy()) <= 2e-3
+
+
+def test_cluster_splitk_auto_for_few_tiles_long_k():
+    """qi_b200_gemm picks the cluster split-K kernel on its own for very few
+    tiles over a long K (the DiT action expert's FFN-down shape); INT8
+    outputs stay bit-identical to the unsplit kernel."""
+    M, N, Kd = 32, 1024, 4096
+    x, w, b = make_small_case(M, N, Kd, seed=77)
+    qw, sw, _ = O.quantize_weight_rtn(w.numpy(), 8, -1, True)
+    qa, sa = K.quantize_int8_rowwise(x.to(DEV))
+    qwd, swd, bd = torch.from_numpy(qw).to(DEV), torch.from_numpy(sw[:, 0]).to(DEV), b.to(DEV)
+    y = K.gemm(_lib.KIND_INT8, qa, qwd, sa, swd, bd)
+    assert _lib.last_launch()["kernel"] == "gemm_int8_csk"
+    y_ref = K.gemm(_lib.KIND_INT8, qa, qwd, sa, swd, bd, tile_n=128)
+    assert _lib.last_launch()["kernel"] == "gemm_int8"
+    assert torch.equal(y, y_ref)
+    yo, _, _, _ = O.int8_linear(bits(x), qw, sw[:, 0], bits(b))
+    np.testing.assert_array_equal(bits(K.int8_linear(x.to(DEV), qwd, swd, bd)), yo)
