@@ -116,6 +116,18 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// gelu_tanh_fast on two values with packed fp32x2 arithmetic: the same
+// operations in the same order (each rounds the same way), half the
+// instructions.
+__device__ __forceinline__ float2 gelu_tanh_fast2(float2 v) {
+  const float2 k0 = make_float2(0.7978845608028654f, 0.7978845608028654f);
+  const float2 k1 = make_float2(0.044715f, 0.044715f);
+  const float2 t = __fmul2_rn(__fmul2_rn(k1, v), v);
+  const float2 inner = __fmul2_rn(k0, __ffma2_rn(t, v, v));
+  const float2 one_th = __fadd2_rn(make_float2(1.0f, 1.0f), make_float2(tanh_hw(inner.x), tanh_hw(inner.y)));
+  return __fmul2_rn(__fmul2_rn(make_float2(0.5f, 0.5f), v), one_th);
+}
+
 // Standalone INT8 epilogue over raw int32 accumulators, used after a
 // cross-rank sum of K-sharded partial accumulators.  Same operation order as
 // the fused epilogue: bf16(((float)acc * sa[m]) * sb[n] + bias[n]), then GELU
@@ -221,47 +233,46 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], const Ep
     }
     return;
   }
-  float y[32];
+  // ((acc * sa) * sb + bias) -> bf16 -> GELU, on pairs of columns with packed
+  // fp32x2 operations (each element rounds exactly as with scalar ones)
+  float2 y[16];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    if constexpr (KIND == MmaKind::I8) y[j] = __int2float_rn(static_cast<int>(r[j]));
-    else y[j] = __uint_as_float(r[j]);
+  for (int j = 0; j < 16; ++j) {
+    if constexpr (KIND == MmaKind::I8)
+      y[j] = make_float2(__int2float_rn(static_cast<int>(r[2 * j])), __int2float_rn(static_cast<int>(r[2 * j + 1])));
+    else
+      y[j] = make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
   }
   if (KIND != MmaKind::BF16 || p.sa != nullptr) {
+    const float2 sa2 = make_float2(sa, sa);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) y[j] = __fmul_rn(y[j], sa);
+    for (int j = 0; j < 16; ++j) y[j] = __fmul2_rn(y[j], sa2);
   }
   if (p.sb != nullptr) {
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      const float4 s4 = *reinterpret_cast<const float4*>(sb_s + j);
-      y[j] = __fmul_rn(y[j], s4.x);
-      y[j + 1] = __fmul_rn(y[j + 1], s4.y);
-      y[j + 2] = __fmul_rn(y[j + 2], s4.z);
-      y[j + 3] = __fmul_rn(y[j + 3], s4.w);
+    for (int j = 0; j < 16; j += 2) {
+      const float4 s4 = *reinterpret_cast<const float4*>(sb_s + 2 * j);
+      y[j] = __fmul2_rn(y[j], make_float2(s4.x, s4.y));
+      y[j + 1] = __fmul2_rn(y[j + 1], make_float2(s4.z, s4.w));
     }
   }
   if (p.bias != nullptr) {
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      const uint4 b4 = *reinterpret_cast<const uint4*>(bias_s + j);
+    for (int j = 0; j < 16; j += 4) {
+      const uint4 b4 = *reinterpret_cast<const uint4*>(bias_s + 2 * j);
       const __nv_bfloat162* bh = reinterpret_cast<const __nv_bfloat162*>(&b4);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 bf = __bfloat1622float2(bh[i]);
-        y[j + 2 * i] = __fadd_rn(y[j + 2 * i], bf.x);
-        y[j + 2 * i + 1] = __fadd_rn(y[j + 2 * i + 1], bf.y);
-      }
+      for (int i = 0; i < 4; ++i) y[j + i] = __fadd2_rn(y[j + i], __bfloat1622float2(bh[i]));
     }
   }
   uint32_t packed[16];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) packed[j] = pack_bf16x2(y[2 * j], y[2 * j + 1]);
+  for (int j = 0; j < 16; ++j) packed[j] = pack_bf16x2(y[j].x, y[j].y);
   if (p.flags & kEpiGelu) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&packed[j]));
-      packed[j] = pack_bf16x2(gelu_tanh_fast(f.x), gelu_tanh_fast(f.y));
+      const float2 g = gelu_tanh_fast2(__bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&packed[j])));
+      packed[j] = pack_bf16x2(g.x, g.y);
     }
   }
   if (packed_out != nullptr) {  // the caller stores the bf16 row chunk itself
