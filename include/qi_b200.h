@@ -87,6 +87,12 @@ int qi_b200_quantize_int8_rowwise(const void* x_bf16, void* q_int8, float* scale
  * the reference): q = clamp(rint(x * (1/s[row])), -127, 127).  Used when a
  * row's K extent is split over ranks: the per-row scales are first reduced
  * with MAX across ranks, so every rank quantizes with the single-GPU scale. */
+/* qi_b200_quantize_int8_rowwise of x / input_scale, fused: the SmoothQuant /
+ * AWQ smoothing of Int8W8A8Backend.linear (int8_w8a8_ops.py:138-139), done
+ * in bf16 as there: x' = bf16(fp32(x) / fp32(bf16(input_scale[k]))).
+ * input_scale fp32 [cols]. */
+int qi_b200_quantize_int8_rowwise_smooth(const void* x_bf16, const float* input_scale, void* q_int8, float* scales,
+                                         int rows, int cols, cudaStream_t stream);
 int qi_b200_quantize_int8_rowwise_given(const void* x_bf16, const float* scales, void* q_int8, int rows, int cols,
                                         cudaStream_t stream);
 

@@ -915,6 +915,13 @@ int qi_b200_quantize_int8_rowwise(const void* x_bf16, void* q_int8, float* scale
   return quant_status(launch_rowquant<QuantInt8>(x_bf16, q_int8, scales, nullptr, rows, cols, stream));
 }
 
+int qi_b200_quantize_int8_rowwise_smooth(const void* x_bf16, const float* input_scale, void* q_int8, float* scales,
+                                         int rows, int cols, cudaStream_t stream) {
+  if (rows < 0 || cols < 0) return QI_B200_ESHAPE;
+  if (x_bf16 == nullptr || input_scale == nullptr || q_int8 == nullptr || scales == nullptr) return QI_B200_EINVAL;
+  return quant_status(launch_rowquant<QuantInt8>(x_bf16, q_int8, scales, nullptr, rows, cols, stream, input_scale));
+}
+
 int qi_b200_quantize_int8_rowwise_given(const void* x_bf16, const float* scales, void* q_int8, int rows, int cols,
                                         cudaStream_t stream) {
   if (rows < 0 || cols < 0) return QI_B200_ESHAPE;

@@ -80,6 +80,26 @@ __device__ __forceinline__ float absmax_bf16x8(const uint4& v) {
   return m;
 }
 
+// SmoothQuant / AWQ input smoothing of 8 bf16 values, x / input_scale in
+// bf16 as the reference does it (int8_w8a8_ops.py:138-139: the fp32 scale is
+// first cast to the activation dtype): bf16(fp32(x) / fp32(bf16(d))).
+__device__ __forceinline__ uint4 smooth_bf16x8(const uint4& v, const float* __restrict__ d8) {
+  const float4 d0 = __ldg(reinterpret_cast<const float4*>(d8));
+  const float4 d1 = __ldg(reinterpret_cast<const float4*>(d8) + 1);
+  const float d[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    const float a = __fdiv_rn(f.x, __bfloat162float(__float2bfloat16_rn(d[2 * i])));
+    const float b = __fdiv_rn(f.y, __bfloat162float(__float2bfloat16_rn(d[2 * i + 1])));
+    __nv_bfloat162 r = __floats2bfloat162_rn(a, b);
+    o[i] = *reinterpret_cast<uint32_t*>(&r);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 template <class Op>
 __device__ __forceinline__ uint2 quant_bf16x8(const uint4& v, float s, float aux) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
@@ -100,7 +120,7 @@ __device__ __forceinline__ uint2 quant_bf16x8(const uint4& v, float s, float aux
 template <class Op, int TPR>
 __global__ void __launch_bounds__(kQuantThreads)
 k_rowquant_vec(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, float* __restrict__ scales,
-               const float* __restrict__ static_scale, int rows, int cols) {
+               const float* __restrict__ static_scale, int rows, int cols, const float* __restrict__ col_div) {
   griddep_wait();
   griddep_launch_dependents();
   constexpr int RPB = kQuantThreads / TPR;
@@ -120,6 +140,7 @@ k_rowquant_vec(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, flo
     const int idx = c * TPR + t;
     if (valid && idx < nvec) {
       v[c] = __ldg(xr + idx);
+      if (col_div != nullptr) v[c] = smooth_bf16x8(v[c], col_div + idx * 8);
       if (Op::kNeedsAmax) amax = fmaxf(amax, absmax_bf16x8(v[c]));
     }
   }
@@ -154,17 +175,23 @@ k_rowquant_vec(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, flo
 template <class Op>
 __global__ void __launch_bounds__(kQuantThreads)
 k_rowquant_scalar(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, float* __restrict__ scales,
-                  const float* __restrict__ static_scale, int rows, int cols) {
+                  const float* __restrict__ static_scale, int rows, int cols, const float* __restrict__ col_div) {
   griddep_wait();
   griddep_launch_dependents();
   const int row = blockIdx.x * (kQuantThreads / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const __nv_bfloat16* xr = x + static_cast<size_t>(row) * cols;
+  // element j, smoothed as in smooth_bf16x8 when col_div is given
+  auto xv = [&](int j) {
+    const float f = __bfloat162float(xr[j]);
+    if (col_div == nullptr) return f;
+    return __bfloat162float(__float2bfloat16_rn(__fdiv_rn(f, __bfloat162float(__float2bfloat16_rn(col_div[j])))));
+  };
   float s;
   if (Op::kNeedsAmax) {
     float amax = 0.f;
-    for (int j = lane; j < cols; j += 32) amax = fmaxf(amax, fabsf(__bfloat162float(xr[j])));
+    for (int j = lane; j < cols; j += 32) amax = fmaxf(amax, fabsf(xv(j)));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
     s = Op::scale_from_amax(amax);
@@ -175,17 +202,18 @@ k_rowquant_scalar(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, 
   if (!Op::kStoreQ) return;
   const float aux = Op::aux(s);
   uint8_t* qr = q + static_cast<size_t>(row) * cols;
-  for (int j = lane; j < cols; j += 32) qr[j] = Op::q1(__bfloat162float(xr[j]), s, aux);
+  for (int j = lane; j < cols; j += 32) qr[j] = Op::q1(xv(j), s, aux);
 }
 
 template <class Op>
 inline cudaError_t launch_rowquant(const void* x, void* q, float* scales, const float* static_scale, int rows,
-                                   int cols, cudaStream_t stream) {
+                                   int cols, cudaStream_t stream, const float* col_div = nullptr) {
   if (rows <= 0 || cols <= 0) return cudaSuccess;
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   auto* qb = static_cast<uint8_t*>(q);
   const bool aligned = (cols % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
-                       (reinterpret_cast<uintptr_t>(q) % 8 == 0);
+                       (reinterpret_cast<uintptr_t>(q) % 8 == 0) &&
+                       (col_div == nullptr || reinterpret_cast<uintptr_t>(col_div) % 16 == 0);
   const int nvec = cols / 8;
   const dim3 blk(kQuantThreads);
   if (aligned) {
@@ -193,24 +221,25 @@ inline cudaError_t launch_rowquant(const void* x, void* q, float* scales, const 
     if (fits(32)) {
       constexpr int RPB = kQuantThreads / 32;
       launch_pdl(k_rowquant_vec<Op, 32>, dim3((rows + RPB - 1) / RPB), blk, 0, stream, 1, xb, qb, scales,
-                 static_scale, rows, cols);
+                 static_scale, rows, cols, col_div);
     } else if (fits(64)) {
       constexpr int RPB = kQuantThreads / 64;
       launch_pdl(k_rowquant_vec<Op, 64>, dim3((rows + RPB - 1) / RPB), blk, 0, stream, 1, xb, qb, scales,
-                 static_scale, rows, cols);
+                 static_scale, rows, cols, col_div);
     } else if (fits(128)) {
       constexpr int RPB = kQuantThreads / 128;
       launch_pdl(k_rowquant_vec<Op, 128>, dim3((rows + RPB - 1) / RPB), blk, 0, stream, 1, xb, qb, scales,
-                 static_scale, rows, cols);
+                 static_scale, rows, cols, col_div);
     } else if (fits(256)) {
-      launch_pdl(k_rowquant_vec<Op, 256>, dim3(rows), blk, 0, stream, 1, xb, qb, scales, static_scale, rows, cols);
+      launch_pdl(k_rowquant_vec<Op, 256>, dim3(rows), blk, 0, stream, 1, xb, qb, scales, static_scale, rows, cols,
+                 col_div);
     } else {
       launch_pdl(k_rowquant_scalar<Op>, dim3((rows + 7) / 8), blk, 0, stream, 1, xb, qb, scales, static_scale, rows,
-                 cols);
+                 cols, col_div);
     }
   } else {
     launch_pdl(k_rowquant_scalar<Op>, dim3((rows + 7) / 8), blk, 0, stream, 1, xb, qb, scales, static_scale, rows,
-               cols);
+               cols, col_div);
   }
   count_launches(1);
   return cudaGetLastError();

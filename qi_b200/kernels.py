@@ -44,12 +44,21 @@ def _check(t: torch.Tensor, name: str, dtype=None, dim=None, device=None) -> Non
 
 
 def quantize_int8_rowwise(x: torch.Tensor, out: torch.Tensor | None = None,
-                          scales: torch.Tensor | None = None):
-    """bf16 [M,K] -> (int8 [M,K], fp32 [M]) with the reference K1 semantics."""
+                          scales: torch.Tensor | None = None, input_scale: torch.Tensor | None = None):
+    """bf16 [M,K] -> (int8 [M,K], fp32 [M]) with the reference K1 semantics.
+    ``input_scale`` (fp32 [K]) first divides x as the reference's SmoothQuant
+    path does, in bf16 (``int8_w8a8_ops.py:138-139``), inside the same kernel."""
     _check(x, "x", torch.bfloat16, 2)
     M, K = x.shape
     q = out if out is not None else torch.empty((M, K), dtype=torch.int8, device=x.device)
     s = scales if scales is not None else torch.empty((M,), dtype=torch.float32, device=x.device)
+    if input_scale is not None:
+        isc = input_scale.reshape(-1).to(device=x.device, dtype=torch.float32).contiguous()
+        if isc.numel() != K:
+            raise ValueError(f"input_scale must have {K} values, got {isc.numel()}.")
+        _lib.call("qi_b200_quantize_int8_rowwise_smooth", _ptr(x), _ptr(isc), _ptr(q), _ptr(s), M, K,
+                  _stream(x.device))
+        return q, s
     _lib.call("qi_b200_quantize_int8_rowwise", _ptr(x), _ptr(q), _ptr(s), M, K, _stream(x.device))
     return q, s
 
@@ -238,10 +247,12 @@ def gemm(kind: int, a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor | No
 
 
 def int8_linear(x_bf16_2d: torch.Tensor, qweight: torch.Tensor, weight_scales: torch.Tensor,
-                bias: torch.Tensor | None = None, gelu: bool = False) -> torch.Tensor:
+                bias: torch.Tensor | None = None, gelu: bool = False,
+                input_scale: torch.Tensor | None = None) -> torch.Tensor:
     """Same contract as the reference torch op
     ``qi_int8_w8a8::linear(Tensor x_bf16_2d, Tensor qweight, Tensor weight_scales, Tensor? bias)``
-    (``bindings.cpp:87-165``); ``gelu`` additionally fuses GELU(tanh) into the epilogue."""
+    (``bindings.cpp:87-165``); ``gelu`` additionally fuses GELU(tanh) into the epilogue, and
+    ``input_scale`` the backend's SmoothQuant division into the activation quantizer."""
     _check(x_bf16_2d, "x_bf16_2d", torch.bfloat16, 2)
     dev = x_bf16_2d.device
     _check(qweight, "qweight", torch.int8, 2, dev)
@@ -258,9 +269,9 @@ def int8_linear(x_bf16_2d: torch.Tensor, qweight: torch.Tensor, weight_scales: t
             raise ValueError("bias length must match qweight N dimension.")
     ws_q = torch.empty((M, K), dtype=torch.int8, device=dev)
     ws_s = torch.empty((M,), dtype=torch.float32, device=dev)
-    if gelu:
-        quantize_int8_rowwise(x_bf16_2d, ws_q, ws_s)
-        return gemm(_lib.KIND_INT8, ws_q, qweight, ws_s, weight_scales, bias, gelu=True)
+    if gelu or input_scale is not None:
+        quantize_int8_rowwise(x_bf16_2d, ws_q, ws_s, input_scale=input_scale)
+        return gemm(_lib.KIND_INT8, ws_q, qweight, ws_s, weight_scales, bias, gelu=gelu)
     out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
     _lib.call("qi_b200_int8_linear", _ptr(x_bf16_2d), _ptr(qweight), _ptr(weight_scales), _ptr(bias),
               _ptr(out), _ptr(ws_q), _ptr(ws_s), M, N, K, _stream(dev))

@@ -97,7 +97,12 @@ class B200Backend:
         gelu = self.fuse_gelu if gelu is None else gelu
         out_dtype = _output_dtype(x, keep_output_dtype)
         xk = x
-        if input_scale is not None:  # SmoothQuant / AWQ smoothing (int8_w8a8_ops.py:138-139)
+        int8_path = (weight_fp8 is None and qweight_packed is None and bits == 8
+                     and activation_granularity == "per_token")
+        # SmoothQuant / AWQ smoothing (int8_w8a8_ops.py:138-139): on the INT8 path
+        # with bf16 input it runs inside the activation quantizer (same bf16 division)
+        fuse_smooth = input_scale is not None and int8_path and x.dtype == torch.bfloat16
+        if input_scale is not None and not fuse_smooth:
             xk = xk / input_scale.to(device=x.device, dtype=x.dtype)
         k_in = int(xk.shape[-1])
         x2 = xk.reshape(-1, k_in).to(torch.bfloat16).contiguous()
@@ -121,7 +126,8 @@ class B200Backend:
             if gelu:
                 raise ValueError("GELU fusion is not available on the W4A16 path.")
         elif bits == 8 and activation_granularity == "per_token":
-            y = self._int8(x2, qweight, scales, group_size, symmetric, weight_granularity, bias, gelu)
+            y = self._int8(x2, qweight, scales, group_size, symmetric, weight_granularity, bias, gelu,
+                           input_scale if fuse_smooth else None)
         else:
             raise ValueError(
                 "B200 backend: unsupported buffer combination (bits=%s, activation_granularity=%s, packed=%s)"
@@ -130,7 +136,7 @@ class B200Backend:
 
     # -- formats ------------------------------------------------------------
 
-    def _int8(self, x2, qweight, scales, group_size, symmetric, weight_granularity, bias, gelu):
+    def _int8(self, x2, qweight, scales, group_size, symmetric, weight_granularity, bias, gelu, input_scale=None):
         if group_size != -1:
             raise ValueError("INT8 W8A8 backend requires per-channel weights with group_size=-1.")
         if not symmetric:
@@ -148,7 +154,8 @@ class B200Backend:
                 raise ValueError(f"Expected per-channel scales shape {(n, 1)}, got {tuple(ws.shape)}.")
             ws = ws[:, 0]
         ws = ws.contiguous().float()
-        return K.int8_linear(x2, qweight.contiguous(), ws, _bias_bf16(bias, n, x2.device), gelu=gelu)
+        return K.int8_linear(x2, qweight.contiguous(), ws, _bias_bf16(bias, n, x2.device), gelu=gelu,
+                             input_scale=input_scale)
 
     def _w4a16(self, x2, qp, s16, zp, group_size, bias):
         if s16 is None or zp is None:

@@ -330,3 +330,50 @@ def test_cluster_splitk_auto_for_few_tiles_long_k():
     assert torch.equal(y, y_ref)
     yo, _, _, _ = O.int8_linear(bits(x), qw, sw[:, 0], bits(b))
     np.testing.assert_array_equal(bits(K.int8_linear(x.to(DEV), qwd, swd, bd)), yo)
+
+
+@pytest.mark.parametrize("M,Kd", [(33, 512), (7, 100), (256, 3072)])
+def test_int8_quantizer_fused_smoothing(M, Kd):
+    """SmoothQuant / AWQ input smoothing fused into the activation quantizer
+    (int8_w8a8_ops.py:138-139: x / input_scale.to(x.dtype), in bf16): codes
+    and scales bit-identical to dividing first with torch, and to the oracle
+    on the smoothed rows.  K = 100 takes the scalar (unaligned) kernel."""
+    x, _, _ = make_small_case(M, 8, Kd, seed=M + Kd, outlier_frac=0.01)
+    g = torch.Generator().manual_seed(Kd)
+    isc = (0.25 + 2 * torch.rand(Kd, generator=g)).float()
+    xd, isd = x.to(DEV), isc.to(DEV)
+    q, s = K.quantize_int8_rowwise(xd, input_scale=isd)
+    xs = xd / isd.to(torch.bfloat16)
+    q_ref, s_ref = K.quantize_int8_rowwise(xs.contiguous())
+    assert torch.equal(q, q_ref) and torch.equal(s, s_ref)
+    qo, so = O.quantize_int8_rowwise(bits(xs))
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+
+
+def test_int8_module_with_input_scale_fuses_smoothing():
+    """A WeightOnlyLinear with an input_scale buffer on the B200 backend gives
+    the same bits as the reference order (divide, then the INT8 linear)."""
+    from qi_b200.quantization import WeightActivationQuantConfig, replace_linear_with_weight_only
+
+    M, N, Kd = 40, 256, 512
+    x, w, b = make_small_case(M, N, Kd, seed=5)
+    model = torch.nn.Module()
+    model.ffn = torch.nn.Sequential(torch.nn.Linear(Kd, N))  # a target name of the swap
+    with torch.no_grad():
+        model.ffn[0].weight.copy_(w)
+        model.ffn[0].bias.copy_(b.float())
+    cfg = WeightActivationQuantConfig(enabled=True, algo="rtn", quant_dtype="int", backend="b200",
+                                      activation_granularity="per_token", weight_granularity="per_channel")
+    replace_linear_with_weight_only(model, cfg)
+    model.to(DEV)
+    lin = model.ffn[0]
+    assert type(lin).__name__ == "WeightOnlyLinear"
+    g = torch.Generator().manual_seed(3)
+    isc = (0.5 + torch.rand(Kd, generator=g)).float().to(DEV)
+    lin.input_scale = isc
+    xd = x.to(DEV)
+    y = lin(xd)
+    y_ref = K.int8_linear((xd / isc.to(torch.bfloat16)).contiguous(), lin.qweight, lin.scales[:, 0].contiguous(),
+                          lin.bias.to(torch.bfloat16))
+    assert torch.equal(y, y_ref)
