@@ -116,6 +116,29 @@ __device__ __forceinline__ uint4 pack8_exact(const float (&v)[8]) {
   return u;
 }
 
+// Packed-pair forms of the helpers above.
+__device__ __forceinline__ void unpack8x2(const uint4& u, float2 (&f)[4]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) f[i] = __bfloat1622float2(h[i]);
+}
+__device__ __forceinline__ uint4 pack8x2(const float2 (&f)[4]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[i].x, f[i].y);
+  return u;
+}
+__device__ __forceinline__ float2 round2(float2 v) { return __bfloat1622float2(__floats2bfloat162_rn(v.x, v.y)); }
+__device__ __forceinline__ uint4 pack8x2_exact(const float2 (&v)[4]) {
+  uint4 u;
+  u.x = __byte_perm(__float_as_uint(v[0].x), __float_as_uint(v[0].y), 0x7632);
+  u.y = __byte_perm(__float_as_uint(v[1].x), __float_as_uint(v[1].y), 0x7632);
+  u.z = __byte_perm(__float_as_uint(v[2].x), __float_as_uint(v[2].y), 0x7632);
+  u.w = __byte_perm(__float_as_uint(v[3].x), __float_as_uint(v[3].y), 0x7632);
+  return u;
+}
+
 // INT8 codes clamp(rint(v * inv), -127, 127) of 8 values.  rint is done by
 // adding 1.5 * 2^23 in the FP32 adder (round-to-nearest-even, exact for the
 // pre-clamped |t| <= 128), which equals cvt.rni without the conversion unit.
@@ -391,84 +414,83 @@ __global__ void __launch_bounds__(kWarpRowThreads) k_resid_ln_quant_warp(ResLnPa
     uint4 yu[C];
 #pragma unroll
     for (int c = 0; c < C; ++c) yu[c] = yr[c * 32 + lane];
+    // packed fp32x2 arithmetic: each element rounds as with scalar operations
 #pragma unroll
     for (int c = 0; c < C; ++c) {
-      float v[8], yv[8];
-      unpack8(xu[c], v);
-      unpack8(yu[c], yv);
+      float2 v[4], yv[4];
+      unpack8x2(xu[c], v);
+      unpack8x2(yu[c], yv);
       if (p.gate != nullptr) {
-        float g[8];
-        unpack8(vecs[c * 32 + lane], g);
+        float2 g[4];
+        unpack8x2(vecs[c * 32 + lane], g);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) yv[e] = __fmul_rn(g[e], yv[e]);
-        round8(yv);
+        for (int e = 0; e < 4; ++e) yv[e] = round2(__fmul2_rn(g[e], yv[e]));
       }
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], yv[e]);
-      xu[c] = pack8(v);
+      for (int e = 0; e < 4; ++e) v[e] = __fadd2_rn(v[e], yv[e]);
+      xu[c] = pack8x2(v);
       xr[c * 32 + lane] = xu[c];
     }
   }
   if (p.q == nullptr && p.xn == nullptr) return;
 
-  float sum = 0.f;
+  // row statistics: per-lane pairwise sums, then the warp
+  float2 sum2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int c = 0; c < C; ++c) {
-    float v[8];
-    unpack8(xu[c], v);
+    float2 v[4];
+    unpack8x2(xu[c], v);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sum += v[e];
+    for (int e = 0; e < 4; ++e) sum2 = __fadd2_rn(sum2, v[e]);
   }
-  const float mean = warp_sum(sum) / static_cast<float>(p.D);
-  float sq = 0.f;
+  const float mean = warp_sum(sum2.x + sum2.y) / static_cast<float>(p.D);
+  const float2 negmean2 = make_float2(-mean, -mean);  // v + (-mean) rounds as v - mean
+  float2 sq2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int c = 0; c < C; ++c) {
-    float v[8];
-    unpack8(xu[c], v);
+    float2 v[4];
+    unpack8x2(xu[c], v);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float d = v[e] - mean;
-      sq = fmaf(d, d, sq);
+    for (int e = 0; e < 4; ++e) {
+      const float2 d = __fadd2_rn(v[e], negmean2);
+      sq2 = __ffma2_rn(d, d, sq2);
     }
   }
-  const float rstd = rsqrtf(warp_sum(sq) / static_cast<float>(p.D) + p.eps);
+  const float rstd = rsqrtf(warp_sum(sq2.x + sq2.y) / static_cast<float>(p.D) + p.eps);
+  const float2 rstd2 = make_float2(rstd, rstd);
 
-  float amax = 0.f;
+  __nv_bfloat162 amax2 = __float2bfloat162_rn(0.f);
 #pragma unroll
   for (int c = 0; c < C; ++c) {
     const int j = c * 32 + lane;
-    float v[8];
-    unpack8(xu[c], v);
-    float w[8], b[8], s1[8], sh[8];
+    float2 v[4];
+    unpack8x2(xu[c], v);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = __fmul2_rn(__fadd2_rn(v[e], negmean2), rstd2);
     if (p.ln_w != nullptr) {
-      unpack8(vecs[1 * C * 32 + j], w);
-      unpack8(vecs[2 * C * 32 + j], b);
+      float2 w[4], b[4];
+      unpack8x2(vecs[1 * C * 32 + j], w);
+      unpack8x2(vecs[2 * C * 32 + j], b);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = __ffma2_rn(v[e], w[e], b[e]);
     }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = round2(v[e]);
     if (p.mod_scale1 != nullptr) {
-      unpack8(vecs[3 * C * 32 + j], s1);
-      unpack8(vecs[4 * C * 32 + j], sh);
+      float2 s1[4], sh[4];
+      unpack8x2(vecs[3 * C * 32 + j], s1);
+      unpack8x2(vecs[4 * C * 32 + j], sh);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = round2(__fadd2_rn(round2(__fmul2_rn(v[e], s1[e])), sh[e]));
     }
+    xu[c] = pack8x2_exact(v);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&xu[c]);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float n = (v[e] - mean) * rstd;
-      if (p.ln_w != nullptr) n = fmaf(n, w[e], b[e]);
-      v[e] = n;
-    }
-    round8(v);
-    if (p.mod_scale1 != nullptr) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], s1[e]);
-      round8(v);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], sh[e]);
-      round8(v);
-    }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[e]));
-    xu[c] = pack8_exact(v);
+    for (int e = 0; e < 4; ++e) amax2 = __hmax2(amax2, __habs2(h[e]));  // exact: the values are bf16
     if (p.xn != nullptr) reinterpret_cast<uint4*>(p.xn + static_cast<long long>(row) * p.D)[j] = xu[c];
   }
   if (p.q == nullptr) return;
+  float amax = fmaxf(__low2float(amax2), __high2float(amax2));
   amax = warp_max(amax);
   const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-10f);
   const float inv = __frcp_rn(s);
@@ -516,27 +538,30 @@ __global__ void __launch_bounds__(kWarpRowThreads) k_rms_rope_warp(RmsRopeParams
   if (row >= p.M) return;
   uint4* orow = reinterpret_cast<uint4*>((part ? p.out[1] : p.out[0]) + static_cast<long long>(row) * p.ld_out);
   const uint4* wp = wsm;
-  float sq = 0.f;
+  float2 sq2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int c = 0; c < C; ++c) {
-    float v[8];
-    unpack8(u[c], v);
+    float2 v2[4];
+    unpack8x2(u[c], v2);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sq = fmaf(v[e], v[e], sq);
+    for (int e = 0; e < 4; ++e) sq2 = __ffma2_rn(v2[e], v2[e], sq2);
   }
-  const float r = rsqrtf(warp_sum(sq) / static_cast<float>(p.A) + p.eps);
+  const float r = rsqrtf(warp_sum(sq2.x + sq2.y) / static_cast<float>(p.A) + p.eps);
+  const float2 r2 = make_float2(r, r);
 #pragma unroll
   for (int c = 0; c < C; ++c) {
     const int j = c * 32 + lane;
-    float v[8], w[8];
-    unpack8(u[c], v);
-    unpack8(wp[j], w);
+    float2 v2[4], w2[4];
+    unpack8x2(u[c], v2);
+    unpack8x2(wp[j], w2);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], r);
-    round8(v);
+    for (int e = 0; e < 4; ++e) v2[e] = round2(__fmul2_rn(round2(__fmul2_rn(v2[e], r2)), w2[e]));
+    float v[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], w[e]);
-    round8(v);
+    for (int e = 0; e < 4; ++e) {
+      v[2 * e] = v2[e].x;
+      v[2 * e + 1] = v2[e].y;
+    }
     if (p.rope != nullptr) {
       const int pair0 = (j * 4) % p.pairs_per_head;
       const float4* tab = reinterpret_cast<const float4*>(
