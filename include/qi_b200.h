@@ -53,6 +53,16 @@ extern "C" {
  * single-CTA 128 x 128), 1 = single-CTA 128 x 128, 2 = CTA pair 256 x 128,
  * 3 = CTA pair 256 x 256. */
 #define QI_B200_NVFP4_TILE_SHIFT 8
+/* qi_b200_gemm flags bits 12-15: the CTA-pair kernel's partial last wave.
+ * When tiles % pairs tiles are left for a last wave, each of them can have
+ * its K range split over S pairs that would otherwise sit idle; the partial
+ * accumulators meet in a per-stream workspace (allocated by the library on
+ * first use on a stream, about 19 MB) and are summed in a fixed order, so
+ * INT8 results stay bit-exact.  0 = the library's choice, 1 = no split,
+ * 2..15 = at most that many splits per tile (further capped at 8 and at the
+ * idle pairs).  Replaces nothing in the reference (its CUTLASS kernels run
+ * one tile per CTA with no split); a scheduling choice of this library. */
+#define QI_B200_TAIL_SPLIT_SHIFT 12
 
 int qi_b200_abi_version(void);
 const char* qi_b200_error_string(int code);
@@ -71,6 +81,9 @@ int qi_b200_device_status(unsigned int* out4, int clear);
  * (or padded M for kernel 6, M for kernel 7), pipeline stages, dynamic shared
  * memory bytes}. */
 int qi_b200_last_launch(int* out6);
+/* Splits per tail tile (see QI_B200_TAIL_SPLIT_SHIFT) of the calling thread's
+ * most recent CTA-pair GEMM launch; 1 = its last wave ran unsplit. */
+int qi_b200_last_tail_split(void);
 
 /* Number of kernels this library has launched in this process, counting
  * launches recorded into a CUDA graph under capture once (at capture). */

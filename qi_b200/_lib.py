@@ -19,6 +19,7 @@ KIND_INT8, KIND_FP8_E4M3, KIND_BF16 = 0, 1, 2
 EPI_GELU, EPI_RAW_ACC = 1, 2
 W4A16_DEQUANT_MIN_M = 257  # QI_B200_W4A16_DEQUANT_MIN_M (measured crossover: M=512 26 us vs 43 us fused)
 NVFP4_TILE_SHIFT = 8  # flags bits 8-9: 0 auto, 1 single-CTA 128x128, 2 pair 256x128, 3 pair 256x256
+TAIL_SPLIT_SHIFT = 12  # flags bits 12-15 of qi_b200_gemm: 0 auto, 1 no split, S = at most S splits per tail tile
 
 
 class QiB200Unavailable(RuntimeError):
@@ -44,6 +45,7 @@ SIGNATURES = {
     "qi_b200_error_string": [_I],
     "qi_b200_device_status": [_P, _I],
     "qi_b200_last_launch": [_P],
+    "qi_b200_last_tail_split": [],
     "qi_b200_launch_count": [_P],
     "qi_b200_quantize_int8_rowwise_smooth": [_P, _P, _P, _P, _I, _I, _P],
     "qi_b200_w4a16_dequant": [_P, _P, _P, _I, _P, _I, _I, _P],
@@ -138,6 +140,11 @@ def last_launch() -> dict:
     v = list(buf)
     return {"kernel": names.get(v[0], "none"), "grid": v[1], "cluster": v[2], "tile_n": v[3], "stages": v[4],
             "smem": v[5]}
+
+
+def last_tail_split() -> int:
+    """Splits per tail tile of this thread's most recent CTA-pair GEMM (1 = none)."""
+    return int(load().qi_b200_last_tail_split())
 
 
 def device_status(clear: bool = False) -> tuple[int, int, int, int]:

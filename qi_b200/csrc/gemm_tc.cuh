@@ -60,7 +60,15 @@ struct EpiParams {
   // contiguous range of K blocks; split s stores at D + s * split_stride
   int ksplit = 1;
   long long split_stride = 0;
+  // CTA-pair kernel: each of the last (tiles % pairs) tiles, the partial last
+  // wave, is split along K over tail_split pairs (1 = no split).  Partial
+  // accumulators go to tail_ws (tail tiles x tail_split x 256 x BN words);
+  // tail_cnt holds 2 x kMaxTailTiles counters that are zero between launches.
+  int tail_split = 1;
+  uint32_t* tail_ws = nullptr;
+  unsigned int* tail_cnt = nullptr;
 };
+constexpr int kMaxTailTiles = 128;
 constexpr int kMaxPeers = 8;
 
 template <MmaKind KIND, int BN_, int STAGES_>
@@ -220,24 +228,26 @@ __device__ __forceinline__ void mma_issue(uint32_t d, uint64_t a, uint64_t b, ui
 // Epilogue for one 32-column chunk of one row (this thread's row).  Column
 // scales and bias come from the per-tile shared-memory copy (sb_s, bias_s,
 // indexed from the chunk's first column); the row scale is in a register.
-template <MmaKind KIND>
-__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], const EpiParams& p, int m, int n0,
+// W columns (8, 16 or 32) from the chunk's first column n0.
+template <MmaKind KIND, int W = 32>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[W], const EpiParams& p, int m, int n0,
                                                float sa, const float* sb_s, const __nv_bfloat16* bias_s,
                                                uint32_t* packed_out = nullptr, int split = 0) {
-  const int n_valid = p.N - n0;  // >= 1; a multiple of 8 when < 32 (N % 8 == 0)
+  static_assert(W == 8 || W == 16 || W == 32, "chunk width");
+  const int n_valid = p.N - n0;  // >= 1; a multiple of 8 when < W (N % 8 == 0)
   if (p.flags & kEpiRawAcc) {
     uint32_t* drow = static_cast<uint32_t*>(p.D) + split * p.split_stride + static_cast<long long>(m) * p.ldd;
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
+    for (int j = 0; j < W; j += 4) {
       if (j < n_valid) *reinterpret_cast<uint4*>(drow + n0 + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
     }
     return;
   }
   // ((acc * sa) * sb + bias) -> bf16 -> GELU, on pairs of columns with packed
   // fp32x2 operations (each element rounds exactly as with scalar ones)
-  float2 y[16];
+  float2 y[W / 2];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
+  for (int j = 0; j < W / 2; ++j) {
     if constexpr (KIND == MmaKind::I8)
       y[j] = make_float2(__int2float_rn(static_cast<int>(r[2 * j])), __int2float_rn(static_cast<int>(r[2 * j + 1])));
     else
@@ -246,11 +256,11 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], const Ep
   if (KIND != MmaKind::BF16 || p.sa != nullptr) {
     const float2 sa2 = make_float2(sa, sa);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) y[j] = __fmul2_rn(y[j], sa2);
+    for (int j = 0; j < W / 2; ++j) y[j] = __fmul2_rn(y[j], sa2);
   }
   if (p.sb != nullptr) {
 #pragma unroll
-    for (int j = 0; j < 16; j += 2) {
+    for (int j = 0; j < W / 2; j += 2) {
       const float4 s4 = *reinterpret_cast<const float4*>(sb_s + 2 * j);
       y[j] = __fmul2_rn(y[j], make_float2(s4.x, s4.y));
       y[j + 1] = __fmul2_rn(y[j + 1], make_float2(s4.z, s4.w));
@@ -258,31 +268,31 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], const Ep
   }
   if (p.bias != nullptr) {
 #pragma unroll
-    for (int j = 0; j < 16; j += 4) {
+    for (int j = 0; j < W / 2; j += 4) {
       const uint4 b4 = *reinterpret_cast<const uint4*>(bias_s + 2 * j);
       const __nv_bfloat162* bh = reinterpret_cast<const __nv_bfloat162*>(&b4);
 #pragma unroll
       for (int i = 0; i < 4; ++i) y[j + i] = __fadd2_rn(y[j + i], __bfloat1622float2(bh[i]));
     }
   }
-  uint32_t packed[16];
+  uint32_t packed[W / 2];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) packed[j] = pack_bf16x2(y[j].x, y[j].y);
+  for (int j = 0; j < W / 2; ++j) packed[j] = pack_bf16x2(y[j].x, y[j].y);
   if (p.flags & kEpiGelu) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < W / 2; ++j) {
       const float2 g = gelu_tanh_fast2(__bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&packed[j])));
       packed[j] = pack_bf16x2(g.x, g.y);
     }
   }
   if (packed_out != nullptr) {  // the caller stores the bf16 row chunk itself
 #pragma unroll
-    for (int j = 0; j < 16; ++j) packed_out[j] = packed[j];
+    for (int j = 0; j < W / 2; ++j) packed_out[j] = packed[j];
     return;
   }
   __nv_bfloat16* drow = static_cast<__nv_bfloat16*>(p.D) + static_cast<long long>(m) * p.ldd;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < W / 8; ++j) {
     if (8 * j < n_valid)
       *reinterpret_cast<uint4*>(drow + n0 + 8 * j) =
           make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);

@@ -95,6 +95,127 @@ struct Gemm2Cfg {
   static_assert(!GATHER_ || BN % 128 == 0, "gather boxes are 64 columns per epilogue warp");
 };
 
+// One work item of a pair: a whole tile, or (tail split) a K range of one of
+// the tiles of the partial last wave.  With S > 1 the first tiles - tail
+// tiles (tail = tiles % pairs, a whole number of waves) go round-robin to the
+// pairs; then pair u < tail * S takes K blocks [s kb / S, (s + 1) kb / S) of
+// tail tile u / S, s = u % S.  unit = u, or -1 for a whole tile.
+struct PairWork {
+  int tile, kb0, kb1, unit;
+};
+__device__ __forceinline__ bool pair_work(int w, int pair, int npairs, int num_tiles, int S, int k_blocks,
+                                          PairWork& o) {
+  const int tail = S > 1 ? num_tiles % npairs : 0;
+  const int whole = num_tiles - tail;
+  const int tile = pair + w * npairs;
+  if (tile < whole) {
+    o = {tile, 0, k_blocks, -1};
+    return true;
+  }
+  if (S > 1 && w == whole / npairs && pair < tail * S) {
+    const int s = pair % S;
+    o = {whole + pair / S, s * k_blocks / S, (s + 1) * k_blocks / S, pair};
+    return true;
+  }
+  return false;
+}
+
+// Tail split, run by the 256 epilogue threads of each CTA of a tail unit once
+// its partial accumulators are in the workspace: wait (bounded) until all 2S
+// CTAs of the tile have stored theirs, then sum this CTA's share of the tile
+// (1/2S of its 8-column row pieces, splits added in a fixed order, so the
+// result is deterministic and exact for INT8) and run the usual epilogue on
+// it.  The last CTA to finish resets the tile's counters for the next launch.
+// Returns false when the CTA is aborting.
+constexpr int kMaxTailSplit = 8;
+template <MmaKind KIND, int BN>
+__device__ __forceinline__ bool tail_reduce(const EpiParams& p, const PairWork& wk, int S, int rank, int mb, int nb,
+                                              int et, const float* sb_t, const __nv_bfloat16* bias_t,
+                                              uint64_t* tail_sync, uint32_t& ph, volatile int* abort_flag,
+                                              unsigned int tag) {
+  auto epi_bar = [&](unsigned int site) {
+    mbar_arrive(tail_sync);
+    const bool ok = mbar_wait(tail_sync, ph, abort_flag, tag, site);
+    ph ^= 1u;
+    return ok;
+  };
+  const int tt = wk.unit / S;
+  unsigned int* cnt = p.tail_cnt + tt;
+  unsigned int* done = p.tail_cnt + kMaxTailTiles + tt;
+  const unsigned int need = 2u * static_cast<unsigned int>(S);
+  if (!epi_bar(10)) return false;  // every partial store of this CTA is issued
+  if (et == 0) {
+    __threadfence();
+    atomicAdd(cnt, 1u);
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_gpu(cnt) < need) {
+      if (*abort_flag) break;
+      if (globaltimer_ns() - t0 > QI_WAIT_TIMEOUT_NS) {
+        record_error(kDevWaitTimeout, tag, 11);
+        *abort_flag = 1;
+        break;
+      }
+      __nanosleep(64);
+    }
+    __threadfence();
+  }
+  if (!epi_bar(12) || *abort_flag) return false;
+
+  constexpr int PPR = BN / 8;   // 8-column pieces per row
+  constexpr int P = 256 * PPR;  // pieces per tile
+  const int R = 2 * S, c = 2 * (wk.unit % S) + rank;
+  const int q1 = (c + 1) * P / R;
+  const uint32_t* base = p.tail_ws + static_cast<size_t>(tt) * S * 256 * BN;
+  for (int q = c * P / R + et; q < q1; q += kEpiThreads) {
+    const int rt = q / PPR, j0 = (q - rt * PPR) * 8;
+    const int m = mb * 256 + rt, n0 = nb * BN + j0;
+    if (m >= p.M || n0 >= p.N) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(base + static_cast<size_t>(rt) * BN + j0);
+    constexpr int kSplitWords = 256 * BN / 4;  // uint4 per split
+    constexpr int kBatch = 4;                  // splits loaded together (registers: 8 per split)
+    uint32_t r[8];
+#pragma unroll
+    for (int s0 = 0; s0 < kMaxTailSplit; s0 += kBatch) {
+      if (s0 < S) {
+        uint4 part[kBatch][2];
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+          if (s0 + i < S) {
+            part[i][0] = __ldcg(src + (s0 + i) * kSplitWords);
+            part[i][1] = __ldcg(src + (s0 + i) * kSplitWords + 1);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+          if (s0 + i < S) {
+            const uint32_t v[8] = {part[i][0].x, part[i][0].y, part[i][0].z, part[i][0].w,
+                                   part[i][1].x, part[i][1].y, part[i][1].z, part[i][1].w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              if (s0 + i == 0) r[e] = v[e];
+              else if constexpr (KIND == MmaKind::I8) r[e] += v[e];  // two's-complement int32 sum
+              else r[e] = __float_as_uint(__fadd_rn(__uint_as_float(r[e]), __uint_as_float(v[e])));
+            }
+          }
+        }
+      }
+    }
+    float sa = 1.0f;
+    if (p.sa != nullptr) sa = __ldg(p.sa + static_cast<long long>(m) * p.sa_stride);
+    epilogue_chunk<KIND, 8>(r, p, m, n0, sa, sb_t + j0, bias_t + j0);
+  }
+
+  if (!epi_bar(13)) return false;  // this CTA has read its share
+  if (et == 0) {
+    __threadfence();
+    if (atomicAdd(done, 1u) == need - 1u) {  // every CTA of the tile is past its wait and its reads
+      atomicExch(cnt, 0u);
+      atomicExch(done, 0u);
+    }
+  }
+  return true;
+}
+
 template <MmaKind KIND, int BN, int STAGES, bool GATHER = false>
 __global__ void __launch_bounds__(Gemm2Cfg<KIND, BN, STAGES, GATHER>::THREADS, 1)
 k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -119,7 +240,8 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
   uint64_t* sf_full = epi_sync + 2;          // [STAGES] this CTA's scale atoms landed (NVFP4)
   uint64_t* sf_ready = sf_full + STAGES;     // [SF_SLOTS] even CTA: both CTAs' slot written
   uint64_t* sf_free = sf_ready + C::SF_SLOTS;  // [SF_SLOTS] the MMAs reading the slot are done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_free + C::SF_SLOTS);
+  uint64_t* tail_sync = sf_free + C::SF_SLOTS;  // epilogue threads of a tail-split unit
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tail_sync + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   constexpr int kFirstEpi = C::EPI_WARP0;
 
@@ -147,6 +269,7 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
       }
     }
     mbar_init(drain, 1);
+    mbar_init(tail_sync, kEpiThreads);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -177,6 +300,7 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
   const int num_tiles = m_tiles * n_tiles;
   const int k_units = C::NVF4 ? p.K / 2 : p.K;  // K in TMA elements
   const int k_blocks = (k_units + C::BK - 1) / C::BK;
+  const int S = (C::NVF4 || GATHER) ? 1 : p.tail_split;  // tail split (host: tail * S <= pairs, S <= k_blocks)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -185,9 +309,10 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-        const int mb = tile % m_tiles, nb = tile / m_tiles;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+      PairWork wk;
+      for (int w = 0; ok && pair_work(w, pair, npairs, num_tiles, S, k_blocks, wk); ++w) {
+        const int mb = wk.tile % m_tiles, nb = wk.tile / m_tiles;
+        for (int kb = wk.kb0; kb < wk.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kTag, 1)) { ok = false; break; }
           const uint32_t lfull = map_shared_rank(smem_u32(&full[stage]), 0);
           if (leader) mbar_expect_tx(&full[stage], 2 * (C::A_BYTES + C::B_BYTES));
@@ -236,13 +361,14 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
       int local = 0;
       int g = 0;  // K slices issued so far (scale slot ring)
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++local) {
+      PairWork wk;
+      for (int w = 0; ok && pair_work(w, pair, npairs, num_tiles, S, k_blocks, wk); ++w, ++local) {
         const int buf = local % C::ACC_BUFS;
         const uint32_t tph = (local / C::ACC_BUFS) & 1;
         if (!mbar_wait(&tempty[buf], tph ^ 1u, abort_flag, kTag, 2)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * C::ACC_COLS);
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = wk.kb0; kb < wk.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, kTag, 3)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
@@ -257,14 +383,15 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
               mma_nvf4_pair(d_tmem, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32), C::IDESC,
-                            tsfa + 4 * kk, tsfb + (BN / 32) * kk, (kb | kk) != 0 ? 1u : 0u);
+                            tsfa + 4 * kk, tsfb + (BN / 32) * kk, (kb != wk.kb0 || kk != 0) ? 1u : 0u);
             tc_commit_pair_mc(&sf_free[slot], 0x3);
             ++g;
           } else {
 #pragma unroll
             for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk)
               mma_pair<static_cast<int>(KIND)>(d_tmem, sw128_kmajor_desc(a0 + kk * 32),
-                                               sw128_kmajor_desc(b0 + kk * 32), C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+                                               sw128_kmajor_desc(b0 + kk * 32), C::IDESC,
+                                               (kb != wk.kb0 || kk != 0) ? 1u : 0u);
           }
           tc_commit_pair_mc(&empty[stage], 0x3);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -289,8 +416,9 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
     uint32_t phase = 0;
     int g = 0;
     bool ok = true;
-    for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-      for (int kb = 0; kb < k_blocks; ++kb, ++g) {
+    PairWork wk;
+    for (int w = 0; ok && pair_work(w, pair, npairs, num_tiles, S, k_blocks, wk); ++w) {
+      for (int kb = wk.kb0; kb < wk.kb1; ++kb, ++g) {
         const int slot = g % C::SF_SLOTS;
         if (!mbar_wait(&sf_free[slot], ((g / C::SF_SLOTS) & 1) ^ 1u, abort_flag, kTag, 7)) { ok = false; break; }
         if (!mbar_wait(&sf_full[stage], phase, abort_flag, kTag, 8)) { ok = false; break; }
@@ -327,8 +455,10 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
     const int half = (warp - kFirstEpi) >> 2;
     constexpr int COLS = BN / 2;
     int local = 0;
-    for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
-      const int mb = tile % m_tiles, nb = tile / m_tiles;
+    uint32_t tail_ph = 0;
+    PairWork wk;
+    for (int w = 0; pair_work(w, pair, npairs, num_tiles, S, k_blocks, wk); ++w, ++local) {
+      const int mb = wk.tile % m_tiles, nb = wk.tile / m_tiles;
       const int buf = local % C::ACC_BUFS;
       const uint32_t tph = (local / C::ACC_BUFS) & 1;
       float* sb_t = col_scale + buf * BN;
@@ -361,7 +491,19 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
         tmem_ld_wait();
         const int j0 = half * COLS + c;
         if constexpr (!GATHER) {
-          if (m < p.M) {
+          if (wk.unit >= 0) {
+            // K range of a tail tile: raw partial accumulators to the workspace
+            uint4* wrow = reinterpret_cast<uint4*>(
+                p.tail_ws + (static_cast<size_t>(wk.unit) * 256 + static_cast<int>(rank) * C::BM + row) * BN + j0);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              __stcg(wrow + q, make_uint4(r0[4 * q], r0[4 * q + 1], r0[4 * q + 2], r0[4 * q + 3]));
+            if (two) {
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                __stcg(wrow + 8 + q, make_uint4(r1[4 * q], r1[4 * q + 1], r1[4 * q + 2], r1[4 * q + 3]));
+            }
+          } else if (m < p.M) {
             epilogue_chunk<KIND>(r0, p, m, n0, sa, sb_t + j0, bias_t + j0);
             if (two && n0 + 32 < p.N) epilogue_chunk<KIND>(r1, p, m, n0 + 32, sa, sb_t + j0 + 32, bias_t + j0 + 32);
           }
@@ -391,6 +533,12 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(map_shared_rank(smem_u32(&tempty[buf]), 0));
+      if constexpr (!GATHER && !C::NVF4) {
+        if (wk.unit >= 0 &&
+            !tail_reduce<KIND, BN>(p, wk, S, static_cast<int>(rank), mb, nb, et, sb_t, bias_t, tail_sync, tail_ph,
+                                   abort_flag, kTag))
+          break;
+      }
     }
   }
 

@@ -32,13 +32,86 @@ namespace qib {
 // ---------------------------------------------------------------------------
 // per-device host state
 // ---------------------------------------------------------------------------
+// Tail-split workspace of the CTA-pair GEMM, one per stream (up to
+// kTailSlots streams per device; further streams run without the split):
+// partial accumulators for one wave of 256 x 256 tiles, and the slot's
+// arrival / done counters in g_tail_cnt (zero at load; each launch leaves
+// them zero unless it aborted, and qi_b200_device_status(clear) re-zeroes
+// them after an error).
+constexpr int kTailSlots = 8;
+__device__ unsigned int g_tail_cnt[kTailSlots][2 * kMaxTailTiles];
+struct TailSlot {
+  cudaStream_t stream;
+  uint32_t* ws;
+};
+
 struct DeviceInfo {
   int checked = 0;  // 0 unknown, 1 ok, -1 wrong arch
   int num_sms = 0;
+  int n_tail = 0;
+  TailSlot tail[kTailSlots] = {};
+  unsigned int* tail_cnt = nullptr;
 };
 constexpr int kMaxDevices = 64;
 static DeviceInfo g_dev[kMaxDevices];
 static std::mutex g_dev_mu;
+
+// Workspace and counters for tail-split launches on `stream`; false when none
+// can be had (the launch then runs without the split).  The first use on a
+// stream allocates in relaxed capture mode, so it also works while the
+// stream is being captured into a CUDA graph.
+static bool tail_workspace(DeviceInfo* di, cudaStream_t stream, uint32_t** ws, unsigned int** cnt) {
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (di->tail_cnt == nullptr) {
+    void* a = nullptr;
+    if (cudaGetSymbolAddress(&a, g_tail_cnt) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    di->tail_cnt = static_cast<unsigned int*>(a);
+  }
+  int i = 0;
+  while (i < di->n_tail && di->tail[i].stream != stream) ++i;
+  if (i == di->n_tail) {
+    if (i == kTailSlots) return false;
+    const size_t bytes = static_cast<size_t>(di->num_sms / 2) * 256 * 256 * 4;
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    void* w = nullptr;
+    const cudaError_t e = cudaMalloc(&w, bytes);
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    di->tail[i] = {stream, static_cast<uint32_t*>(w)};
+    di->n_tail = i + 1;
+  }
+  *ws = di->tail[i].ws;
+  *cnt = di->tail_cnt + static_cast<size_t>(i) * 2 * kMaxTailTiles;
+  return true;
+}
+
+// Splits per tail tile for `tiles` pair tiles on `pairs` pairs: the partial
+// last wave (tiles % pairs tiles) spreads its K over the idle pairs.  mode 0
+// is automatic: only when it takes at least 64 K blocks (about 16 us at the
+// 8-bit MMA rate) off the critical path.  A split unit costs a pipeline fill,
+// a workspace round trip and a wait for the slowest pair of its group
+// (pairs finish their whole tiles up to a tile apart), which measured on
+// B200 ate the gain at K = 3072: FP8 4096 x 14336 x 3072 139 -> 150 us,
+// INT8 3120 x 9216 x 3072 74 -> 86 us, while INT8 3120 x 3072 x 14336 went
+// 125 -> 107 us.  1 = none; S >= 2 = at most S.
+static int tail_plan(int tiles, int pairs, int k_blocks, int mode) {
+  if (mode == 1 || tiles <= pairs) return 1;
+  const int tail = tiles % pairs;
+  if (tail == 0 || tail > kMaxTailTiles) return 1;
+  int S = pairs / tail;
+  if (mode >= 2) S = std::min(S, mode);
+  S = std::min(S, std::min(kMaxTailSplit, k_blocks));
+  if (S < 2) return 1;
+  if (mode == 0 && k_blocks - (k_blocks + S - 1) / S < 64) return 1;
+  return S;
+}
 
 static int device_info(DeviceInfo** out) {
   int dev = 0;
@@ -105,6 +178,7 @@ struct LaunchPlan {
   int kernel, grid, cluster, tile_n, stages, smem;
 };
 static thread_local LaunchPlan g_last_plan = {0, 0, 0, 0, 0, 0};
+static thread_local int g_last_tail = 1;  // splits per tail tile of the last CTA-pair launch
 enum PlanKernel { kPlanGemmI8 = 1, kPlanGemmF8 = 2, kPlanGemmBF16 = 3, kPlanGemmNVF4 = 4, kPlanW4Tile = 5,
                   kPlanW4Skinny = 6, kPlanW4Small = 7,
                   kPlanGemmPair = 8 /* + kind: 8 int8, 9 fp8, 10 bf16, 11 nvfp4 */,
@@ -179,9 +253,18 @@ static int launch_gemm2_cfg(const void* A, const void* B, const EpiParams& p, in
   }
   const int tiles = ((p.M + 255) / 256) * ((p.N + BN - 1) / BN);
   const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
+  EpiParams q = p;
+  q.tail_split = 1;
+  if (!C::NVF4 && !GATHER && p.tail_split != 1) {
+    const int S = tail_plan(tiles, pairs, static_cast<int>((ku + C::BK - 1) / C::BK), p.tail_split);
+    DeviceInfo* di = nullptr;
+    if (S > 1 && device_info(&di) == QI_B200_OK && tail_workspace(di, stream, &q.tail_ws, &q.tail_cnt))
+      q.tail_split = S;
+  }
   g_last_plan = {kPlanGemmPair + static_cast<int>(KIND), 2 * pairs, 2, BN, STAGES, C::SMEM_BYTES};
+  g_last_tail = q.tail_split;
   const cudaError_t e = launch_pdl(k_gemm_tc2<KIND, BN, STAGES, GATHER>, dim3(2 * pairs), dim3(C::THREADS),
-                                   C::SMEM_BYTES, stream, 2, ta, tb, tsa, tsb, p, om);
+                                   C::SMEM_BYTES, stream, 2, ta, tb, tsa, tsb, q, om);
   count_launches(1);
   return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
@@ -318,6 +401,15 @@ static int launch_gemm(const void* A, const void* B, const EpiParams& p, cudaStr
         if (cbn != 0) return launch_gemm_csk<KIND>(A, B, p, cbn, cs, stream);
       }
     }
+    if (force_bn == 0 && p.M >= 1024 && p.tail_split != 1) {
+      // long K with a partial last wave: CTA pairs with that wave split along
+      // K (INT8 3120 x 3072 x 14336: 124 us on single-CTA 192-wide tiles,
+      // 107 us as pairs with the split)
+      const int bk = KIND == MmaKind::BF16 ? 64 : 128;
+      const int ptiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
+      if (ptiles >= di->num_sms / 2 && tail_plan(ptiles, di->num_sms / 2, (p.K + bk - 1) / bk, p.tail_split) > 1)
+        return launch_gemm2_cfg<KIND, 256, 6>(A, B, p, di->num_sms, stream);
+    }
     const int bn = force_bn > 0 ? force_bn : pick_bn(p.M, p.N, di->num_sms);
     // Large problems on 256-wide tiles run as CTA pairs (256 x 256 tiles on two
     // SMs): a third less L2 -> SMEM traffic per MMA.  Measured on B200: FP8
@@ -356,9 +448,12 @@ static int check_gemm_args(int kind, const void* A, const void* B, const float* 
 static int gemm_dispatch(int kind, const void* A, const void* B, const float* sa, int sa_stride, const float* sb,
                          int sb_stride, const void* bias, void* D, long long ldd, int M, int N, int K, int flags,
                          int force_bn, cudaStream_t stream) {
+  const int tail_mode = (flags >> QI_B200_TAIL_SPLIT_SHIFT) & 15;
+  flags &= ~(15 << QI_B200_TAIL_SPLIT_SHIFT);
   int rc = check_gemm_args(kind, A, B, sa, sa_stride, sb, sb_stride, bias, D, ldd, M, N, K, flags);
   if (rc) return rc;
   EpiParams p{};
+  p.tail_split = tail_mode;  // 0 automatic, 1 none, S >= 2 at most S (resolved by the pair launcher)
   p.sa = sa;
   p.sa_stride = sa_stride;
   p.sb = sb;
@@ -895,6 +990,8 @@ int qi_b200_last_launch(int* out6) {
   return QI_B200_OK;
 }
 
+int qi_b200_last_tail_split(void) { return g_last_tail; }
+
 int qi_b200_device_status(unsigned int* out4, int clear) {
   unsigned int h[4] = {0, 0, 0, 0};
   if (cudaMemcpyFromSymbol(h, g_status, sizeof(h)) != cudaSuccess) return QI_B200_ECUDA;
@@ -903,6 +1000,10 @@ int qi_b200_device_status(unsigned int* out4, int clear) {
   if (clear) {
     unsigned int z[4] = {0, 0, 0, 0};
     if (cudaMemcpyToSymbol(g_status, z, sizeof(z)) != cudaSuccess) return QI_B200_ECUDA;
+    if (h[0] != 0) {  // an aborted tail-split launch may have left its counters raised
+      static const unsigned int zc[kTailSlots][2 * kMaxTailTiles] = {};
+      if (cudaMemcpyToSymbol(g_tail_cnt, zc, sizeof(zc)) != cudaSuccess) return QI_B200_ECUDA;
+    }
   }
   return QI_B200_OK;
 }
@@ -1154,8 +1255,11 @@ int qi_b200_nvfp4_linear(const void* x_bf16, const void* weight_packed, const vo
                     out_bf16, N, M, N, K, flags, stream);
 }
 
-int qi_b200_int8_linear(const void* x_bf16, const void* qweight, const float* weight_scale, const void* bias,
-                        void* out_bf16, void* ws_q, float* ws_scales, int M, int N, int K, cudaStream_t stream) {
+// gemm_flags: tail-split mode bits only (the entry point that allocates
+// nothing turns the split, whose workspace is allocated on first use, off)
+static int int8_linear_impl(const void* x_bf16, const void* qweight, const float* weight_scale, const void* bias,
+                            void* out_bf16, void* ws_q, float* ws_scales, int M, int N, int K, int gemm_flags,
+                            cudaStream_t stream) {
   if (M == 0) return QI_B200_OK;
   if (ws_q == nullptr || ws_scales == nullptr || weight_scale == nullptr) return QI_B200_EINVAL;
   int rc = check_gemm_args(QI_B200_KIND_INT8, ws_q, qweight, ws_scales, 1, weight_scale, 1, bias, out_bf16, N, M, N,
@@ -1164,7 +1268,12 @@ int qi_b200_int8_linear(const void* x_bf16, const void* qweight, const float* we
   rc = qi_b200_quantize_int8_rowwise(x_bf16, ws_q, ws_scales, M, K, stream);
   if (rc) return rc;
   return gemm_dispatch(QI_B200_KIND_INT8, ws_q, qweight, ws_scales, 1, weight_scale, 1, bias, out_bf16, N, M, N, K,
-                       0, 0, stream);
+                       gemm_flags, 0, stream);
+}
+
+int qi_b200_int8_linear(const void* x_bf16, const void* qweight, const float* weight_scale, const void* bias,
+                        void* out_bf16, void* ws_q, float* ws_scales, int M, int N, int K, cudaStream_t stream) {
+  return int8_linear_impl(x_bf16, qweight, weight_scale, bias, out_bf16, ws_q, ws_scales, M, N, K, 0, stream);
 }
 
 int qi_b200_fp8_linear(const void* x_bf16, const void* weight_fp8, const float* weight_scale,
@@ -1259,5 +1368,6 @@ extern "C" int qi_b200_int8_linear_noalloc(const void* x_bf16, const void* qweig
   float* scales = nullptr;
   int rc = noalloc_scratch(&q, &scales);
   if (rc) return rc;
-  return qi_b200_int8_linear(x_bf16, qweight, weight_scale, bias, out_bf16, q, scales, M, N, K, stream);
+  return int8_linear_impl(x_bf16, qweight, weight_scale, bias, out_bf16, q, scales, M, N, K,
+                          1 << QI_B200_TAIL_SPLIT_SHIFT, stream);
 }

@@ -190,13 +190,15 @@ def splitk_plan(kind: int, M: int, N: int, K: int) -> tuple:
 def gemm(kind: int, a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor | None,
          b_scale: torch.Tensor | None, bias: torch.Tensor | None = None, *, gelu: bool = False,
          raw_acc: bool = False, out: torch.Tensor | None = None, tile_n: int = 0,
-         splits: int = 1) -> torch.Tensor:
+         splits: int = 1, tail_split: int = 0) -> torch.Tensor:
     """D = epi(A[M,K] . B[N,K]^T); see ``qi_b200_gemm`` in include/qi_b200.h.
 
     Scales of one element broadcast (per tensor); otherwise a_scale is [M]
     and b_scale is [N].  ``raw_acc`` returns the 32-bit accumulators (int32
     for INT8, fp32 otherwise) instead of bf16.  ``splits > 1`` splits K over
-    that many CTAs per output tile (``qi_b200_gemm_splitk``).
+    that many CTAs per output tile (``qi_b200_gemm_splitk``).  ``tail_split``
+    sets how the CTA-pair kernel spreads its partial last wave over idle pairs
+    (0 the library's choice, 1 no split, S at most S splits per tile).
     """
     dt = {_lib.KIND_INT8: (torch.int8,), _lib.KIND_FP8_E4M3: (torch.uint8, torch.float8_e4m3fn),
           _lib.KIND_BF16: (torch.bfloat16,)}[kind]
@@ -227,6 +229,8 @@ def gemm(kind: int, a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor | No
         odt = (torch.int32 if kind == _lib.KIND_INT8 else torch.float32) if raw_acc else torch.bfloat16
         out = torch.empty((M, N), dtype=odt, device=a.device)
     flags = (_lib.EPI_GELU if gelu else 0) | (_lib.EPI_RAW_ACC if raw_acc else 0)
+    if not 0 <= tail_split <= 15:
+        raise ValueError(f"tail_split must be in [0, 15], got {tail_split}.")
     if splits > 1:  # split K over several CTAs per tile, sum the partials in a second kernel
         if raw_acc or tile_n != 0:
             raise ValueError("splits > 1 takes bf16 outputs and the library's tile choice")
@@ -236,6 +240,7 @@ def gemm(kind: int, a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor | No
                   _ptr(bias), _ptr(out), out.stride(0), M, N, K, flags, splits, _ptr(ws), ws_bytes,
                   _stream(a.device))
         return out
+    flags |= tail_split << _lib.TAIL_SPLIT_SHIFT
     _lib.call("qi_b200_gemm", kind, _ptr(a), _ptr(b), _ptr(sa), sa_stride, _ptr(sb), sb_stride,
               _ptr(bias), _ptr(out), out.stride(0), M, N, K, flags, tile_n, _stream(a.device))
     return out

@@ -377,3 +377,104 @@ def test_int8_module_with_input_scale_fuses_smoothing():
     y_ref = K.int8_linear((xd / isc.to(torch.bfloat16)).contiguous(), lin.qweight, lin.scales[:, 0].contiguous(),
                           lin.bias.to(torch.bfloat16))
     assert torch.equal(y, y_ref)
+
+
+def _expected_tail_split(M, N, Kd, bn, elem, mode):
+    """Splits per tail tile the library should pick (its rule, restated)."""
+    pairs = torch.cuda.get_device_properties(0).multi_processor_count // 2
+    tiles = -(-M // 256) * -(-N // bn)
+    kb = -(-Kd * elem // 128)
+    rem = tiles % pairs
+    if mode == 1 or tiles <= pairs or rem == 0:
+        return 1
+    s = pairs // rem
+    if mode >= 2:
+        s = min(s, mode)
+    s = min(s, 8, kb)
+    if s < 2 or (mode == 0 and kb - -(-kb // s) < 64):
+        return 1
+    return s
+
+
+@pytest.mark.parametrize("M,N,Kd,tile_n,tail", [(1000, 4744, 1024, -256, 8), (1000, 4744, 1024, -192, 2),
+                                                (1000, 4744, 1024, -128, 5), (2304, 2304, 12288, -256, 0),
+                                                (3120, 3072, 14336, 0, 0)])
+@pytest.mark.parametrize("gelu", [False, True])
+def test_pair_tail_split_matches_unsplit(M, N, Kd, tile_n, tail, gelu):
+    """The CTA-pair kernel's partial last wave (tiles % pairs tiles) split
+    along K over the idle pairs: INT8 outputs bit-identical to the same
+    kernel without the split (and to the oracle); FP8 and BF16 agree to fp32
+    summation order.  Ragged M and N put partial tiles into the tail; the
+    last two cases are the library's own choice (long K), the last one also
+    of the kernel (the DiT FFN-down shape; unsplit it runs single-CTA
+    tiles)."""
+    x, w, b = make_small_case(M, N, Kd, seed=M + N + Kd, outlier_frac=0.002)
+    qw, sw, _ = O.quantize_weight_rtn(w.numpy(), 8, -1, True)
+    qa, sa = K.quantize_int8_rowwise(x.to(DEV))
+    qwd, swd, bd = torch.from_numpy(qw).to(DEV), torch.from_numpy(sw[:, 0]).to(DEV), b.to(DEV)
+    bn = -tile_n if tile_n else 256
+
+    y = K.gemm(_lib.KIND_INT8, qa, qwd, sa, swd, bd, gelu=gelu, tile_n=tile_n, tail_split=tail)
+    want = _expected_tail_split(M, N, Kd, bn, 1, tail)
+    assert _lib.last_launch()["kernel"] == "gemm_int8_pair"
+    assert want > 1 and _lib.last_tail_split() == want
+    y_ref = K.gemm(_lib.KIND_INT8, qa, qwd, sa, swd, bd, gelu=gelu, tile_n=tile_n, tail_split=1)
+    assert _lib.last_tail_split() == 1 or _lib.last_launch()["kernel"] == "gemm_int8"
+    assert torch.equal(y, y_ref)
+    if not gelu and tile_n == -256 and M == 1000:
+        yo, _, _, _ = O.int8_linear(bits(x), qw, sw[:, 0], bits(b))
+        np.testing.assert_array_equal(bits(y), yo)
+
+    qf, sf = K.quantize_fp8_rowwise(x.to(DEV))
+    wf = (w * 20).to(torch.float8_e4m3fn).view(torch.uint8).to(DEV)
+    wsf = torch.full((N,), 0.05, device=DEV)
+    f = K.gemm(_lib.KIND_FP8_E4M3, qf, wf, sf, wsf, bd, gelu=gelu, tile_n=tile_n, tail_split=tail)
+    assert _lib.last_tail_split() == _expected_tail_split(M, N, Kd, bn, 1, tail)
+    f_ref = K.gemm(_lib.KIND_FP8_E4M3, qf, wf, sf, wsf, bd, gelu=gelu, tile_n=tile_n, tail_split=1)
+    assert O.rel_fro(f.float().cpu().numpy(), f_ref.float().cpu().numpy()) <= 1e-3
+
+    xb, wb = x.to(DEV), w.to(torch.bfloat16).to(DEV)
+    h = K.gemm(_lib.KIND_BF16, xb, wb, None, None, bd, gelu=gelu, tile_n=tile_n, tail_split=tail)
+    assert _lib.last_tail_split() == _expected_tail_split(M, N, Kd, bn, 2, tail)
+    h_ref = K.gemm(_lib.KIND_BF16, xb, wb, None, None, bd, gelu=gelu, tile_n=tile_n, tail_split=1)
+    assert O.rel_fro(h.float().cpu().numpy(), h_ref.float().cpu().numpy()) <= 1e-3
+    assert _lib.device_status() == (0, 0, 0, 0)
+
+
+def test_pair_tail_split_repeated_and_in_cuda_graph():
+    """Tail-split launches leave their counters at zero: back-to-back launches
+    on new data, and replays of a CUDA graph captured on a stream that had
+    not used the split before (its workspace is allocated during capture),
+    all stay bit-identical to the unsplit kernel."""
+    M, N, Kd = 1000, 4744, 1024
+    qwd = swd = bd = None
+    outs = []
+    for seed in (5, 6, 7):
+        x, w, b = make_small_case(M, N, Kd, seed=seed, outlier_frac=0.002)
+        if qwd is None:
+            qw, sw, _ = O.quantize_weight_rtn(w.numpy(), 8, -1, True)
+            qwd, swd, bd = torch.from_numpy(qw).to(DEV), torch.from_numpy(sw[:, 0]).to(DEV), b.to(DEV)
+        qa, sa = K.quantize_int8_rowwise(x.to(DEV))
+        y = K.gemm(_lib.KIND_INT8, qa, qwd, sa, swd, bd, tile_n=-256, tail_split=8)
+        assert _lib.last_tail_split() == 8
+        assert torch.equal(y, K.gemm(_lib.KIND_INT8, qa, qwd, sa, swd, bd, tile_n=-256, tail_split=1))
+        outs.append((qa, sa, y))
+
+    qa_s = outs[0][0].clone()
+    sa_s = outs[0][1].clone()
+    y_s = torch.empty((M, N), dtype=torch.bfloat16, device=DEV)
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g, stream=side):
+            K.gemm(_lib.KIND_INT8, qa_s, qwd, sa_s, swd, bd, out=y_s, tile_n=-256, tail_split=8)
+    assert _lib.last_tail_split() == 8
+    for qa, sa, y in outs[1:] + outs[:1]:
+        qa_s.copy_(qa)
+        sa_s.copy_(sa)
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(y_s, y)
+    del g
+    assert _lib.device_status() == (0, 0, 0, 0)
