@@ -297,7 +297,9 @@ int qi_b200_w4a16_linear_ws(const void* x_bf16, const void* qweight_packed, cons
  *   g = max(amax / 2688, 1e-12); sf = e4m3(min(amax16 / (6 g), 448));
  *   q = e2m1(clamp(x / (sf g), +-6)).
  * Activation quantization, g_mode: 0 = static per-tensor g (g_in), 1 =
- * dynamic per-tensor (two passes; ws_amax is one uint32 of scratch; g_out[0]),
+ * dynamic per-tensor (two passes; ws_amax is one uint32 of scratch, needing
+ * no clearing; the amax pass keeps per-block maxima in a library slot of the
+ * calling stream; g_out[0]),
  * 2 = dynamic per-row (g_out[rows]).  cols % 64 == 0; x and sf_atoms
  * 16-byte aligned, q_packed 8-byte aligned. */
 int qi_b200_quantize_nvfp4(const void* x_bf16, int rows, int cols, int g_mode, const float* g_in,

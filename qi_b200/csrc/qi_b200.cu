@@ -32,14 +32,20 @@ namespace qib {
 // ---------------------------------------------------------------------------
 // per-device host state
 // ---------------------------------------------------------------------------
-// Tail-split workspace of the CTA-pair GEMM, one per stream (up to
-// kTailSlots streams per device; further streams run without the split):
+// Per-stream slots (up to kTailSlots streams per device; further streams run
+// without what a slot provides).  Tail-split workspace of the CTA-pair GEMM:
 // partial accumulators for one wave of 256 x 256 tiles, and the slot's
 // arrival / done counters in g_tail_cnt (zero at load; each launch leaves
 // them zero unless it aborted, and qi_b200_device_status(clear) re-zeroes
 // them after an error).
 constexpr int kTailSlots = 8;
 __device__ unsigned int g_tail_cnt[kTailSlots][2 * kMaxTailTiles];
+// Per-stream slots also hold the NVFP4 tensor amax pass's per-block maxima
+// and its ticket (zero at load and after every launch), so that pass needs
+// no memset before it.
+constexpr int kAmaxParts = 2048;
+__device__ unsigned int g_amax_part[kTailSlots][kAmaxParts];
+__device__ unsigned int g_amax_ticket[kTailSlots];
 struct TailSlot {
   cudaStream_t stream;
   uint32_t* ws;
@@ -51,6 +57,8 @@ struct DeviceInfo {
   int n_tail = 0;
   TailSlot tail[kTailSlots] = {};
   unsigned int* tail_cnt = nullptr;
+  unsigned int* amax_part = nullptr;
+  unsigned int* amax_ticket = nullptr;
 };
 constexpr int kMaxDevices = 64;
 static DeviceInfo g_dev[kMaxDevices];
@@ -60,20 +68,36 @@ static std::mutex g_dev_mu;
 // can be had (the launch then runs without the split).  The first use on a
 // stream allocates in relaxed capture mode, so it also works while the
 // stream is being captured into a CUDA graph.
-static bool tail_workspace(DeviceInfo* di, cudaStream_t stream, uint32_t** ws, unsigned int** cnt) {
-  std::lock_guard<std::mutex> lk(g_dev_mu);
+// Slot of `stream` (registered on first use, up to kTailSlots per device),
+// -1 when the table is full or the slot arrays cannot be located.  Call with
+// g_dev_mu held.
+static int stream_slot(DeviceInfo* di, cudaStream_t stream) {
   if (di->tail_cnt == nullptr) {
-    void* a = nullptr;
-    if (cudaGetSymbolAddress(&a, g_tail_cnt) != cudaSuccess) {
+    void *a = nullptr, *b = nullptr, *c = nullptr;
+    if (cudaGetSymbolAddress(&a, g_tail_cnt) != cudaSuccess || cudaGetSymbolAddress(&b, g_amax_part) != cudaSuccess ||
+        cudaGetSymbolAddress(&c, g_amax_ticket) != cudaSuccess) {
       cudaGetLastError();
-      return false;
+      return -1;
     }
+    di->amax_part = static_cast<unsigned int*>(b);
+    di->amax_ticket = static_cast<unsigned int*>(c);
     di->tail_cnt = static_cast<unsigned int*>(a);
   }
   int i = 0;
   while (i < di->n_tail && di->tail[i].stream != stream) ++i;
   if (i == di->n_tail) {
-    if (i == kTailSlots) return false;
+    if (i == kTailSlots) return -1;
+    di->tail[i] = {stream, nullptr};
+    di->n_tail = i + 1;
+  }
+  return i;
+}
+
+static bool tail_workspace(DeviceInfo* di, cudaStream_t stream, uint32_t** ws, unsigned int** cnt) {
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  const int i = stream_slot(di, stream);
+  if (i < 0) return false;
+  if (di->tail[i].ws == nullptr) {
     const size_t bytes = static_cast<size_t>(di->num_sms / 2) * 256 * 256 * 4;
     cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
     cudaThreadExchangeStreamCaptureMode(&mode);
@@ -84,8 +108,7 @@ static bool tail_workspace(DeviceInfo* di, cudaStream_t stream, uint32_t** ws, u
       cudaGetLastError();
       return false;
     }
-    di->tail[i] = {stream, static_cast<uint32_t*>(w)};
-    di->n_tail = i + 1;
+    di->tail[i].ws = static_cast<uint32_t*>(w);
   }
   *ws = di->tail[i].ws;
   *cnt = di->tail_cnt + static_cast<size_t>(i) * 2 * kMaxTailTiles;
@@ -747,15 +770,39 @@ static int nvfp4_quantize(const void* x, int rows, int cols, int g_mode, const f
   const int ka = cols / 64;
   const int rows_pad = (rows + 127) & ~127;
   const long long blocks = (long long)rows_pad * (cols / 16);
-  const int grid_flat = (int)std::min<long long>((blocks + 255) / 256, (long long)di->num_sms * 16);
+  // the tensor-scale kernels walk x from its end in grid-stride order: a grid
+  // of exactly the resident blocks keeps that order (all blocks run together)
+  static int occ[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (occ[dev] == 0) {
+    int o = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k_quant_nvfp4_tensor<1>, 256, 0) != cudaSuccess || o < 1)
+      o = 4;
+    occ[dev] = o;
+  }
+  const int grid_flat = (int)std::min<long long>((blocks + 255) / 256, (long long)di->num_sms * occ[dev]);
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   auto* qb = static_cast<uint8_t*>(q);
   auto* sb = static_cast<uint8_t*>(sf);
   if (g_mode == 1) {
-    if (cudaMemsetAsync(ws_amax, 0, sizeof(unsigned int), stream) != cudaSuccess) return QI_B200_ECUDA;
     const long long n = (long long)rows * cols;
-    const int g2 = (int)std::min<long long>((n / 8 + 255) / 256 + 1, (long long)di->num_sms * 8);
-    launch_pdl(k_amax_bf16, dim3(g2), dim3(256), 0, stream, 1, xb, n, ws_amax);
+    const int g2 = (int)std::min<long long>(
+        std::min<long long>((n / 8 + 255) / 256 + 1, (long long)di->num_sms * 8), kAmaxParts);
+    // per-block maxima in this stream's slot, reduced by the last block: no
+    // memset of ws_amax (and no graph node that breaks the launch chain)
+    unsigned int *part = nullptr, *ticket = nullptr;
+    {
+      std::lock_guard<std::mutex> lk(g_dev_mu);
+      const int slot = stream_slot(di, stream);
+      if (slot >= 0) {
+        part = di->amax_part + static_cast<size_t>(slot) * kAmaxParts;
+        ticket = di->amax_ticket + slot;
+      }
+    }
+    if (part == nullptr && cudaMemsetAsync(ws_amax, 0, sizeof(unsigned int), stream) != cudaSuccess)
+      return QI_B200_ECUDA;
+    launch_pdl(k_amax_bf16, dim3(g2), dim3(256), 0, stream, 1, xb, n, ws_amax, part, ticket);
     launch_pdl(k_quant_nvfp4_tensor<1>, dim3(grid_flat), dim3(256), 0, stream, 1, xb, rows, cols,
                static_cast<const float*>(nullptr), static_cast<const unsigned int*>(ws_amax), g_out, qb, sb, ka);
     count_launches(2);
@@ -1000,9 +1047,11 @@ int qi_b200_device_status(unsigned int* out4, int clear) {
   if (clear) {
     unsigned int z[4] = {0, 0, 0, 0};
     if (cudaMemcpyToSymbol(g_status, z, sizeof(z)) != cudaSuccess) return QI_B200_ECUDA;
-    if (h[0] != 0) {  // an aborted tail-split launch may have left its counters raised
+    if (h[0] != 0) {  // an aborted launch may have left its slot counters raised
       static const unsigned int zc[kTailSlots][2 * kMaxTailTiles] = {};
+      static const unsigned int zt[kTailSlots] = {};
       if (cudaMemcpyToSymbol(g_tail_cnt, zc, sizeof(zc)) != cudaSuccess) return QI_B200_ECUDA;
+      if (cudaMemcpyToSymbol(g_amax_ticket, zt, sizeof(zt)) != cudaSuccess) return QI_B200_ECUDA;
     }
   }
   return QI_B200_OK;

@@ -42,33 +42,63 @@ __device__ __forceinline__ long long sf_atom_offset(int row, int blk, int ka_per
   return (static_cast<long long>(ra) * ka_per_rowblock + ka) * 512 + (r & 31) * 16 + (r >> 5) * 4 + j;
 }
 
-// amax of a whole bf16 tensor into *amax_bits (float bits; must start at 0)
+// amax of a whole bf16 tensor into *amax_bits (float bits).  part == nullptr:
+// blocks atomicMax into *amax_bits, which must start at 0.  Otherwise each
+// block stores its maximum in part[blockIdx.x] and the last block to finish
+// (ticket, zero on entry and left zero) reduces them into *amax_bits, so the
+// word needs no clearing before the launch.
 __global__ void __launch_bounds__(256)
-k_amax_bf16(const __nv_bfloat16* __restrict__ x, long long n, unsigned int* __restrict__ amax_bits) {
+k_amax_bf16(const __nv_bfloat16* __restrict__ x, long long n, unsigned int* __restrict__ amax_bits,
+            unsigned int* __restrict__ part, unsigned int* __restrict__ ticket) {
   griddep_wait();
   griddep_launch_dependents();
   float m = 0.f;
   const long long nvec = n / 8;
   const uint4* xv = reinterpret_cast<const uint4*>(x);
-  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < nvec; i += 256ll * gridDim.x) {
+  // two 16-byte loads in flight per thread; bf16 |x| max taken exactly in bf16x2
+  const long long stride = 256ll * gridDim.x;
+  __nv_bfloat162 m2 = __float2bfloat162_rn(0.f);
+  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < nvec; i += 2 * stride) {
     const uint4 v = __ldg(xv + i);
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+    const uint4 u = i + stride < nvec ? __ldg(xv + i + stride) : make_uint4(0, 0, 0, 0);
+    const uint32_t w[8] = {v.x, v.y, v.z, v.w, u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float2 f = __bfloat1622float2(h[k]);
-      m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
-    }
+    for (int k = 0; k < 8; ++k) m2 = __hmax2(m2, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&w[k])));
   }
+  m = fmaxf(__low2float(m2), __high2float(m2));
   for (long long i = nvec * 8 + blockIdx.x * 256ll + threadIdx.x; i < n; i += 256ll * gridDim.x)
     m = fmaxf(m, fabsf(__bfloat162float(x[i])));
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
   __shared__ float wm[8];
+  __shared__ unsigned int last_sh;
   if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m;
   __syncthreads();
   if (threadIdx.x == 0) {
     for (int w = 1; w < 8; ++w) m = fmaxf(m, wm[w]);
-    atomicMax(amax_bits, __float_as_uint(m));  // non-negative floats order like their bits
+    if (part == nullptr) {
+      atomicMax(amax_bits, __float_as_uint(m));  // non-negative floats order like their bits
+    } else {
+      part[blockIdx.x] = __float_as_uint(m);
+      __threadfence();
+      last_sh = atomicAdd(ticket, 1u) == gridDim.x - 1 ? 1u : 0u;
+    }
+  }
+  if (part == nullptr) return;
+  __syncthreads();
+  if (last_sh == 0) return;
+  __threadfence();  // every block's part is visible
+  unsigned int r = 0;
+  for (int i = threadIdx.x; i < static_cast<int>(gridDim.x); i += 256) r = max(r, __ldcg(part + i));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) r = max(r, __shfl_xor_sync(0xffffffffu, r, off));
+  __shared__ unsigned int wr[8];
+  if ((threadIdx.x & 31) == 0) wr[threadIdx.x >> 5] = r;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 8; ++w) r = max(r, wr[w]);
+    *amax_bits = r;
+    atomicExch(ticket, 0u);  // ready for the next launch
   }
 }
 
@@ -114,6 +144,26 @@ __device__ __forceinline__ float rcp_approx(float v) {
 __device__ __forceinline__ uint32_t e4m3_code(float v) {
   return static_cast<uint32_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
 }
+// E4M3 codes of two floats in one conversion: lo in bits 0-7, hi in 8-15.
+__device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
+  uint16_t out;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(out) : "f"(hi), "f"(lo));
+  return out;
+}
+// E2M1 codes of 8 floats (pairs a..d, .x the lower nibble of each byte),
+// packed into 4 bytes in element order.
+__device__ __forceinline__ uint32_t e2m1x8(float2 a, float2 b, float2 c, float2 d) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}\n"
+      : "=r"(out)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y), "f"(d.x), "f"(d.y));
+  return out;
+}
 
 // nvfp4_block with divisions only where they decide the result, for a
 // per-tensor g.  Each quotient the recipe rounds (bm / fl(6 g) for the block
@@ -124,9 +174,13 @@ __device__ __forceinline__ uint32_t e4m3_code(float v) {
 // monotonic, so when both ends convert to the same code that code is the
 // recipe's.  Where they differ (a quotient within a few ulp of a rounding
 // boundary; exact ties occur, e.g. when sf carries a factor that cancels
-// against g's), that scale or that pair of codes is recomputed with
-// correctly rounded divisions.  rg = the bracket ends of 1 / fl(6 g).
-// Saturating conversions are the recipe's clamps (448, +-6).
+// against g's), that scale or the block's codes are recomputed with
+// correctly rounded divisions.  Both bracket ends of the scale go through one
+// E4M3x2 conversion and the codes eight at a time (E2M1x2 conversions packed
+// into a word), so the common case costs one comparison per 8 codes.  A zero
+// block scale gives +0 codes (the recipe's q = 0 where sf == 0, also for
+// negative inputs).  rg = the bracket ends of 1 / fl(6 g).  Saturating
+// conversions are the recipe's clamps (448, +-6).
 __device__ __forceinline__ uint2 nvfp4_block_fast(const uint4& v0, const uint4& v1, float g, float g6, float2 rg,
                                                   uint8_t& sfc) {
   const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
@@ -134,24 +188,33 @@ __device__ __forceinline__ uint2 nvfp4_block_fast(const uint4& v0, const uint4& 
 #pragma unroll
   for (int k = 1; k < 8; ++k) m2 = __hmax2(m2, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&w[k])));
   const float bm = fmaxf(__low2float(m2), __high2float(m2));  // exact: max of the same values
-  uint32_t c = e4m3_code(__fmul_rn(bm, rg.x));
-  if (c != e4m3_code(__fmul_rn(bm, rg.y))) c = e4m3_code(fminf(__fdiv_rn(bm, g6), 448.0f));
+  const uint32_t cc = e4m3x2(__fmul_rn(bm, rg.x), __fmul_rn(bm, rg.y));  // both bracket ends at once
+  uint32_t c = cc & 0xffu;
+  if (c != (cc >> 8)) c = e4m3_code(fminf(__fdiv_rn(bm, g6), 448.0f));
   sfc = static_cast<uint8_t>(c);
+  if (c == 0) return make_uint2(0u, 0u);  // sf == 0: every code is +0
   __half_raw hr = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(sfc), __NV_E4M3);
   const float denom = __fmul_rn(__half2float(__half(hr)), g);
-  const float inv = denom > 0.f ? rcp_approx(denom) : 0.f;
+  const float inv = rcp_approx(denom);
   const float il = inv * (1.0f - 0x1p-20f), ih = inv * (1.0f + 0x1p-20f);
   const float2 il2 = make_float2(il, il), ih2 = make_float2(ih, ih);
-  uint32_t lo = 0, hi = 0;
+  float2 f[8], a[8], b[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
-    const float2 a = __fmul2_rn(f, il2), b = __fmul2_rn(f, ih2);
-    uint32_t byte = e2m1x2(a.x, a.y);
-    if (byte != e2m1x2(b.x, b.y))
-      byte = e2m1x2(fminf(fmaxf(__fdiv_rn(f.x, denom), -6.f), 6.f), fminf(fmaxf(__fdiv_rn(f.y, denom), -6.f), 6.f));
-    if (k < 4) lo |= byte << (8 * k);
-    else hi |= byte << (8 * (k - 4));
+    f[k] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+    a[k] = __fmul2_rn(f[k], il2);
+    b[k] = __fmul2_rn(f[k], ih2);
+  }
+  uint32_t lo = e2m1x8(a[0], a[1], a[2], a[3]), hi = e2m1x8(a[4], a[5], a[6], a[7]);
+  if (lo != e2m1x8(b[0], b[1], b[2], b[3]) || hi != e2m1x8(b[4], b[5], b[6], b[7])) {
+    // a quotient within a few ulp of a rounding boundary: the block's codes by
+    // correctly rounded division (identical to the bracket's code elsewhere)
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      a[k] = make_float2(fminf(fmaxf(__fdiv_rn(f[k].x, denom), -6.f), 6.f),
+                         fminf(fmaxf(__fdiv_rn(f[k].y, denom), -6.f), 6.f));
+    lo = e2m1x8(a[0], a[1], a[2], a[3]);
+    hi = e2m1x8(a[4], a[5], a[6], a[7]);
   }
   return make_uint2(lo, hi);
 }
@@ -182,14 +245,11 @@ k_quant_nvfp4_tensor(const __nv_bfloat16* __restrict__ x, int rows, int cols, co
   const float rg0 = rcp_approx(g6);
   const float2 rg = make_float2(rg0 * (1.0f - 0x1p-20f), rg0 * (1.0f + 0x1p-20f));
   const int chunks = rows_pad * bpr / 32;  // the host keeps rows_pad * bpr < 2^31
-  for (int ch = (blockIdx.x * 256 + threadIdx.x) / 32; ch < chunks; ch += 256 * gridDim.x / 32) {
-    const int t = (chunks - 1 - ch) * 32 + lane;
-    const int row = t / bpr;
-    const int b = t - row * bpr;
+  const int cstride = 256 * gridDim.x / 32;
+  // quantize + store one block (row < rows), then the atom word of 4 lanes
+  auto finish = [&](const uint4& v0, const uint4& v1, int row, int b) {
     uint8_t sfc = 0;
     if (row < rows) {
-      const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<long long>(row) * cols + b * 16);
-      const uint4 v0 = __ldg(p), v1 = __ldg(p + 1);
       const uint2 packed = nvfp4_block_fast(v0, v1, g, g6, rg, sfc);
       *reinterpret_cast<uint2*>(q + static_cast<long long>(row) * (cols >> 1) + b * 8) = packed;
     }
@@ -200,6 +260,32 @@ k_quant_nvfp4_tensor(const __nv_bfloat16* __restrict__ x, int rows, int cols, co
     const uint32_t s3 = __shfl_down_sync(0xffffffffu, s0, 3);
     if ((b & 3) == 0)
       *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(row, b, ka_per_rowblock)) = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
+  };
+  // two chunks per iteration: both chunks' loads are in flight before either
+  // is quantized (chunk indices are warp-uniform, so are the branches)
+  for (int ch = (blockIdx.x * 256 + threadIdx.x) / 32; ch < chunks; ch += 2 * cstride) {
+    const int ch2 = ch + cstride;
+    const int t = (chunks - 1 - ch) * 32 + lane;
+    const int row = t / bpr, b = t - row * bpr;
+    uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0, w0 = v0, w1 = v0;
+    if (row < rows) {
+      const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<long long>(row) * cols + b * 16);
+      v0 = __ldg(p);
+      v1 = __ldg(p + 1);
+    }
+    int row2 = rows, b2 = 0;
+    if (ch2 < chunks) {
+      const int t2 = (chunks - 1 - ch2) * 32 + lane;
+      row2 = t2 / bpr;
+      b2 = t2 - row2 * bpr;
+      if (row2 < rows) {
+        const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<long long>(row2) * cols + b2 * 16);
+        w0 = __ldg(p);
+        w1 = __ldg(p + 1);
+      }
+    }
+    finish(v0, v1, row, b);
+    if (ch2 < chunks) finish(w0, w1, row2, b2);
   }
 }
 

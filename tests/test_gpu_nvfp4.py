@@ -52,6 +52,8 @@ def test_quantize_nvfp4_bit_exact(M, Kd, mode):
     x, _, _ = make_small_case(M, 8, Kd, seed=M + Kd + mode)
     x = x.clone()
     x[0, :16] = 0.0  # an all-zero block -> scale 0, codes 0
+    x[0, 16:32] = -0.0  # negative zeros, and tiny negatives whose block scale
+    x[0, 32:48] = -1e-30  # rounds to 0: codes +0 as well (q = 0 where sf == 0)
     xf = O.bf16_to_f32(bits(x))
     gstat = torch.tensor([0.0031], dtype=torch.float32)
     q, sf, g = K.quantize_nvfp4(x.to(DEV), mode, gstat.to(DEV) if mode == 0 else None)
