@@ -300,7 +300,7 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
   const int num_tiles = m_tiles * n_tiles;
   const int k_units = C::NVF4 ? p.K / 2 : p.K;  // K in TMA elements
   const int k_blocks = (k_units + C::BK - 1) / C::BK;
-  const int S = (C::NVF4 || GATHER) ? 1 : p.tail_split;  // tail split (host: tail * S <= pairs, S <= k_blocks)
+  const int S = GATHER ? 1 : p.tail_split;  // tail split (host: tail * S <= pairs, S <= k_blocks)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -461,8 +461,14 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
       const int mb = wk.tile % m_tiles, nb = wk.tile / m_tiles;
       const int buf = local % C::ACC_BUFS;
       const uint32_t tph = (local / C::ACC_BUFS) & 1;
-      float* sb_t = col_scale + buf * BN;
-      __nv_bfloat16* bias_t = col_bias + buf * BN;
+      // column parameters alternate between two buffers whatever ACC_BUFS is:
+      // a warp that is done with work item w stages those of w + 1 while other
+      // warps may still read w's; epi_sync of w + 1 proves all are done with
+      // w - 1, whose buffer w + 1 reuses
+      const int pb = local & 1;
+      const uint32_t pph = (local >> 1) & 1;
+      float* sb_t = col_scale + pb * BN;
+      __nv_bfloat16* bias_t = col_bias + pb * BN;
       for (int j = et; j < BN; j += kEpiThreads) {
         const int n = nb * BN + j;
         float sv = 1.0f;
@@ -474,8 +480,8 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
       const int m = mb * 256 + static_cast<int>(rank) * C::BM + row;
       float sa = 1.0f;
       if (p.sa != nullptr && m < p.M) sa = __ldg(p.sa + static_cast<long long>(m) * p.sa_stride);
-      mbar_arrive(&epi_sync[buf]);
-      if (!mbar_wait(&epi_sync[buf], tph, abort_flag, kTag, 5)) break;
+      mbar_arrive(&epi_sync[pb]);
+      if (!mbar_wait(&epi_sync[pb], pph, abort_flag, kTag, 5)) break;
       if (!mbar_wait(&tfull[buf], tph, abort_flag, kTag, 4)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) +
@@ -533,7 +539,7 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(map_shared_rank(smem_u32(&tempty[buf]), 0));
-      if constexpr (!GATHER && !C::NVF4) {
+      if constexpr (!GATHER) {
         if (wk.unit >= 0 &&
             !tail_reduce<KIND, BN>(p, wk, S, static_cast<int>(rank), mb, nb, et, sb_t, bias_t, tail_sync, tail_ph,
                                    abort_flag, kTag))
