@@ -307,8 +307,7 @@ int qi_b200_quantize_nvfp4(const void* x_bf16, int rows, int cols, int g_mode, c
 /* D = bf16( (acc * a_g[m or 0]) * b_g[0] + bias ), acc = sum over 16-blocks of
  * (q_a q_b) sf_a sf_b on tcgen05 kind::mxf4nvf4 (block16).  K % 256 == 0.
  * flags: QI_B200_EPI_GELU, QI_B200_EPI_RAW_ACC, tile choice (see
- * QI_B200_NVFP4_TILE_SHIFT), split of the CTA-pair kernel's last wave (see
- * QI_B200_TAIL_SPLIT_SHIFT). */
+ * QI_B200_NVFP4_TILE_SHIFT). */
 int qi_b200_nvfp4_gemm(const void* A_packed, const void* A_sf, const void* B_packed, const void* B_sf,
                        const float* a_global_scale, int a_scale_per_row, const float* b_global_scale,
                        const void* bias, void* D, long long ldd, int M, int N, int K, int flags, cudaStream_t stream);

@@ -300,7 +300,10 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
   const int num_tiles = m_tiles * n_tiles;
   const int k_units = C::NVF4 ? p.K / 2 : p.K;  // K in TMA elements
   const int k_blocks = (k_units + C::BK - 1) / C::BK;
-  const int S = GATHER ? 1 : p.tail_split;  // tail split (host: tail * S <= pairs, S <= k_blocks)
+  // tail split (host: tail * S <= pairs, S <= k_blocks).  Not for NVFP4: its
+  // 512-thread CTA has 128 registers a thread, and the split's reduction
+  // made the kernel spill (measured 92 -> 98 us at config 4)
+  const int S = (C::NVF4 || GATHER) ? 1 : p.tail_split;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -539,7 +542,7 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(map_shared_rank(smem_u32(&tempty[buf]), 0));
-      if constexpr (!GATHER) {
+      if constexpr (!GATHER && !C::NVF4) {
         if (wk.unit >= 0 &&
             !tail_reduce<KIND, BN>(p, wk, S, static_cast<int>(rank), mb, nb, et, sb_t, bias_t, tail_sync, tail_ph,
                                    abort_flag, kTag))

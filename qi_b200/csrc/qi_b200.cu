@@ -278,7 +278,7 @@ static int launch_gemm2_cfg(const void* A, const void* B, const EpiParams& p, in
   const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
   EpiParams q = p;
   q.tail_split = 1;
-  if (!GATHER && p.tail_split != 1) {
+  if (!C::NVF4 && !GATHER && p.tail_split != 1) {
     const int S = tail_plan(tiles, pairs, static_cast<int>((ku + C::BK - 1) / C::BK), p.tail_split);
     DeviceInfo* di = nullptr;
     if (S > 1 && device_info(&di) == QI_B200_OK && tail_workspace(di, stream, &q.tail_ws, &q.tail_cnt))
@@ -827,8 +827,7 @@ static int nvfp4_gemm(const void* A, const void* SFA, const void* B, const void*
   if (K % 256 != 0 || N % 8 != 0 || ldd < N || ldd % 8 != 0) return QI_B200_ESHAPE;
   if (!aligned16(A) || !aligned16(B) || !aligned16(D) || !aligned16(SFA) || !aligned16(SFB)) return QI_B200_EALIGN;
   const int tile = (flags >> QI_B200_NVFP4_TILE_SHIFT) & 3;
-  const int tail_mode = (flags >> QI_B200_TAIL_SPLIT_SHIFT) & 15;
-  flags &= ~((3 << QI_B200_NVFP4_TILE_SHIFT) | (15 << QI_B200_TAIL_SPLIT_SHIFT));
+  flags &= ~(3 << QI_B200_NVFP4_TILE_SHIFT);
   if (flags & ~(kEpiGelu | kEpiRawAcc)) return QI_B200_EINVAL;
   EpiParams p = {};
   p.sa = a_g;
@@ -841,7 +840,6 @@ static int nvfp4_gemm(const void* A, const void* SFA, const void* B, const void*
   p.M = M;
   p.N = N;
   p.K = K;
-  p.tail_split = tail_mode;
   p.flags = flags;
   p.sfa = static_cast<const uint8_t*>(SFA);
   p.sfb = static_cast<const uint8_t*>(SFB);

@@ -354,8 +354,7 @@ def quantize_nvfp4(x: torch.Tensor, mode: int = NVFP4_DYNAMIC_TENSOR, global_sca
     return q, sf, g
 
 
-def nvfp4_gemm(a_packed, a_sf, b_packed, b_sf, a_g, b_g, bias=None, out=None, raw_acc=False, tile: int = 0,
-               tail_split: int = 0):
+def nvfp4_gemm(a_packed, a_sf, b_packed, b_sf, a_g, b_g, bias=None, out=None, raw_acc=False, tile: int = 0):
     """NVFP4 GEMM on packed operands and scale atoms.  ``tile``: 0 the
     library's choice, 1 single-CTA 128x128, 2 CTA pair 256x128, 3 CTA pair 256x256."""
     M, Kh = a_packed.shape
@@ -366,8 +365,7 @@ def nvfp4_gemm(a_packed, a_sf, b_packed, b_sf, a_g, b_g, bias=None, out=None, ra
         out = torch.empty((M, N), dtype=torch.float32 if raw_acc else torch.bfloat16, device=a_packed.device)
     _lib.call("qi_b200_nvfp4_gemm", _ptr(a_packed), _ptr(a_sf), _ptr(b_packed), _ptr(b_sf), _ptr(a_g),
               int(a_g.numel() > 1), _ptr(b_g), _ptr(bias), _ptr(out), out.stride(0), M, N, 2 * Kh,
-              (_lib.EPI_RAW_ACC if raw_acc else 0) | (tile << _lib.NVFP4_TILE_SHIFT)
-              | (tail_split << _lib.TAIL_SPLIT_SHIFT), _stream(a_packed.device))
+              (_lib.EPI_RAW_ACC if raw_acc else 0) | (tile << _lib.NVFP4_TILE_SHIFT), _stream(a_packed.device))
     return out
 
 

@@ -154,27 +154,3 @@ def test_nvfp4_config4_full_size_sampled_rows():
     e = O.rel_fro(O.bf16_to_f32(bits(y)[rows]), O.bf16_to_f32(yo))
     assert e <= 2e-3, e
 
-
-@pytest.mark.parametrize("M,N,Kd,tile,tail", [(1024, 4864, 2048, 2, 8), (1100, 4000, 1024, 3, 3)])
-def test_nvfp4_pair_tail_split(M, N, Kd, tile, tail):
-    """The CTA-pair NVFP4 kernel with its partial last wave split along K over
-    idle pairs: accumulators within 1e-5 of the exact block-scaled sum and
-    bf16 outputs within 1e-3 of the unsplit kernel (fp32 summation order)."""
-    x, w, b = make_small_case(M, N, Kd, seed=M + N + Kd)
-    wq, wsf, wg, wq_np, wsf_np, wg_f = weights(w)
-    qa, sfa, ga = K.quantize_nvfp4(x.to(DEV), K.NVFP4_DYNAMIC_TENSOR)
-    one = torch.ones(1, dtype=torch.float32, device=DEV)
-    acc = K.nvfp4_gemm(qa, sfa, wq, wsf, one, one, raw_acc=True, tile=tile, tail_split=tail)
-    assert _lib.last_launch()["kernel"] == "gemm_nvfp4_pair" and _lib.last_tail_split() > 1
-    a_nib = O.unpack_fp4(qa.cpu().numpy())
-    a_sf = O.sf_from_atom_layout(sfa.cpu().numpy(), M, Kd // 16)
-    ref = O.nvfp4_dequant(a_nib, a_sf, 1.0) @ O.nvfp4_dequant(O.unpack_fp4(wq_np), wsf_np, 1.0).T
-    got = acc.cpu().numpy().astype(np.float64)
-    err = np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30)
-    assert err < 1e-5, err
-    bd = b.to(DEV)
-    y = K.nvfp4_gemm(qa, sfa, wq, wsf, ga, wg, bd, tile=tile, tail_split=tail)
-    y_ref = K.nvfp4_gemm(qa, sfa, wq, wsf, ga, wg, bd, tile=tile, tail_split=1)
-    assert _lib.last_tail_split() == 1
-    assert O.rel_fro(y.float().cpu().numpy(), y_ref.float().cpu().numpy()) <= 1e-3
-    assert _lib.device_status() == (0, 0, 0, 0)
