@@ -1,11 +1,11 @@
 #!/usr/bin/env python
 """Benchmark of the B200 quantized-linear hot path.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config fp8|int8] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config fp8|int8|...] [--only] [--impl ours|reference]
 
 One step = one quantized linear forward over one batch of synthetic input
 (activation quantization kernel + tcgen05 GEMM with fused epilogue; for N > 1
-also the NCCL all-gather of the column-sharded outputs).  Default config is
+also the all-gather of the column-sharded outputs).  The headline config is
 BASELINE config 2 (FP8-E4M3 FFN up-projection, M=4096 N=14336 K=3072,
 per-token activations, per-channel weights, bias + GELU).
 
@@ -13,9 +13,12 @@ Prints ONE JSON line on rank 0.  ``value`` = whole-job TOPS (2*M*N*K per
 step / max-over-ranks device time), inputs resident in HBM; ``e2e`` = the
 same through the public module API (``WeightOnlyLinear.forward``) with the
 activations copied in from pinned host memory and the output copied back
-every step.  ``--impl reference`` times the reference's own CPU algorithm
-(the dequantise-then-matmul port in ``oracle/reference_port.py``) on this
-host's cores instead.
+every step.  Without ``--only`` the same line carries a ``configs`` map with
+every other BASELINE config measured the same way in the same process
+(N = 1: configs 1, 3 at M = 1/16/256/4096, 4 and 5; N > 1: the DiT step of
+config 5 on N GPUs).  ``--impl reference`` times the reference's own CPU
+algorithm (the dequantise-then-matmul port in ``oracle/reference_port.py``)
+on this host's cores instead, on the full config.
 """
 
 from __future__ import annotations
@@ -176,17 +179,43 @@ def build_layer(cfg_name: str, w_shard: torch.Tensor, b_shard: torch.Tensor, dev
     return layer
 
 
-def run_ours(args):
+def linear_config(cfg_name: str) -> dict:
+    """The workload keys of a single-linear config (the same in both arms)."""
+    c = CONFIGS[cfg_name]
+    case = c["case"]
+    return {"workload": case.name, "M": case.M, "N": case.N, "K": case.K, "bias": True, "gelu": c["gelu"],
+            "act_quant": {"w4a16": "none (bf16)",
+                          "nvfp4": "nvfp4 block16, dynamic per-tensor global scale"}.get(c["kind"], "per_token"),
+            "weight_quant": {"w4a16": "int4 asym g128 packed",
+                             "nvfp4": "nvfp4 block16 + per-tensor global scale"}.get(c["kind"], "per_channel")}
+
+
+_KERNEL_NAMES = {"gemm_int8": "k_gemm_tc<int8>", "gemm_fp8": "k_gemm_tc<fp8>", "gemm_bf16": "k_gemm_tc<bf16>",
+                 "gemm_nvfp4": "k_gemm_tc<nvfp4>", "gemm_int8_pair": "k_gemm_tc2<int8>",
+                 "gemm_fp8_pair": "k_gemm_tc2<fp8>", "gemm_bf16_pair": "k_gemm_tc2<bf16>",
+                 "gemm_nvfp4_pair": "k_gemm_tc2<nvfp4>", "gemm_int8_csk": "k_gemm_csk<int8>",
+                 "gemm_fp8_csk": "k_gemm_csk<fp8>", "gemm_bf16_csk": "k_gemm_csk<bf16>",
+                 "w4a16_small": "k_gemm_w4a16_small", "w4a16_splitk": "k_gemm_w4a16_skinny"}
+
+
+def kernel_label(plan: dict) -> str:
+    """Name and tile of the kernel the library launched last (qi_b200_last_launch)."""
+    k = plan["kernel"]
+    name = _KERNEL_NAMES.get(k, k)
+    if k.endswith("_pair"):
+        return f"{name} (CTA pair, 256 x {plan['tile_n']} tiles, grid {plan['grid']})"
+    if k.startswith("gemm_"):
+        return f"{name} (128 x {plan['tile_n']} tiles, grid {plan['grid']}, cluster {plan['cluster']})"
+    return f"{name} (grid {plan['grid']}, cluster {plan['cluster']})"
+
+
+def measure_linear(cfg_name: str, args, world: int, rank: int, local: int, device) -> dict:
+    """One single-linear config: the device-timed
+    step, the dominant kernel alone, the roofline, e2e through the module
+    API and (rank 0, N = 1) the CPU baseline.  Returns the result dict."""
     from qi_b200 import _lib, kernels as K
 
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-    c = CONFIGS[args.config]
+    c = CONFIGS[cfg_name]
     case = c["case"]
     M, N, Kd = case.M, case.N, case.K
     if N % (8 * world):
@@ -199,7 +228,7 @@ def run_ours(args):
     if c["kind"] == "nvfp4":
         from qi_b200.quantization.quantize import nvfp4_global_scale
         g_full = nvfp4_global_scale(w_cpu.float().abs().amax())
-    layer = build_layer(args.config, w_shard, b_shard, device, nvfp4_global=g_full)
+    layer = build_layer(cfg_name, w_shard, b_shard, device, nvfp4_global=g_full)
     kind = {"fp8": _lib.KIND_FP8_E4M3, "int8": _lib.KIND_INT8, "w4a16": None, "nvfp4": None}[c["kind"]]
     if c["kind"] == "fp8":
         wq, ws = layer.weight_fp8, layer.weight_scale
@@ -286,6 +315,7 @@ def run_ours(args):
     for i in range(args.warmup):
         step(i)
         gemm_only(i)
+    plan = _lib.last_launch()  # the dominant kernel (last launch of gemm_only)
     barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     graph = None
@@ -330,9 +360,7 @@ def run_ours(args):
         gemm_ms = g0.elapsed_time(g1) / args.steps
         gemm_src = f"cuda events around {args.steps} back-to-back eager launches"
     gemm_ms = max_over_ranks(gemm_ms, world, device)
-    st = _lib.device_status()
-    if st[0] != 0:
-        raise SystemExit(f"device status word reports a timed-out wait: {st}")
+    _lib.raise_on_device_error()  # a bounded device wait timed out: the numbers are void
 
     flops_total = 2.0 * M * N * Kd
     ms_step = ms_total / args.steps
@@ -371,7 +399,7 @@ def run_ours(args):
     # ---- roofline of the dominant kernel (the GEMM)
     hbm_gbs, bf16_tf, src = peaks()
     gemm_flops_launch = 2.0 * M * Nl * Kd
-    traffic = load_traffic(args.config, world)
+    traffic = load_traffic(cfg_name, world)
     if c["kind"] == "w4a16":
         alg_bytes = wq_bytes + Nl * 2 + M * Kd * 2 + M * Nl * 2
         hbm_bound = M <= 16
@@ -409,27 +437,24 @@ def run_ours(args):
         roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                     "frac": round(achieved / peak, 4), "traffic": traffic, "algorithmic_bytes": alg_bytes,
                     "peak_source": f"{mult:g} x bf16 dense, " + src}
-    roofline.update({"kernel": ("k_w4a16_dequant + bf16 GEMM (k_gemm_tc2<bf16>), timed together" if w4_dequant
-                                else "k_gemm_w4a16") if c["kind"] == "w4a16" else
-                     (f"k_gemm_tc2<{c['kind']}> with the all-gather fused into its epilogue (TMA stores to "
-                      "every rank) + 2 barriers (activation quantizer included)" if peer
-                      else f"k_gemm_tc<{c['kind']}>"),
-                     "kernel_ms": round(gemm_ms, 5), "kernel_timing": gemm_src})
+    label = kernel_label(plan)
+    if w4_dequant:
+        label = "k_w4a16_dequant + " + label + ", timed together"
+    elif peer:
+        label += (" with the all-gather fused into its epilogue (TMA stores to every rank) + 2 barriers "
+                  "(activation quantizer included)")
+    roofline.update({"kernel": label, "kernel_ms": round(gemm_ms, 5), "kernel_timing": gemm_src})
 
     result = {
         "metric": "quantized_gemm_tops", "value": round(value, 2), "unit": "TOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": c["dtype"], "data": "synthetic (seeded, BASELINE shapes)",
-        "config": {"workload": case.name, "M": M, "N": N, "K": Kd, "bias": True, "gelu": c["gelu"],
-                   "act_quant": {"w4a16": "none (bf16)",
-                                 "nvfp4": "nvfp4 block16, dynamic per-tensor global scale"}.get(c["kind"], "per_token"),
-                   "weight_quant": {"w4a16": "int4 asym g128 packed",
-                                    "nvfp4": "nvfp4 block16 + per-tensor global scale"}.get(c["kind"], "per_channel"),
-                   "parallelism": (f"N-shard x{world}, all-gather fused into the GEMM epilogue (TMA stores "
-                                   "into IPC-mapped peer buffers over NVLink)"
-                                   if peer else f"N-shard x{world} + NCCL all_gather") if world > 1 else "single GPU",
-                   "launch": "cuda_graph" if use_graph else "eager",
-                   "l2": f"{ncopy} rotating input copies ({ncopy * per_copy / 2**20:.0f} MiB > L2)"},
+        "config": dict(linear_config(cfg_name),
+                       parallelism=(f"N-shard x{world}, all-gather fused into the GEMM epilogue (TMA stores "
+                                    "into IPC-mapped peer buffers over NVLink)" if peer
+                                    else f"N-shard x{world} + NCCL all_gather") if world > 1 else "single GPU",
+                       launch="cuda_graph" if use_graph else "eager",
+                       l2=f"{ncopy} rotating input copies ({ncopy * per_copy / 2**20:.0f} MiB > L2)"),
         "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
                 "api": "qi_b200.quantization.WeightOnlyLinear.forward" if world == 1
@@ -440,16 +465,12 @@ def run_ours(args):
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(args.config, samples=3)
+        result["cpu_baseline"] = cpu_baseline(cfg_name, samples=3)
     graph = None
     if peer:
+        peer_api.check()
         peer_api.close()
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        emit(result)
+    return result
 
 
 # --------------------------------------------------------------------------
@@ -457,20 +478,15 @@ def run_ours(args):
 # --------------------------------------------------------------------------
 
 
-def run_dit(args):
+def measure_dit(args, world: int, rank: int, local: int, device) -> dict:
     """One MoT DiT denoising step (30 blocks, video 3120 + action 32 tokens,
     every Linear INT8 W8A8) replayed from a CUDA graph.  N > 1: video tokens
     sharded by sequence, K/V all-gathered over NCCL once per layer."""
     from qi_b200 import _lib, dit as D, kernels as K
 
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
     group = None
     if world > 1:
-        import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
         group = dist.group.WORLD
     cfg = D.CFG5 if not args.layers else D.DiTConfig(layers=args.layers)
     model = D.build_mot_dit(cfg, device=device, seed=0)
@@ -514,9 +530,7 @@ def run_dit(args):
     gpu_launches = (_lib.launch_count() - c0 if per_step_launches is None
                     else per_step_launches * args.steps)
     ms_step = max_over_ranks(t0.elapsed_time(t1), world, device) / args.steps
-    st = _lib.device_status()
-    if st[0] != 0:
-        raise SystemExit(f"device status word reports a timed-out wait: {st}")
+    runner.check()  # raises if a bounded device wait timed out during the timed steps
 
     # e2e: host tokens in (pinned), graph replay, this rank's tokens back to host
     host_in = {n: x.cpu().pin_memory() for n, x in tok_l.items()}
@@ -593,6 +607,36 @@ def run_dit(args):
         result["cpu_baseline"] = dit_cpu_baseline()
     runner.graph = None
     del g
+    return result
+
+
+# the configs of one full run: N = 1 every BASELINE config, N > 1 the ones
+# that shard (config 2 is the headline line itself)
+ALL_CONFIGS_1GPU = ["int8", "w4a16_m1", "w4a16_m16", "w4a16_m256", "w4a16_m4096", "nvfp4", "fp8", "dit"]
+ALL_CONFIGS_NGPU = ["fp8", "dit"]
+
+
+def run_ours(args):
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+
+    def measure(name):
+        torch.cuda.empty_cache()
+        if name == "dit":
+            return measure_dit(args, world, rank, local, device)
+        return measure_linear(name, args, world, rank, local, device)
+
+    result = measure(args.config)
+    if not args.only:
+        result["configs"] = {}
+        for name in (ALL_CONFIGS_1GPU if world == 1 else ALL_CONFIGS_NGPU):
+            if name != args.config:
+                result["configs"][name] = measure(name)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -636,7 +680,8 @@ def dit_cpu_baseline():
     t = time.perf_counter()
     fn()
     dt = time.perf_counter() - t
-    return {"value": round(dt * 1e3 * cfg.layers, 1), "unit": "ms", "cores": torch.get_num_threads(), "kind": "port",
+    return {"value": round(dt * 1e3 * cfg.layers, 1), "unit": "ms", "cores": torch.get_num_threads(),
+            "cpu_model": cpu_model(), "kind": "port",
             "sample": "ReferenceBackend.linear port over the 20 INT8 Linears of 1 of 30 layers (full token "
                       "counts), scaled x30; attention and norms not included",
             "ms_per_layer": round(dt * 1e3, 1)}
@@ -674,15 +719,29 @@ def load_traffic(cfg_name: str, world: int):
 # --------------------------------------------------------------------------
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), for the baseline's record."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 def _cpu_sample(cfg_name: str):
-    """Inputs and a callable for one bounded CPU call of the reference path."""
+    """Inputs and a callable for one CPU call of the reference path over the
+    config's full input (every row)."""
     from oracle import reference_port as RP
     from qi_b200.quantization.quantize import quantize_to_fp8_e4m3_rowwise, quantize_weight_rtn
 
     c = CONFIGS[cfg_name]
     case = c["case"]
     x, w, b = make_linear_inputs(case)
-    rows = min(case.M, 512 if c["kind"] == "int8" else 256)
+    rows = case.M
     xs = x[:rows].contiguous()
     if c["kind"] == "nvfp4":
         from qi_b200.quantization.quantize import quantize_nvfp4
@@ -715,8 +774,8 @@ def cpu_baseline(cfg_name: str, samples: int = 3):
         ts.append(time.perf_counter() - t)
     t = statistics.median(ts)
     return {"value": round(2.0 * rows * case.N * case.K / t / 1e12, 5), "unit": "TOPS",
-            "cores": torch.get_num_threads(), "kind": "port", "sample": desc + f", median of {samples}",
-            "ms_per_call": round(t * 1e3, 2)}
+            "cores": torch.get_num_threads(), "cpu_model": cpu_model(), "kind": "port",
+            "sample": desc + f", median of {samples}", "ms_per_call": round(t * 1e3, 2)}
 
 
 def run_reference(args):
@@ -724,41 +783,57 @@ def run_reference(args):
     if rank != 0:
         return
     torch.set_num_threads(os.cpu_count() or 1)
-    if args.config == "dit":
+    result = reference_result(args.config, args, world)
+    if not args.only:
+        # the other configs' reference CPU path, a few calls each (same keys as ours)
+        result["configs"] = {}
+        for name in (ALL_CONFIGS_1GPU if world == 1 else ALL_CONFIGS_NGPU):
+            if name != args.config:
+                result["configs"][name] = reference_result(name, args, world, steps=2, warmup=1)
+    emit(result)
+
+
+def reference_result(cfg_name: str, args, world: int, steps: int | None = None, warmup: int | None = None) -> dict:
+    """The reference's CPU algorithm (port) for one config, timed on all host threads."""
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
+    if cfg_name == "dit":
         fn, cfg = _dit_cpu_layer_sample()
-        fn()
-        t = time.perf_counter()
-        for _ in range(args.steps):
+        for _ in range(max(1, warmup)):
             fn()
-        ms = (time.perf_counter() - t) / args.steps * 1e3 * cfg.layers
-        emit({
+        t = time.perf_counter()
+        for _ in range(steps):
+            fn()
+        ms = (time.perf_counter() - t) / steps * 1e3 * cfg.layers
+        return {
             "impl": "reference", "metric": "dit_step_latency_ms", "value": round(ms, 1), "unit": "ms",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 1),
+            "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": round(ms, 1),
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": CONFIGS["dit"]["dtype"],
             "data": "synthetic", "config": {"workload": "mot_dit_step_cfg5"},
-            "cpu_baseline": {"value": round(ms, 1), "unit": "ms", "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": "20 INT8 Linears of 1 of 30 layers per step, scaled x30"},
+            "cpu_baseline": {"value": round(ms, 1), "unit": "ms", "cores": torch.get_num_threads(),
+                             "cpu_model": cpu_model(), "kind": "port",
+                             "sample": "20 INT8 Linears of 1 of 30 layers per step (full token counts), scaled x30"},
             "e2e": {"value": round(ms, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        })
-        return
-    fn, rows, case, desc = _cpu_sample(args.config)
-    for _ in range(args.warmup):
+        }
+    fn, rows, case, desc = _cpu_sample(cfg_name)
+    for _ in range(warmup):
         fn()
     t = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(steps):
         fn()
-    dt = (time.perf_counter() - t) / args.steps
+    dt = (time.perf_counter() - t) / steps
     value = 2.0 * rows * case.N * case.K / dt / 1e12
-    emit({
+    c = CONFIGS[cfg_name]
+    return {
         "impl": "reference", "metric": "quantized_gemm_tops", "value": round(value, 5), "unit": "TOPS",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": CONFIGS[args.config]["dtype"],
+        "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": c["dtype"],
         "data": "synthetic (seeded, BASELINE shapes)",
-        "config": {"workload": case.name, "M": case.M, "N": case.N, "K": case.K, "sample_rows": rows},
-        "cpu_baseline": {"value": round(value, 5), "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": desc},
+        "config": linear_config(cfg_name),
+        "cpu_baseline": {"value": round(value, 5), "unit": "TOPS", "cores": torch.get_num_threads(),
+                         "cpu_model": cpu_model(), "kind": "port", "sample": desc},
         "e2e": {"value": round(value, 5), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    })
+    }
 
 
 # The JSON result line goes to the process's original stdout; everything
@@ -788,6 +863,7 @@ def main():
     ap.add_argument("--config", default="fp8", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", action="store_true", help="measure --config alone (no configs map)")
     ap.add_argument("--eager", action="store_true", help="no CUDA graph for the timed steps")
     ap.add_argument("--gather", default="auto", choices=["auto", "peer", "nccl"],
                     help="N > 1, INT8/FP8: all-gather fused into the GEMM epilogue (peer), a separate "
@@ -799,8 +875,6 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.config == "dit":
-        run_dit(args)
     else:
         run_ours(args)
 

@@ -9,8 +9,11 @@
  *   - all pointers are device pointers on the current CUDA device; tensors
  *     are dense row-major; bf16 = IEEE bfloat16 bits, fp8 = E4M3 ("fn")
  *     codes, int8 = two's complement;
- *   - work is enqueued on `stream`; nothing synchronizes, nothing allocates
- *     (callers own every buffer), so calls can be captured in CUDA graphs;
+ *   - work is enqueued on `stream`; nothing synchronizes and nothing
+ *     allocates device memory (callers own every buffer, workspaces
+ *     included; only qi_b200_peer_alloc / qi_b200_peer_free allocate, and
+ *     they are explicit set-up calls), so calls can be captured in CUDA
+ *     graphs;
  *   - the return value is a status code (QI_B200_OK = 0); a non-zero code
  *     means nothing was enqueued, except QI_B200_ECUDA which reports a launch
  *     error from the CUDA runtime;
@@ -53,15 +56,16 @@ extern "C" {
  * single-CTA 128 x 128), 1 = single-CTA 128 x 128, 2 = CTA pair 256 x 128,
  * 3 = CTA pair 256 x 256. */
 #define QI_B200_NVFP4_TILE_SHIFT 8
-/* qi_b200_gemm flags bits 12-15: the CTA-pair kernel's partial last wave.
+/* qi_b200_gemm_ws flags bits 12-15: the CTA-pair kernel's partial last wave.
  * When tiles % pairs tiles are left for a last wave, each of them can have
  * its K range split over S pairs that would otherwise sit idle; the partial
- * accumulators meet in a per-stream workspace (allocated by the library on
- * first use on a stream, about 19 MB) and are summed in a fixed order, so
- * INT8 results stay bit-exact.  0 = the library's choice, 1 = no split,
- * 2..15 = at most that many splits per tile (further capped at 8 and at the
- * idle pairs).  Replaces nothing in the reference (its CUTLASS kernels run
- * one tile per CTA with no split); a scheduling choice of this library. */
+ * accumulators meet in the caller's workspace (qi_b200_gemm_workspace_bytes
+ * gives its size) and are summed in a fixed order, so INT8 results stay
+ * bit-exact.  0 = the library's choice, 1 = no split, 2..15 = at most that
+ * many splits per tile (further capped at 8 and at the idle pairs).  Without
+ * a workspace (qi_b200_gemm) there is no split.  Replaces nothing in the
+ * reference (its CUTLASS kernels run one tile per CTA with no split); a
+ * scheduling choice of this library. */
 #define QI_B200_TAIL_SPLIT_SHIFT 12
 
 int qi_b200_abi_version(void);
@@ -74,12 +78,11 @@ const char* qi_b200_error_string(int code);
 int qi_b200_device_status(unsigned int* out4, int clear);
 
 /* Launch plan of the calling thread's most recent GEMM launch, for
- * diagnostics: out6 = {kernel (1 int8, 2 fp8, 3 bf16, 4 nvfp4, 5 w4a16 tiles,
- * 6 w4a16 split-K clusters, 7 w4a16 small-M, 8/9/10/11 int8 / fp8 / bf16 /
- * nvfp4 CTA-pair tiles, 12/13/14 int8 / fp8 / bf16 cluster split-K), grid,
- * cluster size (K splits for kernels 1-3 under qi_b200_gemm_splitk), tile N
- * (or padded M for kernel 6, M for kernel 7), pipeline stages, dynamic shared
- * memory bytes}. */
+ * diagnostics: out6 = {kernel (1 int8, 2 fp8, 3 bf16, 4 nvfp4, 6 w4a16
+ * split-K clusters, 7 w4a16 small-M, 8/9/10/11 int8 / fp8 / bf16 / nvfp4
+ * CTA-pair tiles, 12/13/14 int8 / fp8 / bf16 cluster split-K), grid, cluster
+ * size, tile N (or padded M for kernel 6, M for kernel 7), pipeline stages,
+ * dynamic shared memory bytes}. */
 int qi_b200_last_launch(int* out6);
 /* Splits per tail tile (see QI_B200_TAIL_SPLIT_SHIFT) of the calling thread's
  * most recent CTA-pair GEMM launch; 1 = its last wave ran unsplit. */
@@ -96,16 +99,17 @@ int qi_b200_launch_count(unsigned long long* out);
 int qi_b200_quantize_int8_rowwise(const void* x_bf16, void* q_int8, float* scales, int rows, int cols,
                                   cudaStream_t stream);
 
-/* INT8 quantization with caller-provided per-row scales (no counterpart in
- * the reference): q = clamp(rint(x * (1/s[row])), -127, 127).  Used when a
- * row's K extent is split over ranks: the per-row scales are first reduced
- * with MAX across ranks, so every rank quantizes with the single-GPU scale. */
 /* qi_b200_quantize_int8_rowwise of x / input_scale, fused: the SmoothQuant /
  * AWQ smoothing of Int8W8A8Backend.linear (int8_w8a8_ops.py:138-139), done
  * in bf16 as there: x' = bf16(fp32(x) / fp32(bf16(input_scale[k]))).
  * input_scale fp32 [cols]. */
 int qi_b200_quantize_int8_rowwise_smooth(const void* x_bf16, const float* input_scale, void* q_int8, float* scales,
                                          int rows, int cols, cudaStream_t stream);
+
+/* INT8 quantization with caller-provided per-row scales (no counterpart in
+ * the reference): q = clamp(rint(x * (1/s[row])), -127, 127).  Used when a
+ * row's K extent is split over ranks: the per-row scales are first reduced
+ * with MAX across ranks, so every rank quantizes with the single-GPU scale. */
 int qi_b200_quantize_int8_rowwise_given(const void* x_bf16, const float* scales, void* q_int8, int rows, int cols,
                                         cudaStream_t stream);
 
@@ -123,21 +127,6 @@ int qi_b200_int8_row_scales(const void* x_bf16, float* scales, int rows, int col
 int qi_b200_int8_epilogue(const void* acc_int32, const float* act_scale, const float* weight_scale,
                           const void* bias, void* out_bf16, int M, int N, int flags, cudaStream_t stream);
 
-/* qi_b200_gemm split over K for problems whose 128 x 256 tiles cannot fill
- * the GPU (small M: the reference's INT8 config 1 at M = 512 has 48 tiles for
- * 148 SMs; the DiT action expert's M = 32 linears fewer still).  `splits`
- * CTAs share each output tile, each over a contiguous range of K; their raw
- * accumulators go to `workspace` (splits x M x N x 4 bytes, caller-owned),
- * and a second kernel sums them (int32 exactly for INT8, so INT8 outputs are
- * bit-identical to qi_b200_gemm) and applies the epilogue.  bf16 output only
- * (flags: QI_B200_EPI_GELU).  qi_b200_gemm_splitk_plan gives the split count
- * at which 128 x 256 tiles fill the SMs (1 = they already do) and the
- * workspace it needs.  qi_b200_gemm never splits on its own: measured on a
- * B200, writing and re-reading the partials cost more than the idle SMs at
- * the reference's shapes (M = 512, N = K = 3072: 21.2 us at 2 splits against
- * 13.6 us unsplit). */
-int qi_b200_gemm_splitk_plan(int kind, int M, int N, int K, int* splits, size_t* workspace_bytes);
-
 /* qi_b200_gemm split over K inside a thread-block cluster: `splits` (2..8)
  * CTAs share one 128 x tile_n output tile (tile_n 128, 192 or 256), each
  * over a contiguous range of K; the partial tiles are added in rank order
@@ -149,10 +138,6 @@ int qi_b200_gemm_splitk_plan(int kind, int M, int N, int K, int* splits, size_t*
 int qi_b200_gemm_csk(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
                      const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd, int M, int N,
                      int K, int flags, int tile_n, int splits, cudaStream_t stream);
-int qi_b200_gemm_splitk(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
-                        const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd, int M,
-                        int N, int K, int flags, int splits, void* workspace, size_t workspace_bytes,
-                        cudaStream_t stream);
 
 /* ---- Peer memory for the column-parallel linear with an overlapped all-gather
  * (no counterpart in the reference, which runs on one GPU).  One process per
@@ -176,10 +161,16 @@ int qi_b200_peer_free(void* ptr);
  * writes it into word `rank` of every block (release, system scope) and
  * waits until every rank has written the same value into its own block
  * (acquire).  All ranks must run the same sequence of barriers.  The wait is
- * bounded (2 s): on timeout the device status word records tag 0x300 and the
- * kernel returns. */
+ * bounded (2 s): on timeout the device status word records kernel tag 0x300
+ * with the rank that did not arrive as the wait site, and the kernel
+ * returns. */
 #define QI_B200_PEER_FLAG_BYTES 256
 int qi_b200_peer_barrier(void* const* flags, int P, int rank, cudaStream_t stream);
+/* qi_b200_peer_barrier with the wait limited to timeout_ns (0 < timeout_ns
+ * <= 2 s): a caller that wants a failed peer reported sooner, e.g. a health
+ * check between steps. */
+int qi_b200_peer_barrier_timed(void* const* flags, int P, int rank, unsigned long long timeout_ns,
+                               cudaStream_t stream);
 
 /* qi_b200_gemm (INT8 / FP8 / BF16, bf16 out, optional GELU) on the CTA-pair
  * kernel with the column-parallel all-gather fused into its epilogue: every
@@ -192,12 +183,6 @@ int qi_b200_peer_barrier(void* const* flags, int P, int rank, cudaStream_t strea
 int qi_b200_gemm_gather(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
                         const float* b_scale, int b_scale_stride, const void* bias, void* const* dst, int ndst,
                         long long ldd, int M, int N, int K, int flags, cudaStream_t stream);
-
-/* cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, stream): moves a
- * finished row block of this rank's output into a peer's buffer (mapped with
- * qi_b200_peer_open) on a copy engine, so the NVLink transfer runs beside
- * the GEMM of the next row block without taking SMs. */
-int qi_b200_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream);
 
 /* ---- Fused elementwise stages of the MoT DiT block (no counterpart in the
  * reference's quantization package: they fuse the bf16 tensor ops of
@@ -258,6 +243,19 @@ int qi_b200_gemm(int kind, const void* A, const void* B, const float* a_scale, i
                  const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd, int M, int N,
                  int K, int flags, int tile_n, cudaStream_t stream);
 
+/* qi_b200_gemm with a caller-owned workspace for the CTA-pair kernel's split
+ * of its partial last wave (QI_B200_TAIL_SPLIT_SHIFT): at least
+ * qi_b200_gemm_workspace_bytes bytes, 16-byte aligned, used by one launch at
+ * a time (calls that overlap on the GPU need separate workspaces).  A null
+ * or too small workspace runs the launch without the split.  Same result
+ * either way (bit-identical for INT8). */
+int qi_b200_gemm_ws(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
+                    const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd, int M, int N,
+                    int K, int flags, int tile_n, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+/* Workspace bytes qi_b200_gemm_ws needs for this problem, flags and tile_n on
+ * the current device (0: that launch does not split).  Host only. */
+int qi_b200_gemm_workspace_bytes(int kind, int M, int N, int K, int flags, int tile_n, size_t* bytes);
+
 /* ---- W4A16 (INT4 weight-only) ----------------------------------------
  * Replaces the weight-only INT4 path of ReferenceBackend.linear
  * (backends/reference.py:48-91, dequantize_weight at quantize.py:81-119) and
@@ -267,7 +265,9 @@ int qi_b200_gemm(int kind, const void* A, const void* B, const float* a_scale, i
  * scales_fp16 [N, G], zeros_packed int32 [N, ceil(G/8)] (uint4, group g in
  * word g/8 nibble g%8), G = ceil(K / group_size); group_size <= 0 means one
  * group per row.  Needs K % 32 == 0, N % 8 == 0, group_size % 32 == 0.
- * M <= 256 runs a split-K kernel over a thread-block cluster. */
+ * M <= 16: a streaming kernel over bulk-copied weight rows; M <= 256: a
+ * split-K kernel over a thread-block cluster; larger M: that kernel per
+ * 256-row block (qi_b200_w4a16_linear_ws is faster there). */
 int qi_b200_w4a16_linear(const void* x_bf16, const void* qweight_packed, const void* scales_fp16,
                          const void* zeros_packed, int group_size, const void* bias, void* out_bf16, int M, int N,
                          int K, cudaStream_t stream);

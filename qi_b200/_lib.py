@@ -19,7 +19,7 @@ KIND_INT8, KIND_FP8_E4M3, KIND_BF16 = 0, 1, 2
 EPI_GELU, EPI_RAW_ACC = 1, 2
 W4A16_DEQUANT_MIN_M = 257  # QI_B200_W4A16_DEQUANT_MIN_M (measured crossover: M=512 26 us vs 43 us fused)
 NVFP4_TILE_SHIFT = 8  # flags bits 8-9: 0 auto, 1 single-CTA 128x128, 2 pair 256x128, 3 pair 256x256
-TAIL_SPLIT_SHIFT = 12  # flags bits 12-15 of qi_b200_gemm: 0 auto, 1 no split, S = at most S splits per tail tile
+TAIL_SPLIT_SHIFT = 12  # flags bits 12-15 of qi_b200_gemm_ws: 0 auto, 1 no split, S = at most S splits per tail tile
 
 
 class QiB200Unavailable(RuntimeError):
@@ -58,10 +58,10 @@ SIGNATURES = {
     "qi_b200_peer_close": [_P],
     "qi_b200_peer_free": [_P],
     "qi_b200_peer_barrier": [_P, _I, _I, _P],
-    "qi_b200_copy_async": [_P, _P, ctypes.c_size_t, _P],
-    "qi_b200_gemm_splitk_plan": [_I, _I, _I, _I, _P, _P],
+    "qi_b200_peer_barrier_timed": [_P, _I, _I, ctypes.c_ulonglong, _P],
     "qi_b200_gemm_csk": [_I, _P, _P, _P, _I, _P, _I, _P, _P, _LL, _I, _I, _I, _I, _I, _I, _P],
-    "qi_b200_gemm_splitk": [_I, _P, _P, _P, _I, _P, _I, _P, _P, _LL, _I, _I, _I, _I, _I, _P, ctypes.c_size_t, _P],
+    "qi_b200_gemm_ws": [_I, _P, _P, _P, _I, _P, _I, _P, _P, _LL, _I, _I, _I, _I, _I, _P, ctypes.c_size_t, _P],
+    "qi_b200_gemm_workspace_bytes": [_I, _I, _I, _I, _I, _I, _P],
     "qi_b200_gemm_gather": [_I, _P, _P, _P, _I, _P, _I, _P, _P, _I, _LL, _I, _I, _I, _I, _P],
     "qi_b200_resid_ln_quant": [_P, _P, _LL, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _P],
     "qi_b200_rms_rope": [_P, _P, _LL, _P, _P, _LL, _P, _P, _P, _I, _I, _I, _I, _F, _P],
@@ -134,7 +134,7 @@ def last_launch() -> dict:
     """Plan of this thread's most recent GEMM launch (see qi_b200_last_launch)."""
     buf = (ctypes.c_int * 6)()
     check("qi_b200_last_launch", load().qi_b200_last_launch(ctypes.cast(buf, _P)))
-    names = {1: "gemm_int8", 2: "gemm_fp8", 3: "gemm_bf16", 4: "gemm_nvfp4", 5: "w4a16_tiles", 6: "w4a16_splitk",
+    names = {1: "gemm_int8", 2: "gemm_fp8", 3: "gemm_bf16", 4: "gemm_nvfp4", 6: "w4a16_splitk",
              7: "w4a16_small", 8: "gemm_int8_pair", 9: "gemm_fp8_pair", 10: "gemm_bf16_pair",
              11: "gemm_nvfp4_pair", 12: "gemm_int8_csk", 13: "gemm_fp8_csk", 14: "gemm_bf16_csk"}
     v = list(buf)
@@ -151,3 +151,29 @@ def device_status(clear: bool = False) -> tuple[int, int, int, int]:
     buf = (ctypes.c_uint * 4)()
     check("qi_b200_device_status", load().qi_b200_device_status(ctypes.cast(buf, _P), int(clear)))
     return tuple(int(v) for v in buf)
+
+
+class QiB200DeviceError(RuntimeError):
+    """A kernel of this library gave up a bounded wait (device status word set).
+
+    The kernel returned early, so the outputs of the launch that set the word
+    (and of every launch after it on that device) are incomplete."""
+
+    def __init__(self, status: tuple):
+        self.status = tuple(status)
+        super().__init__(
+            "qi_b200: a bounded device wait timed out (kernel tag 0x%x, wait site %d, block %d); outputs of the "
+            "launches since the last status check are incomplete" % (status[1], status[2], status[3]))
+
+
+def raise_on_device_error(clear: bool = True) -> None:
+    """Read the current device's status word (synchronous: the host waits for
+    the device) and raise ``QiB200DeviceError`` if a bounded wait timed out.
+    ``clear`` resets the word (and the counters an aborted launch may have
+    left) so the context can run again.  Call it at a point where the caller
+    synchronizes anyway: after a step, between graph replays, at shutdown."""
+    st = device_status(clear=False)
+    if st[0] != 0:
+        if clear:
+            device_status(clear=True)
+        raise QiB200DeviceError(st)

@@ -56,16 +56,14 @@ struct EpiParams {
   const uint8_t* sfa;
   const uint8_t* sfb;
   int sf_ka;
-  // split-K (raw accumulators only): ksplit CTAs share a tile, each over a
-  // contiguous range of K blocks; split s stores at D + s * split_stride
-  int ksplit = 1;
-  long long split_stride = 0;
   // CTA-pair kernel: each of the last (tiles % pairs) tiles, the partial last
   // wave, is split along K over tail_split pairs (1 = no split).  Partial
-  // accumulators go to tail_ws (tail tiles x tail_split x 256 x BN words);
+  // accumulators go to tail_ws, the caller's workspace (tail tiles x
+  // tail_split x 256 x BN words; tail_ws_bytes is read on the host only);
   // tail_cnt holds 2 x kMaxTailTiles counters that are zero between launches.
   int tail_split = 1;
   uint32_t* tail_ws = nullptr;
+  size_t tail_ws_bytes = 0;
   unsigned int* tail_cnt = nullptr;
 };
 constexpr int kMaxTailTiles = 128;
@@ -154,70 +152,6 @@ k_int8_epilogue(const int32_t* __restrict__ acc, const float* __restrict__ sa, c
   }
 }
 
-// Epilogue over split-K partial accumulators: sums the nsplit slices (int32
-// exactly for INT8, fp32 in split order otherwise), then the operation order of
-// the fused epilogue: ((acc * sa[m]) * sb[n]) + bias[n] -> bf16 -> GELU.
-// One thread per 8 output columns of one row (N % 8 == 0).
-template <bool INT>
-__global__ void __launch_bounds__(256)
-k_splitk_epilogue(const void* __restrict__ acc, int nsplit, long long stride, const float* __restrict__ sa,
-                  int sa_stride, const float* __restrict__ sb, int sb_stride, const __nv_bfloat16* __restrict__ bias,
-                  __nv_bfloat16* __restrict__ out, long long ldo, int M, int N, int gelu) {
-  const int nv = N >> 3;
-  const long long total = static_cast<long long>(M) * nv;
-  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < total; i += 256ll * gridDim.x) {
-    const int m = static_cast<int>(i / nv), n0 = static_cast<int>(i - static_cast<long long>(m) * nv) * 8;
-    const long long off = static_cast<long long>(m) * N + n0;
-    float y[8];
-    if constexpr (INT) {
-      int sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int s = 0; s < nsplit; ++s) {
-        const int4* a = reinterpret_cast<const int4*>(static_cast<const int32_t*>(acc) + s * stride + off);
-        const int4 u = a[0], v = a[1];
-        sum[0] += u.x; sum[1] += u.y; sum[2] += u.z; sum[3] += u.w;
-        sum[4] += v.x; sum[5] += v.y; sum[6] += v.z; sum[7] += v.w;
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = __int2float_rn(sum[e]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = 0.f;
-      for (int s = 0; s < nsplit; ++s) {
-        const float4* a = reinterpret_cast<const float4*>(static_cast<const float*>(acc) + s * stride + off);
-        const float4 u = a[0], v = a[1];
-        y[0] = __fadd_rn(y[0], u.x); y[1] = __fadd_rn(y[1], u.y); y[2] = __fadd_rn(y[2], u.z);
-        y[3] = __fadd_rn(y[3], u.w); y[4] = __fadd_rn(y[4], v.x); y[5] = __fadd_rn(y[5], v.y);
-        y[6] = __fadd_rn(y[6], v.z); y[7] = __fadd_rn(y[7], v.w);
-      }
-    }
-    if (sa != nullptr) {
-      const float s0 = __ldg(sa + static_cast<long long>(m) * sa_stride);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = __fmul_rn(y[e], s0);
-    }
-    if (sb != nullptr) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = __fmul_rn(y[e], __ldg(sb + static_cast<long long>(n0 + e) * sb_stride));
-    }
-    if (bias != nullptr) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = __fadd_rn(y[e], __bfloat162float(bias[n0 + e]));
-    }
-    uint32_t packed[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) packed[j] = pack_bf16x2(y[2 * j], y[2 * j + 1]);
-    if (gelu) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&packed[j]));
-        packed[j] = pack_bf16x2(gelu_tanh_fast(f.x), gelu_tanh_fast(f.y));
-      }
-    }
-    *reinterpret_cast<uint4*>(out + static_cast<long long>(m) * ldo + n0) =
-        make_uint4(packed[0], packed[1], packed[2], packed[3]);
-  }
-}
-
 template <MmaKind KIND>
 __device__ __forceinline__ void mma_issue(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   if constexpr (KIND == MmaKind::I8) mma_i8(d, a, b, idesc, acc);
@@ -232,11 +166,11 @@ __device__ __forceinline__ void mma_issue(uint32_t d, uint64_t a, uint64_t b, ui
 template <MmaKind KIND, int W = 32>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[W], const EpiParams& p, int m, int n0,
                                                float sa, const float* sb_s, const __nv_bfloat16* bias_s,
-                                               uint32_t* packed_out = nullptr, int split = 0) {
+                                               uint32_t* packed_out = nullptr) {
   static_assert(W == 8 || W == 16 || W == 32, "chunk width");
   const int n_valid = p.N - n0;  // >= 1; a multiple of 8 when < W (N % 8 == 0)
   if (p.flags & kEpiRawAcc) {
-    uint32_t* drow = static_cast<uint32_t*>(p.D) + split * p.split_stride + static_cast<long long>(m) * p.ldd;
+    uint32_t* drow = static_cast<uint32_t*>(p.D) + static_cast<long long>(m) * p.ldd;
 #pragma unroll
     for (int j = 0; j < W; j += 4) {
       if (j < n_valid) *reinterpret_cast<uint4*>(drow + n0 + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
@@ -358,10 +292,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
   const int n_tiles = (p.N + BN - 1) / BN;
   const int k_units = C::NVF4 ? p.K / 2 : p.K;  // K in TMA elements
   const int k_blocks = (k_units + C::BK - 1) / C::BK;
-  // work items: (m tile, n tile, K split), m fastest; the host makes every split's range non-empty
-  const int nsplit = p.ksplit > 1 ? p.ksplit : 1;
-  const int kb_per = (k_blocks + nsplit - 1) / nsplit;
-  const int num_tiles = m_tiles * n_tiles * nsplit;
+  // work items: (m tile, n tile), m fastest
+  const int num_tiles = m_tiles * n_tiles;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -371,9 +303,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
       int issued = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int mb = tile % m_tiles, nb = (tile / m_tiles) % n_tiles, sk = tile / (m_tiles * n_tiles);
-        const int kb0 = sk * kb_per, kb1 = min(k_blocks, kb0 + kb_per);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        const int mb = tile % m_tiles, nb = tile / m_tiles;
+        for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kTag, 1)) { ok = false; break; }
           mbar_expect_tx(&full[stage], C::STAGE_BYTES);
           tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * C::BK, mb * C::BM);
@@ -413,8 +344,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         if (!mbar_wait(&tempty[buf], tph ^ 1u, abort_flag, kTag, 2)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * C::ACC_COLS);
-        const int kb0 = (tile / (m_tiles * n_tiles)) * kb_per, kb1 = min(k_blocks, kb0 + kb_per);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, kTag, 3)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
@@ -433,13 +363,13 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
               mma_nvf4(d_tmem, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32), C::IDESC,
-                       tsfa + 4 * kk, tsfb + 4 * kk, (kb != kb0 || kk != 0) ? 1u : 0u);
+                       tsfa + 4 * kk, tsfb + 4 * kk, (kb != 0 || kk != 0) ? 1u : 0u);
           } else {
 #pragma unroll
             for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk) {
               const uint64_t ad = sw128_kmajor_desc(a0 + kk * 32);
               const uint64_t bd = sw128_kmajor_desc(b0 + kk * 32);
-              mma_issue<KIND>(d_tmem, ad, bd, C::IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
+              mma_issue<KIND>(d_tmem, ad, bd, C::IDESC, (kb != 0 || kk != 0) ? 1u : 0u);
             }
           }
           tc_commit(&empty[stage]);
@@ -463,7 +393,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     constexpr int COLS = BN / 2;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-      const int mb = tile % m_tiles, nb = (tile / m_tiles) % n_tiles, sk = tile / (m_tiles * n_tiles);
+      const int mb = tile % m_tiles, nb = tile / m_tiles;
       const int buf = local & 1;
       const uint32_t tph = (local >> 1) & 1;
       // stage this tile's column scales / bias in shared memory
@@ -499,9 +429,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         tmem_ld_wait();
         if (m < p.M) {
           const int j0 = half * COLS + c;
-          epilogue_chunk<KIND>(r0, p, m, n0, sa, sb_t + j0, bias_t + j0, nullptr, sk);
+          epilogue_chunk<KIND>(r0, p, m, n0, sa, sb_t + j0, bias_t + j0);
           if (two && n0 + 32 < p.N)
-            epilogue_chunk<KIND>(r1, p, m, n0 + 32, sa, sb_t + j0 + 32, bias_t + j0 + 32, nullptr, sk);
+            epilogue_chunk<KIND>(r1, p, m, n0 + 32, sa, sb_t + j0 + 32, bias_t + j0 + 32);
         }
       }
       tc_fence_before();

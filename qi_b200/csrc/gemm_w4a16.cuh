@@ -194,156 +194,6 @@ __device__ __forceinline__ void mma_stage_ts(uint32_t d_tmem, uint32_t a_tmem, u
 }
 
 // ---------------------------------------------------------------------------
-// Large M: persistent tiles of 128 weight rows x 256 tokens.
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(w4::kThreads, 1)
-k_gemm_w4a16(const __grid_constant__ CUtensorMap tmX, const EpiParams p, const W4Params q) {
-  constexpr int BT = 256;
-  using C = W4Cfg<BT>;
-  constexpr int STAGES = C::STAGES;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sX = smem;  // [STAGES][256 token rows x 128 B]
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BUF_BYTES);
-  uint64_t* aready = full + STAGES;
-  uint64_t* empty = aready + STAGES;
-  uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 1;
-  uint64_t* drain = tempty + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  constexpr unsigned int kTag = 0x200u;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&aready[s], w4::kDeqThr);
-      mbar_init(&empty[s], 1);
-    }
-    mbar_init(tfull, 1);
-    mbar_init(tempty, w4::kEpiThr);
-    mbar_init(drain, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 0 && lane == 0) tma_prefetch_map(&tmX);
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, w4::TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  const int m_tiles = (p.M + BT - 1) / BT;
-  const int n_tiles = (p.N + w4::BN - 1) / w4::BN;
-  const int num_tiles = m_tiles * n_tiles;
-  const int k_blocks = (p.K + w4::BK - 1) / w4::BK;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      int stage = 0, issued = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int mb = tile % m_tiles;
-        for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kTag, 1)) { ok = false; break; }
-          mbar_expect_tx(&full[stage], C::X_BYTES);
-          tma_load_2d(sX + stage * C::X_BYTES, &tmX, &full[stage], kb * w4::BK, mb * BT);
-          ++issued;
-          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
-        }
-      }
-      if (!ok) {
-        int s = stage;
-        uint32_t ph = phase;
-        for (int i = 0; i < STAGES && i < issued; ++i) {
-          if (--s < 0) { s = STAGES - 1; ph ^= 1u; }
-          mbar_wait_drain(&full[s], ph);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      int stage = 0, local = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      const uint32_t acc = tmem_base + C::ACC_COL;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
-        if (!mbar_wait(tempty, (local & 1) ^ 1u, abort_flag, kTag, 2)) { ok = false; break; }
-        tc_fence_after();
-        for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, kTag, 3)) { ok = false; break; }
-          if (!mbar_wait(&aready[stage], phase, abort_flag, kTag, 6)) { ok = false; break; }
-          tc_fence_after();
-          mma_stage_ts<BT>(acc, tmem_base + stage * w4::A_COLS, smem_u32(sX + stage * C::X_BYTES), kb == 0);
-          tc_commit(&empty[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
-        }
-        if (ok) tc_commit(tfull);
-      }
-      if (!ok) {
-        tc_commit(drain);
-        mbar_wait_drain(drain, 0);
-      }
-    }
-  } else if (warp >= w4::kDeqWarp0) {
-    const int wq = warp & 3, h = (warp - w4::kDeqWarp0) >> 2;
-    const uint32_t tmem_a = tmem_base + (static_cast<uint32_t>(wq * 32) << 16);
-    int stage = 0;
-    uint32_t phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int n = (tile / m_tiles) * w4::BN + wq * 32 + lane;
-      if (!dequant_rows_tmem(q, n, n < p.N, h, 0, k_blocks, tmem_a, STAGES, empty, aready, stage, phase,
-                             abort_flag, kTag))
-        break;
-    }
-  } else if (warp >= w4::kEpiWarp0) {
-    const int wq = warp & 3;
-    const uint32_t tacc = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + C::ACC_COL;
-    int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-      const int mb = tile % m_tiles, nb = tile / m_tiles;
-      const int n = nb * w4::BN + wq * 32 + lane;
-      const float bias = (p.bias != nullptr && n < p.N) ? __bfloat162float(p.bias[n]) : 0.0f;
-      if (!warp_wait(tfull, local & 1, abort_flag, kTag, 4)) break;
-      tc_fence_after();
-      __nv_bfloat16* dcol = static_cast<__nv_bfloat16*>(p.D) + n;
-#pragma unroll 1
-      for (int m0 = 0; m0 < BT; m0 += 32) {
-        const int mbase = mb * BT + m0;
-        if (mbase >= p.M) break;  // warp-uniform
-        uint32_t rr[32];
-        tmem_ld_32x32b_x32(tacc + m0, rr);
-        tmem_ld_wait();
-        if (n < p.N) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (mbase + j < p.M)
-              dcol[static_cast<long long>(mbase + j) * p.ldd] = __float2bfloat16_rn(__fadd_rn(__uint_as_float(rr[j]), bias));
-          }
-        }
-      }
-      tc_fence_before();
-      mbar_arrive_relaxed(tempty);  // accumulator read (wait::ld); output stores need no ordering
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 1) {
-    __syncwarp();
-    tmem_dealloc(tmem_base, w4::TMEM_COLS);
-  }
-}
-
-// ---------------------------------------------------------------------------
 // Skinny W4A16 (M <= 256, BT = M rounded up to 16/32/64/128/256): one token
 // tile; K split over the CTAs of a thread-block cluster (up to 8).  Each CTA
 // writes its fp32 partial tile to its own shared memory and the cluster sums

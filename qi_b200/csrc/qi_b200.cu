@@ -4,8 +4,9 @@
 // same module).  Every entry point:
 //   * takes plain device pointers, sizes and a cudaStream_t,
 //   * launches asynchronously on that stream, never synchronizes, never
-//     allocates (callers own all memory), so calls can be captured in CUDA
-//     graphs,
+//     allocates device memory (callers own all memory; the only allocating
+//     entry points are the explicit qi_b200_peer_alloc / _free), so calls can
+//     be captured in CUDA graphs,
 //   * returns an int status (0 = ok), see include/qi_b200.h.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -15,6 +16,7 @@
 #include <cstdio>
 #include <cstring>
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "dit_fused.cuh"
@@ -33,11 +35,11 @@ namespace qib {
 // per-device host state
 // ---------------------------------------------------------------------------
 // Per-stream slots (up to kTailSlots streams per device; further streams run
-// without what a slot provides).  Tail-split workspace of the CTA-pair GEMM:
-// partial accumulators for one wave of 256 x 256 tiles, and the slot's
-// arrival / done counters in g_tail_cnt (zero at load; each launch leaves
-// them zero unless it aborted, and qi_b200_device_status(clear) re-zeroes
-// them after an error).
+// without what a slot provides).  A slot holds the arrival / done counters of
+// the CTA-pair GEMM's tail split in g_tail_cnt (zero at load; each launch
+// leaves them zero unless it aborted, and qi_b200_device_status(clear)
+// re-zeroes them after an error); the partial accumulators themselves go to
+// a workspace the caller passes (qi_b200_gemm_ws).
 constexpr int kTailSlots = 8;
 __device__ unsigned int g_tail_cnt[kTailSlots][2 * kMaxTailTiles];
 // Per-stream slots also hold the NVFP4 tensor amax pass's per-block maxima
@@ -46,16 +48,12 @@ __device__ unsigned int g_tail_cnt[kTailSlots][2 * kMaxTailTiles];
 constexpr int kAmaxParts = 2048;
 __device__ unsigned int g_amax_part[kTailSlots][kAmaxParts];
 __device__ unsigned int g_amax_ticket[kTailSlots];
-struct TailSlot {
-  cudaStream_t stream;
-  uint32_t* ws;
-};
 
 struct DeviceInfo {
   int checked = 0;  // 0 unknown, 1 ok, -1 wrong arch
   int num_sms = 0;
   int n_tail = 0;
-  TailSlot tail[kTailSlots] = {};
+  cudaStream_t tail[kTailSlots] = {};
   unsigned int* tail_cnt = nullptr;
   unsigned int* amax_part = nullptr;
   unsigned int* amax_ticket = nullptr;
@@ -64,10 +62,6 @@ constexpr int kMaxDevices = 64;
 static DeviceInfo g_dev[kMaxDevices];
 static std::mutex g_dev_mu;
 
-// Workspace and counters for tail-split launches on `stream`; false when none
-// can be had (the launch then runs without the split).  The first use on a
-// stream allocates in relaxed capture mode, so it also works while the
-// stream is being captured into a CUDA graph.
 // Slot of `stream` (registered on first use, up to kTailSlots per device),
 // -1 when the table is full or the slot arrays cannot be located.  Call with
 // g_dev_mu held.
@@ -84,33 +78,21 @@ static int stream_slot(DeviceInfo* di, cudaStream_t stream) {
     di->tail_cnt = static_cast<unsigned int*>(a);
   }
   int i = 0;
-  while (i < di->n_tail && di->tail[i].stream != stream) ++i;
+  while (i < di->n_tail && di->tail[i] != stream) ++i;
   if (i == di->n_tail) {
     if (i == kTailSlots) return -1;
-    di->tail[i] = {stream, nullptr};
+    di->tail[i] = stream;
     di->n_tail = i + 1;
   }
   return i;
 }
 
-static bool tail_workspace(DeviceInfo* di, cudaStream_t stream, uint32_t** ws, unsigned int** cnt) {
+// Tail-split counters of `stream`'s slot; false when the slot table is full
+// (the launch then runs without the split).  Nothing is allocated.
+static bool tail_counters(DeviceInfo* di, cudaStream_t stream, unsigned int** cnt) {
   std::lock_guard<std::mutex> lk(g_dev_mu);
   const int i = stream_slot(di, stream);
   if (i < 0) return false;
-  if (di->tail[i].ws == nullptr) {
-    const size_t bytes = static_cast<size_t>(di->num_sms / 2) * 256 * 256 * 4;
-    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
-    cudaThreadExchangeStreamCaptureMode(&mode);
-    void* w = nullptr;
-    const cudaError_t e = cudaMalloc(&w, bytes);
-    cudaThreadExchangeStreamCaptureMode(&mode);
-    if (e != cudaSuccess) {
-      cudaGetLastError();
-      return false;
-    }
-    di->tail[i].ws = static_cast<uint32_t*>(w);
-  }
-  *ws = di->tail[i].ws;
   *cnt = di->tail_cnt + static_cast<size_t>(i) * 2 * kMaxTailTiles;
   return true;
 }
@@ -202,7 +184,7 @@ struct LaunchPlan {
 };
 static thread_local LaunchPlan g_last_plan = {0, 0, 0, 0, 0, 0};
 static thread_local int g_last_tail = 1;  // splits per tail tile of the last CTA-pair launch
-enum PlanKernel { kPlanGemmI8 = 1, kPlanGemmF8 = 2, kPlanGemmBF16 = 3, kPlanGemmNVF4 = 4, kPlanW4Tile = 5,
+enum PlanKernel { kPlanGemmI8 = 1, kPlanGemmF8 = 2, kPlanGemmBF16 = 3, kPlanGemmNVF4 = 4,
                   kPlanW4Skinny = 6, kPlanW4Small = 7,
                   kPlanGemmPair = 8 /* + kind: 8 int8, 9 fp8, 10 bf16, 11 nvfp4 */,
                   kPlanGemmCsk = 12 /* + kind: 12 int8, 13 fp8, 14 bf16 */ };
@@ -230,9 +212,9 @@ static int launch_gemm_cfg(const void* A, const void* B, const EpiParams& p, int
       return QI_B200_ECUDA;
     attr_done[dev] = true;
   }
-  const int tiles = ((p.M + C::BM - 1) / C::BM) * ((p.N + BN - 1) / BN) * (p.ksplit > 1 ? p.ksplit : 1);
+  const int tiles = ((p.M + C::BM - 1) / C::BM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < num_sms ? tiles : num_sms;
-  g_last_plan = {1 + static_cast<int>(KIND), grid, p.ksplit > 1 ? p.ksplit : 1, BN, STAGES, C::SMEM_BYTES};
+  g_last_plan = {1 + static_cast<int>(KIND), grid, 1, BN, STAGES, C::SMEM_BYTES};
   const cudaError_t e =
       launch_pdl(k_gemm_tc<KIND, BN, STAGES>, dim3(grid), dim3(kGemmThreads), C::SMEM_BYTES, stream, 1, ta, tb, p);
   count_launches(1);
@@ -278,10 +260,14 @@ static int launch_gemm2_cfg(const void* A, const void* B, const EpiParams& p, in
   const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
   EpiParams q = p;
   q.tail_split = 1;
-  if (!C::NVF4 && !GATHER && p.tail_split != 1) {
+  q.tail_cnt = nullptr;
+  if (!C::NVF4 && !GATHER && p.tail_split != 1 && p.tail_ws != nullptr) {
+    // the split needs the caller's workspace to hold every tail tile's S
+    // partial accumulators (256 x BN words each)
     const int S = tail_plan(tiles, pairs, static_cast<int>((ku + C::BK - 1) / C::BK), p.tail_split);
+    const size_t need = static_cast<size_t>(tiles % pairs) * S * 256 * BN * 4;
     DeviceInfo* di = nullptr;
-    if (S > 1 && device_info(&di) == QI_B200_OK && tail_workspace(di, stream, &q.tail_ws, &q.tail_cnt))
+    if (S > 1 && need <= p.tail_ws_bytes && device_info(&di) == QI_B200_OK && tail_counters(di, stream, &q.tail_cnt))
       q.tail_split = S;
   }
   g_last_plan = {kPlanGemmPair + static_cast<int>(KIND), 2 * pairs, 2, BN, STAGES, C::SMEM_BYTES};
@@ -412,7 +398,7 @@ static int launch_gemm(const void* A, const void* B, const EpiParams& p, cudaStr
         default: return QI_B200_EINVAL;
       }
     }
-    if (force_bn == 0 && p.ksplit <= 1) {
+    if (force_bn == 0) {
       // very few tiles over a long K (e.g. the DiT action expert's FFN-down,
       // M = 32, N = 1024, K = 4096: 12.5 -> 8.8 us): split K inside clusters
       const int bk = KIND == MmaKind::BF16 ? 64 : 128;
@@ -468,15 +454,51 @@ static int check_gemm_args(int kind, const void* A, const void* B, const float* 
   return QI_B200_OK;
 }
 
+// Workspace bytes the tail split of the GEMM that launch_gemm would run for
+// this problem needs (0 when that launch does not split): the same kernel
+// and tile choice as launch_gemm, then tail tiles x splits x 256 x BN words.
+static size_t tail_ws_plan(int kind, int M, int N, int K, int mode, int force_bn, int num_sms) {
+  if (mode == 1 || kind < 0 || kind > 2 || M <= 0 || N <= 0 || K <= 0 || force_bn > 0) return 0;
+  const int bk = kind == QI_B200_KIND_BF16 ? 64 : 128;
+  const int k_blocks = (K + bk - 1) / bk;
+  const int pairs_max = num_sms / 2;
+  int bn = 0;
+  if (force_bn < 0) {
+    bn = -force_bn;
+  } else {
+    const int tiles128 = ((M + 127) / 128) * ((N + 127) / 128);
+    if (tiles128 <= 16 && k_blocks >= 32) {
+      int cbn, cs;
+      csk_plan(kind, M, N, K, num_sms, &cbn, &cs);
+      if (cbn != 0) return 0;  // cluster split-K: no workspace
+    }
+    const long long ptiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+    if (M >= 1024 && ptiles >= pairs_max) {
+      if (tail_plan(static_cast<int>(ptiles), pairs_max, k_blocks, mode) > 1 || pick_bn(M, N, num_sms) == 256)
+        bn = 256;
+    }
+  }
+  if (bn == 0) return 0;
+  const int tiles = ((M + 255) / 256) * ((N + bn - 1) / bn);
+  const int pairs = tiles < pairs_max ? tiles : pairs_max;
+  const int S = tail_plan(tiles, pairs, k_blocks, mode);
+  return S > 1 ? static_cast<size_t>(tiles % pairs) * S * 256 * bn * 4 : 0;
+}
+
+// workspace == nullptr runs without the tail split (as tail mode 1).
 static int gemm_dispatch(int kind, const void* A, const void* B, const float* sa, int sa_stride, const float* sb,
                          int sb_stride, const void* bias, void* D, long long ldd, int M, int N, int K, int flags,
-                         int force_bn, cudaStream_t stream) {
-  const int tail_mode = (flags >> QI_B200_TAIL_SPLIT_SHIFT) & 15;
+                         int force_bn, cudaStream_t stream, void* workspace = nullptr, size_t workspace_bytes = 0) {
+  int tail_mode = (flags >> QI_B200_TAIL_SPLIT_SHIFT) & 15;
   flags &= ~(15 << QI_B200_TAIL_SPLIT_SHIFT);
   int rc = check_gemm_args(kind, A, B, sa, sa_stride, sb, sb_stride, bias, D, ldd, M, N, K, flags);
   if (rc) return rc;
+  if (workspace != nullptr && !aligned16(workspace)) return QI_B200_EALIGN;
+  if (workspace == nullptr || workspace_bytes == 0) tail_mode = 1;
   EpiParams p{};
   p.tail_split = tail_mode;  // 0 automatic, 1 none, S >= 2 at most S (resolved by the pair launcher)
+  p.tail_ws = static_cast<uint32_t*>(workspace);
+  p.tail_ws_bytes = workspace_bytes;
   p.sa = sa;
   p.sa_stride = sa_stride;
   p.sb = sb;
@@ -507,12 +529,13 @@ static int quant_status(cudaError_t e) { return e == cudaSuccess ? QI_B200_OK : 
 struct PeerFlags {
   unsigned int* flag[kMaxPeers];  // rank i's flag block: word j written by rank j; word kMaxPeers = i's counter
   int P, rank;
+  unsigned long long timeout_ns;  // wait limit per lane
 };
 
 // One warp.  This rank's barrier counter (in its own flag block, so a CUDA
 // graph replay advances it too) gives the epoch.  Lane i < P publishes the
 // epoch in rank i's block (release, system scope), then waits (acquire,
-// bounded by the 2 s budget) until rank i has published the same epoch in
+// bounded by f.timeout_ns) until rank i has published the same epoch in
 // this rank's block.  Every rank runs the same sequence of barriers.
 __global__ void k_peer_barrier(PeerFlags f) {
   const int lane = threadIdx.x;
@@ -531,7 +554,7 @@ __global__ void k_peer_barrier(PeerFlags f) {
       unsigned int v;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
       if (static_cast<int>(v - epoch) >= 0) break;
-      if (globaltimer_ns() - t0 > QI_WAIT_TIMEOUT_NS) {
+      if (globaltimer_ns() - t0 > f.timeout_ns) {
         record_error(kDevWaitTimeout, 0x300u, static_cast<unsigned int>(lane));
         break;
       }
@@ -579,8 +602,10 @@ extern "C" int qi_b200_peer_free(void* ptr) {
   return cudaFree(ptr) == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
-extern "C" int qi_b200_peer_barrier(void* const* flags, int P, int rank, cudaStream_t stream) {
+extern "C" int qi_b200_peer_barrier_timed(void* const* flags, int P, int rank, unsigned long long timeout_ns,
+                                          cudaStream_t stream) {
   if (flags == nullptr || P < 1 || P > kMaxPeers || rank < 0 || rank >= P) return QI_B200_EINVAL;
+  if (timeout_ns == 0 || timeout_ns > QI_WAIT_TIMEOUT_NS) return QI_B200_EINVAL;
   PeerFlags f{};
   for (int i = 0; i < P; ++i) {
     if (flags[i] == nullptr || (reinterpret_cast<uintptr_t>(flags[i]) & 3u) != 0) return QI_B200_EALIGN;
@@ -588,9 +613,14 @@ extern "C" int qi_b200_peer_barrier(void* const* flags, int P, int rank, cudaStr
   }
   f.P = P;
   f.rank = rank;
+  f.timeout_ns = timeout_ns;
   k_peer_barrier<<<1, 32, 0, stream>>>(f);
   count_launches(1);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+extern "C" int qi_b200_peer_barrier(void* const* flags, int P, int rank, cudaStream_t stream) {
+  return qi_b200_peer_barrier_timed(flags, P, rank, QI_WAIT_TIMEOUT_NS, stream);
 }
 
 extern "C" int qi_b200_gemm_gather(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
@@ -634,81 +664,6 @@ extern "C" int qi_b200_gemm_gather(int kind, const void* A, const void* B, const
   }
 }
 
-// Split-K plan for problems too small to fill the GPU with 128 x 256 tiles:
-// splits so that tiles x splits ~ #SMs, at least 4 K blocks per split (a
-// shorter main loop does not pay for the second kernel).
-static int splitk_splits(int kind, int M, int N, int K, int num_sms) {
-  if (kind < 0 || kind > 2 || M <= 0 || N <= 0 || K <= 0) return 1;
-  const int bk = kind == QI_B200_KIND_BF16 ? 64 : 128;
-  const int k_blocks = (K + bk - 1) / bk;
-  const long long tiles = (long long)((M + 127) / 128) * ((N + 255) / 256);
-  if (tiles * 2 > num_sms) return 1;
-  int sp = static_cast<int>(num_sms / tiles);
-  sp = std::min(sp, k_blocks / 4);
-  sp = std::min(sp, 16);
-  if (sp < 2) return 1;
-  const int kbp = (k_blocks + sp - 1) / sp;
-  return (k_blocks + kbp - 1) / kbp;  // every split gets a non-empty K range
-}
-
-extern "C" int qi_b200_gemm_splitk_plan(int kind, int M, int N, int K, int* splits, size_t* workspace_bytes) {
-  if (splits == nullptr || workspace_bytes == nullptr) return QI_B200_EINVAL;
-  DeviceInfo* di = nullptr;
-  int rc = device_info(&di);
-  if (rc) return rc;
-  *splits = splitk_splits(kind, M, N, K, di->num_sms);
-  *workspace_bytes = *splits > 1 ? static_cast<size_t>(*splits) * M * N * 4 : 0;
-  return QI_B200_OK;
-}
-
-extern "C" int qi_b200_gemm_splitk(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
-                                   const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd,
-                                   int M, int N, int K, int flags, int splits, void* workspace,
-                                   size_t workspace_bytes, cudaStream_t stream) {
-  if (flags & ~kEpiGelu) return QI_B200_EINVAL;  // bf16 outputs
-  if (kind < 0 || kind > 2 || splits < 2 || splits > 16) return QI_B200_EINVAL;
-  int rc = check_gemm_args(kind, A, B, a_scale, a_scale_stride, b_scale, b_scale_stride, bias, D, ldd, M, N, K,
-                           flags);
-  if (rc) return rc;
-  const int bk = kind == QI_B200_KIND_BF16 ? 64 : 128;
-  const int k_blocks = (K + bk - 1) / bk;
-  const int kbp = (k_blocks + splits - 1) / splits;
-  if ((long long)kbp * (splits - 1) >= k_blocks) return QI_B200_ESHAPE;  // a split with no K blocks
-  if (workspace == nullptr || !aligned16(workspace) || workspace_bytes < static_cast<size_t>(splits) * M * N * 4)
-    return QI_B200_EINVAL;
-  DeviceInfo* di = nullptr;
-  rc = device_info(&di);
-  if (rc) return rc;
-  EpiParams p{};
-  p.D = workspace;
-  p.ldd = N;
-  p.M = M;
-  p.N = N;
-  p.K = K;
-  p.flags = kEpiRawAcc;
-  p.ksplit = splits;
-  p.split_stride = (long long)M * N;
-  switch (kind) {
-    case QI_B200_KIND_INT8: rc = launch_gemm_cfg<MmaKind::I8, 256, 4>(A, B, p, di->num_sms, stream); break;
-    case QI_B200_KIND_FP8_E4M3: rc = launch_gemm_cfg<MmaKind::F8, 256, 4>(A, B, p, di->num_sms, stream); break;
-    default: rc = launch_gemm_cfg<MmaKind::BF16, 256, 4>(A, B, p, di->num_sms, stream); break;
-  }
-  if (rc) return rc;
-  const long long vec = (long long)M * (N / 8);
-  const int grid = (int)std::min<long long>((vec + 255) / 256, (long long)di->num_sms * 8);
-  const auto* bsp = static_cast<const __nv_bfloat16*>(bias);
-  auto* out = static_cast<__nv_bfloat16*>(D);
-  const int gelu = flags & kEpiGelu;
-  if (kind == QI_B200_KIND_INT8)
-    k_splitk_epilogue<true><<<grid, 256, 0, stream>>>(workspace, splits, p.split_stride, a_scale, a_scale_stride,
-                                                       b_scale, b_scale_stride, bsp, out, ldd, M, N, gelu);
-  else
-    k_splitk_epilogue<false><<<grid, 256, 0, stream>>>(workspace, splits, p.split_stride, a_scale, a_scale_stride,
-                                                        b_scale, b_scale_stride, bsp, out, ldd, M, N, gelu);
-  count_launches(1);
-  return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
-}
-
 extern "C" int qi_b200_gemm_csk(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
                                 const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd,
                                 int M, int N, int K, int flags, int tile_n, int splits, cudaStream_t stream) {
@@ -742,12 +697,6 @@ extern "C" int qi_b200_gemm_csk(int kind, const void* A, const void* B, const fl
     case QI_B200_KIND_FP8_E4M3: return launch_gemm_csk<MmaKind::F8>(A, B, p, tile_n, splits, stream);
     default: return launch_gemm_csk<MmaKind::BF16>(A, B, p, tile_n, splits, stream);
   }
-}
-
-extern "C" int qi_b200_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
-  if (bytes == 0) return QI_B200_OK;
-  if (dst == nullptr || src == nullptr) return QI_B200_EINVAL;
-  return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, stream) == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
 // ---------------------------------------------------------------------------
@@ -977,25 +926,21 @@ static int launch_w4a16(const void* X, const void* wq, const void* scales, const
   if (M <= 64) return launch_w4_skinny<64>(X, p, q, di->num_sms, stream);
   if (M <= 128) return launch_w4_skinny<128>(X, p, q, di->num_sms, stream);
   if (M <= 256) return launch_w4_skinny<256>(X, p, q, di->num_sms, stream);
-  CUtensorMap tx;
-  rc = make_tmap_2d(&tx, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, w4::BK,
-                    256);
-  if (rc) return rc;
-  static bool attr_done[kMaxDevices] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_done[dev]) {
-    if (cudaFuncSetAttribute(k_gemm_w4a16, cudaFuncAttributeMaxDynamicSharedMemorySize, W4Cfg<256>::SMEM_BYTES) !=
-        cudaSuccess)
-      return QI_B200_ECUDA;
-    attr_done[dev] = true;
+  // M > 256 without a workspace (qi_b200_w4a16_linear): the skinny kernel
+  // over 256-row blocks of x.  With a workspace, qi_b200_w4a16_linear_ws
+  // dequantizes the weights once instead, which is faster at these M.
+  const auto* xb = static_cast<const __nv_bfloat16*>(X);
+  auto* db = static_cast<__nv_bfloat16*>(D);
+  for (int m0 = 0; m0 < M; m0 += 256) {
+    EpiParams pc = p;
+    pc.M = std::min(256, M - m0);
+    pc.D = db + static_cast<long long>(m0) * ldd;
+    const void* xc = xb + static_cast<long long>(m0) * K;
+    rc = pc.M <= 128 ? launch_w4_skinny<128>(xc, pc, q, di->num_sms, stream)
+                     : launch_w4_skinny<256>(xc, pc, q, di->num_sms, stream);
+    if (rc) return rc;
   }
-  const int tiles = ((M + 255) / 256) * ((N + w4::BN - 1) / w4::BN);
-  const int grid = tiles < di->num_sms ? tiles : di->num_sms;
-  g_last_plan = {kPlanW4Tile, grid, 1, 256, W4Cfg<256>::STAGES, W4Cfg<256>::SMEM_BYTES};
-  k_gemm_w4a16<<<grid, w4::kThreads, W4Cfg<256>::SMEM_BYTES, stream>>>(tx, p, q);
-  count_launches(1);
-  return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+  return QI_B200_OK;
 }
 
 }  // namespace qib
@@ -1213,6 +1158,24 @@ int qi_b200_gemm(int kind, const void* A, const void* B, const float* a_scale, i
                        tile_n, stream);
 }
 
+int qi_b200_gemm_ws(int kind, const void* A, const void* B, const float* a_scale, int a_scale_stride,
+                    const float* b_scale, int b_scale_stride, const void* bias, void* D, long long ldd, int M, int N,
+                    int K, int flags, int tile_n, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return gemm_dispatch(kind, A, B, a_scale, a_scale_stride, b_scale, b_scale_stride, bias, D, ldd, M, N, K, flags,
+                       tile_n, stream, workspace, workspace_bytes);
+}
+
+int qi_b200_gemm_workspace_bytes(int kind, int M, int N, int K, int flags, int tile_n, size_t* bytes) {
+  if (bytes == nullptr) return QI_B200_EINVAL;
+  *bytes = 0;
+  if (kind < 0 || kind > 2) return QI_B200_EINVAL;
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  *bytes = tail_ws_plan(kind, M, N, K, (flags >> QI_B200_TAIL_SPLIT_SHIFT) & 15, tile_n, di->num_sms);
+  return QI_B200_OK;
+}
+
 int qi_b200_int8_rowwise_bf16out(const void* A, const void* B, const void* act_scale, const void* weight_scale,
                                  void* D, int M, int N, int K, cudaStream_t stream) {
   return gemm_dispatch(QI_B200_KIND_INT8, A, B, static_cast<const float*>(act_scale), 1,
@@ -1304,8 +1267,8 @@ int qi_b200_nvfp4_linear(const void* x_bf16, const void* weight_packed, const vo
                     out_bf16, N, M, N, K, flags, stream);
 }
 
-// gemm_flags: tail-split mode bits only (the entry point that allocates
-// nothing turns the split, whose workspace is allocated on first use, off)
+// gemm_flags: epilogue flags only; these entry points take no GEMM
+// workspace, so the CTA-pair kernel's tail split does not run
 static int int8_linear_impl(const void* x_bf16, const void* qweight, const float* weight_scale, const void* bias,
                             void* out_bf16, void* ws_q, float* ws_scales, int M, int N, int K, int gemm_flags,
                             cudaStream_t stream) {
@@ -1371,7 +1334,7 @@ static __device__ __align__(256) int8_t g_noalloc_q[QI_B200_NOALLOC_MAX_ACT_BYTE
 static __device__ __align__(256) float g_noalloc_scales[QI_B200_NOALLOC_MAX_ROWS];
 
 struct NoAllocScratch {
-  int ready = 0;
+  std::atomic<int> ready{0};  // release-stored after q / scales are set
   void* q = nullptr;
   float* scales = nullptr;
 };
@@ -1387,16 +1350,19 @@ static int noalloc_scratch(void** q, float** scales) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QI_B200_ECUDA;
   NoAllocScratch& e = g_noalloc[dev];
-  if (!e.ready) {
+  if (!e.ready.load(std::memory_order_acquire)) {
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!e.ready) {
+    if (!e.ready.load(std::memory_order_relaxed)) {
       void* pq = nullptr;
       void* ps = nullptr;
-      if (cudaGetSymbolAddress(&pq, g_noalloc_q) != cudaSuccess) return QI_B200_ECUDA;
-      if (cudaGetSymbolAddress(&ps, g_noalloc_scales) != cudaSuccess) return QI_B200_ECUDA;
+      if (cudaGetSymbolAddress(&pq, g_noalloc_q) != cudaSuccess ||
+          cudaGetSymbolAddress(&ps, g_noalloc_scales) != cudaSuccess) {
+        cudaGetLastError();  // leave no sticky error for the caller's next cudaGetLastError
+        return QI_B200_ECUDA;
+      }
       e.q = pq;
       e.scales = static_cast<float*>(ps);
-      e.ready = 1;
+      e.ready.store(1, std::memory_order_release);
     }
   }
   *q = e.q;
@@ -1417,6 +1383,5 @@ extern "C" int qi_b200_int8_linear_noalloc(const void* x_bf16, const void* qweig
   float* scales = nullptr;
   int rc = noalloc_scratch(&q, &scales);
   if (rc) return rc;
-  return int8_linear_impl(x_bf16, qweight, weight_scale, bias, out_bf16, q, scales, M, N, K,
-                          1 << QI_B200_TAIL_SPLIT_SHIFT, stream);
+  return int8_linear_impl(x_bf16, qweight, weight_scale, bias, out_bf16, q, scales, M, N, K, 0, stream);
 }

@@ -10,7 +10,8 @@
 //   int8  (csrc/int8_w8a8/quantize_int8.cu:7-59): s = max(amax/127, 1e-10),
 //         q = clamp(rint(x * (1/s)), -127, 127) with an IEEE reciprocal.
 //   fp8   (backends/flashrt_fp8_ops.py:38-48, one scale per row instead of one
-//         per tensor): s = max(amax/448, 1e-12), q = e4m3_rn(clamp(x/s, +-448)).
+//         per tensor): s = max(amax/448, 1e-12), q = e4m3_rn(clamp(x/s, +-448)),
+//         x/s proven from a bracketed reciprocal product (see QuantFp8).
 //   fp8 static (flashrt_fp8_ops.py:207-216): q = e4m3_rn(clamp(x/s_static, +-448)).
 #pragma once
 
@@ -37,7 +38,20 @@ struct QuantInt8 {
     q = q < -127 ? -127 : (q > 127 ? 127 : q);
     return static_cast<uint8_t>(static_cast<int8_t>(q));
   }
+  // two elements -> two codes (low byte = f.x)
+  __device__ __forceinline__ static uint32_t q2(float2 f, float s, float inv) {
+    return q1(f.x, s, inv) | (static_cast<uint32_t>(q1(f.y, s, inv)) << 8);
+  }
 };
+
+// Two fp32 values -> two E4M3 codes, round to nearest even, saturating to
+// +-448 (NaN stays NaN); low byte = lo.  cvt...e4m3x2.f32 puts its first
+// source operand in the upper byte.
+__device__ __forceinline__ uint32_t e4m3x2_rn_sat(float lo, float hi) {
+  unsigned short r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
 
 // int8 with per-row scales supplied by the caller (e.g. reduced across ranks
 // that each hold a K-slice of the row): q = clamp(rint(x * (1/s)), -127, 127).
@@ -52,16 +66,35 @@ struct QuantInt8ScalesOnly : QuantInt8 {
   static constexpr bool kStoreQ = false;
 };
 
+// FP8 codes are e4m3_rn(clamp(fl32(x / s), +-448)) (flashrt_fp8_ops.py:43-48;
+// the saturating conversion is that clamp).  The division is avoided: with
+// r = rn(1/s), t = rn(x r) is within 2^-22.4 (relative) of fl32(x / s)
+// (x r carries 2^-23 + 2^-48, fl32(x / s) 2^-24), so fl32(x / s) lies between
+// t (1 - 2^-20) and t (1 + 2^-20), both ends computed with one more rounding
+// of 2^-24.  Rounding to E4M3 is monotone, so when both ends give the same
+// code that code is proven; otherwise (the bracket straddles a rounding
+// boundary, about 1 in 2^16 elements) the pair is redone with the correctly
+// rounded division.  Below fp32's normal range every value involved is
+// smaller than half the least E4M3 subnormal, so all three give a zero of
+// the same sign.
 struct QuantFp8 {
   static constexpr bool kNeedsAmax = true;
   static constexpr bool kStoreQ = true;
   __device__ __forceinline__ static float scale_from_amax(float amax) {
     return fmaxf(__fdiv_rn(amax, 448.0f), 1e-12f);
   }
-  __device__ __forceinline__ static float aux(float s) { return s; }
+  __device__ __forceinline__ static float aux(float s) { return __frcp_rn(s); }
   __device__ __forceinline__ static uint8_t q1(float x, float s, float /*aux*/) {
-    float v = fminf(fmaxf(__fdiv_rn(x, s), -448.0f), 448.0f);
-    return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+    const float v = __fdiv_rn(x, s);
+    return static_cast<uint8_t>(e4m3x2_rn_sat(v, 0.0f) & 0xFFu);
+  }
+  __device__ __forceinline__ static uint32_t q2(float2 f, float s, float r) {
+    constexpr float kLo = 1.0f - 0x1p-20f, kHi = 1.0f + 0x1p-20f;
+    const float2 t = __fmul2_rn(f, make_float2(r, r));
+    const uint32_t lo = e4m3x2_rn_sat(__fmul_rn(t.x, kLo), __fmul_rn(t.y, kLo));
+    const uint32_t hi = e4m3x2_rn_sat(__fmul_rn(t.x, kHi), __fmul_rn(t.y, kHi));
+    if (__builtin_expect(lo == hi, 1)) return lo;
+    return e4m3x2_rn_sat(__fdiv_rn(f.x, s), __fdiv_rn(f.y, s));
   }
 };
 
@@ -106,9 +139,7 @@ __device__ __forceinline__ uint2 quant_bf16x8(const uint4& v, float s, float aux
   uint32_t lo = 0, hi = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    float2 f = __bfloat1622float2(h[i]);
-    uint32_t b0 = Op::q1(f.x, s, aux), b1 = Op::q1(f.y, s, aux);
-    uint32_t pair = b0 | (b1 << 8);
+    const uint32_t pair = Op::q2(__bfloat1622float2(h[i]), s, aux);
     if (i < 2) lo |= pair << (16 * i);
     else hi |= pair << (16 * (i - 2));
   }

@@ -585,6 +585,14 @@ class DiTStepRunner:
 
     # -- CUDA graph ---------------------------------------------------------
 
+    def check(self) -> None:
+        """Raise ``QiB200DeviceError`` if a kernel of the step gave up a
+        bounded wait since the last check (its outputs are then incomplete).
+        Synchronizes the host with the device: call it between steps."""
+        from . import _lib
+
+        _lib.raise_on_device_error()
+
     def capture(self, tokens: dict, rope: dict, ctx: dict, t_mod: dict, warmup: int = 2):
         """Capture one step on static input buffers; ``replay()`` reruns it."""
         self.static_in = ({n: t.clone() for n, t in tokens.items()}, rope, ctx, t_mod)
@@ -594,6 +602,8 @@ class DiTStepRunner:
             for _ in range(warmup):
                 self.step(*self.static_in)
         torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        self.check()  # the eager warm-up steps ran clean before they are captured
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             self.static_out = self.step(*self.static_in)

@@ -172,33 +172,37 @@ def quantize_fp8_static(x: torch.Tensor, scale: torch.Tensor):
 # ---------------------------------------------------------------------------
 
 
-_SPLITK_PLANS: dict = {}
+_WS_PLANS: dict = {}
 
 
-def splitk_plan(kind: int, M: int, N: int, K: int) -> tuple:
-    """(splits, workspace bytes) that fill the SMs with 128 x 256 tiles; 1 = the tiles already do."""
-    key = (kind, M, N, K, torch.cuda.current_device())
-    plan = _SPLITK_PLANS.get(key)
-    if plan is None:
+def gemm_workspace_bytes(kind: int, M: int, N: int, K: int, tail_split: int = 0, tile_n: int = 0) -> int:
+    """Workspace bytes ``qi_b200_gemm_ws`` needs for the CTA-pair kernel's
+    split of its partial last wave (0: the launch for this problem does not
+    split).  Host-side plan, cached per shape and device."""
+    key = (kind, M, N, K, tail_split, tile_n, torch.cuda.current_device())
+    v = _WS_PLANS.get(key)
+    if v is None:
         import ctypes
-        sp, wb = ctypes.c_int(0), ctypes.c_size_t(0)
-        _lib.call("qi_b200_gemm_splitk_plan", kind, M, N, K, ctypes.byref(sp), ctypes.byref(wb))
-        plan = _SPLITK_PLANS[key] = (sp.value, wb.value)
-    return plan
+        nb = ctypes.c_size_t(0)
+        _lib.call("qi_b200_gemm_workspace_bytes", kind, M, N, K, tail_split << _lib.TAIL_SPLIT_SHIFT, tile_n,
+                  ctypes.byref(nb))
+        v = _WS_PLANS[key] = int(nb.value)
+    return v
 
 
 def gemm(kind: int, a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor | None,
          b_scale: torch.Tensor | None, bias: torch.Tensor | None = None, *, gelu: bool = False,
          raw_acc: bool = False, out: torch.Tensor | None = None, tile_n: int = 0,
-         splits: int = 1, tail_split: int = 0) -> torch.Tensor:
-    """D = epi(A[M,K] . B[N,K]^T); see ``qi_b200_gemm`` in include/qi_b200.h.
+         tail_split: int = 0) -> torch.Tensor:
+    """D = epi(A[M,K] . B[N,K]^T); see ``qi_b200_gemm_ws`` in include/qi_b200.h.
 
     Scales of one element broadcast (per tensor); otherwise a_scale is [M]
     and b_scale is [N].  ``raw_acc`` returns the 32-bit accumulators (int32
-    for INT8, fp32 otherwise) instead of bf16.  ``splits > 1`` splits K over
-    that many CTAs per output tile (``qi_b200_gemm_splitk``).  ``tail_split``
-    sets how the CTA-pair kernel spreads its partial last wave over idle pairs
-    (0 the library's choice, 1 no split, S at most S splits per tile).
+    for INT8, fp32 otherwise) instead of bf16.  ``tail_split`` sets how the
+    CTA-pair kernel spreads its partial last wave over idle pairs (0 the
+    library's choice, 1 no split, S at most S splits per tile); the workspace
+    that needs comes from torch's caching allocator (so it also works inside
+    CUDA-graph capture).
     """
     dt = {_lib.KIND_INT8: (torch.int8,), _lib.KIND_FP8_E4M3: (torch.uint8, torch.float8_e4m3fn),
           _lib.KIND_BF16: (torch.bfloat16,)}[kind]
@@ -231,18 +235,11 @@ def gemm(kind: int, a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor | No
     flags = (_lib.EPI_GELU if gelu else 0) | (_lib.EPI_RAW_ACC if raw_acc else 0)
     if not 0 <= tail_split <= 15:
         raise ValueError(f"tail_split must be in [0, 15], got {tail_split}.")
-    if splits > 1:  # split K over several CTAs per tile, sum the partials in a second kernel
-        if raw_acc or tile_n != 0:
-            raise ValueError("splits > 1 takes bf16 outputs and the library's tile choice")
-        ws_bytes = splits * M * N * 4
-        ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=a.device)
-        _lib.call("qi_b200_gemm_splitk", kind, _ptr(a), _ptr(b), _ptr(sa), sa_stride, _ptr(sb), sb_stride,
-                  _ptr(bias), _ptr(out), out.stride(0), M, N, K, flags, splits, _ptr(ws), ws_bytes,
-                  _stream(a.device))
-        return out
+    ws_bytes = gemm_workspace_bytes(kind, M, N, K, tail_split, tile_n)
+    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=a.device) if ws_bytes else None
     flags |= tail_split << _lib.TAIL_SPLIT_SHIFT
-    _lib.call("qi_b200_gemm", kind, _ptr(a), _ptr(b), _ptr(sa), sa_stride, _ptr(sb), sb_stride,
-              _ptr(bias), _ptr(out), out.stride(0), M, N, K, flags, tile_n, _stream(a.device))
+    _lib.call("qi_b200_gemm_ws", kind, _ptr(a), _ptr(b), _ptr(sa), sa_stride, _ptr(sb), sb_stride,
+              _ptr(bias), _ptr(out), out.stride(0), M, N, K, flags, tile_n, _ptr(ws), ws_bytes, _stream(a.device))
     return out
 
 
@@ -274,7 +271,9 @@ def int8_linear(x_bf16_2d: torch.Tensor, qweight: torch.Tensor, weight_scales: t
             raise ValueError("bias length must match qweight N dimension.")
     ws_q = torch.empty((M, K), dtype=torch.int8, device=dev)
     ws_s = torch.empty((M,), dtype=torch.float32, device=dev)
-    if gelu or input_scale is not None:
+    if gelu or input_scale is not None or gemm_workspace_bytes(_lib.KIND_INT8, M, N, K):
+        # the fused SmoothQuant division, the GELU epilogue or the tail split's
+        # workspace: the quantizer and the GEMM as two calls
         quantize_int8_rowwise(x_bf16_2d, ws_q, ws_s, input_scale=input_scale)
         return gemm(_lib.KIND_INT8, ws_q, qweight, ws_s, weight_scales, bias, gelu=gelu)
     out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)

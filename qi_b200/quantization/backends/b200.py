@@ -80,11 +80,19 @@ def _bias_bf16(bias, n, device):
 
 
 class B200Backend:
-    """Quantized linear on B200 tensor cores (tcgen05)."""
+    """Quantized linear on B200 tensor cores (tcgen05).
 
-    def __init__(self, gelu: bool = False) -> None:
+    ``check_errors=True`` reads the device status word after every call and
+    raises ``QiB200DeviceError`` if a kernel gave up a bounded wait (its
+    output is then incomplete).  That read synchronizes the host with the
+    device, so it is off by default; callers that run many layers check once
+    per step instead (``qi_b200._lib.raise_on_device_error``, which
+    ``DiTStepRunner.check`` and ``bench.py`` call)."""
+
+    def __init__(self, gelu: bool = False, check_errors: bool = False) -> None:
         self._lib = load_b200_ops(required=False)
         self.fuse_gelu = gelu
+        self.check_errors = check_errors
 
     def linear(self, x, qweight, scales, zeros, bias, bits, group_size, symmetric, input_scale,
                keep_output_dtype, qweight_packed=None, scale_factors=None, weight_global_scale=None,
@@ -132,6 +140,8 @@ class B200Backend:
             raise ValueError(
                 "B200 backend: unsupported buffer combination (bits=%s, activation_granularity=%s, packed=%s)"
                 % (bits, activation_granularity, None if qweight_packed is None else qweight_packed.dtype))
+        if self.check_errors:
+            _lib.raise_on_device_error()
         return y.reshape(*x.shape[:-1], y.shape[-1]).to(out_dtype)
 
     # -- formats ------------------------------------------------------------

@@ -267,27 +267,22 @@ class PeerBuffer:
 
 
 class PeerGatherLinear(nn.Module):
-    """Column-parallel INT8 / FP8 W8A8 linear whose all-gather overlaps the
+    """Column-parallel INT8 / FP8 W8A8 linear whose all-gather runs inside the
     GEMM.
 
-    ``mode="fused"`` (default): one CTA-pair GEMM kernel whose epilogue
-    writes every finished 32 x 32 output box with TMA stores into this
-    rank's block of all P buffers.  The NVLink transfer of each tile runs
-    while the tensor cores compute the next ones, inside one kernel.
-    ``mode="copy"``: the description below (row-block GEMMs + copy engines).
-
     Rank r writes its [M, N/P] output into block r of a rank-major
-    [P, M, N/P] buffer that every rank has mapped (``PeerBuffer``).  The
-    GEMM runs in ``chunks`` row blocks on the current stream.  As each block
-    finishes, a side stream copies it into block r of every peer's buffer
-    with ``cudaMemcpyAsync`` over NVLink.  So the transfer of block i runs
-    beside the GEMM of block i+1, and no SM time goes to the collective.
+    [P, M, N/P] buffer that every rank has mapped (``PeerBuffer``).  One
+    CTA-pair GEMM kernel (``qi_b200_gemm_gather``) writes every finished
+    32 x 64 output box with TMA stores into block r of all P buffers: its own
+    HBM and, over NVLink, the peers'.  The transfer of each tile runs while the
+    tensor cores compute the next ones, so no separate collective runs and no
+    SM time is set aside for one.
 
     Per call:
 
     1. a barrier (every rank has finished reading the previous output);
     2. the activation quantizer;
-    3. the pipelined GEMM and copies;
+    3. the GEMM with the gather in its epilogue;
     4. a barrier (all blocks have landed).
 
     Both barriers are bounded.  Every column is computed by one rank with
@@ -298,8 +293,7 @@ class PeerGatherLinear(nn.Module):
     layout of ``ColumnShardedLinear(gather="rank")``).  It stays valid until
     the layer's next call."""
 
-    def __init__(self, layer: WeightOnlyLinear, max_tokens: int, group=None, shard: bool = True, chunks: int = 0,
-                 copy_streams: int = 0, split: str = "peers", mode: str = "fused"):
+    def __init__(self, layer: WeightOnlyLinear, max_tokens: int, group=None, shard: bool = True):
         super().__init__()
         from . import _lib
         from . import kernels as K
@@ -327,25 +321,7 @@ class PeerGatherLinear(nn.Module):
         self.bias = None if loc.bias is None else loc.bias.to(torch.bfloat16).contiguous()
         self.gelu = bool(loc.fuse_gelu)
         self.max_tokens = int(max_tokens)
-        self.chunks = int(chunks)
         self.buf = PeerBuffer(self.world * self.max_tokens * self.n_local * 2, group)
-        # Copies run on several streams so several copy engines drive NVLink:
-        # split="peers" gives each stream its own subset of destination peers
-        # (default min(P-1, 4) streams); split="rows" splits every row block.
-        if split not in ("peers", "rows"):
-            raise ValueError("split must be 'peers' or 'rows'.")
-        if mode not in ("fused", "copy"):
-            raise ValueError("mode must be 'fused' or 'copy'.")
-        self.mode = mode
-        self.split = split
-        ns = int(copy_streams) if copy_streams > 0 else max(1, min(self.world - 1, 4))
-        self._side = [torch.cuda.Stream() for _ in range(ns)]
-
-    def _plan(self, m: int) -> list:
-        c = self.chunks if self.chunks > 0 else (4 if m >= 2048 else (2 if m >= 512 else 1))
-        step = -(-m // c)
-        step = -(-step // 128) * 128  # whole 128-row GEMM tiles per block
-        return [(r0, min(m, r0 + step)) for r0 in range(0, m, step)]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         K, L = self.K, self._lib
@@ -364,48 +340,21 @@ class PeerGatherLinear(nn.Module):
         blk = self.max_tokens * nl * 2                     # bytes of one rank block
         out = self.buf.local((P, self.max_tokens, nl))     # rank-major, this GPU's copy
         self.buf.barrier(main)  # every rank has finished reading the previous output
-        if self.mode == "fused":
-            # one CTA-pair GEMM whose epilogue TMA-stores every output box into
-            # this rank's block of all P buffers (own HBM first, then NVLink)
-            dst = [self.buf.data[(r + j) % P] + r * blk for j in range(P)]
-            L.call("qi_b200_gemm_gather", self.kind, q.data_ptr(), self.w.data_ptr(), s.data_ptr(),
-                   0 if s.numel() == 1 else 1, self.ws.data_ptr(), 0 if self.ws.numel() == 1 else 1,
-                   None if self.bias is None else self.bias.data_ptr(), (ctypes.c_void_p * P)(*dst), P, nl, m, nl,
-                   self.w.shape[1], L.EPI_GELU if self.gelu else 0, main.cuda_stream)
-            self.buf.barrier(main)  # every rank's tiles have landed here
-            return out[:, :m]
-        for sd in self._side:
-            sd.wait_stream(main)
-        ns = len(self._side)
-        for r0, r1 in self._plan(m):
-            s_blk = s if s.numel() == 1 else s[r0:r1]
-            K.gemm(self.kind, q[r0:r1], self.w, s_blk, self.ws, self.bias, gelu=self.gelu, out=out[r, r0:r1])
-            ev = torch.cuda.Event()
-            ev.record(main)
-            if self.split == "peers":
-                off = r * blk + r0 * nl * 2
-                for sd in self._side:
-                    sd.wait_event(ev)
-                for j in range(1, P):
-                    peer = (r + j) % P
-                    L.call("qi_b200_copy_async", self.buf.data[peer] + off, self.buf.data[r] + off,
-                           (r1 - r0) * nl * 2, self._side[(j - 1) % ns].cuda_stream)
-                continue
-            rows = -(-(r1 - r0) // ns)
-            for i, sd in enumerate(self._side):
-                a0, a1 = r0 + i * rows, min(r1, r0 + (i + 1) * rows)
-                if a0 >= a1:
-                    continue
-                sd.wait_event(ev)
-                off = r * blk + a0 * nl * 2
-                for j in range(1, P):
-                    peer = (r + j) % P
-                    L.call("qi_b200_copy_async", self.buf.data[peer] + off, self.buf.data[r] + off,
-                           (a1 - a0) * nl * 2, sd.cuda_stream)
-        for sd in self._side:
-            main.wait_stream(sd)
-        self.buf.barrier(main)  # every rank's blocks have landed here
+        # this rank's block of all P buffers, own HBM first, then the peers' over NVLink
+        dst = [self.buf.data[(r + j) % P] + r * blk for j in range(P)]
+        L.call("qi_b200_gemm_gather", self.kind, q.data_ptr(), self.w.data_ptr(), s.data_ptr(),
+               0 if s.numel() == 1 else 1, self.ws.data_ptr(), 0 if self.ws.numel() == 1 else 1,
+               None if self.bias is None else self.bias.data_ptr(), (ctypes.c_void_p * P)(*dst), P, nl, m, nl,
+               self.w.shape[1], L.EPI_GELU if self.gelu else 0, main.cuda_stream)
+        self.buf.barrier(main)  # every rank's tiles have landed here
         return out[:, :m]
+
+    def check(self) -> None:
+        """Raise ``QiB200DeviceError`` if a barrier or GEMM wait of this rank
+        timed out since the last check (a peer that never arrived, for
+        example); the outputs of those calls are incomplete.  Synchronizes
+        the host with the device: call it between steps."""
+        self._lib.raise_on_device_error()
 
     def close(self):
         self.buf.close()

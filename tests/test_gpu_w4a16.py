@@ -158,9 +158,9 @@ def test_w4a16_dequant_kernel_bit_exact(N, Kd, group):
 
 @pytest.mark.parametrize("M", [64, 256, 300, 600])
 def test_w4a16_fused_kernels_large_m(M):
-    """The fused kernels (split-K cluster for M <= 256, 256 x 128 tiles above)
-    stay reachable through qi_b200_w4a16_linear without a workspace; from
-    M = 257 the module path dequantizes once and runs the bf16 GEMM."""
+    """Without a workspace (qi_b200_w4a16_linear) the split-K cluster kernel
+    serves every M (per 256-row block above 256); from M = 257 the module
+    path dequantizes once into a workspace and runs the bf16 GEMM."""
     N, Kd, group = 256, 1024, 128
     x, w, b = make_small_case(M, N, Kd, seed=M + 11)
     qp, s16, zp = packed(w.numpy(), group)
@@ -170,7 +170,7 @@ def test_w4a16_fused_kernels_large_m(M):
     y = torch.empty((M, N), dtype=torch.bfloat16, device=DEV)
     _lib.call("qi_b200_w4a16_linear", xd.data_ptr(), qp_d.data_ptr(), s_d.data_ptr(), zp_d.data_ptr(), group,
               bd.data_ptr(), y.data_ptr(), M, N, Kd, torch.cuda.current_stream().cuda_stream)
-    assert _lib.last_launch()["kernel"] == ("w4a16_splitk" if M <= 256 else "w4a16_tiles")
+    assert _lib.last_launch()["kernel"] == "w4a16_splitk"
     yo = O.w4a16_linear(bits(x), qp, s16, zp, group, bits(b))
     assert O.rel_fro(O.bf16_to_f32(bits(y)), O.bf16_to_f32(yo)) <= 2e-3
     y2 = K.w4a16_linear(xd, qp_d, s_d, zp_d, group, bd)
