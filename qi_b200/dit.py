@@ -309,11 +309,13 @@ def _init_block(blk: DiTBlock, gen: torch.Generator):
 
 
 def build_mot_dit(cfg: DiTConfig = CFG5, device="cuda", seed: int = 0, quantize: bool = True,
-                  dtype=torch.bfloat16) -> MoTDiT:
-    """Random-init MoT DiT (seeded) with every target Linear swapped for an
-    INT8 W8A8 ``WeightOnlyLinear`` as each block is built.  The fp32 weights
-    of one block at a time are resident, so peak memory is the INT8 model
-    plus one block."""
+                  dtype=torch.bfloat16, state_dict=None) -> MoTDiT:
+    """MoT DiT with every target Linear swapped for an INT8 W8A8
+    ``WeightOnlyLinear`` as each block is built.  Weights are random (seeded)
+    or, with ``state_dict``, an unquantized checkpoint of the reference's MoT
+    (same parameter names: ``mixtures.<expert>.blocks.<i>.<module>``).  The
+    fp32 weights of one block at a time are resident, so peak memory is the
+    INT8 model plus one block."""
     from .quantization import WeightActivationQuantConfig, fuse_ffn_gelu, replace_linear_with_weight_only
 
     qcfg = WeightActivationQuantConfig(**INT8_DIT_CFG)
@@ -321,9 +323,13 @@ def build_mot_dit(cfg: DiTConfig = CFG5, device="cuda", seed: int = 0, quantize:
     gen = torch.Generator(device=device).manual_seed(seed)
     for spec in cfg.experts:
         ex = model.mixtures[spec.name]
-        for _ in range(cfg.layers):
+        for li in range(cfg.layers):
             blk = DiTBlock(spec.hidden, spec.ffn, cfg.heads, cfg.head_dim, cfg.eps).to(device)
-            _init_block(blk, gen)
+            if state_dict is None:
+                _init_block(blk, gen)
+            else:
+                pre = f"mixtures.{spec.name}.blocks.{li}."
+                blk.load_state_dict({k[len(pre):]: v for k, v in state_dict.items() if k.startswith(pre)})
             if quantize:
                 replace_linear_with_weight_only(blk, qcfg)
                 fuse_ffn_gelu(blk)

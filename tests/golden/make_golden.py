@@ -13,9 +13,16 @@ Reference functions exercised (paths inside the reference project):
   quantize_weight_rtn      src/qi/quantization/quantize.py:32-78
   dequantize_weight        src/qi/quantization/quantize.py:81-119
   quantize_to_fp8_e4m3     src/qi/quantization/backends/flashrt_fp8_ops.py:43-48
+                           (also applied to one row at a time: per-token / per-channel FP8)
+  dequantize_fp8_e4m3      src/qi/quantization/backends/flashrt_fp8_ops.py:51-53
   ReferenceBackend.linear  src/qi/quantization/backends/reference.py:48-91
   WeightOnlyLinear         src/qi/quantization/modules.py:7-133
   replace_linear_with_weight_only src/qi/quantization/swap.py:126-150
+  MoT.forward              src/qi/models/wan22/mot.py:465-574 (blocks: wan_video_dit.py:147-268)
+
+The MoT step fixture needs ``qi.models.wan22`` too: bare ``qi.utils``,
+``qi.models``, ``qi.models.wan22`` and ``qi.models.wan22.helpers`` packages
+are registered so that only the modules the step needs are imported.
 """
 
 from __future__ import annotations
@@ -38,9 +45,12 @@ from qi_b200.synthetic import CFG_INT8, CFG_W4A16, make_linear_inputs, make_smal
 
 
 def import_reference(ref_root: Path):
-    pkg = types.ModuleType("qi")
-    pkg.__path__ = [str(ref_root / "src" / "qi")]
-    sys.modules["qi"] = pkg
+    src = ref_root / "src" / "qi"
+    for name, sub in (("qi", ""), ("qi.utils", "utils"), ("qi.models", "models"), ("qi.models.wan22", "models/wan22"),
+                      ("qi.models.wan22.helpers", "models/wan22/helpers")):
+        pkg = types.ModuleType(name)
+        pkg.__path__ = [str(src / sub) if sub else str(src)]
+        sys.modules[name] = pkg
     import qi.quantization as qq  # noqa: F401
     from qi.quantization import quantize as Q
     from qi.quantization.backends import flashrt_fp8_ops as F8
@@ -148,6 +158,10 @@ def main() -> None:
                         bias=lin.bias.detach().numpy(), x=xm.numpy(), y=ym.detach().numpy(),
                         qweight=model.ffn[0].qweight.numpy(), scales=model.ffn[0].scales.numpy())
 
+    fp8_per_token(R)
+    w4a16_cfg3(R)
+    mot_step(R)
+
     # ---- hashes of the reference quantizer at the full BASELINE sizes
     _, w1, _ = make_linear_inputs(CFG_INT8)
     q1, s1, _ = R.Q.quantize_weight_rtn(w1, bits=8, group_size=-1, symmetric=True)
@@ -160,6 +174,137 @@ def main() -> None:
     out["cfg3_int4_zeros"] = sha(z3.numpy())
     (HERE / "baseline_hashes.json").write_text(json.dumps(out, indent=1) + "\n")
     print("wrote fixtures to", HERE)
+
+
+def fp8_rows(R, t: torch.Tensor):
+    """The reference's per-tensor FP8 quantizer applied to each row as a
+    one-row tensor: per-token (activations) / per-channel (weights) codes."""
+    qs, ss = zip(*(R.F8.quantize_to_fp8_e4m3(t[i:i + 1]) for i in range(t.shape[0])))
+    return torch.cat(qs, 0), torch.cat(ss, 0)
+
+
+def fp8_per_token(R) -> None:
+    """Per-token / per-channel FP8 W8A8 (BASELINE config 2's scheme) from the
+    reference's own quantizer, and the reference-style dequantise-then-matmul
+    output (reference.py:48-91's structure: dequantise both operands with
+    dequantize_fp8_e4m3, F.linear in fp32, output in the input dtype), with
+    and without the FFN's GELU(tanh) (wan_video_dit.py:244-245)."""
+    M, N, K = 33, 256, 512
+    x, w, b = make_small_case(M, N, K, seed=13, outlier_frac=0.01)
+    x = x.clone()
+    x[4] = 0  # all-zero token -> the 1e-12 scale floor
+    qx, sx = fp8_rows(R, x)
+    qw, sw = fp8_rows(R, w)
+    xd = torch.cat([R.F8.dequantize_fp8_e4m3(qx[i], sx[i]).reshape(1, -1) for i in range(M)], 0)
+    wd = torch.cat([R.F8.dequantize_fp8_e4m3(qw[i], sw[i]).reshape(1, -1) for i in range(N)], 0)
+    y = torch.nn.functional.linear(xd, wd, b.float())
+    yb = y.to(torch.bfloat16)
+    yg = torch.nn.functional.gelu(yb.float(), approximate="tanh").to(torch.bfloat16)
+    np.savez_compressed(HERE / "fp8_per_token_M33_N256_K512.npz", x=bf16_bits(x), w=w.numpy(), bias=bf16_bits(b),
+                        qx=qx.numpy(), sx=sx.numpy(), qw=qw.numpy(), sw=sw.numpy(), y_ref=bf16_bits(yb),
+                        y_ref_gelu=bf16_bits(yg))
+
+
+def w4a16_cfg3(R) -> None:
+    """ReferenceBackend.linear (bf16 input, INT4 asym g128) at BASELINE
+    config 3's full weight (3072 x 3072) for M = 1 and M = 16.  Only the
+    outputs are stored; the inputs are regenerated by qi_b200.synthetic
+    (their hashes are stored to prove it)."""
+    rec = {}
+    for m in (1, 16):
+        x, w, b = make_linear_inputs(CFG_W4A16[m])
+        q, s, z = R.Q.quantize_weight_rtn(w, bits=4, group_size=128, symmetric=False)
+        y = ref_linear(R, x, q, s, z, 4, 128, False, b, False)
+        rec[f"y_M{m}"] = bf16_bits(y)
+        rec[f"x_sha_M{m}"] = np.frombuffer(sha(bf16_bits(x)).encode(), np.uint8)
+        rec[f"q_sha_M{m}"] = np.frombuffer(sha(q.numpy()).encode(), np.uint8)
+    np.savez_compressed(HERE / "linear_w4a16_cfg3_M1_M16.npz", **rec)
+
+
+# the small MoT used for the step fixture: 2 layers, 2 heads x 32, video 3
+# frames x 8 tokens at hidden 128 / FFN 256, action 4 tokens at hidden 64 /
+# FFN 128, 8 context tokens
+MOT_SMALL = dict(layers=2, heads=2, head_dim=32, ctx=8, tokens_per_frame=8,
+                 experts=(("video", 128, 256, 24), ("action", 64, 128, 4)))
+
+
+def mot_step(R) -> None:
+    """One MoT.forward of the reference (mot.py:465-574) with every target
+    Linear swapped for the reference's INT8 W8A8 WeightOnlyLinear
+    (ReferenceBackend, per-token activations), run on the CPU in bf16 and in
+    fp32, on seeded weights and inputs.  Stores the unquantized weights, the
+    inputs (RoPE as cos/sin of the reference's complex frequencies), the
+    joint first_frame_causal mask and both outputs."""
+    from qi.models.wan22.mot import MoT
+    from qi.models.wan22.wan_video_dit import DiTBlock, precompute_freqs_cis
+
+    c = MOT_SMALL
+    g = torch.Generator().manual_seed(2024)
+
+    class Expert(torch.nn.Module):
+        def __init__(self, hidden, ffn):
+            super().__init__()
+            self.num_heads, self.attn_head_dim = c["heads"], c["head_dim"]
+            self.blocks = torch.nn.ModuleList(
+                DiTBlock(hidden, c["head_dim"], c["heads"], ffn, 1e-6) for _ in range(c["layers"]))
+
+    mot = MoT({n: Expert(h, f) for n, h, f, _ in c["experts"]}, mot_checkpoint_mixed_attn=False)
+    with torch.no_grad():   # bf16-valued master weights (stored as bf16 bits)
+        for name, p in mot.named_parameters():
+            if name.endswith("modulation"):
+                v = torch.randn(p.shape, generator=g) / p.shape[-1] ** 0.5
+            elif "norm" in name:   # RMSNorm / affine LayerNorm: near 1 (weights) and 0 (biases)
+                v = (1.0 if name.endswith("weight") else 0.0) + 0.1 * torch.randn(p.shape, generator=g)
+            elif name.endswith("weight"):   # 1/sqrt(fan_in): every sublayer changes the residual visibly
+                v = torch.randn(p.shape, generator=g) / p.shape[1] ** 0.5
+            else:
+                v = torch.randn(p.shape, generator=g) * 0.1
+            p.copy_(v.bfloat16().float())
+    state = {k: v.clone() for k, v in mot.state_dict().items()}
+    cfg = R.WAQ(enabled=True, algo="rtn", quant_dtype="int", backend="reference",
+                activation_granularity="per_token", weight_granularity="per_channel")
+    R.swap(mot, cfg)
+    n_q = sum(type(m).__name__ == "WeightOnlyLinear" for m in mot.modules())
+    assert n_q == 10 * c["layers"] * len(c["experts"]), n_q
+    mot.eval()
+
+    sv, sa = c["experts"][0][3], c["experts"][1][3]
+    t = min(c["tokens_per_frame"], sv)
+    mask = torch.zeros((sv + sa, sv + sa), dtype=torch.bool)   # fastwam.py:914-935, first_frame_causal
+    mask[:sv, :sv] = True
+    mask[:t, t:sv] = False
+    mask[sv:, sv:] = True
+    mask[sv:, :t] = True
+    fr = precompute_freqs_cis(c["head_dim"], 64)
+    tok, ctx, tmod, freqs, rope = {}, {}, {}, {}, {}
+    for name, hidden, _, n in c["experts"]:
+        # inputs are bf16 values, so the fp32 and bf16 runs see the same numbers
+        tok[name] = torch.randn(1, n, hidden, generator=g).bfloat16().float()
+        ctx[name] = torch.randn(1, c["ctx"], hidden, generator=g).bfloat16().float()
+        tmod[name] = (torch.randn(1, 6, hidden, generator=g) * 0.5).bfloat16().float()
+        off = 0 if name == "video" else 7   # action positions differ from video's
+        freqs[name] = fr[off:off + n].unsqueeze(1)
+        rope[name] = torch.stack([freqs[name].real, freqs[name].imag], -1).reshape(n, -1, 2).double()
+
+    out = {}
+    # fp32 first: casting the model to bf16 also rounds its fp32 scale buffers
+    for dt, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
+        m = mot.to(dt)
+        with torch.no_grad():
+            y = m({k: v.to(dt) for k, v in tok.items()}, mask, freqs,
+                  {k: {"context": v.to(dt), "mask": None} for k, v in ctx.items()},
+                  {k: v.to(dt) for k, v in tmod.items()})
+        for k, v in y.items():
+            out[f"y_{tag}_{k}"] = bf16_bits(v) if dt == torch.bfloat16 else v.float().numpy()
+    rec = {f"w::{k}": bf16_bits(v.bfloat16()) for k, v in state.items()}
+    for k in tok:
+        rec[f"tok_{k}"] = bf16_bits(tok[k].to(torch.bfloat16))
+        rec[f"ctx_{k}"] = bf16_bits(ctx[k].to(torch.bfloat16))
+        rec[f"tmod_{k}"] = bf16_bits(tmod[k].to(torch.bfloat16))
+        rec[f"rope_{k}"] = rope[k].float().numpy()
+    rec["mask"] = mask.numpy()
+    rec["meta"] = np.frombuffer(json.dumps(c).encode(), np.uint8)
+    np.savez_compressed(HERE / "mot_step_small_int8.npz", **rec, **out)
 
 
 if __name__ == "__main__":

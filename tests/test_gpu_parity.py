@@ -212,22 +212,96 @@ def test_fp8_per_tensor_static_matches_reference_semantics():
     assert O.rel_fro(O.bf16_to_f32(bits(y)), yref) <= 1e-1  # per-tensor fp8 vs unquantized
 
 
-def test_fp8_config2_full_size_sampled_rows():
-    """BASELINE config 2 (M=4096, N=14336, K=3072, bias + GELU) at full size;
-    the oracle is evaluated on a sample of rows (size-independent check)."""
+def test_fp8_per_token_vs_reference_fixture():
+    """Per-token / per-channel FP8 against the reference's own quantizer
+    applied row by row (tests/golden/fp8_per_token_M33_N256_K512.npz): the
+    kernel's activation codes and scales bit-exact, the module path's weight
+    codes bit-exact, and the linear (with and without the fused GELU) within
+    the north-star 1e-2 of the reference-style dequantise-then-F.linear
+    output (measured ~1e-3: fp32 summation order and scale order only)."""
+    from pathlib import Path
+
+    from qi_b200.quantization import WeightActivationQuantConfig, WeightOnlyLinear
+    from qi_b200.quantization.backends import get_backend
+    from qi_b200.quantization.quantize import quantize_linear_weight
+
+    f = dict(np.load(Path(__file__).resolve().parent / "golden" / "fp8_per_token_M33_N256_K512.npz"))
+    xb = torch.from_numpy(f["x"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    bb = torch.from_numpy(f["bias"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    q, s = K.quantize_fp8_rowwise(xb)
+    np.testing.assert_array_equal(u8(q), f["qx"])
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), f["sx"].view(np.uint32))
+    qw, sw = torch.from_numpy(f["qw"]).to(DEV), torch.from_numpy(f["sw"]).to(DEV)
+    for gelu, key in ((False, "y_ref"), (True, "y_ref_gelu")):
+        y = K.fp8_linear(xb, qw, sw, None, bb, gelu=gelu)
+        e = O.rel_fro(y.float().cpu().numpy(), O.bf16_to_f32(f[key]))
+        assert e <= 1e-2, (key, e)
+    cfg = WeightActivationQuantConfig(enabled=True, quant_dtype="fp8", backend="b200",
+                                      activation_granularity="per_token", weight_granularity="per_channel")
+    lin = torch.nn.Linear(f["w"].shape[1], f["w"].shape[0])
+    with torch.no_grad():
+        lin.weight.copy_(torch.from_numpy(f["w"]))
+        lin.bias.copy_(bb.float().cpu())
+    layer = WeightOnlyLinear.from_linear(lin, quantize_linear_weight(lin.weight.detach(), cfg), cfg,
+                                         get_backend("b200")).to(DEV)
+    layer.bias = bb
+    np.testing.assert_array_equal(u8(layer.weight_fp8), f["qw"])
+    e = O.rel_fro(layer(xb).float().cpu().numpy(), O.bf16_to_f32(f["y_ref"]))
+    assert e <= 1e-2, e
+
+
+def _decode_e4m3(codes: torch.Tensor) -> torch.Tensor:
+    """E4M3 codes (uint8, on the GPU) -> exact fp64 values."""
+    return codes.view(torch.float8_e4m3fn).to(torch.float32).to(torch.float64)
+
+
+def test_fp8_config2_full_size_all_rows():
+    """BASELINE config 2 (M=4096, N=14336, K=3072, bias + GELU) at full size,
+    every one of the 4096 x 14336 outputs checked.
+
+    * activation codes and per-token scales: bit-exact against the oracle on
+      all rows (the oracle's per-row quantizer is pinned to the reference's
+      quantize_to_fp8_e4m3 applied row by row, tests/test_oracle.py);
+    * raw fp32 accumulators: within 1e-5 (relative to the largest) of the
+      exact sum.  The checker is a test-only fp64 GEMM on the GPU of the
+      decoded codes: E4M3 x E4M3 products are exact and 3072 of them sum
+      exactly in 53 bits;
+    * bf16 output: rel-Frobenius <= 2e-3 against the fused epilogue applied to
+      the exact sum, and <= 1e-2 against the
+      reference-style dequantise-then-matmul path (both operands dequantised,
+      product + bias, bf16, GELU), before and after GELU.
+    """
     x, w, b = make_linear_inputs(CFG_FP8)
     qw, sw = O.quantize_fp8_rowwise(w.numpy())
-    y = K.fp8_linear(x.to(DEV), torch.from_numpy(qw).to(DEV), torch.from_numpy(sw).to(DEV), None,
-                     b.to(DEV), gelu=True)
-    rows = np.r_[0:64, 2000:2032, 4064:4096]
-    xs = bits(x)[rows]
-    qa, sa = O.quantize_fp8_rowwise(O.bf16_to_f32(xs))
-    yo = O.fp8_linear(qa, sa, qw, sw, bits(b), gelu=True)
-    e = O.rel_fro(O.bf16_to_f32(bits(y)[rows]), O.bf16_to_f32(yo))
-    assert e <= 2e-3, e
-    # vs the unquantized bf16 linear (reference semantics of the model): <= 1e-2 is not
-    # guaranteed for fp8 of raw N(0,1) data after GELU; report the pre-GELU bound instead
-    assert np.isfinite(O.bf16_to_f32(bits(y))).all()
+    xd, bd = x.to(DEV), b.to(DEV)
+    qwd, swd = torch.from_numpy(qw).to(DEV), torch.from_numpy(sw).to(DEV)
+    qa, sa = K.quantize_fp8_rowwise(xd)
+    qo, so = O.quantize_fp8_rowwise(O.bf16_to_f32(bits(x)))
+    np.testing.assert_array_equal(sa.cpu().numpy().view(np.uint32), so.view(np.uint32))
+    np.testing.assert_array_equal(u8(qa), qo)
+    del qo
+    exact = _decode_e4m3(qa) @ _decode_e4m3(qwd).T                      # [4096, 14336] fp64, exact
+    acc = K.gemm(_lib.KIND_FP8_E4M3, qa, qwd, None, None, raw_acc=True)
+    e_acc = ((acc.double() - exact).abs().max() / exact.abs().max()).item()
+    assert e_acc <= 1e-5, e_acc
+    del acc
+    y = K.fp8_linear(xd, qwd, swd, None, bd, gelu=True)
+    lin = K.gemm(_lib.KIND_FP8_E4M3, qa, qwd, sa, swd, bd)             # the same without GELU
+    # the kernel's epilogue order on the exact sum: ((acc * s_tok) * s_ch) + bias -> bf16 -> GELU -> bf16
+    t = (exact.float() * sa[:, None]) * swd[None, :] + bd.float()[None, :]
+    y_epi = torch.nn.functional.gelu(t.bfloat16().float(), approximate="tanh").bfloat16()
+    e_epi = O.rel_fro(y.float().cpu().numpy(), y_epi.float().cpu().numpy())
+    assert e_epi <= 2e-3, e_epi
+    # reference-style: dequantise both operands, matmul, + bias (fp64), bf16, GELU
+    ref = (_decode_e4m3(qa) * sa.double()[:, None]) @ (_decode_e4m3(qwd) * swd.double()[:, None]).T
+    ref_lin = (ref + bd.double()[None, :]).bfloat16()
+    ref_gelu = torch.nn.functional.gelu(ref_lin.float(), approximate="tanh").bfloat16()
+    e_lin = O.rel_fro(lin.float().cpu().numpy(), ref_lin.float().cpu().numpy())
+    e_gelu = O.rel_fro(y.float().cpu().numpy(), ref_gelu.float().cpu().numpy())
+    print(f"cfg2 all rows: acc {e_acc:.2e}, vs epilogue(exact) {e_epi:.2e}, vs dequantise-then-matmul "
+          f"{e_lin:.2e} (pre-GELU) / {e_gelu:.2e} (GELU)")
+    assert e_lin <= 1e-2 and e_gelu <= 1e-2, (e_lin, e_gelu)
+    assert _lib.device_status()[0] == 0
 
 
 # --------------------------------------------------------------------------

@@ -177,3 +177,24 @@ def test_w4a16_fused_kernels_large_m(M):
     if M >= _lib.W4A16_DEQUANT_MIN_M:
         assert _lib.last_launch()["kernel"] in ("gemm_bf16", "gemm_bf16_pair")
     assert O.rel_fro(O.bf16_to_f32(bits(y2)), O.bf16_to_f32(yo)) <= 2e-3
+
+
+@pytest.mark.parametrize("M", [1, 16])
+def test_w4a16_config3_vs_reference_fixture(M):
+    """BASELINE config 3 (W [3072, 3072], asym g128) at M = 1 and M = 16
+    against the reference's own ReferenceBackend.linear output on the same
+    inputs (tests/golden/linear_w4a16_cfg3_M1_M16.npz), through the small-M
+    kernel, within the north-star INT4 bound of 5e-3.  That kernel applies
+    each group scale to fp32 partial sums instead of rounding every weight to
+    bf16 first, so this bound is its stated margin at the config's shapes."""
+    from pathlib import Path
+
+    f = np.load(Path(__file__).resolve().parent / "golden" / "linear_w4a16_cfg3_M1_M16.npz")
+    x, w, b = make_linear_inputs(CFG_W4A16[M])
+    qp, s16, zp = packed(w.numpy(), 128)
+    qp_d, zp_d = dev(qp, zp)
+    y = K.w4a16_linear(x.to(DEV), qp_d, torch.from_numpy(s16).to(DEV), zp_d, 128, b.to(DEV))
+    assert _lib.last_launch()["kernel"] == "w4a16_small"
+    e = O.rel_fro(O.bf16_to_f32(bits(y)), O.bf16_to_f32(f[f"y_M{M}"]))
+    print(f"cfg3 M={M}: small-M kernel vs ReferenceBackend {e:.2e} (bound 5e-3)")
+    assert e <= 5e-3, e

@@ -43,6 +43,50 @@ def test_fp8_per_tensor_bit_exact():
     np.testing.assert_array_equal(q, f["q"])
 
 
+def test_fp8_per_token_pinned_to_reference_rows():
+    """Per-token (activations) and per-channel (weights) FP8: the oracle's
+    per-row quantizer against the reference's quantize_to_fp8_e4m3 applied
+    to each row as a one-row tensor (codes and scales bit-exact, including an
+    all-zero token), and the oracle's FP8 linear against the reference-style
+    dequantise-then-F.linear output (<= 2e-3: only the fp32 summation order
+    and the scale order differ), with and without GELU."""
+    f = load("fp8_per_token_M33_N256_K512")
+    qx, sx = O.quantize_fp8_rowwise(O.bf16_to_f32(f["x"]))
+    np.testing.assert_array_equal(qx, f["qx"])
+    np.testing.assert_array_equal(sx.view(np.uint32), f["sx"].view(np.uint32))
+    qw, sw = O.quantize_fp8_rowwise(f["w"])
+    np.testing.assert_array_equal(qw, f["qw"])
+    np.testing.assert_array_equal(sw.view(np.uint32), f["sw"].view(np.uint32))
+    for gelu, key in ((False, "y_ref"), (True, "y_ref_gelu")):
+        y = O.fp8_linear(qx, sx, qw, sw, f["bias"], gelu=gelu)
+        e = O.rel_fro(O.bf16_to_f32(y), O.bf16_to_f32(f[key]))
+        assert e <= 2e-3, (key, e)
+
+
+def test_torch_fp8_rowwise_quantizer_matches_reference_rows():
+    """The product's offline per-channel FP8 weight quantizer
+    (qi_b200.quantization.quantize) gives the reference's per-row codes."""
+    from qi_b200.quantization.quantize import quantize_to_fp8_e4m3_rowwise
+
+    f = load("fp8_per_token_M33_N256_K512")
+    q, s = quantize_to_fp8_e4m3_rowwise(torch.from_numpy(f["w"]))
+    np.testing.assert_array_equal(q.numpy(), f["qw"])
+    np.testing.assert_array_equal(s.numpy().reshape(-1).view(np.uint32), f["sw"].reshape(-1).view(np.uint32))
+
+
+def test_w4a16_cfg3_fixture_inputs_regenerate():
+    """The config-3 W4A16 fixture (reference outputs at M = 1 and 16 over the
+    full 3072 x 3072 weight) was made from exactly the inputs and quantized
+    weights that qi_b200.synthetic and the oracle reproduce here."""
+    f = load("linear_w4a16_cfg3_M1_M16")
+    for m in (1, 16):
+        x, w, _ = make_linear_inputs(CFG_W4A16[m])
+        xb = x.contiguous().view(torch.int16).numpy().view(np.uint16)
+        assert hashlib.sha256(xb.tobytes()).hexdigest() == bytes(f[f"x_sha_M{m}"]).decode()
+        q, _, _ = O.quantize_weight_rtn(w.numpy(), 4, 128, False)
+        assert hashlib.sha256(np.ascontiguousarray(q).tobytes()).hexdigest() == bytes(f[f"q_sha_M{m}"]).decode()
+
+
 @pytest.mark.parametrize("name", ["linear_int8_M17_N192_K256", "linear_int8_M1_N64_K128"])
 def test_int8_linear_vs_reference_backend(name):
     """K1+K2 semantics (exact int32 accumulators) vs the reference's own
