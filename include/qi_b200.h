@@ -204,10 +204,28 @@ int qi_b200_resid_ln_quant(void* x_bf16, const void* y_bf16, long long ldy, cons
  *   out = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w)            (RMSNorm over all A)
  *   then, with rope ([M, head_dim/2, 2] fp32 cos/sin per token), rotate each
  *   (even, odd) pair of every head: (e c - o s, e s + o c) in fp32.
- * A % 8 == 0, A <= 4096, head_dim % 8 == 0. */
+ * A % 8 == 0, A <= 4096, head_dim % 8 == 0.  With head_dim a power of two
+ * in [8, 256] dividing A, mean(x^2) is the sum of per-head sums of squares
+ * taken in head order, the same bits however the heads are split over GPUs
+ * (qi_b200_rms_head_partials / qi_b200_rms_rope_partials). */
 int qi_b200_rms_rope(const void* in0, const void* in1, long long ld_in, void* out0, void* out1, long long ld_out,
                      const void* w0, const void* w1, const float* rope, int head_dim, int nparts, int M, int A,
                      float eps, cudaStream_t stream);
+
+/* Head-parallel RMSNorm (no counterpart in the reference, which runs the
+ * q/k RMSNorm of wan_video_dit.py:147-158 over all heads on one GPU).  A rank
+ * holding a contiguous range of whole heads (A = its columns) writes its
+ * per-head sums of squares, partials[nparts][M][A / head_dim] fp32; the ranks
+ * all-gather them (rank-major: [ranks][nparts][M][A / head_dim], i.e. head
+ * order); qi_b200_rms_rope_partials then normalizes this rank's columns over
+ * all ranks * A columns.  The outputs are bit-identical to qi_b200_rms_rope
+ * on the unsplit row.  head_dim a power of two in [8, 256] dividing A. */
+int qi_b200_rms_head_partials(const void* in0, const void* in1, long long ld_in, float* partials, int head_dim,
+                              int nparts, int M, int A, cudaStream_t stream);
+int qi_b200_rms_rope_partials(const void* in0, const void* in1, long long ld_in, void* out0, void* out1,
+                              long long ld_out, const void* w0, const void* w1, const float* rope, int head_dim,
+                              int nparts, int M, int A, const float* partials, int ranks, float eps,
+                              cudaStream_t stream);
 
 /* Per-token FP8: s = max(amax/448, 1e-12), q = e4m3_rn(clamp(x/s, +-448)).
  * Generalises backends/flashrt_fp8_ops.py:38-48 (per tensor) to per row. */

@@ -293,6 +293,15 @@ struct RmsRopeParams {
   int pairs_per_head;          // head_dim / 2
   int M, A;
   float eps;
+  // per-head reduction (k_rms_rope_heads): head width, and for rows whose
+  // heads are split over ranks the per-head partial sums of squares:
+  // part_out [nparts][M][A / head_dim] written by this rank; part_in
+  // [ranks][nparts][M][A / head_dim] from every rank (rank-major = head
+  // order), normalizing over A_total = ranks * A columns
+  int head_dim;
+  float* part_out;
+  const float* part_in;
+  int ranks;
 };
 
 // One row of one part per CTA.  RMSNorm: bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w)
@@ -562,6 +571,124 @@ __global__ void __launch_bounds__(kWarpRowThreads) k_rms_rope_warp(RmsRopeParams
       v[2 * e] = v2[e].x;
       v[2 * e + 1] = v2[e].y;
     }
+    if (p.rope != nullptr) {
+      const int pair0 = (j * 4) % p.pairs_per_head;
+      const float4* tab = reinterpret_cast<const float4*>(
+          p.rope + (static_cast<long long>(row) * p.pairs_per_head + pair0) * 2);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float4 cs = rope_fixed ? cs_fixed[i] : tab[i];
+        const float e0 = v[4 * i], o0 = v[4 * i + 1], e1 = v[4 * i + 2], o1 = v[4 * i + 3];
+        v[4 * i] = __fsub_rn(__fmul_rn(e0, cs.x), __fmul_rn(o0, cs.y));
+        v[4 * i + 1] = __fadd_rn(__fmul_rn(e0, cs.y), __fmul_rn(o0, cs.x));
+        v[4 * i + 2] = __fsub_rn(__fmul_rn(e1, cs.z), __fmul_rn(o1, cs.w));
+        v[4 * i + 3] = __fadd_rn(__fmul_rn(e1, cs.w), __fmul_rn(o1, cs.z));
+      }
+    }
+    orow[j] = pack8(v);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm (+ RoPE) with a reduction that does not depend on how the heads
+// are split over ranks.  Every head's sum of squares is formed the same way
+// (each lane adds the squares of its 8 consecutive elements in order, then a
+// butterfly over the head_dim/8 lanes of the head), and the row total is the
+// sum of the per-head sums in head order.  A rank that holds a contiguous
+// range of whole heads computes those heads' sums bit for bit as one GPU
+// does; with every rank's sums gathered (part_in), its total and hence its
+// normalized outputs are bit-identical to the single-GPU kernel's.
+//   MODE 0: whole row on this GPU: per-head sums, total, normalize, RoPE.
+//   MODE 1: per-head sums only, written to part_out.
+//   MODE 2: total from part_in (every rank's sums), normalize, RoPE.
+// Warp per row, C = ceil(A / 256) 16-byte chunks per lane (chunk c of lane l
+// = elements (32 c + l) * 8 ..+7); head_dim in {8, 16, 32, 64, 128, 256}.
+// ---------------------------------------------------------------------------
+template <int C, int MODE>
+__global__ void __launch_bounds__(kWarpRowThreads) k_rms_rope_heads(RmsRopeParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
+  extern __shared__ __align__(16) uint4 wsm[];  // [A / 8] RMSNorm weight of this part (MODE != 1)
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (kWarpRowThreads / 32) + (threadIdx.x >> 5);
+  const int part = blockIdx.y;
+  const int nvec = p.A >> 3;
+  if (MODE != 1) {
+    const uint4* wsrc = reinterpret_cast<const uint4*>(part ? p.w[1] : p.w[0]);
+    for (int i = threadIdx.x; i < nvec; i += kWarpRowThreads) wsm[i] = __ldg(wsrc + i);
+  }
+  uint4 u[C];
+  if (row < p.M) {
+    const uint4* ir = reinterpret_cast<const uint4*>((part ? p.in[1] : p.in[0]) + static_cast<long long>(row) * p.ld_in);
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+      if (c * 32 + lane < nvec) u[c] = ir[c * 32 + lane];
+  }
+  if (MODE != 1) __syncthreads();
+  if (row >= p.M) return;
+  const int lph = p.head_dim >> 3;        // lanes per head
+  const int hpc = 32 / lph;               // heads per chunk
+  const int heads = p.A / p.head_dim;     // heads on this GPU
+  float hs[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    float s = 0.f;
+    if (c * 32 + lane < nvec) {
+      float v[8];
+      unpack8(u[c], v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s = fmaf(v[e], v[e], s);
+    }
+    for (int o = lph >> 1; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    hs[c] = s;
+  }
+  if (MODE == 1) {
+    float* dst = p.part_out + (static_cast<long long>(part) * p.M + row) * heads;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int h = c * hpc + lane / lph;
+      if (lane % lph == 0 && h < heads) dst[h] = hs[c];
+    }
+    return;
+  }
+  float tot = 0.f;
+  if (MODE == 0) {
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+      for (int g = 0; g < hpc; ++g) {
+        const float hv = __shfl_sync(0xffffffffu, hs[c], g * lph);
+        if (c * hpc + g < heads) tot += hv;
+      }
+  } else {
+    const int nparts = gridDim.y;
+    for (int r = 0; r < p.ranks; ++r) {
+      const float* src = p.part_in + ((static_cast<long long>(r) * nparts + part) * p.M + row) * heads;
+      for (int h = 0; h < heads; ++h) tot += __ldg(src + h);
+    }
+  }
+  const float rr = rsqrtf(tot / static_cast<float>(p.A * (MODE == 2 ? p.ranks : 1)) + p.eps);
+  uint4* orow = reinterpret_cast<uint4*>((part ? p.out[1] : p.out[0]) + static_cast<long long>(row) * p.ld_out);
+  const bool rope_fixed = p.rope != nullptr && (128 % p.pairs_per_head) == 0;
+  float4 cs_fixed[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  if (rope_fixed) {
+    const float4* tab = reinterpret_cast<const float4*>(
+        p.rope + (static_cast<long long>(row) * p.pairs_per_head + (lane * 4) % p.pairs_per_head) * 2);
+    cs_fixed[0] = tab[0];
+    cs_fixed[1] = tab[1];
+  }
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int j = c * 32 + lane;
+    if (j >= nvec) continue;
+    float v[8], w[8];
+    unpack8(u[c], v);
+    unpack8(wsm[j], w);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], rr);
+    round8(v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], w[e]);
+    round8(v);
     if (p.rope != nullptr) {
       const int pair0 = (j * 4) % p.pairs_per_head;
       const float4* tab = reinterpret_cast<const float4*>(

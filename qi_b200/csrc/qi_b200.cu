@@ -1068,9 +1068,115 @@ int qi_b200_resid_ln_quant(void* x_bf16, const void* y_bf16, long long ldy, cons
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
 
+}  // extern "C"
+
+namespace qib {
+
+// k_rms_rope_heads<C, MODE> for C = ceil(A / 256) chunks per lane (A <= 4096).
+template <int MODE>
+static cudaError_t launch_rms_heads(const RmsRopeParams& p, int nparts, cudaStream_t stream) {
+  const dim3 grid((p.M + kWarpRowThreads / 32 - 1) / (kWarpRowThreads / 32), nparts);
+  const size_t smem = MODE == 1 ? 0 : static_cast<size_t>(p.A) * 2;
+  switch ((p.A + 255) / 256) {
+#define QI_RMS_HEADS_CASE(c) \
+  case c: return launch_pdl(k_rms_rope_heads<c, MODE>, grid, dim3(kWarpRowThreads), smem, stream, 1, p);
+    QI_RMS_HEADS_CASE(1) QI_RMS_HEADS_CASE(2) QI_RMS_HEADS_CASE(3) QI_RMS_HEADS_CASE(4)
+    QI_RMS_HEADS_CASE(5) QI_RMS_HEADS_CASE(6) QI_RMS_HEADS_CASE(7) QI_RMS_HEADS_CASE(8)
+    QI_RMS_HEADS_CASE(9) QI_RMS_HEADS_CASE(10) QI_RMS_HEADS_CASE(11) QI_RMS_HEADS_CASE(12)
+    QI_RMS_HEADS_CASE(13) QI_RMS_HEADS_CASE(14) QI_RMS_HEADS_CASE(15) QI_RMS_HEADS_CASE(16)
+#undef QI_RMS_HEADS_CASE
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+static bool rms_heads_ok(int A, int head_dim) {
+  return head_dim >= 8 && head_dim <= 256 && (head_dim & (head_dim - 1)) == 0 && A % head_dim == 0 && A <= 4096;
+}
+
+// Shared argument checks and parameter block of the RMSNorm entry points.
+static int rms_params(RmsRopeParams* p, const void* in0, const void* in1, long long ld_in, void* out0, void* out1,
+                      long long ld_out, const void* w0, const void* w1, const float* rope, int head_dim, int nparts,
+                      int M, int A, float eps, bool need_out) {
+  if (M < 0 || A <= 0 || nparts < 1 || nparts > 2) return QI_B200_ESHAPE;
+  if (A % 8 != 0 || A > kRowMaxThreads * 8 || ld_in < A || ld_in % 8) return QI_B200_ESHAPE;
+  if (need_out && (ld_out < A || ld_out % 8)) return QI_B200_ESHAPE;
+  if (rope != nullptr && (head_dim <= 0 || head_dim % 8 != 0 || A % head_dim != 0)) return QI_B200_ESHAPE;
+  const void* ins[2] = {in0, in1};
+  void* outs[2] = {out0, out1};
+  const void* ws[2] = {w0, w1};
+  for (int i = 0; i < nparts; ++i) {
+    if (ins[i] == nullptr || (need_out && (outs[i] == nullptr || ws[i] == nullptr))) return QI_B200_EINVAL;
+    if (!aligned16(ins[i]) || (need_out && (!aligned16(outs[i]) || !aligned16(ws[i])))) return QI_B200_EALIGN;
+  }
+  if (rope != nullptr && !aligned16(rope)) return QI_B200_EALIGN;
+  for (int i = 0; i < 2; ++i) {
+    const int k = i < nparts ? i : 0;
+    p->in[i] = static_cast<const __nv_bfloat16*>(ins[k]);
+    p->out[i] = static_cast<__nv_bfloat16*>(outs[k]);
+    p->w[i] = static_cast<const __nv_bfloat16*>(ws[k]);
+  }
+  p->ld_in = ld_in;
+  p->ld_out = ld_out;
+  p->rope = rope;
+  p->pairs_per_head = rope != nullptr ? head_dim / 2 : 1;
+  p->M = M;
+  p->A = A;
+  p->eps = eps;
+  p->head_dim = head_dim;
+  p->part_out = nullptr;
+  p->part_in = nullptr;
+  p->ranks = 1;
+  return QI_B200_OK;
+}
+
+}  // namespace qib
+
+extern "C" {
+
+int qi_b200_rms_head_partials(const void* in0, const void* in1, long long ld_in, float* partials, int head_dim,
+                              int nparts, int M, int A, cudaStream_t stream) {
+  RmsRopeParams p;
+  int rc = rms_params(&p, in0, in1, ld_in, nullptr, nullptr, 0, nullptr, nullptr, nullptr, head_dim, nparts, M, A,
+                      0.f, false);
+  if (rc) return rc;
+  if (!rms_heads_ok(A, head_dim)) return QI_B200_ESHAPE;
+  if (partials == nullptr) return QI_B200_EINVAL;
+  if (M == 0) return QI_B200_OK;
+  p.part_out = partials;
+  const cudaError_t e = launch_rms_heads<1>(p, nparts, stream);
+  count_launches(1);
+  return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+int qi_b200_rms_rope_partials(const void* in0, const void* in1, long long ld_in, void* out0, void* out1,
+                              long long ld_out, const void* w0, const void* w1, const float* rope, int head_dim,
+                              int nparts, int M, int A, const float* partials, int ranks, float eps,
+                              cudaStream_t stream) {
+  RmsRopeParams p;
+  int rc = rms_params(&p, in0, in1, ld_in, out0, out1, ld_out, w0, w1, rope, head_dim, nparts, M, A, eps, true);
+  if (rc) return rc;
+  if (!rms_heads_ok(A, head_dim)) return QI_B200_ESHAPE;
+  if (partials == nullptr || ranks < 1 || ranks > kMaxPeers) return QI_B200_EINVAL;
+  if (M == 0) return QI_B200_OK;
+  p.part_in = partials;
+  p.ranks = ranks;
+  const cudaError_t e = launch_rms_heads<2>(p, nparts, stream);
+  count_launches(1);
+  return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
 int qi_b200_rms_rope(const void* in0, const void* in1, long long ld_in, void* out0, void* out1, long long ld_out,
                      const void* w0, const void* w1, const float* rope, int head_dim, int nparts, int M, int A,
                      float eps, cudaStream_t stream) {
+  if (rms_heads_ok(A, head_dim)) {  // the head-order reduction (same bits however the heads are split)
+    RmsRopeParams p;
+    int rc = rms_params(&p, in0, in1, ld_in, out0, out1, ld_out, w0, w1, rope, head_dim, nparts, M, A, eps, true);
+    if (rc) return rc;
+    if (M == 0) return QI_B200_OK;
+    const cudaError_t e = launch_rms_heads<0>(p, nparts, stream);
+    count_launches(1);
+    return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+  }
   if (M < 0 || A <= 0 || nparts < 1 || nparts > 2) return QI_B200_ESHAPE;
   if (M == 0) return QI_B200_OK;
   if (A % 8 != 0 || A > kRowMaxThreads * 8 || ld_in < A || ld_out < A || ld_in % 8 || ld_out % 8)

@@ -16,9 +16,11 @@
 #pragma once
 
 #include "launch_count.cuh"
+#include "sm100_ptx.cuh"
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <cstdint>
 
 namespace qib {
@@ -236,6 +238,183 @@ k_rowquant_scalar(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, 
   for (int j = lane; j < cols; j += 32) qr[j] = Op::q1(xv(j), s, aux);
 }
 
+// ---------------------------------------------------------------------------
+// Persistent row quantizer fed by bulk copies (cp.async.bulk, one destination
+// CTA).  The register kernels above hold a row in registers between the amax
+// and the quantization pass; at 90+ registers a thread that caps an SM at 16
+// warps, and each CTA's loads are in flight only at its start, so HBM sits at
+// about 20 % (ncu, 4096 x 3072 FP8).  Here a CTA of 128 threads keeps a ring
+// of `stages` whole rows in shared memory: thread 0 keeps the next rows'
+// copies in flight while all threads reduce and quantize the current one out
+// of shared memory, so every SM always has several rows of loads outstanding
+// and a thread needs few registers.  Rows r = blockIdx.x + i * gridDim.x.
+// Requires cols % 8 == 0 and 16-byte aligned rows; the same per-element
+// arithmetic as k_rowquant_vec (bit-identical codes and scales).
+// ---------------------------------------------------------------------------
+constexpr int kBulkQuantThreads = 128;
+constexpr unsigned int kTagRowQuant = 0x500u;
+
+__host__ __device__ constexpr int bulk_row_stride(int cols) { return (cols * 2 + 127) & ~127; }
+
+template <class Op>
+__global__ void __launch_bounds__(kBulkQuantThreads)
+k_rowquant_bulk(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, float* __restrict__ scales,
+                const float* __restrict__ static_scale, int rows, int cols, const float* __restrict__ col_div,
+                int stages) {
+  extern __shared__ __align__(128) uint8_t qsm[];
+  const int stride = bulk_row_stride(cols);
+  uint64_t* full = reinterpret_cast<uint64_t*>(qsm + static_cast<size_t>(stages) * stride);
+  float* red = reinterpret_cast<float*>(full + stages);   // [kBulkQuantThreads / 32]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(red + kBulkQuantThreads / 32);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t row_bytes = static_cast<uint32_t>(cols) * 2u;
+  const int nvec = cols >> 3;
+  if (tid == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  griddep_wait();
+  griddep_launch_dependents();
+  const int my_rows = rows > static_cast<int>(blockIdx.x) ? (rows - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
+  auto issue = [&](int i) {  // row i of this CTA into stage i % stages
+    uint64_t* bar = &full[i % stages];
+    mbar_expect_tx(bar, row_bytes);
+    bulk_load(qsm + static_cast<size_t>(i % stages) * stride,
+              x + (static_cast<long long>(blockIdx.x) + static_cast<long long>(i) * gridDim.x) * cols, row_bytes, bar);
+  };
+  if (tid == 0)
+    for (int i = 0; i < stages && i < my_rows; ++i) issue(i);
+  int i = 0;
+  for (; i < my_rows; ++i) {
+    const int st = i % stages;
+    const bool ok = mbar_wait(&full[st], static_cast<uint32_t>(i / stages) & 1u, abort_flag, kTagRowQuant, 1);
+    if (!__syncthreads_and(ok)) break;
+    const long long row = static_cast<long long>(blockIdx.x) + static_cast<long long>(i) * gridDim.x;
+    const uint4* rb = reinterpret_cast<const uint4*>(qsm + static_cast<size_t>(st) * stride);
+    float s;
+    if (Op::kNeedsAmax) {
+      float amax = 0.f;
+      for (int j = tid; j < nvec; j += kBulkQuantThreads) {
+        uint4 v = rb[j];
+        if (col_div != nullptr) v = smooth_bf16x8(v, col_div + j * 8);
+        amax = fmaxf(amax, absmax_bf16x8(v));
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+      if (lane == 0) red[warp] = amax;
+      __syncthreads();
+      amax = red[0];
+#pragma unroll
+      for (int w = 1; w < kBulkQuantThreads / 32; ++w) amax = fmaxf(amax, red[w]);
+      s = Op::scale_from_amax(amax);
+      if (tid == 0 && scales != nullptr) scales[row] = s;
+    } else {
+      s = static_scale != nullptr ? __ldg(static_scale) : __ldg(scales + row);
+    }
+    const float aux = Op::aux(s);
+    uint2* qr = reinterpret_cast<uint2*>(q + row * cols);
+    for (int j = tid; j < nvec; j += kBulkQuantThreads) {
+      uint4 v = rb[j];
+      if (col_div != nullptr) v = smooth_bf16x8(v, col_div + j * 8);
+      qr[j] = quant_bf16x8<Op>(v, s, aux);
+    }
+    __syncthreads();  // every thread is done with this stage (and with red[])
+    if (tid == 0 && i + stages < my_rows) {
+      fence_async_shared();  // the threads' reads of the stage precede the copy that overwrites it
+      issue(i + stages);
+    }
+  }
+  if (i < my_rows && tid == 0) {
+    // aborted: let the copies still in flight land before the CTA exits
+    for (int k = i; k < my_rows && k < i + stages; ++k)
+      mbar_wait_drain(&full[k % stages], static_cast<uint32_t>(k / stages) & 1u);
+  }
+}
+
+// Warp-per-row form of k_rowquant_bulk for short rows (a row of up to 8 KB):
+// each warp owns a ring of `stages` row buffers and its own mbarriers, lane 0
+// keeps the warp's next rows in flight, and the whole row is reduced and
+// quantized by the warp with shuffles only (no block barrier per row).  Rows
+// r = gwarp + i * total_warps.
+constexpr int kBulkWarpRowThreads = 128;
+
+template <class Op>
+__global__ void __launch_bounds__(kBulkWarpRowThreads)
+k_rowquant_bulk_warp(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, float* __restrict__ scales,
+                     const float* __restrict__ static_scale, int rows, int cols, const float* __restrict__ col_div,
+                     int stages) {
+  extern __shared__ __align__(128) uint8_t qsm[];
+  constexpr int kWarps = kBulkWarpRowThreads / 32;
+  const int stride = bulk_row_stride(cols);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint8_t* ring = qsm + static_cast<size_t>(warp) * stages * stride;
+  uint64_t* full = reinterpret_cast<uint64_t*>(qsm + static_cast<size_t>(kWarps) * stages * stride) + warp * stages;
+  volatile int* abort_flag =
+      reinterpret_cast<volatile int*>(reinterpret_cast<uint64_t*>(qsm + static_cast<size_t>(kWarps) * stages * stride) +
+                                      kWarps * stages) + warp;
+  const uint32_t row_bytes = static_cast<uint32_t>(cols) * 2u;
+  const int nvec = cols >> 3;
+  if (lane == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncwarp();
+  griddep_wait();
+  griddep_launch_dependents();
+  const long long nw = static_cast<long long>(gridDim.x) * kWarps;
+  const long long gw = static_cast<long long>(blockIdx.x) * kWarps + warp;
+  const int my_rows = rows > gw ? static_cast<int>((rows - 1 - gw) / nw) + 1 : 0;
+  auto issue = [&](int i) {
+    uint64_t* bar = &full[i % stages];
+    mbar_expect_tx(bar, row_bytes);
+    bulk_load(ring + static_cast<size_t>(i % stages) * stride, x + (gw + static_cast<long long>(i) * nw) * cols,
+              row_bytes, bar);
+  };
+  if (lane == 0)
+    for (int i = 0; i < stages && i < my_rows; ++i) issue(i);
+  int i = 0;
+  for (; i < my_rows; ++i) {
+    const int st = i % stages;
+    const bool ok = mbar_wait(&full[st], static_cast<uint32_t>(i / stages) & 1u, abort_flag, kTagRowQuant, 2);
+    if (!__all_sync(0xffffffffu, ok)) break;
+    const long long row = gw + static_cast<long long>(i) * nw;
+    const uint4* rb = reinterpret_cast<const uint4*>(ring + static_cast<size_t>(st) * stride);
+    float s;
+    if (Op::kNeedsAmax) {
+      float amax = 0.f;
+      for (int j = lane; j < nvec; j += 32) {
+        uint4 v = rb[j];
+        if (col_div != nullptr) v = smooth_bf16x8(v, col_div + j * 8);
+        amax = fmaxf(amax, absmax_bf16x8(v));
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+      s = Op::scale_from_amax(amax);
+      if (lane == 0 && scales != nullptr) scales[row] = s;
+    } else {
+      s = static_scale != nullptr ? __ldg(static_scale) : __ldg(scales + row);
+    }
+    const float aux = Op::aux(s);
+    uint2* qr = reinterpret_cast<uint2*>(q + row * cols);
+    for (int j = lane; j < nvec; j += 32) {
+      uint4 v = rb[j];
+      if (col_div != nullptr) v = smooth_bf16x8(v, col_div + j * 8);
+      qr[j] = quant_bf16x8<Op>(v, s, aux);
+    }
+    __syncwarp();  // the warp is done with this stage
+    if (lane == 0 && i + stages < my_rows) {
+      fence_async_shared();
+      issue(i + stages);
+    }
+  }
+  if (i < my_rows && lane == 0)
+    for (int k = i; k < my_rows && k < i + stages; ++k)
+      mbar_wait_drain(&full[k % stages], static_cast<uint32_t>(k / stages) & 1u);
+}
+
 template <class Op>
 inline cudaError_t launch_rowquant(const void* x, void* q, float* scales, const float* static_scale, int rows,
                                    int cols, cudaStream_t stream, const float* col_div = nullptr) {
@@ -247,6 +426,33 @@ inline cudaError_t launch_rowquant(const void* x, void* q, float* scales, const 
                        (col_div == nullptr || reinterpret_cast<uintptr_t>(col_div) % 16 == 0);
   const int nvec = cols / 8;
   const dim3 blk(kQuantThreads);
+  // many rows: the persistent bulk-copy kernels (whole rows in flight per
+  // warp for short rows, per CTA for long ones)
+  if (aligned && Op::kStoreQ && rows >= 256 && bulk_row_stride(cols) <= 48 * 1024 &&
+      reinterpret_cast<uintptr_t>(x) % 16 == 0) {
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int stride = bulk_row_stride(cols);
+    const bool per_warp = stride <= 8 * 1024;
+    const int threads = per_warp ? kBulkWarpRowThreads : kBulkQuantThreads;
+    const int rings = per_warp ? kBulkWarpRowThreads / 32 : 1;    // row rings per CTA
+    const int stages = std::max(2, std::min(8, (48 * 1024) / (rings * stride)));
+    const size_t smem = static_cast<size_t>(rings) * stages * stride + rings * stages * 8 + 64;
+    auto kern = per_warp ? k_rowquant_bulk_warp<Op> : k_rowquant_bulk<Op>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) ==
+        cudaSuccess) {
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
+        per_sm = 1;
+      const int grid = std::min((rows + rings - 1) / rings, sms * per_sm);
+      launch_pdl(kern, dim3(grid), dim3(threads), smem, stream, 1, xb, qb, scales, static_scale, rows, cols, col_div,
+                 stages);
+      count_launches(1);
+      return cudaGetLastError();
+    }
+    cudaGetLastError();
+  }
   if (aligned) {
     auto fits = [&](int tpr) { return (nvec + tpr - 1) / tpr <= kQuantMaxChunks; };
     if (fits(32)) {

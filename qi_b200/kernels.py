@@ -147,6 +147,39 @@ def rms_rope(inputs, weights, rope: torch.Tensor | None, head_dim: int, eps: flo
     return outs
 
 
+def rms_head_partials(inputs, head_dim: int) -> torch.Tensor:
+    """Per-head sums of squares of one or two [M, A] bf16 row blocks (a
+    rank's contiguous range of whole heads): fp32 [nparts, M, A / head_dim]."""
+    x0 = inputs[0]
+    M, A = x0.shape
+    for t in inputs:
+        if t.dtype != torch.bfloat16 or t.stride(1) != 1 or t.shape != (M, A) or t.stride(0) != x0.stride(0):
+            raise ValueError("rms_head_partials inputs must be bf16 [M, A] with a shared row stride.")
+    out = torch.empty((len(inputs), M, A // head_dim), dtype=torch.float32, device=x0.device)
+    _lib.call("qi_b200_rms_head_partials", _ptr(inputs[0]), _ptr(inputs[-1]), x0.stride(0), _ptr(out),
+              int(head_dim), len(inputs), M, A, _stream(x0.device))
+    return out
+
+
+def rms_rope_partials(inputs, weights, rope: torch.Tensor | None, head_dim: int, partials: torch.Tensor,
+                      eps: float = 1e-6, outs=None):
+    """``rms_rope`` of this rank's head columns with the row norm taken from
+    every rank's per-head sums (``partials``: fp32 [ranks, nparts, M, heads],
+    rank-major); bit-identical to ``rms_rope`` on the unsplit rows."""
+    n = len(inputs)
+    x0 = inputs[0]
+    M, A = x0.shape
+    _check(partials, "partials", torch.float32, 4, x0.device)
+    if tuple(partials.shape[1:]) != (n, M, A // head_dim):
+        raise ValueError(f"partials must be [ranks, {n}, {M}, {A // head_dim}], got {tuple(partials.shape)}.")
+    outs = outs if outs is not None else [torch.empty((M, A), dtype=torch.bfloat16, device=x0.device)
+                                          for _ in range(n)]
+    _lib.call("qi_b200_rms_rope_partials", _ptr(inputs[0]), _ptr(inputs[-1]), x0.stride(0), _ptr(outs[0]),
+              _ptr(outs[-1]), outs[0].stride(0), _ptr(weights[0]), _ptr(weights[-1]), _ptr(rope), int(head_dim), n,
+              M, A, _ptr(partials), partials.shape[0], float(eps), _stream(x0.device))
+    return outs
+
+
 def quantize_fp8_rowwise(x: torch.Tensor):
     """bf16 [M,K] -> (e4m3 codes uint8 [M,K], fp32 [M]) per-token scales."""
     _check(x, "x", torch.bfloat16, 2)

@@ -185,6 +185,40 @@ def test_rms_rope_matches_tensor_ops():
         assert (diff > 0).float().mean().item() < 0.05
 
 
+@pytest.mark.parametrize("ranks", [1, 2, 4, 8])
+@pytest.mark.parametrize("a,head_dim,rope", [(3072, 128, True), (3072, 128, False), (1024, 128, True),
+                                             (128, 32, True)])
+def test_rms_head_partials_bit_identical_to_unsplit(ranks, a, head_dim, rope):
+    """Head-parallel RMSNorm: each of `ranks` emulated ranks (a contiguous
+    slice of whole heads) computes its per-head sums, the sums are gathered
+    rank-major, and each rank normalizes its slice.  The result is the same
+    bytes as the unsplit kernel's, for q and k together, with and without
+    RoPE."""
+    from qi_b200 import kernels as K
+
+    heads = a // head_dim
+    if heads % ranks:
+        pytest.skip("heads do not split")
+    g = torch.Generator(device=DEV).manual_seed(a + ranks)
+    M = 777
+    qk = torch.randn(M, 2 * a, generator=g, device=DEV).to(torch.bfloat16) * 3
+    w = [(1 + 0.1 * torch.randn(a, generator=g, device=DEV)).to(torch.bfloat16) for _ in range(2)]
+    tab = None
+    if rope:
+        ang = torch.rand(M, head_dim // 2, generator=g, device=DEV) * 6.28
+        tab = torch.stack([ang.cos(), ang.sin()], -1).contiguous()
+    full = K.rms_rope([qk[:, :a], qk[:, a:]], w, tab, head_dim)
+    al = a // ranks
+    parts = torch.cat([K.rms_head_partials([qk[:, r * al:(r + 1) * al], qk[:, a + r * al:a + (r + 1) * al]],
+                                           head_dim).unsqueeze(0) for r in range(ranks)], 0)
+    for r in range(ranks):
+        sl = slice(r * al, (r + 1) * al)
+        got = K.rms_rope_partials([qk[:, r * al:(r + 1) * al], qk[:, a + r * al:a + (r + 1) * al]],
+                                  [w[0][sl].contiguous(), w[1][sl].contiguous()], tab, head_dim, parts)
+        for i in range(2):
+            assert torch.equal(got[i], full[i][:, sl]), (r, i)
+
+
 def test_graph_replay_bit_exact():
     model = D.build_mot_dit(SMALL, device=DEV, seed=1)
     tokens, rope, ctx, t_mod, _ = D.make_step_inputs(SMALL, DEV, seed=1)
