@@ -47,7 +47,12 @@ CONFIGS = {
 for _m in (1, 16, 256, 4096):
     CONFIGS[f"w4a16_m{_m}"] = dict(case=CFG_W4A16[_m], kind="w4a16", gelu=False, group=128,
                                    dtype="bf16 x int4-g128 (fp32 accumulate)")
-CONFIGS["dit"] = dict(case=None, kind="dit", gelu=True, dtype="int8 (int32 accumulate) linears, bf16 attention")
+CONFIGS["dit"] = dict(case=None, kind="dit", gelu=True, dtype="int8 (int32 accumulate) linears, bf16 attention",
+                      partition="sequence")
+# config 5 with the partition BASELINE names (QKV / FFN N-sharded; o / ffn.2
+# row-parallel so attention stays head-local); the same as "dit" on one GPU
+CONFIGS["dit_tp"] = dict(case=None, kind="dit", gelu=True, dtype="int8 (int32 accumulate) linears, bf16 attention",
+                         partition="heads")
 L2_BYTES = 126 * 2**20
 
 
@@ -478,10 +483,12 @@ def measure_linear(cfg_name: str, args, world: int, rank: int, local: int, devic
 # --------------------------------------------------------------------------
 
 
-def measure_dit(args, world: int, rank: int, local: int, device) -> dict:
+def measure_dit(args, world: int, rank: int, local: int, device, partition: str = "sequence") -> dict:
     """One MoT DiT denoising step (30 blocks, video 3120 + action 32 tokens,
-    every Linear INT8 W8A8) replayed from a CUDA graph.  N > 1: video tokens
-    sharded by sequence, K/V all-gathered over NCCL once per layer."""
+    every Linear INT8 W8A8) replayed from a CUDA graph.  N > 1, partition
+    "sequence": video tokens sharded, K/V all-gathered over NCCL once per
+    layer; "heads": QKV / cross / ffn.0 N-sharded by heads and FFN columns,
+    o / cross-o / ffn.2 row-parallel with exact int32 reductions."""
     from qi_b200 import _lib, dit as D, kernels as K
 
     group = None
@@ -491,7 +498,7 @@ def measure_dit(args, world: int, rank: int, local: int, device) -> dict:
     cfg = D.CFG5 if not args.layers else D.DiTConfig(layers=args.layers)
     model = D.build_mot_dit(cfg, device=device, seed=0)
     tokens, rope, ctx, t_mod, _ = D.make_step_inputs(cfg, device, seed=0)
-    runner = D.DiTStepRunner(model, group=group)
+    runner = D.DiTStepRunner(model, group=group, partition=partition)
     tok_l, rope_l = runner.shard(tokens, rope)
     stream = torch.cuda.current_stream(device)
 
@@ -558,10 +565,11 @@ def measure_dit(args, world: int, rank: int, local: int, device) -> dict:
 
     # dominant kernel: the video FFN GEMMs (55 % of the step's INT8 ops);
     # time ffn.0 (M = this rank's video tokens, N 14336, K 3072, bias+GELU)
-    plan = runner.plans["video"][0]
-    w0, s0, b0 = plan.f0
+    w0, s0, b0 = runner.tp["video"][0].f0 if partition == "heads" else runner.plans["video"][0].f0
     xa = torch.randn(runner.video_local, cfg.experts[0].hidden, device=device).to(torch.bfloat16)
     qa, sa = K.quantize_int8_rowwise(xa)
+    K.gemm(_lib.KIND_INT8, qa, w0, sa, s0, b0, gelu=True)
+    plan = _lib.last_launch()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         for _ in range(20):
@@ -581,8 +589,9 @@ def measure_dit(args, world: int, rank: int, local: int, device) -> dict:
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(2 * bf16_tf, 1),
                 "unit": "TFLOP/s", "frac": round(achieved / (2 * bf16_tf), 4),
                 "traffic": load_traffic(f"dit_ffn0_m{m_l}", 1),
-                "algorithmic_bytes": m_l * 3072 + w0.numel() + 14336 * 6 + m_l * 4 + m_l * 14336 * 2,
-                "peak_source": "2 x bf16 dense, " + src, "kernel": "k_gemm_tc<int8> (video ffn.0 + GELU)",
+                "algorithmic_bytes": m_l * w0.shape[1] + w0.numel() + w0.shape[0] * 6 + m_l * 4
+                                     + m_l * w0.shape[0] * 2,
+                "peak_source": "2 x bf16 dense, " + src, "kernel": kernel_label(plan) + ", video ffn.0 + GELU",
                 "kernel_ms": round(gemm_ms, 5), "kernel_timing": "cuda events over 20 graph-captured launches",
                 "step_linear_tops": round(cfg.linear_ops() / world / (ms_step * 1e-3) / 1e12, 1)}
     result = {
@@ -593,8 +602,12 @@ def measure_dit(args, world: int, rank: int, local: int, device) -> dict:
         "config": {"workload": "mot_dit_step_cfg5", "layers": cfg.layers, "video_tokens": cfg.experts[0].tokens,
                    "action_tokens": cfg.experts[1].tokens, "heads": f"{cfg.heads}x{cfg.head_dim}",
                    "ctx_tokens": cfg.ctx_tokens, "attention": "bf16 SDPA, first_frame_causal mask in block form",
-                   "parallelism": f"video tokens sharded x{world} + NCCL all_gather of K/V per layer"
-                   if world > 1 else "single GPU",
+                   "parallelism": ("single GPU" if world == 1 else
+                                   f"video tokens sharded x{world} + NCCL all_gather of K/V per layer"
+                                   if partition == "sequence" else
+                                   f"heads / FFN columns sharded x{world}: QKV, cross, ffn.0 column-parallel; o, "
+                                   "cross-o, ffn.2 row-parallel (NCCL all_reduce MAX of scales + SUM of int32); "
+                                   "per-head RMS sums all-gathered"),
                    "launch": "eager" if args.eager else "cuda_graph", "linear_ops_per_step": cfg.linear_ops(),
                    "l2": "5.9 GB of INT8 weights streamed per step (> L2), no flush needed"},
         "e2e": {"value": round(e2e_ms, 4), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -613,7 +626,7 @@ def measure_dit(args, world: int, rank: int, local: int, device) -> dict:
 # the configs of one full run: N = 1 every BASELINE config, N > 1 the ones
 # that shard (config 2 is the headline line itself)
 ALL_CONFIGS_1GPU = ["int8", "w4a16_m1", "w4a16_m16", "w4a16_m256", "w4a16_m4096", "nvfp4", "fp8", "dit"]
-ALL_CONFIGS_NGPU = ["fp8", "dit"]
+ALL_CONFIGS_NGPU = ["fp8", "dit", "dit_tp"]
 
 
 def run_ours(args):
@@ -627,8 +640,8 @@ def run_ours(args):
 
     def measure(name):
         torch.cuda.empty_cache()
-        if name == "dit":
-            return measure_dit(args, world, rank, local, device)
+        if CONFIGS[name]["kind"] == "dit":
+            return measure_dit(args, world, rank, local, device, CONFIGS[name]["partition"])
         return measure_linear(name, args, world, rank, local, device)
 
     result = measure(args.config)
@@ -797,7 +810,7 @@ def reference_result(cfg_name: str, args, world: int, steps: int | None = None, 
     """The reference's CPU algorithm (port) for one config, timed on all host threads."""
     steps = args.steps if steps is None else steps
     warmup = args.warmup if warmup is None else warmup
-    if cfg_name == "dit":
+    if CONFIGS[cfg_name]["kind"] == "dit":
         fn, cfg = _dit_cpu_layer_sample()
         for _ in range(max(1, warmup)):
             fn()

@@ -305,6 +305,24 @@ int qi_b200_w4a16_linear_ws(const void* x_bf16, const void* qweight_packed, cons
                             const void* zeros_packed, int group_size, const void* bias, void* out_bf16, int M, int N,
                             int K, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* ---- Weight-only linears on the reference's own buffers ----------------
+ * Replaces the reserved CudaExtBackend (backends/reference.py:94-96) for the
+ * weight-only configs the reference's ReferenceBackend.linear serves
+ * (reference.py:48-91): WeightOnlyQuantConfig's default bits=8, group 128,
+ * symmetric (W8A16), and INT4 kept one value per int8.  qweight int8 [N, K]
+ * (codes; symmetric: -qmax..qmax, asymmetric: 0..2^bits-1), scales fp32
+ * [N, G], zeros int16 [N, G] or NULL (symmetric), G = ceil(K / group_size),
+ * group_size <= 0 = one group per row.  The dequantization is the
+ * reference's, bit for bit: W = bf16(fp32(q - z) * s).  K % 16 == 0. */
+int qi_b200_wo_dequant(const void* qweight_int8, const float* scales, const void* zeros_int16, int group_size,
+                       void* out_bf16, int N, int K, cudaStream_t stream);
+/* out[M, N] = bf16(x . W^T + bias): W dequantized into the caller's
+ * workspace (>= N * K * 2 bytes, 16-byte aligned), then the bf16 tcgen05
+ * GEMM. */
+int qi_b200_wo_linear_ws(const void* x_bf16, const void* qweight_int8, const float* scales, const void* zeros_int16,
+                         int group_size, const void* bias, void* out_bf16, int M, int N, int K, void* workspace,
+                         size_t workspace_bytes, cudaStream_t stream);
+
 /* ---- NVFP4 W4A4 (no counterpart in the reference, which only names the
  * buffers qweight_packed / scale_factors / weight_global_scale at
  * src/qi/quantization/modules.py:21-23) ------------------------------------

@@ -49,6 +49,8 @@ SIGNATURES = {
     "qi_b200_launch_count": [_P],
     "qi_b200_quantize_int8_rowwise_smooth": [_P, _P, _P, _P, _I, _I, _P],
     "qi_b200_w4a16_dequant": [_P, _P, _P, _I, _P, _I, _I, _P],
+    "qi_b200_wo_dequant": [_P, _P, _P, _I, _P, _I, _I, _P],
+    "qi_b200_wo_linear_ws": [_P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _P, ctypes.c_size_t, _P],
     "qi_b200_w4a16_linear_ws": [_P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _P, ctypes.c_size_t, _P],
     "qi_b200_quantize_int8_rowwise": [_P, _P, _P, _I, _I, _P],
     "qi_b200_quantize_int8_rowwise_given": [_P, _P, _P, _I, _I, _P],

@@ -387,6 +387,43 @@ __device__ __forceinline__ uint32_t dequant_pair(uint32_t w, int t, float s16x, 
   return pack_bf16x2(f0, f1);
 }
 
+// Weight-only quantized weights in the reference's own layout
+// (quantize.py:32-78: one int8 code per value, fp32 scales [N, G], int16
+// zero points [N, G] or none) -> bf16 [N, K], computed as the reference's
+// dequantize_weight (quantize.py:81-119) does: w = fp32(q - z) * s rounded
+// to fp32, then to bf16.  Serves weight-only INT8 (W8A16) and INT4 stored
+// one value per byte.  16 elements per thread (one 16-byte load); K % 16 == 0.
+__global__ void __launch_bounds__(256)
+k_wo_dequant(const int8_t* __restrict__ q, const float* __restrict__ scales, const int16_t* __restrict__ zeros,
+             int G, int group, __nv_bfloat16* __restrict__ out, int N, int K) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int per_row = K >> 4;
+  const long long total = static_cast<long long>(N) * per_row;
+  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < total; i += 256ll * gridDim.x) {
+    const int n = static_cast<int>(i / per_row);
+    const int k0 = static_cast<int>(i - static_cast<long long>(n) * per_row) << 4;
+    const int4 raw = __ldg(reinterpret_cast<const int4*>(q + static_cast<long long>(n) * K + k0));
+    const int8_t* c = reinterpret_cast<const int8_t*>(&raw);
+    uint32_t packed[8];
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) {
+      float w2[2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int g = (k0 + e + t) / group;
+        const float sc = __ldg(scales + static_cast<long long>(n) * G + g);
+        const float zc = zeros != nullptr ? static_cast<float>(__ldg(zeros + static_cast<long long>(n) * G + g)) : 0.f;
+        w2[t] = __fmul_rn(__fsub_rn(static_cast<float>(c[e + t]), zc), sc);
+      }
+      packed[e >> 1] = pack_bf16x2(w2[0], w2[1]);
+    }
+    uint4* o = reinterpret_cast<uint4*>(out + static_cast<long long>(n) * K + k0);
+    o[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    o[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+  }
+}
+
 // Dequantize packed INT4 weights to bf16 [N, K] (the reference's
 // bf16((q - z) s), exact), four packed words (32 elements) per thread.
 // HBM-bound: K/2 + 2K bytes per row (+ scales).  group % 32 == 0, K % 32 == 0.

@@ -1346,6 +1346,39 @@ int qi_b200_w4a16_linear_ws(const void* x_bf16, const void* qweight_packed, cons
                        0, stream);
 }
 
+int qi_b200_wo_dequant(const void* qweight_int8, const float* scales, const void* zeros_int16, int group_size,
+                       void* out_bf16, int N, int K, cudaStream_t stream) {
+  if (qweight_int8 == nullptr || scales == nullptr || out_bf16 == nullptr) return QI_B200_EINVAL;
+  if (N <= 0 || K <= 0 || K % 16 != 0) return QI_B200_ESHAPE;
+  int group = group_size;
+  if (group <= 0 || group > K) group = K;
+  if (!aligned16(qweight_int8) || !aligned16(out_bf16)) return QI_B200_EALIGN;
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const int G = (K + group - 1) / group;
+  const long long chunks = (long long)N * (K / 16);
+  const int grid = (int)std::min<long long>((chunks + 255) / 256, (long long)di->num_sms * 16);
+  launch_pdl(k_wo_dequant, dim3(grid), dim3(256), 0, stream, 1, static_cast<const int8_t*>(qweight_int8), scales,
+             static_cast<const int16_t*>(zeros_int16), G, group, static_cast<__nv_bfloat16*>(out_bf16), N, K);
+  count_launches(1);
+  return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+
+int qi_b200_wo_linear_ws(const void* x_bf16, const void* qweight_int8, const float* scales, const void* zeros_int16,
+                         int group_size, const void* bias, void* out_bf16, int M, int N, int K, void* workspace,
+                         size_t workspace_bytes, cudaStream_t stream) {
+  if (M == 0) return QI_B200_OK;
+  if (workspace == nullptr || workspace_bytes < (size_t)N * K * 2) return QI_B200_EINVAL;
+  int rc = check_gemm_args(QI_B200_KIND_BF16, x_bf16, workspace, nullptr, 0, nullptr, 0, bias, out_bf16, N, M, N, K,
+                           0);
+  if (rc) return rc;
+  rc = qi_b200_wo_dequant(qweight_int8, scales, zeros_int16, group_size, workspace, N, K, stream);
+  if (rc) return rc;
+  return gemm_dispatch(QI_B200_KIND_BF16, x_bf16, workspace, nullptr, 0, nullptr, 0, bias, out_bf16, N, M, N, K, 0,
+                       0, stream);
+}
+
 int qi_b200_quantize_nvfp4(const void* x_bf16, int rows, int cols, int g_mode, const float* g_in,
                            unsigned int* ws_amax, float* g_out, void* q_packed, void* sf_atoms, cudaStream_t stream) {
   if (rows == 0) return QI_B200_OK;

@@ -388,6 +388,49 @@ class _BlockPlan:
         self.modulation = blk.modulation
 
 
+class _nullctx:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+class _TPBlockPlan:
+    """One rank's shard of a block for the head-parallel step: rows of the
+    fused q/k/v, cross-q, cross-k/v and ffn.0 weights for this rank's heads /
+    FFN columns (column parallel), and the matching input columns of o,
+    cross-o and ffn.2 (row parallel; their per-channel scales and bias stay
+    whole and are applied once after the int32 sum).  INT8 per-channel rows
+    slice exactly, so every output element is the single-GPU one."""
+
+    def __init__(self, p: _BlockPlan, cfg: DiTConfig, spec: ExpertSpec, rank: int, world: int):
+        if cfg.heads % world or spec.ffn % (8 * world):
+            raise ValueError(f"{cfg.heads} heads / FFN {spec.ffn} do not split over {world} ranks.")
+        a = cfg.attn_dim
+        self.heads = cfg.heads // world
+        self.al = al = a // world
+        fl = spec.ffn // world
+        lo, hi = rank * al, (rank + 1) * al
+
+        def rows(wsb, ranges):
+            return tuple(torch.cat([t[r0:r1] for r0, r1 in ranges], 0).contiguous() for t in wsb)
+
+        def cols(wsb, c0, c1):
+            return wsb[0][:, c0:c1].contiguous(), wsb[1], wsb[2]
+
+        self.qkv = rows(p.qkv, [(lo, hi), (a + lo, a + hi), (2 * a + lo, 2 * a + hi)])
+        self.cq = rows(p.cq, [(lo, hi)])
+        self.ckv = rows(p.ckv, [(lo, hi), (a + lo, a + hi)])
+        self.f0 = rows(p.f0, [(rank * fl, (rank + 1) * fl)])
+        self.o = cols(p.o, lo, hi)
+        self.co = cols(p.co, lo, hi)
+        self.f2 = cols(p.f2, rank * fl, (rank + 1) * fl)
+        self.nq, self.nk = p.nq.weight[lo:hi].contiguous(), p.nk.weight[lo:hi].contiguous()
+        self.cnq, self.cnk = p.cnq.weight[lo:hi].contiguous(), p.cnk.weight[lo:hi].contiguous()
+        self.norm3 = p.norm3
+
+
 class DiTStepRunner:
     """One MoT DiT step on B200 (INT8 tcgen05 GEMMs, fused QKV, block-mask
     attention), optionally captured as a CUDA graph.
@@ -402,14 +445,20 @@ class DiTStepRunner:
     bound by weight bandwidth, so splitting them would not shorten the step.
     """
 
-    def __init__(self, model: MoTDiT, group=None, fused: bool = True):
+    def __init__(self, model: MoTDiT, group=None, fused: bool = True, partition: str = "sequence", kernels=None):
         from . import _lib
-        from . import kernels as K
 
+        if kernels is None:
+            from . import kernels as K
+        else:
+            K = kernels  # a stand-in with the same functions (CPU tests of the multi-rank logic)
+        if partition not in ("sequence", "heads"):
+            raise ValueError("partition must be 'sequence' or 'heads'")
         self.K = K
         self.kind_int8 = _lib.KIND_INT8
         self.cfg = model.cfg
         self.names = model.expert_order
+        self.partition = partition
         self.plans = {n: [_BlockPlan(b) for b in model.mixtures[n].blocks] for n in self.names}
         # all layers' modulation tables of an expert, [L, 6, D]: one add per step
         self.mod_tables = {n: torch.cat([p.modulation for p in self.plans[n]], 0).contiguous() for n in self.names}
@@ -423,6 +472,20 @@ class DiTStepRunner:
         else:
             self.rank, self.world = 0, 1
         sv = self.cfg.experts[0].tokens
+        if partition == "heads":
+            # tensor parallel: every rank holds all tokens and a contiguous range of heads / FFN columns
+            self.video_local, self.video_offset = sv, 0
+            self.tp = {n: [_TPBlockPlan(p, self.cfg, spec, self.rank, self.world)
+                           for p in self.plans[n]] for n, spec in zip(self.names, self.cfg.experts)}
+            self.tp_groups = {self.names[0]: group}
+            if group is not None:
+                import torch.distributed as dist
+
+                # the action expert's collectives run on a side stream: a communicator of its own
+                self.tp_groups[self.names[1]] = dist.new_group(dist.get_process_group_ranks(group))
+            else:
+                self.tp_groups[self.names[1]] = None
+            return
         if sv % self.world:
             raise ValueError(f"{sv} video tokens do not split over {self.world} ranks.")
         self.video_local = sv // self.world
@@ -459,9 +522,129 @@ class DiTStepRunner:
 
     @torch.no_grad()
     def step(self, tokens: dict, rope: dict, ctx: dict, t_mod: dict) -> dict:
+        if self.partition == "heads":
+            return self._step_tp(tokens, rope, ctx, t_mod)
         if self.fused:
             return self._step_fused(tokens, rope, ctx, t_mod)
         return self._step_unfused(tokens, rope, ctx, t_mod)
+
+    # -- tensor parallel (heads) ---------------------------------------------
+
+    def _all_gather(self, t, group):
+        if group is None:
+            return t.unsqueeze(0)
+        import torch.distributed as dist
+
+        out = torch.empty((self.world * t.numel(),), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(out, t.contiguous().reshape(-1), group=group)
+        return out.view((self.world,) + tuple(t.shape))
+
+    def _all_reduce(self, t, group, op):
+        if group is not None:
+            import torch.distributed as dist
+
+            dist.all_reduce(t, op=op, group=group)
+        return t
+
+    def _row_parallel(self, x_l, wsb, group):
+        """Row-parallel INT8 linear, exact: per-token scales reduced with MAX
+        (the scale of the whole row), int32 partial sums reduced with SUM,
+        then the epilogue.  Bit-identical to the single-GPU INT8 linear."""
+        import torch.distributed as dist
+
+        K = self.K
+        w, sw, b = wsb
+        s = self._all_reduce(K.int8_row_scales(x_l), group, dist.ReduceOp.MAX if group is not None else None)
+        q = K.quantize_int8_rowwise_given(x_l, s)
+        acc = K.gemm(self.kind_int8, q, w, None, None, raw_acc=True)
+        acc = self._all_reduce(acc, group, dist.ReduceOp.SUM if group is not None else None)
+        return K.int8_epilogue(acc, s, sw, b)
+
+    def _norm_heads(self, parts, weights, rope, group, eps):
+        """RMSNorm (+ RoPE) of this rank's head columns with the row norm over
+        all heads: per-head sums gathered from every rank (head order)."""
+        K, hd = self.K, self.cfg.head_dim
+        sums = self._all_gather(K.rms_head_partials(parts, hd), group)
+        return K.rms_rope_partials(parts, weights, rope, hd, sums, eps)
+
+    def _tp_pre(self, n, li, x, y_ffn, mods, sc1, rope):
+        """Residual + norm1 + modulate + INT8 (all rows, every rank) -> this
+        rank's heads of q, k, v -> RMSNorm over all heads + RoPE."""
+        K, cfg = self.K, self.cfg
+        tp, m, g = self.tp[n][li], mods[n][li], self.tp_groups[n]
+        if li == 0:
+            q8, s8 = K.resid_ln_quant(x[n], mod_scale1=sc1[n][li, 0], mod_shift=m[0], eps=cfg.eps)
+        else:
+            q8, s8 = K.resid_ln_quant(x[n], y_ffn[n], gate=mods[n][li - 1][5], mod_scale1=sc1[n][li, 0],
+                                      mod_shift=m[0], eps=cfg.eps)
+        qkv = self._gemm(q8, s8, tp.qkv)
+        al = tp.al
+        qn, kn = self._norm_heads([qkv[:, :al], qkv[:, al:2 * al]], [tp.nq, tp.nk], rope[n], g, cfg.eps)
+        return qn.unsqueeze(0), kn.unsqueeze(0), qkv[:, 2 * al:].unsqueeze(0)
+
+    def _tp_post(self, n, li, att, x, y_ffn, mods, sc1, ctxq):
+        """Row-parallel o -> gate-residual + norm3 -> cross-attention over this
+        rank's heads -> row-parallel cross-o -> norm2 + modulate -> ffn.0 on
+        this rank's FFN columns (GELU fused) -> row-parallel ffn.2."""
+        K, cfg = self.K, self.cfg
+        tp, m, g = self.tp[n][li], mods[n][li], self.tp_groups[n]
+        al, hl, eps = tp.al, tp.heads, cfg.eps
+        y_o = self._row_parallel(att.reshape(-1, al), tp.o, g)
+        q8, s8 = K.resid_ln_quant(x[n], y_o, gate=m[2], ln_w=tp.norm3.weight, ln_b=tp.norm3.bias, eps=eps)
+        cq = self._gemm(q8, s8, tp.cq)
+        ckv = self._gemm(*ctxq[n], tp.ckv)
+        cqn = self._norm_heads([cq], [tp.cnq], None, g, eps)[0]
+        ckn = self._norm_heads([ckv[:, :al]], [tp.cnk], None, g, eps)[0]
+        ca = attention(cqn.unsqueeze(0), ckn.unsqueeze(0), ckv[:, al:].unsqueeze(0), hl)
+        y_co = self._row_parallel(ca.reshape(-1, al), tp.co, g)
+        q8, s8 = K.resid_ln_quant(x[n], y_co, mod_scale1=sc1[n][li, 1], mod_shift=m[3], eps=eps)
+        f = self._gemm(q8, s8, tp.f0, gelu=True)
+        y_ffn[n] = self._row_parallel(f, tp.f2, g)
+
+    def _step_tp(self, tokens, rope, ctx, t_mod):
+        """The step with heads and FFN columns split over the ranks (config 5's
+        N-sharded QKV / FFN, completed Megatron-style so attention is head-local):
+        per expert and layer 2 all-gathers of per-head RMS sums and 3 exact
+        row-parallel reductions (MAX of [M] scales, SUM of int32 [M, D]).  Every
+        rank ends with all tokens, bit-identical to one GPU."""
+        K, cfg = self.K, self.cfg
+        x = {n: t.reshape(-1, t.shape[-1]).clone() for n, t in tokens.items()}
+        mods, sc1, ctxq = {}, {}, {}
+        for n in self.names:
+            mods[n] = self.mod_tables[n] + t_mod[n]
+            sc1[n] = 1 + mods[n][:, 1::3]
+            ctxq[n] = K.quantize_int8_rowwise(ctx[n].reshape(-1, ctx[n].shape[-1]).contiguous())
+        cuda = x[self.names[0]].is_cuda
+        main = torch.cuda.current_stream() if cuda else None
+        side = self._side_stream() if cuda else None
+        if cuda:
+            side.wait_stream(main)
+        t = min(cfg.tokens_per_frame, cfg.experts[0].tokens)
+        hl = cfg.heads // self.world
+        y_ffn = {}
+        va_name, ac_name = self.names
+        for li in range(cfg.layers):
+            qv, kv, vv = self._tp_pre(va_name, li, x, y_ffn, mods, sc1, rope)
+            kf, vf = kv[:, :t].contiguous(), vv[:, :t].contiguous()
+            if cuda:
+                side.wait_stream(main)
+            with (torch.cuda.stream(side) if cuda else _nullctx()):
+                qa, ka, va = self._tp_pre(ac_name, li, x, y_ffn, mods, sc1, rope)
+                att_a = attention(qa, torch.cat([kf, ka], 1), torch.cat([vf, va], 1), hl)
+                self._tp_post(ac_name, li, att_a, x, y_ffn, mods, sc1, ctxq)
+            if cuda:
+                kf.record_stream(side)
+                vf.record_stream(side)
+            att_v = self._video_attention(qv, kv, vv, heads=hl)
+            self._tp_post(va_name, li, att_v, x, y_ffn, mods, sc1, ctxq)
+        with (torch.cuda.stream(side) if cuda else _nullctx()):
+            K.resid_ln_quant(x[ac_name], y_ffn[ac_name], gate=mods[ac_name][cfg.layers - 1][5], quant=False)
+        K.resid_ln_quant(x[va_name], y_ffn[va_name], gate=mods[va_name][cfg.layers - 1][5], quant=False)
+        if cuda:
+            main.wait_stream(side)
+            for n in self.names:
+                x[n].record_stream(side)
+        return {n: x[n].view(tokens[n].shape) for n in self.names}
 
     def _gemm(self, q8, s8, wsb, gelu=False):
         w, sw, b = wsb
@@ -497,12 +680,12 @@ class DiTStepRunner:
         f = self._gemm(q8, s8, p.f0, gelu=True)
         y_ffn[n] = K.int8_linear(f, *p.f2)
 
-    def _video_attention(self, q, k, v):
+    def _video_attention(self, q, k, v, heads=None):
         """Video queries of this rank under the first_frame_causal mask: all
         video keys, except first-frame queries, which see first-frame keys
         only (recomputed for those rows and written over them, so the bulk
         attention output needs no concatenation)."""
-        h = self.cfg.heads
+        h = self.cfg.heads if heads is None else heads
         sv = k.shape[1]
         t = min(self.cfg.tokens_per_frame, sv)
         nf = max(0, min(t - self.video_offset, q.shape[1]))

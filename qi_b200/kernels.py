@@ -347,6 +347,50 @@ def w4a16_linear(x_bf16_2d: torch.Tensor, qweight_packed: torch.Tensor, scales_f
     return out
 
 
+def weight_only_linear(x_bf16_2d: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
+                       zeros: torch.Tensor | None, group_size: int, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """Weight-only linear on the reference's own buffers (``qweight`` int8
+    codes [N, K], ``scales`` fp32 [N, G], ``zeros`` int16 [N, G] or None):
+    the weights are dequantized exactly as the reference's dequantize_weight
+    into a workspace, then multiplied with the bf16 tcgen05 GEMM
+    (``qi_b200_wo_linear_ws``)."""
+    _check(x_bf16_2d, "x_bf16_2d", torch.bfloat16, 2)
+    dev = x_bf16_2d.device
+    _check(qweight, "qweight", torch.int8, 2, dev)
+    M, K = x_bf16_2d.shape
+    N = qweight.shape[0]
+    if qweight.shape[1] != K:
+        raise ValueError(f"weight-only K mismatch: activation K={K}, weight K={qweight.shape[1]}.")
+    g = K if group_size <= 0 or group_size > K else group_size
+    G = -(-K // g)
+    s = scales.reshape(N, -1).to(device=dev, dtype=torch.float32).contiguous()
+    if s.shape[1] != G:
+        raise ValueError(f"weight-only scales must be [{N}, {G}], got {tuple(scales.shape)}.")
+    z = None
+    if zeros is not None:
+        z = zeros.reshape(N, -1).to(device=dev, dtype=torch.int16).contiguous()
+        if z.shape[1] != G:
+            raise ValueError(f"weight-only zeros must be [{N}, {G}], got {tuple(zeros.shape)}.")
+    if bias is not None:
+        _check(bias, "bias", torch.bfloat16, device=dev)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    ws = torch.empty((N * K * 2,), dtype=torch.uint8, device=dev)
+    _lib.call("qi_b200_wo_linear_ws", _ptr(x_bf16_2d), _ptr(qweight), _ptr(s), _ptr(z), int(g), _ptr(bias),
+              _ptr(out), M, N, K, _ptr(ws), ws.numel(), _stream(dev))
+    return out
+
+
+def wo_dequant(qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor | None, group_size: int):
+    """Reference-layout weight-only codes -> bf16 [N, K] (``qi_b200_wo_dequant``)."""
+    N, K = qweight.shape
+    G = scales.reshape(N, -1).shape[1]
+    out = torch.empty((N, K), dtype=torch.bfloat16, device=qweight.device)
+    z = None if zeros is None else zeros.reshape(N, G).to(torch.int16).contiguous()
+    _lib.call("qi_b200_wo_dequant", _ptr(qweight), _ptr(scales.reshape(N, G).float().contiguous()), _ptr(z),
+              int(group_size), _ptr(out), N, K, _stream(qweight.device))
+    return out
+
+
 def w4a16_dequant(qweight_packed: torch.Tensor, scales_fp16: torch.Tensor, zeros_packed: torch.Tensor,
                   group_size: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """Packed INT4 weights -> bf16 [N, K], exactly bf16((q - z) s) (``qi_b200_w4a16_dequant``)."""

@@ -8,6 +8,8 @@ The format is chosen from the buffers a ``WeightOnlyLinear`` carries:
 format                buffers
 ====================  ==========================================================
 INT8 W8A8             qweight int8 [N,K], scales fp32 [N,1] or [N]; per-token acts
+weight-only (W8A16,   qweight int8 [N,K] codes, scales fp32 [N,G], zeros int16
+INT4 unpacked)        [N,G] or None: the reference's own layout (``cuda_ext``)
 FP8-E4M3 W8A8         weight_fp8 (or qweight_packed uint8) [N,K], weight_scale
                       fp32 [1] or [N]; activation_scale fp32 [1] (static) or
                       activation_granularity="per_token" (dynamic)
@@ -136,6 +138,16 @@ class B200Backend:
         elif bits == 8 and activation_granularity == "per_token":
             y = self._int8(x2, qweight, scales, group_size, symmetric, weight_granularity, bias, gelu,
                            input_scale if fuse_smooth else None)
+        elif qweight is not None and qweight.dtype == torch.int8 and bits in (2, 3, 4, 5, 6, 7, 8):
+            # weight-only on the reference's own buffers (W8A16, or INT4 one value per byte):
+            # ReferenceBackend.linear's dequantise-then-matmul (reference.py:48-91) on the GPU
+            if scales is None:
+                raise ValueError("weight-only backend requires scales.")
+            n = qweight.shape[0]
+            y = K.weight_only_linear(x2, qweight.contiguous(), scales, None if symmetric else zeros, int(group_size),
+                                     _bias_bf16(bias, n, x2.device))
+            if gelu:
+                y = torch.nn.functional.gelu(y.float(), approximate="tanh").to(torch.bfloat16)
         else:
             raise ValueError(
                 "B200 backend: unsupported buffer combination (bits=%s, activation_granularity=%s, packed=%s)"

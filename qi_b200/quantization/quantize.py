@@ -293,17 +293,25 @@ def pack_int4_rows(q: torch.Tensor) -> torch.Tensor:
 
 
 def pack_w4a16(qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor | None):
-    """Reference weight-only INT4 tensors -> (qweight_packed, scale_factors fp16, zeros packed)."""
+    """Reference weight-only INT4 tensors (quantize.py:32-78: one int8 per
+    value, fp32 scales [N, G], int16 zeros [N, G] or None when symmetric) ->
+    (qweight_packed, scale_factors fp16, zeros packed).  Symmetric codes
+    q in [-7, 7] are stored as q + 8 with zero point 8, which dequantizes to
+    the same (q + 8 - 8) * s."""
     N, K = qweight.shape
     G = scales.shape[1]
-    qp = pack_int4_rows(qweight)
-    s16 = scales.to(torch.float16).contiguous()
+    q = qweight.to(torch.int16)
     Gp = -(-G // 8) * 8
     z = torch.zeros((N, Gp), dtype=torch.int32, device=qweight.device)
     if zeros is not None:
         z[:, :G] = zeros.to(torch.int32)
-    else:  # symmetric int4 stored offset-free: q in [-7, 7] -> q + 8, z = 8
+    else:
+        q = q + 8
         z[:, :G] = 8
+    if int(q.min()) < 0 or int(q.max()) > 15:
+        raise ValueError("INT4 codes out of range for the packed layout.")
+    qp = pack_int4_rows(q)
+    s16 = scales.to(torch.float16).contiguous()
     return qp, s16, pack_int4_rows(z)
 
 
@@ -312,8 +320,6 @@ def quantize_weight_w4a16(weight: torch.Tensor, group_size: int, symmetric: bool
     if input_scale is not None:
         w = w * input_scale[None, :]
     q, s, z = quantize_weight_rtn(w, 4, group_size, symmetric)
-    if symmetric:
-        q = (q.to(torch.int16) + 8).to(torch.int8)
     qp, s16, zp = pack_w4a16(q, s, z)
     return QuantizedLinearWeight(qweight=None, scales=None, zeros=zp, qweight_packed=qp, scale_factors=s16,
                                  input_scale=input_scale)

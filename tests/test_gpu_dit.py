@@ -219,6 +219,19 @@ def test_rms_head_partials_bit_identical_to_unsplit(ranks, a, head_dim, rope):
             assert torch.equal(got[i], full[i][:, sl]), (r, i)
 
 
+def test_head_parallel_plan_on_one_gpu_matches_fused():
+    """The head-parallel plan (row-parallel o / cross-o / ffn.2 through raw
+    int32 accumulators and the standalone epilogue, RMSNorm from per-head
+    sums) run with one rank gives the fused single-GPU step's bytes."""
+    model = D.build_mot_dit(SMALL, device=DEV, seed=2)
+    tokens, rope, ctx, t_mod, _ = D.make_step_inputs(SMALL, DEV, seed=2)
+    with torch.no_grad():
+        ref = D.DiTStepRunner(model).step(tokens, rope, ctx, t_mod)
+        tp = D.DiTStepRunner(model, partition="heads").step(tokens, rope, ctx, t_mod)
+    for n in ref:
+        assert torch.equal(tp[n], ref[n]), (n, rel(tp[n], ref[n]))
+
+
 def test_graph_replay_bit_exact():
     model = D.build_mot_dit(SMALL, device=DEV, seed=1)
     tokens, rope, ctx, t_mod, _ = D.make_step_inputs(SMALL, DEV, seed=1)

@@ -186,6 +186,27 @@ def test_torch_packing_matches_oracle():
     np.testing.assert_array_equal(zp.numpy(), zpo)
 
 
+def test_symmetric_int4_repack_dequantizes_like_the_reference():
+    """A reference symmetric INT4 weight (codes in [-7, 7], no zero points)
+    repacked by the product's pack_w4a16 dequantizes, through the packed
+    layout, to the reference's own dequantize_weight bytes."""
+    from qi_b200.quantization.quantize import pack_w4a16
+
+    f = load("rtn_int4_sym_g64")
+    N, K, bits, group, sym = (int(v) for v in f["meta"])
+    assert sym == 1 and "zeros" not in f
+    qp, s16, zp = pack_w4a16(torch.from_numpy(f["qweight"]), torch.from_numpy(f["scales"]), None)
+    got = O.w4a16_dequant_bf16(qp.numpy(), s16.numpy(), zp.numpy(), K, group)
+    # the packed layout keeps fp16 scales (BASELINE config 3's format): bit-exact
+    # against the reference arithmetic on those scales, and within fp16 rounding
+    # of the reference's fp32-scale bytes
+    s_f16 = np.repeat(s16.float().numpy(), group, axis=1)[:, :K]
+    want = O.f32_to_bf16(f["qweight"].astype(np.float32) * s_f16)
+    np.testing.assert_array_equal(got, want)
+    ref = O.bf16_to_f32(f["deq_bf16"])
+    assert np.abs(O.bf16_to_f32(got) - ref).max() <= 2 ** -7 * np.abs(ref).max()  # one bf16 step
+
+
 def test_torch_quantizers_match_reference_fixtures():
     """The product's vectorised RTN / FP8 quantizers give the reference's bytes."""
     from qi_b200.quantization.quantize import quantize_to_fp8_e4m3, quantize_weight_rtn as qrtn
