@@ -93,8 +93,9 @@ struct QuantFp8 {
   __device__ __forceinline__ static uint32_t q2(float2 f, float s, float r) {
     constexpr float kLo = 1.0f - 0x1p-20f, kHi = 1.0f + 0x1p-20f;
     const float2 t = __fmul2_rn(f, make_float2(r, r));
-    const uint32_t lo = e4m3x2_rn_sat(__fmul_rn(t.x, kLo), __fmul_rn(t.y, kLo));
-    const uint32_t hi = e4m3x2_rn_sat(__fmul_rn(t.x, kHi), __fmul_rn(t.y, kHi));
+    const float2 a = __fmul2_rn(t, make_float2(kLo, kLo)), b = __fmul2_rn(t, make_float2(kHi, kHi));
+    const uint32_t lo = e4m3x2_rn_sat(a.x, a.y);
+    const uint32_t hi = e4m3x2_rn_sat(b.x, b.y);
     if (__builtin_expect(lo == hi, 1)) return lo;
     return e4m3x2_rn_sat(__fdiv_rn(f.x, s), __fdiv_rn(f.y, s));
   }
@@ -104,15 +105,12 @@ struct QuantFp8Static : QuantFp8 {
   static constexpr bool kNeedsAmax = false;
 };
 
+// max |x| of 8 bf16 values, taken on packed bf16x2 (|x| and max are exact in
+// bf16, so this equals the fp32 max of the widened values).
 __device__ __forceinline__ float absmax_bf16x8(const uint4& v) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-  float m = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 f = __bfloat1622float2(h[i]);
-    m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
-  }
-  return m;
+  const __nv_bfloat162 m = __hmax2(__hmax2(__habs2(h[0]), __habs2(h[1])), __hmax2(__habs2(h[2]), __habs2(h[3])));
+  return fmaxf(__low2float(m), __high2float(m));
 }
 
 // SmoothQuant / AWQ input smoothing of 8 bf16 values, x / input_scale in

@@ -55,15 +55,22 @@ k_amax_bf16(const __nv_bfloat16* __restrict__ x, long long n, unsigned int* __re
   float m = 0.f;
   const long long nvec = n / 8;
   const uint4* xv = reinterpret_cast<const uint4*>(x);
-  // two 16-byte loads in flight per thread; bf16 |x| max taken exactly in bf16x2
+  // kLoads 16-byte loads in flight per thread (the pass is bound by DRAM
+  // latency with two); bf16 |x| max taken exactly in bf16x2
+  constexpr int kLoads = 8;
   const long long stride = 256ll * gridDim.x;
   __nv_bfloat162 m2 = __float2bfloat162_rn(0.f);
-  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < nvec; i += 2 * stride) {
-    const uint4 v = __ldg(xv + i);
-    const uint4 u = i + stride < nvec ? __ldg(xv + i + stride) : make_uint4(0, 0, 0, 0);
-    const uint32_t w[8] = {v.x, v.y, v.z, v.w, u.x, u.y, u.z, u.w};
+  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < nvec; i += kLoads * stride) {
+    uint4 v[kLoads];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) m2 = __hmax2(m2, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&w[k])));
+    for (int u = 0; u < kLoads; ++u)
+      v[u] = i + u * stride < nvec ? __ldg(xv + i + u * stride) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int u = 0; u < kLoads; ++u) {
+      const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) m2 = __hmax2(m2, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&w[k])));
+    }
   }
   m = fmaxf(__low2float(m2), __high2float(m2));
   for (long long i = nvec * 8 + blockIdx.x * 256ll + threadIdx.x; i < n; i += 256ll * gridDim.x)

@@ -2,8 +2,10 @@
 ``src/qi/quantization/__init__.py``), served by the B200 kernels."""
 
 from .checkpoint import (
+    checkpoint_format,
     checkpoint_is_quantized,
     load_checkpoint_payload,
+    load_quantized_checkpoint,
     prepare_model_for_quantized_checkpoint,
     quant_config_from_metadata,
     quantize_loaded_model,
@@ -32,7 +34,7 @@ from .swap import (
 
 __all__ = [
     "QuantizedLinearWeight", "WeightOnlyLinear", "WeightActivationQuantConfig", "WeightOnlyQuantConfig",
-    "checkpoint_is_quantized", "dequantize_weight", "fuse_ffn_gelu", "load_checkpoint_payload",
+    "checkpoint_format", "checkpoint_is_quantized", "load_quantized_checkpoint", "dequantize_weight", "fuse_ffn_gelu", "load_checkpoint_payload",
     "prepare_model_for_quantized_checkpoint", "prepare_model_for_weight_only_load", "quant_config_from_metadata",
     "quantize_linear_weight", "quantize_loaded_model", "quantize_weight_awq", "quantize_weight_fp8_rtn",
     "quantize_weight_fp8_smoothquant", "quantize_weight_int8_smoothquant", "quantize_weight_nvfp4",

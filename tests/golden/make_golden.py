@@ -56,7 +56,7 @@ def import_reference(ref_root: Path):
     from qi.quantization.backends import flashrt_fp8_ops as F8
     from qi.quantization.backends.reference import ReferenceBackend
     from qi.quantization.config import WeightActivationQuantConfig, WeightOnlyQuantConfig
-    from qi.quantization.swap import replace_linear_with_weight_only
+    from qi.quantization.swap import replace_linear_with_weight_only  # noqa: F401
 
     return types.SimpleNamespace(
         Q=Q, F8=F8, ReferenceBackend=ReferenceBackend,
@@ -161,6 +161,7 @@ def main() -> None:
     fp8_per_token(R)
     w4a16_cfg3(R)
     mot_step(R)
+    reference_checkpoints(R)
 
     # ---- hashes of the reference quantizer at the full BASELINE sizes
     _, w1, _ = make_linear_inputs(CFG_INT8)
@@ -174,6 +175,34 @@ def main() -> None:
     out["cfg3_int4_zeros"] = sha(z3.numpy())
     (HERE / "baseline_hashes.json").write_text(json.dumps(out, indent=1) + "\n")
     print("wrote fixtures to", HERE)
+
+
+def reference_checkpoints(R) -> None:
+    """Quantized checkpoints written by the reference's own
+    save_quantized_checkpoint (checkpoint.py:71-98): a model with a ``mot``
+    whose FFN is weight-only INT4 (asymmetric g64, and symmetric g64), plus
+    an input and the reference model's output (ReferenceBackend)."""
+    from qi.quantization.checkpoint import save_quantized_checkpoint
+
+    for sym in (False, True):
+        g = torch.Generator().manual_seed(31 + sym)
+        model = torch.nn.Module()
+        model.mot = torch.nn.Module()
+        model.mot.ffn = torch.nn.Sequential(torch.nn.Linear(128, 64), torch.nn.GELU(approximate="tanh"),
+                                            torch.nn.Linear(64, 128))
+        with torch.no_grad():
+            for p in model.mot.parameters():
+                p.copy_(torch.randn(p.shape, generator=g) * (0.05 if p.dim() == 2 else 0.01))
+        cfg = R.WOQ(enabled=True, algo="rtn", bits=4, group_size=64, symmetric=sym, backend="reference")
+        R.swap(model.mot, cfg)
+        model.mot.to(torch.bfloat16)
+        x = torch.randn(5, 128, generator=g).to(torch.bfloat16)
+        with torch.no_grad():
+            y = model.mot.ffn(x)
+        name = f"ckpt_ref_int4_{'sym' if sym else 'asym'}_g64"
+        save_quantized_checkpoint(model, HERE / f"{name}.pt", cfg, source_payload={"optimizer": {"step": 1}},
+                                  source_checkpoint="synthetic")
+        np.savez_compressed(HERE / f"{name}_io.npz", x=bf16_bits(x), y=bf16_bits(y))
 
 
 def fp8_rows(R, t: torch.Tensor):

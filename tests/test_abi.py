@@ -80,3 +80,20 @@ def test_backend_refuses_cpu_tensors():
                   weight_granularity="per_channel")
     with pytest.raises(ValueError):
         get_backend("reference")
+
+
+def test_torch_ops_library_registers_reference_schema():
+    """The compiled torch-operator library loads on the CPU (no kernel runs)
+    and registers qi_int8_w8a8::linear with the reference's schema
+    (bindings.cpp:159-165) and the qi_b200 operators."""
+    import torch
+
+    from qi_b200 import build as B, torch_ops
+
+    B.build_torch_ops()
+    torch_ops.load()
+    schema = str(torch.ops.qi_int8_w8a8.linear.default._schema)
+    assert schema == ("qi_int8_w8a8::linear(Tensor x_bf16_2d, Tensor qweight, Tensor weight_scales, "
+                      "Tensor? bias=None) -> Tensor"), schema
+    for op in ("int8_linear", "fp8_linear", "w4a16_linear"):
+        assert hasattr(torch.ops.qi_b200, op)

@@ -84,7 +84,7 @@ def test_w8a16_default_config_through_cuda_ext(M):
         lin.bias.copy_(torch.randn(N, generator=g) * 0.01)
     model = torch.nn.Module()
     model.ffn = torch.nn.Sequential(lin)
-    cfg = WeightOnlyQuantConfig(enabled=True, backend="cuda_ext")  # bits 8, group 128, symmetric
+    cfg = WeightOnlyQuantConfig(enabled=True, algo="rtn", backend="cuda_ext")  # defaults: bits 8, group 128, symmetric
     replace_linear_with_weight_only(model, cfg)
     layer = model.ffn[0]
     assert layer.qweight.dtype == torch.int8 and layer.bits == 8 and layer.group_size == 128
@@ -95,3 +95,30 @@ def test_w8a16_default_config_through_cuda_ext(M):
     ref = x.double() @ wd.double().T + layer.bias.double().cpu()
     e = O.rel_fro(y.float().cpu().numpy(), ref.numpy())
     assert e <= 2e-3, e
+
+
+@pytest.mark.parametrize("sym", [False, True])
+def test_reference_int4_checkpoint_runs_on_b200(sym):
+    """A weight-only INT4 checkpoint written by the reference's own
+    save_quantized_checkpoint, loaded for the B200 backend (repacked at
+    load), runs the reference model's FFN within the INT4 bound (5e-3) of the
+    reference's own output on the same input."""
+    import torch.nn as nn
+
+    from qi_b200.quantization import load_checkpoint_payload, load_quantized_checkpoint
+
+    name = f"ckpt_ref_int4_{'sym' if sym else 'asym'}_g64"
+    payload = load_checkpoint_payload(GOLD / f"{name}.pt")
+    io = np.load(GOLD / f"{name}_io.npz")
+    model = nn.Module()
+    model.mot = nn.Module()
+    model.mot.ffn = nn.Sequential(nn.Linear(128, 64), nn.GELU(approximate="tanh"), nn.Linear(64, 128))
+    load_quantized_checkpoint(model, payload, backend="b200")
+    model.to(DEV)
+    for m in model.mot.ffn:
+        if getattr(m, "bias", None) is not None:
+            m.bias = m.bias.to(torch.bfloat16)
+    with torch.no_grad():
+        y = model.mot.ffn(from_bits(io["x"]).to(DEV))
+    e = O.rel_fro(O.bf16_to_f32(bits(y)), O.bf16_to_f32(io["y"]))
+    assert e <= 5e-3, e
