@@ -47,7 +47,7 @@ def weights(w: torch.Tensor):
     return packed.to(DEV), sf_atom_layout(sf).to(DEV), g.to(DEV), packed.numpy(), sf.numpy(), float(g)
 
 
-@pytest.mark.parametrize("M,Kd", [(1, 64), (17, 256), (130, 512), (256, 14336 // 4)])
+@pytest.mark.parametrize("M,Kd", [(1, 64), (17, 256), (130, 512), (256, 14336 // 4), (300, 1024), (260, 14336)])
 @pytest.mark.parametrize("mode", [0, 1, 2])
 def test_quantize_nvfp4_bit_exact(M, Kd, mode):
     x, _, _ = make_small_case(M, 8, Kd, seed=M + Kd + mode)
