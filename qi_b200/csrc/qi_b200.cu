@@ -702,31 +702,6 @@ extern "C" int qi_b200_gemm_csk(int kind, const void* A, const void* B, const fl
 // ---------------------------------------------------------------------------
 // NVFP4
 // ---------------------------------------------------------------------------
-// The bulk-ring quantize pass (k_quant_nvfp4_bulk<GMODE>) when the problem
-// has enough rows to fill the GPU and a row fits the ring; false = not used.
-template <int GMODE>
-static bool launch_nvfp4_bulk(const __nv_bfloat16* x, int rows, int cols, const float* g_in,
-                              const unsigned int* amax_bits, float* g_out, uint8_t* q, uint8_t* sf, int ka, int num_sms,
-                              cudaStream_t stream) {
-  const int stride = bulk_row_stride(cols);
-  if (rows < 256 || stride > 96 * 1024) return false;
-  const int stages = std::max(2, std::min(8, (96 * 1024) / stride));
-  const size_t smem = static_cast<size_t>(stages) * stride + stages * 8 + 64;
-  if (cudaFuncSetAttribute(k_quant_nvfp4_bulk<GMODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(smem)) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_quant_nvfp4_bulk<GMODE>, kNvfp4BulkThreads, smem) !=
-          cudaSuccess || per_sm < 1)
-    per_sm = 1;
-  const int grid = std::min(rows, num_sms * per_sm);
-  launch_pdl(k_quant_nvfp4_bulk<GMODE>, dim3(grid), dim3(kNvfp4BulkThreads), smem, stream, 1, x, rows, cols, g_in,
-             amax_bits, g_out, q, sf, ka, stages);
-  return true;
-}
-
 static int nvfp4_quantize(const void* x, int rows, int cols, int g_mode, const float* g_in, unsigned int* ws_amax,
                           float* g_out, void* q, void* sf, cudaStream_t stream) {
   if (rows <= 0 || cols <= 0) return QI_B200_ESHAPE;
@@ -777,20 +752,17 @@ static int nvfp4_quantize(const void* x, int rows, int cols, int g_mode, const f
     if (part == nullptr && cudaMemsetAsync(ws_amax, 0, sizeof(unsigned int), stream) != cudaSuccess)
       return QI_B200_ECUDA;
     launch_pdl(k_amax_bf16, dim3(g2), dim3(256), 0, stream, 1, xb, n, ws_amax, part, ticket);
-    if (!launch_nvfp4_bulk<1>(xb, rows, cols, nullptr, ws_amax, g_out, qb, sb, ka, di->num_sms, stream))
-      launch_pdl(k_quant_nvfp4_tensor<1>, dim3(grid_flat), dim3(256), 0, stream, 1, xb, rows, cols,
-                 static_cast<const float*>(nullptr), static_cast<const unsigned int*>(ws_amax), g_out, qb, sb, ka);
+    launch_pdl(k_quant_nvfp4_tensor<1>, dim3(grid_flat), dim3(256), 0, stream, 1, xb, rows, cols,
+               static_cast<const float*>(nullptr), static_cast<const unsigned int*>(ws_amax), g_out, qb, sb, ka);
     count_launches(2);
   } else if (g_mode == 0) {
-    if (!launch_nvfp4_bulk<0>(xb, rows, cols, g_in, nullptr, nullptr, qb, sb, ka, di->num_sms, stream))
-      launch_pdl(k_quant_nvfp4_tensor<0>, dim3(grid_flat), dim3(256), 0, stream, 1, xb, rows, cols, g_in,
-                 static_cast<const unsigned int*>(nullptr), static_cast<float*>(nullptr), qb, sb, ka);
+    launch_pdl(k_quant_nvfp4_tensor<0>, dim3(grid_flat), dim3(256), 0, stream, 1, xb, rows, cols, g_in,
+               static_cast<const unsigned int*>(nullptr), static_cast<float*>(nullptr), qb, sb, ka);
     count_launches(1);
   } else {
     const int g3 = std::min(rows_pad, di->num_sms * 8);
-    if (!launch_nvfp4_bulk<2>(xb, rows, cols, nullptr, nullptr, g_out, qb, sb, ka, di->num_sms, stream))
-      launch_pdl(k_quant_nvfp4<2>, dim3(g3), dim3(256), 0, stream, 1, xb, rows, cols,
-                 static_cast<const float*>(nullptr), static_cast<const unsigned int*>(nullptr), g_out, qb, sb, ka);
+    launch_pdl(k_quant_nvfp4<2>, dim3(g3), dim3(256), 0, stream, 1, xb, rows, cols,
+               static_cast<const float*>(nullptr), static_cast<const unsigned int*>(nullptr), g_out, qb, sb, ka);
     count_launches(1);
   }
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;

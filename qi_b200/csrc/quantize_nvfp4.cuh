@@ -373,113 +373,4 @@ k_quant_nvfp4(const __nv_bfloat16* __restrict__ x, int rows, int cols, const flo
   }
 }
 
-// ---------------------------------------------------------------------------
-// NVFP4 quantization fed by a bulk-copy row ring (as k_rowquant_bulk): a CTA
-// of 128 threads keeps `stages` whole rows in shared memory with copies in
-// flight while it quantizes the current row, one thread per 4 consecutive
-// 16-element blocks (one 4-byte word of a scale-factor atom row, 32 bytes of
-// codes), with the same per-block arithmetic as k_quant_nvfp4_tensor
-// (nvfp4_block_fast: bit-identical codes and scales).  Rows are taken from the
-// last one down, so with a per-tensor scale the rows that the amax pass read
-// last (still in L2) are read first.  GMODE 0 / 1: per-tensor g (from g_in /
-// from *amax_bits, g_out[0] written); 2: per-row g from the row's amax
-// (g_out[row]).  cols % 64 == 0; the scale words of the padding rows up to
-// the next multiple of 128 are written as zero.
-// ---------------------------------------------------------------------------
-constexpr int kNvfp4BulkThreads = 128;
-
-template <int GMODE>
-__global__ void __launch_bounds__(kNvfp4BulkThreads)
-k_quant_nvfp4_bulk(const __nv_bfloat16* __restrict__ x, int rows, int cols, const float* __restrict__ g_in,
-                   const unsigned int* __restrict__ amax_bits, float* __restrict__ g_out, uint8_t* __restrict__ q,
-                   uint8_t* __restrict__ sf, int ka_per_rowblock, int stages) {
-  extern __shared__ __align__(128) uint8_t nsm[];
-  const int stride = bulk_row_stride(cols);
-  uint64_t* full = reinterpret_cast<uint64_t*>(nsm + static_cast<size_t>(stages) * stride);
-  float* red = reinterpret_cast<float*>(full + stages);  // [kNvfp4BulkThreads / 32]
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(red + kNvfp4BulkThreads / 32);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint32_t row_bytes = static_cast<uint32_t>(cols) * 2u;
-  const int groups = cols >> 6;  // 4 blocks of 16 per group
-  const int rows_pad = (rows + 127) & ~127;
-  if (tid == 0) {
-    for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  __syncthreads();
-  griddep_wait();
-  griddep_launch_dependents();
-  float g = 0.f, g6 = 0.f;
-  float2 rg = make_float2(0.f, 0.f);
-  auto set_g = [&](float gv) {
-    g = gv;
-    g6 = __fmul_rn(6.0f, g);
-    const float rg0 = rcp_approx(g6);
-    rg = make_float2(rg0 * (1.0f - 0x1p-20f), rg0 * (1.0f + 0x1p-20f));
-  };
-  if (GMODE == 0) set_g(__ldg(g_in));
-  if (GMODE == 1) {
-    set_g(nvfp4_g_from_amax(__uint_as_float(*amax_bits)));
-    if (blockIdx.x == 0 && tid == 0) g_out[0] = g;
-  }
-  const int my_rows = rows > static_cast<int>(blockIdx.x) ? (rows - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
-  auto row_of = [&](int i) { return rows - 1 - (static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x)); };
-  auto issue = [&](int i) {
-    uint64_t* bar = &full[i % stages];
-    mbar_expect_tx(bar, row_bytes);
-    bulk_load(nsm + static_cast<size_t>(i % stages) * stride, x + static_cast<long long>(row_of(i)) * cols, row_bytes,
-              bar);
-  };
-  if (tid == 0)
-    for (int i = 0; i < stages && i < my_rows; ++i) issue(i);
-  int i = 0;
-  for (; i < my_rows; ++i) {
-    const int st = i % stages;
-    const bool ok = mbar_wait(&full[st], static_cast<uint32_t>(i / stages) & 1u, abort_flag, kTagRowQuant, 3);
-    if (!__syncthreads_and(ok)) break;
-    const int row = row_of(i);
-    const uint4* rb = reinterpret_cast<const uint4*>(nsm + static_cast<size_t>(st) * stride);
-    if (GMODE == 2) {
-      float m = 0.f;
-      for (int j = tid; j < (cols >> 3); j += kNvfp4BulkThreads) m = fmaxf(m, absmax_bf16x8(rb[j]));
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-      if (lane == 0) red[warp] = m;
-      __syncthreads();
-      m = red[0];
-#pragma unroll
-      for (int w = 1; w < kNvfp4BulkThreads / 32; ++w) m = fmaxf(m, red[w]);
-      set_g(nvfp4_g_from_amax(m));
-      if (tid == 0) g_out[row] = g;
-    }
-    uint2* qrow = reinterpret_cast<uint2*>(q + static_cast<long long>(row) * (cols >> 1));
-    for (int gi = tid; gi < groups; gi += kNvfp4BulkThreads) {
-      uint32_t word = 0;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint8_t sfc;
-        qrow[gi * 4 + j] = nvfp4_block_fast(rb[gi * 8 + 2 * j], rb[gi * 8 + 2 * j + 1], g, g6, rg, sfc);
-        word |= static_cast<uint32_t>(sfc) << (8 * j);
-      }
-      *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(row, gi * 4, ka_per_rowblock)) = word;
-    }
-    __syncthreads();  // the stage (and red[]) are free
-    if (tid == 0 && i + stages < my_rows) {
-      fence_async_shared();
-      issue(i + stages);
-    }
-  }
-  if (i < my_rows) {
-    if (tid == 0)
-      for (int k = i; k < my_rows && k < i + stages; ++k)
-        mbar_wait_drain(&full[k % stages], static_cast<uint32_t>(k / stages) & 1u);
-    return;
-  }
-  // zero scale words of the padding rows
-  for (int pr = rows + static_cast<int>(blockIdx.x); pr < rows_pad; pr += gridDim.x)
-    for (int gi = tid; gi < groups; gi += kNvfp4BulkThreads)
-      *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(pr, gi * 4, ka_per_rowblock)) = 0u;
-}
-
 }  // namespace qib
