@@ -210,9 +210,15 @@ def _nccl_worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_nccl_tensor_parallel_bit_exact(tmp_path):
-    world = 2
+def _gpus(world):
+    return pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < world,
+                              reason=f"needs {world} GPUs")
+
+
+@pytest.mark.parametrize("world", [pytest.param(w, marks=_gpus(w)) for w in (2, 4, 8)])
+def test_nccl_tensor_parallel_bit_exact(world, tmp_path):
+    """Column- and row-parallel INT8 linears and the all-gather fused into the
+    GEMM epilogue, on 2, 4 and 8 GPUs, bit-identical to one GPU."""
     mp.spawn(_nccl_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
     for r in range(world):
         ok, st = (tmp_path / f"rank{r}.txt").read_text().split()
@@ -261,13 +267,12 @@ def _dit_worker(rank, world, port, out_dir, partition):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [pytest.param(w, marks=_gpus(w)) for w in (2, 4, 8)])
 @pytest.mark.parametrize("partition", ["sequence", "heads"])
-def test_nccl_dit_step_bit_exact(partition, tmp_path):
-    """Two GPUs: the DiT step sequence-parallel (video tokens split, K/V
+def test_nccl_dit_step_bit_exact(partition, world, tmp_path):
+    """2, 4 and 8 GPUs: the DiT step sequence-parallel (video tokens split, K/V
     gathered) and head-parallel (config 5's N-sharded QKV / FFN), eager and
     replayed from a CUDA graph, each bit-identical to one GPU."""
-    world = 2
     mp.spawn(_dit_worker, args=(world, _free_port(), str(tmp_path), partition), nprocs=world, join=True)
     for r in range(world):
         ok, st, err = (tmp_path / f"{partition}_rank{r}.txt").read_text().split()
