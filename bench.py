@@ -384,9 +384,21 @@ def measure_linear(cfg_name: str, args, world: int, rank: int, local: int, devic
         from qi_b200.sharding import GATHER_RANK_MAJOR, ColumnShardedLinear
         api_layer = ColumnShardedLinear.from_shard(layer, N, gather=GATHER_RANK_MAJOR)
 
-    def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
-        y_host.copy_(api_layer(x_dev), non_blocking=True)
+    if world == 1:
+        # pinned host rows through HostLinearPipeline: the H2D copy of chunk
+        # i + 1, the linear on chunk i and the D2H copy of chunk i - 1 overlap
+        from qi_b200.pipeline import HostLinearPipeline, plan_chunks, rows_independent
+        pipe = HostLinearPipeline(api_layer)
+        e2e_chunks = len(plan_chunks(M, None, rows_independent(api_layer)))
+
+        def e2e_step():
+            pipe(x_host, out=y_host)
+    else:
+        e2e_chunks = 1
+
+        def e2e_step():
+            x_dev.copy_(x_host, non_blocking=True)
+            y_host.copy_(api_layer(x_dev), non_blocking=True)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
@@ -462,7 +474,8 @@ def measure_linear(cfg_name: str, args, world: int, rank: int, local: int, devic
                        l2=f"{ncopy} rotating input copies ({ncopy * per_copy / 2**20:.0f} MiB > L2)"),
         "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
-                "api": "qi_b200.quantization.WeightOnlyLinear.forward" if world == 1
+                "api": (f"qi_b200.pipeline.HostLinearPipeline over WeightOnlyLinear.forward ({e2e_chunks} row "
+                        "chunks; H2D, linear and D2H on three streams)") if world == 1
                        else ("qi_b200.sharding.PeerGatherLinear.forward" if peer
                              else "qi_b200.sharding.ColumnShardedLinear.forward")},
         "gpu_launches": gpu_launches,

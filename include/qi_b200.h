@@ -227,6 +227,20 @@ int qi_b200_rms_rope_partials(const void* in0, const void* in1, long long ld_in,
                               int nparts, int M, int A, const float* partials, int ranks, float eps,
                               cudaStream_t stream);
 
+/* Attention over a short key sequence (no counterpart in the reference's
+ * own code: the DiT blocks call torch's scaled_dot_product_attention,
+ * wan_video_dit.py:14-23).  Per head h of `heads` (head_dim must be 128):
+ *   O[:, h] = softmax(Q[:, h] K[:, h]^T * scale) V[:, h]
+ * for sq query rows and 1 <= sk <= 256 keys, no mask.  q [sq, ldq], k [sk, ldk]
+ * and o [sq, ldo] hold head h in columns h*128 .. h*128+127; V is passed
+ * transposed, vt [heads*128, ldvt] with row h*128 + d holding V[:, h, d] over
+ * the keys (ldvt >= sk).  bf16 in and out, fp32 scores and accumulation,
+ * probabilities rounded to bf16 before the P V product.  All leading
+ * dimensions multiples of 8, pointers 16-byte aligned. */
+int qi_b200_attention_short(const void* q, long long ldq, const void* k, long long ldk, const void* vt,
+                            long long ldvt, void* o, long long ldo, int sq, int sk, int heads, int head_dim,
+                            float scale, cudaStream_t stream);
+
 /* Per-token FP8: s = max(amax/448, 1e-12), q = e4m3_rn(clamp(x/s, +-448)).
  * Generalises backends/flashrt_fp8_ops.py:38-48 (per tensor) to per row. */
 int qi_b200_quantize_fp8_rowwise(const void* x_bf16, void* q_fp8, float* scales, int rows, int cols,

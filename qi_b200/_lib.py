@@ -68,6 +68,7 @@ SIGNATURES = {
     "qi_b200_resid_ln_quant": [_P, _P, _LL, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _P],
     "qi_b200_rms_rope": [_P, _P, _LL, _P, _P, _LL, _P, _P, _P, _I, _I, _I, _I, _F, _P],
     "qi_b200_rms_head_partials": [_P, _P, _LL, _P, _I, _I, _I, _I, _P],
+    "qi_b200_attention_short": [_P, _LL, _P, _LL, _P, _LL, _P, _LL, _I, _I, _I, _I, _F, _P],
     "qi_b200_rms_rope_partials": [_P, _P, _LL, _P, _P, _LL, _P, _P, _P, _I, _I, _I, _I, _P, _I, _F, _P],
     "qi_b200_int8_epilogue": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
     "qi_b200_quantize_fp8_rowwise": [_P, _P, _P, _I, _I, _P],

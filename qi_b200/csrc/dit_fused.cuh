@@ -154,6 +154,25 @@ __device__ __forceinline__ uint2 quant8(const float (&v)[8], float inv) {
   return make_uint2(b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24), b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24));
 }
 
+// quant8 of 8 bf16 values whose absolute maximum over the row gave
+// inv = rcp_rn(max(amax / 127, 1e-10)): then |v * inv| <= 127.00002, so the
+// pre-clamp of quant8 never acts and is left out; packed fp32x2 products,
+// the same 1.5 * 2^23 rounding, bytes packed with byte permutes.
+__device__ __forceinline__ uint2 quant8_bf16x8(const uint4& u, float inv) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  const float2 inv2 = make_float2(inv, inv), magic = make_float2(12582912.0f, 12582912.0f);
+  int qi[8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 t = __fadd2_rn(__fmul2_rn(__bfloat1622float2(h[e]), inv2), magic);
+    qi[2 * e] = max(-127, min(127, static_cast<int>(__float_as_uint(t.x)) - 0x4B400000));
+    qi[2 * e + 1] = max(-127, min(127, static_cast<int>(__float_as_uint(t.y)) - 0x4B400000));
+  }
+  const uint32_t lo = __byte_perm(__byte_perm(qi[0], qi[1], 0x0040), __byte_perm(qi[2], qi[3], 0x0040), 0x5410);
+  const uint32_t hi = __byte_perm(__byte_perm(qi[4], qi[5], 0x0040), __byte_perm(qi[6], qi[7], 0x0040), 0x5410);
+  return make_uint2(lo, hi);
+}
+
 // R rows per CTA: their loads are all issued before the first reduction and
 // the three block reductions (sum, sum of squares, max) serve all R rows, so
 // a CTA keeps R times the bytes in flight per synchronization.
@@ -423,21 +442,23 @@ __global__ void __launch_bounds__(kWarpRowThreads) k_resid_ln_quant_warp(ResLnPa
     uint4 yu[C];
 #pragma unroll
     for (int c = 0; c < C; ++c) yu[c] = yr[c * 32 + lane];
-    // packed fp32x2 arithmetic: each element rounds as with scalar operations
+    // bf16x2 multiply / add, each rounded once (the _rn forms are never
+    // contracted into an fma): the product of two bf16 values is exact in
+    // fp32 and a bf16 sum rounded directly equals the fp32 sum rounded to
+    // bf16, so these are the reference's bf16(gate * y) and bf16(x + t)
 #pragma unroll
     for (int c = 0; c < C; ++c) {
-      float2 v[4], yv[4];
-      unpack8x2(xu[c], v);
-      unpack8x2(yu[c], yv);
+      __nv_bfloat162* xh = reinterpret_cast<__nv_bfloat162*>(&xu[c]);
+      const __nv_bfloat162* yh = reinterpret_cast<const __nv_bfloat162*>(&yu[c]);
       if (p.gate != nullptr) {
-        float2 g[4];
-        unpack8x2(vecs[c * 32 + lane], g);
+        const uint4 gu = vecs[c * 32 + lane];
+        const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gu);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) yv[e] = round2(__fmul2_rn(g[e], yv[e]));
+        for (int e = 0; e < 4; ++e) xh[e] = __hadd2_rn(xh[e], __hmul2_rn(gh[e], yh[e]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) xh[e] = __hadd2_rn(xh[e], yh[e]);
       }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = __fadd2_rn(v[e], yv[e]);
-      xu[c] = pack8x2(v);
       xr[c * 32 + lane] = xu[c];
     }
   }
@@ -483,16 +504,16 @@ __global__ void __launch_bounds__(kWarpRowThreads) k_resid_ln_quant_warp(ResLnPa
 #pragma unroll
       for (int e = 0; e < 4; ++e) v[e] = __ffma2_rn(v[e], w[e], b[e]);
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = round2(v[e]);
+    xu[c] = pack8x2(v);  // bf16(LayerNorm)
     if (p.mod_scale1 != nullptr) {
-      float2 s1[4], sh[4];
-      unpack8x2(vecs[3 * C * 32 + j], s1);
-      unpack8x2(vecs[4 * C * 32 + j], sh);
+      // bf16(bf16(n * scale1) + shift) in bf16x2 (single roundings, as above)
+      const uint4 su = vecs[3 * C * 32 + j], hu = vecs[4 * C * 32 + j];
+      __nv_bfloat162* nh = reinterpret_cast<__nv_bfloat162*>(&xu[c]);
+      const __nv_bfloat162* s1 = reinterpret_cast<const __nv_bfloat162*>(&su);
+      const __nv_bfloat162* sh = reinterpret_cast<const __nv_bfloat162*>(&hu);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = round2(__fadd2_rn(round2(__fmul2_rn(v[e], s1[e])), sh[e]));
+      for (int e = 0; e < 4; ++e) nh[e] = __hadd2_rn(__hmul2_rn(nh[e], s1[e]), sh[e]);
     }
-    xu[c] = pack8x2_exact(v);
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&xu[c]);
 #pragma unroll
     for (int e = 0; e < 4; ++e) amax2 = __hmax2(amax2, __habs2(h[e]));  // exact: the values are bf16
@@ -506,11 +527,7 @@ __global__ void __launch_bounds__(kWarpRowThreads) k_resid_ln_quant_warp(ResLnPa
   if (lane == 0) p.s[row] = s;
   uint2* qr = reinterpret_cast<uint2*>(p.q + static_cast<long long>(row) * p.D);
 #pragma unroll
-  for (int c = 0; c < C; ++c) {
-    float v[8];
-    unpack8(xu[c], v);
-    qr[c * 32 + lane] = quant8(v, inv);
-  }
+  for (int c = 0; c < C; ++c) qr[c * 32 + lane] = quant8_bf16x8(xu[c], inv);
 }
 
 // The RMSNorm weight is staged in shared memory once per CTA; when a head's
@@ -676,23 +693,37 @@ __global__ void __launch_bounds__(kWarpRowThreads) k_rms_rope_heads(RmsRopeParam
     cs_fixed[0] = tab[0];
     cs_fixed[1] = tab[1];
   }
+  const float2 rr2 = make_float2(rr, rr);
 #pragma unroll
   for (int c = 0; c < C; ++c) {
     const int j = c * 32 + lane;
     if (j >= nvec) continue;
-    float v[8], w[8];
-    unpack8(u[c], v);
-    unpack8(wsm[j], w);
+    // bf16(x * rr) (fp32 product, then bf16), then bf16(n * w): a product of
+    // two bf16 values rounded once, in bf16x2 (never contracted)
+    uint4 nb;
+    {
+      float2 f[4];
+      unpack8x2(u[c], f);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], rr);
-    round8(v);
+      for (int e = 0; e < 4; ++e) f[e] = __fmul2_rn(f[e], rr2);
+      nb = pack8x2(f);
+      const uint4 wu = wsm[j];
+      __nv_bfloat162* nh = reinterpret_cast<__nv_bfloat162*>(&nb);
+      const __nv_bfloat162* wh = reinterpret_cast<const __nv_bfloat162*>(&wu);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], w[e]);
-    round8(v);
-    if (p.rope != nullptr) {
-      const int pair0 = (j * 4) % p.pairs_per_head;
-      const float4* tab = reinterpret_cast<const float4*>(
-          p.rope + (static_cast<long long>(row) * p.pairs_per_head + pair0) * 2);
+      for (int e = 0; e < 4; ++e) nh[e] = __hmul2_rn(nh[e], wh[e]);
+    }
+    if (p.rope == nullptr) {
+      orow[j] = nb;
+      continue;
+    }
+    float v[8];
+    unpack8(nb, v);
+    {
+      const float4* tab = nullptr;
+      if (!rope_fixed)
+        tab = reinterpret_cast<const float4*>(
+            p.rope + (static_cast<long long>(row) * p.pairs_per_head + (j * 4) % p.pairs_per_head) * 2);
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         const float4 cs = rope_fixed ? cs_fixed[i] : tab[i];

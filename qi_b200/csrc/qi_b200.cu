@@ -19,6 +19,7 @@
 #include <atomic>
 #include <mutex>
 
+#include "attn_short.cuh"
 #include "dit_fused.cuh"
 #include "launch_count.cuh"
 #include "gemm_tc.cuh"
@@ -1523,4 +1524,62 @@ extern "C" int qi_b200_int8_linear_noalloc(const void* x_bf16, const void* qweig
   int rc = noalloc_scratch(&q, &scales);
   if (rc) return rc;
   return int8_linear_impl(x_bf16, qweight, weight_scale, bias, out_bf16, q, scales, M, N, K, 0, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Attention over at most 256 keys (head dim 128): k_attn_short
+// ---------------------------------------------------------------------------
+namespace qib {
+template <int NKB>
+static int launch_attn_short(const void* q, long long ldq, const void* k, long long ldk, const void* vt,
+                             long long ldvt, void* o, long long ldo, int sq, int sk, int heads, float scale,
+                             cudaStream_t stream) {
+  using C = AttnCfg<NKB>;
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  CUtensorMap tq, tk, tv;
+  const uint64_t width = static_cast<uint64_t>(heads) * 128;
+  if ((rc = make_tmap_2d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, width, sq, ldq * 2, 64, 128))) return rc;
+  if ((rc = make_tmap_2d(&tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, width, sk, ldk * 2, 64, C::KEYS))) return rc;
+  if ((rc = make_tmap_2d(&tv, vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, sk, width, ldvt * 2, 64, 128))) return rc;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(k_attn_short<NKB>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) !=
+        cudaSuccess)
+      return QI_B200_ECUDA;
+    attr_done[dev] = true;
+  }
+  AttnParams p;
+  p.o = static_cast<__nv_bfloat16*>(o);
+  p.ldo = ldo;
+  p.sq = sq;
+  p.sk = sk;
+  p.heads = heads;
+  p.scale_log2e = scale * 1.4426950408889634f;
+  const int items = heads * ((sq + 127) / 128);
+  const int per_sm = NKB == 1 ? 2 : 1;  // shared memory (96 / 160 KB) and TMEM (256 / 512 columns)
+  const int grid = std::min(items, di->num_sms * per_sm);
+  launch_pdl(k_attn_short<NKB>, dim3(grid), dim3(kAttnThreads), C::SMEM_BYTES, stream, 1, tq, tk, tv, p);
+  count_launches(1);
+  return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
+}
+}  // namespace qib
+
+extern "C" int qi_b200_attention_short(const void* q, long long ldq, const void* k, long long ldk, const void* vt,
+                                       long long ldvt, void* o, long long ldo, int sq, int sk, int heads,
+                                       int head_dim, float scale, cudaStream_t stream) {
+  using namespace qib;
+  if (q == nullptr || k == nullptr || vt == nullptr || o == nullptr) return QI_B200_EINVAL;
+  if (head_dim != 128 || heads <= 0 || sq < 0 || sk < 1 || sk > 256) return QI_B200_ESHAPE;
+  if (sq == 0) return QI_B200_OK;
+  const long long width = static_cast<long long>(heads) * 128;
+  if (ldq < width || ldk < width || ldo < width || ldvt < sk) return QI_B200_ESHAPE;
+  if (ldq % 8 || ldk % 8 || ldo % 8 || ldvt % 8) return QI_B200_EALIGN;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(vt) || !aligned16(o)) return QI_B200_EALIGN;
+  if (!(scale > 0.0f)) return QI_B200_EINVAL;
+  return sk <= 128 ? launch_attn_short<1>(q, ldq, k, ldk, vt, ldvt, o, ldo, sq, sk, heads, scale, stream)
+                   : launch_attn_short<2>(q, ldq, k, ldk, vt, ldvt, o, ldo, sq, sk, heads, scale, stream);
 }

@@ -595,7 +595,7 @@ class DiTStepRunner:
         ckv = self._gemm(*ctxq[n], tp.ckv)
         cqn = self._norm_heads([cq], [tp.cnq], None, g, eps)[0]
         ckn = self._norm_heads([ckv[:, :al]], [tp.cnk], None, g, eps)[0]
-        ca = attention(cqn.unsqueeze(0), ckn.unsqueeze(0), ckv[:, al:].unsqueeze(0), hl)
+        ca = self._attn_short(cqn, ckn, ckv[:, al:], heads=hl)
         y_co = self._row_parallel(ca.reshape(-1, al), tp.co, g)
         q8, s8 = K.resid_ln_quant(x[n], y_co, mod_scale1=sc1[n][li, 1], mod_shift=m[3], eps=eps)
         f = self._gemm(q8, s8, tp.f0, gelu=True)
@@ -630,7 +630,7 @@ class DiTStepRunner:
                 side.wait_stream(main)
             with (torch.cuda.stream(side) if cuda else _nullctx()):
                 qa, ka, va = self._tp_pre(ac_name, li, x, y_ffn, mods, sc1, rope)
-                att_a = attention(qa, torch.cat([kf, ka], 1), torch.cat([vf, va], 1), hl)
+                att_a = self._attn_short(qa, torch.cat([kf, ka], 1), torch.cat([vf, va], 1), heads=hl)
                 self._tp_post(ac_name, li, att_a, x, y_ffn, mods, sc1, ctxq)
             if cuda:
                 kf.record_stream(side)
@@ -664,7 +664,35 @@ class DiTStepRunner:
         qn, kn = K.rms_rope([qkv[:, :a], qkv[:, a:2 * a]], [p.nq.weight, p.nk.weight], rope[n], hd, eps)
         return qn.unsqueeze(0), kn.unsqueeze(0), qkv[:, 2 * a:].unsqueeze(0), qkv
 
-    def _post(self, n, li, att, x, y_ffn, mods, sc1, ctxq):
+    def _ctx_kv(self, n, li, ctxq):
+        """Cross-attention K (RMSNorm) and V^T of layer ``li``: they depend on
+        the context tokens only, so they run ahead of the layer on the side
+        stream."""
+        K, cfg = self.K, self.cfg
+        a = cfg.attn_dim
+        ckv = self._gemm(*ctxq[n], self.plans[n][li].ckv)
+        ck = K.rms_rope([ckv[:, :a]], [self.plans[n][li].cnk.weight], None, cfg.head_dim, cfg.eps)[0]
+        return ck, ckv[:, a:].t().contiguous()
+
+    def _attn_short(self, q, k, v=None, heads=None, vt=None, out=None):
+        """softmax(q k^T / sqrt(d)) v over at most 256 keys on the tensor cores
+        (``attention_short``): the cross-attention over the context tokens, the
+        first-frame recompute and the action queries.  q [.., Sq, W],
+        k [.., Sk, W], v [.., Sk, W] (or vt = V^T [W, Sk]); rows may be strided."""
+        h = self.cfg.heads if heads is None else heads
+        w = q.shape[-1]
+        if self.cfg.head_dim != 128:  # the kernel's head dim; other configs (small tests) use SDPA
+            v2 = v.reshape(-1, w) if v is not None else vt.t()
+            o = attention(q.reshape(1, -1, w), k.reshape(1, -1, w), v2.unsqueeze(0), h)[0]
+            if out is not None:
+                out.copy_(o)
+        else:
+            if vt is None:
+                vt = v.reshape(-1, w).t().contiguous()
+            o = self.K.attention_short(q.reshape(-1, w), k.reshape(-1, w), vt, h, out=out)
+        return o.unsqueeze(0) if q.dim() == 3 else o
+
+    def _post(self, n, li, att, x, y_ffn, mods, sc1, ctxq, ctx_kv=None):
         """o GEMM + gate-residual + norm3 -> cross-attention -> norm2 + FFN."""
         K, cfg = self.K, self.cfg
         h, a, hd, eps = cfg.heads, cfg.attn_dim, cfg.head_dim, cfg.eps
@@ -672,9 +700,8 @@ class DiTStepRunner:
         y_o = K.int8_linear(att.reshape(-1, a), *p.o)
         q8, s8 = K.resid_ln_quant(x[n], y_o, gate=m[2], ln_w=p.norm3.weight, ln_b=p.norm3.bias, eps=eps)
         cq = K.rms_rope([self._gemm(q8, s8, p.cq)], [p.cnq.weight], None, hd, eps)[0]
-        ckv = self._gemm(*ctxq[n], p.ckv)
-        ck = K.rms_rope([ckv[:, :a]], [p.cnk.weight], None, hd, eps)[0]
-        ca = attention(cq.unsqueeze(0), ck.unsqueeze(0), ckv[:, a:].unsqueeze(0), h)
+        ck, cvt = self._ctx_kv(n, li, ctxq) if ctx_kv is None else ctx_kv
+        ca = self._attn_short(cq, ck, vt=cvt)
         y_co = K.int8_linear(ca.reshape(-1, a), *p.co)
         q8, s8 = K.resid_ln_quant(x[n], y_co, mod_scale1=sc1[n][li, 1], mod_shift=m[3], eps=eps)
         f = self._gemm(q8, s8, p.f0, gelu=True)
@@ -691,7 +718,7 @@ class DiTStepRunner:
         nf = max(0, min(t - self.video_offset, q.shape[1]))
         out = attention(q, k, v, h)
         if nf > 0 and sv > t:
-            out[:, :nf] = attention(q[:, :nf], k[:, :t], v[:, :t], h)
+            self._attn_short(q[:, :nf], k[:, :t], v[:, :t], heads=h, out=out[0, :nf])
         return out
 
     def _step_fused(self, tokens, rope, ctx, t_mod):
@@ -704,7 +731,10 @@ class DiTStepRunner:
         The action expert runs on a second stream.  It joins the video
         stream once per layer, after the video K/V exist, because action
         queries attend first-frame video keys; video never attends action
-        tokens.  Its small launches then overlap the video GEMMs."""
+        tokens.  Its small launches then overlap the video GEMMs.  The side
+        stream also computes both experts' cross-attention K / V one layer
+        ahead (they depend on the context tokens only), so the video stream
+        only waits on an event for them."""
         K, cfg = self.K, self.cfg
         x = {n: t.reshape(-1, t.shape[-1]).clone() for n, t in tokens.items()}
         mods, sc1, ctxq = {}, {}, {}
@@ -717,20 +747,37 @@ class DiTStepRunner:
         side.wait_stream(main)
         t = min(cfg.tokens_per_frame, cfg.experts[0].tokens)
         y_ffn = {}
+        ckv, ckv_ready = {}, {}
+
+        def ctx_kv_ahead(li):  # on the side stream
+            for n in self.names:
+                ckv[n, li] = self._ctx_kv(n, li, ctxq)
+            ckv_ready[li] = torch.cuda.Event()
+            ckv_ready[li].record(side)
+
+        with torch.cuda.stream(side):
+            ctx_kv_ahead(0)
         for li in range(cfg.layers):
             qv, kv, vv, qkv_v = self._pre("video", li, x, y_ffn, mods, sc1, rope)
             if self.world > 1:
                 kv, vv = self._gather_video_kv(kv, vv)
-            kf, vf = kv[:, :t].contiguous(), vv[:, :t].contiguous()   # first-frame keys for the action queries
             side.wait_stream(main)
             with torch.cuda.stream(side):
+                # the action queries attend the first-frame video keys and their own;
+                # the copies that join them run here, off the video stream
                 qa, ka, va, _ = self._pre("action", li, x, y_ffn, mods, sc1, rope)
-                att_a = attention(qa, torch.cat([kf, ka], 1), torch.cat([vf, va], 1), cfg.heads)
-                self._post("action", li, att_a, x, y_ffn, mods, sc1, ctxq)
-            kf.record_stream(side)
-            vf.record_stream(side)
+                att_a = self._attn_short(qa, torch.cat([kv[:, :t], ka], 1), torch.cat([vv[:, :t], va], 1))
+                self._post("action", li, att_a, x, y_ffn, mods, sc1, ctxq, ckv.pop(("action", li)))
+                if li + 1 < cfg.layers:
+                    ctx_kv_ahead(li + 1)
+            kv.record_stream(side)
+            vv.record_stream(side)  # a view: records the fused QKV output (or the gathered K/V) it lives in
             att_v = self._video_attention(qv, kv, vv)
-            self._post("video", li, att_v, x, y_ffn, mods, sc1, ctxq)
+            main.wait_event(ckv_ready.pop(li))
+            ck, cvt = ckv.pop(("video", li))
+            ck.record_stream(main)
+            cvt.record_stream(main)
+            self._post("video", li, att_v, x, y_ffn, mods, sc1, ctxq, (ck, cvt))
         with torch.cuda.stream(side):
             K.resid_ln_quant(x["action"], y_ffn["action"], gate=mods["action"][cfg.layers - 1][5], quant=False)
         K.resid_ln_quant(x["video"], y_ffn["video"], gate=mods["video"][cfg.layers - 1][5], quant=False)

@@ -147,6 +147,36 @@ def rms_rope(inputs, weights, rope: torch.Tensor | None, head_dim: int, eps: flo
     return outs
 
 
+def attention_short(q: torch.Tensor, k: torch.Tensor, vt: torch.Tensor, heads: int,
+                    scale: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """softmax(Q K^T * scale) V per head for at most 256 keys, head dim 128,
+    on the tensor cores (``qi_b200_attention_short``).  ``q`` [Sq, H*128] and
+    ``k`` [Sk, H*128] (row strides may exceed H*128), ``vt`` = V transposed,
+    [H*128, Sk] (copied into a padded buffer when its row stride is not a
+    multiple of 8 elements).  Returns
+    [Sq, H*128] bf16 (or writes ``out``).  Default scale 1/sqrt(128), the
+    default of torch's scaled_dot_product_attention."""
+    for t, name in ((q, "q"), (k, "k"), (vt, "vt")):
+        if t.dtype != torch.bfloat16 or t.dim() != 2 or t.stride(1) != 1 or not t.is_cuda:
+            raise ValueError(f"attention_short: {name} must be a 2-D bf16 CUDA tensor with unit column stride.")
+    width = heads * 128
+    sq, sk = q.shape[0], k.shape[0]
+    if q.shape[1] != width or k.shape[1] != width or vt.shape != (width, sk):
+        raise ValueError(f"attention_short: q, k must be [S, {width}] and vt [{width}, Sk].")
+    if vt.stride(0) % 8:  # TMA rows start on 16-byte boundaries: pad the key dimension
+        padded = torch.zeros((width, (sk + 7) // 8 * 8), dtype=torch.bfloat16, device=vt.device)
+        padded[:, :sk] = vt
+        vt = padded[:, :sk]
+    if out is None:
+        out = torch.empty((sq, width), dtype=torch.bfloat16, device=q.device)
+    elif out.dtype != torch.bfloat16 or out.shape != (sq, width) or out.stride(1) != 1:
+        raise ValueError("attention_short: out must be bf16 [Sq, H*128] with unit column stride.")
+    _lib.call("qi_b200_attention_short", _ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(vt), vt.stride(0),
+              _ptr(out), out.stride(0), sq, sk, int(heads), 128,
+              float(128 ** -0.5 if scale is None else scale), _stream(q.device))
+    return out
+
+
 def rms_head_partials(inputs, head_dim: int) -> torch.Tensor:
     """Per-head sums of squares of one or two [M, A] bf16 row blocks (a
     rank's contiguous range of whole heads): fp32 [nparts, M, A / head_dim]."""

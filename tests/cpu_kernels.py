@@ -102,3 +102,21 @@ def rms_rope_partials(inputs, weights, rope, head_dim, partials, eps=1e-6, outs=
             v = torch.stack([e * c - o * sn, e * sn + o * c], -1).reshape(m, -1)
         outs.append(v.to(torch.bfloat16))
     return outs
+
+
+def attention_short(q, k, vt, heads, scale=None, out=None):
+    """CPU stand-in of the short-key attention: fp32 scores, row max, exp,
+    probabilities rounded to bf16, their fp32 sum, P V / sum -> bf16."""
+    sq, sk = q.shape[0], k.shape[0]
+    hd = q.shape[1] // heads
+    scale = hd ** -0.5 if scale is None else scale
+    qh = q.float().view(sq, heads, hd).transpose(0, 1)
+    kh = k.float().view(sk, heads, hd).transpose(0, 1)
+    vh = vt.float().reshape(heads, hd, sk).transpose(1, 2)
+    s = torch.bmm(qh, kh.transpose(1, 2)) * scale
+    p = torch.exp(s - s.amax(-1, keepdim=True)).to(torch.bfloat16).float()
+    o = (torch.bmm(p, vh) / p.sum(-1, keepdim=True)).transpose(0, 1).reshape(sq, heads * hd).to(torch.bfloat16)
+    if out is not None:
+        out.copy_(o)
+        return out
+    return o

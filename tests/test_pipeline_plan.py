@@ -1,0 +1,47 @@
+"""CPU: row-chunk planning of ``HostLinearPipeline`` and which activation
+formats may be chunked (rows independent)."""
+
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+from qi_b200.pipeline import plan_chunks, rows_independent
+
+
+def test_plan_chunks_cover_rows_in_order():
+    for rows in (1, 255, 256, 257, 1000, 3120, 4096, 10000):
+        for chunk in (None, 1, 64, 256, 5000):
+            ch = plan_chunks(rows, chunk, True)
+            assert ch[0][0] == 0 and ch[-1][1] == rows
+            assert all(a[1] == b[0] for a, b in zip(ch, ch[1:]))
+            assert all(r1 > r0 for r0, r1 in ch)
+            if chunk is not None:
+                assert all(r1 - r0 == chunk for r0, r1 in ch[:-1])
+
+
+def test_plan_chunks_defaults():
+    assert plan_chunks(4096, None, True) == [(i * 512, (i + 1) * 512) for i in range(8)]
+    assert plan_chunks(512, None, True) == [(0, 256), (256, 512)]
+    assert plan_chunks(16, None, True) == [(0, 16)]
+    assert plan_chunks(4096, 128, False) == [(0, 4096)]
+    assert plan_chunks(0, None, True) == []
+    with pytest.raises(ValueError):
+        plan_chunks(10, 0, True)
+
+
+def _fake(packed_dtype=None, sf=False, g=False, act_scale=None, gran=None):
+    return SimpleNamespace(
+        qweight_packed=None if packed_dtype is None else torch.zeros(1, dtype=packed_dtype),
+        scale_factors=torch.zeros(1, dtype=torch.uint8) if sf else None,
+        weight_global_scale=torch.ones(1) if g else None,
+        activation_scale=act_scale, activation_granularity=gran)
+
+
+def test_rows_independent_formats():
+    assert rows_independent(_fake())                                  # INT8 / FP8 / weight-only
+    assert rows_independent(_fake(torch.int32))                       # W4A16 packed
+    assert rows_independent(_fake(torch.uint8))                       # FP8 stored in qweight_packed
+    assert not rows_independent(_fake(torch.uint8, sf=True, g=True))  # NVFP4, dynamic per tensor
+    assert rows_independent(_fake(torch.uint8, sf=True, g=True, gran="per_token"))
+    assert rows_independent(_fake(torch.uint8, sf=True, g=True, act_scale=torch.ones(1)))
