@@ -262,9 +262,9 @@ def measure_linear(cfg_name: str, args, world: int, rank: int, local: int, devic
     if w4_dequant:
         launches_per_step = 2  # weights dequantized once into a workspace, then the bf16 GEMM
     # N > 1, INT8/FP8: the all-gather fused into the GEMM epilogue (peer stores over NVLink)
-    # auto: the fused gather where it has been validated on the GPU (2 ranks);
-    # NCCL's all-gather beyond that
-    gather = args.gather if args.gather != "auto" else ("peer" if world == 2 else "nccl")
+    # auto: the fused gather where it has been validated on the GPU (2 and 4
+    # ranks: 2x NCCL's all-gather after the GEMM at 4); NCCL beyond that
+    gather = args.gather if args.gather != "auto" else ("peer" if world in (2, 4) else "nccl")
     peer = world > 1 and gather == "peer" and c["kind"] in ("fp8", "int8")
     peer_api = None
     if peer:
@@ -389,7 +389,7 @@ def measure_linear(cfg_name: str, args, world: int, rank: int, local: int, devic
         # i + 1, the linear on chunk i and the D2H copy of chunk i - 1 overlap
         from qi_b200.pipeline import HostLinearPipeline, plan_chunks, rows_independent
         pipe = HostLinearPipeline(api_layer)
-        e2e_chunks = len(plan_chunks(M, None, rows_independent(api_layer)))
+        e2e_chunks = len(plan_chunks(M, None, rows_independent(api_layer), row_bytes=2 * (Kd + N)))
 
         def e2e_step():
             pipe(x_host, out=y_host)
@@ -595,8 +595,13 @@ def measure_dit(args, world: int, rank: int, local: int, device, partition: str 
     k1.record(stream)
     torch.cuda.synchronize(device)
     gemm_ms = k0.elapsed_time(k1) / 20
-    hbm_gbs, bf16_tf, src = peaks()
+    del g
     m_l = runner.video_local
+    # release the step's CUDA graph now: at N > 1 it holds NCCL calls, and a
+    # graph still alive at destroy_process_group makes the exit wait
+    runner.graph = None
+    torch.cuda.synchronize(device)
+    hbm_gbs, bf16_tf, src = peaks()
     gemm_ops = 2.0 * m_l * w0.shape[0] * w0.shape[1]
     achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(2 * bf16_tf, 1),
@@ -631,8 +636,6 @@ def measure_dit(args, world: int, rank: int, local: int, device, partition: str 
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = dit_cpu_baseline()
-    runner.graph = None
-    del g
     return result
 
 

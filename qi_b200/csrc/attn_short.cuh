@@ -18,7 +18,8 @@
 //             shared memory in the swizzled K-major layout the MMA reads (over
 //             the dead Q or K tile), and the row sum of the rounded p;
 //   thread 0: O = P V (V^T as the K-major B operand) into TMEM;
-//   4 warps:  O / sum -> bf16 -> global.
+//   4 warps:  O / sum -> bf16 into a swizzled staging tile; thread 0 stores it
+//             with TMA (asynchronous: it overlaps the next item's loads).
 // Every wait is bounded; an expired wait records the error, raises the CTA's
 // abort flag and the CTA drains its copies / MMAs and exits.
 #pragma once
@@ -51,8 +52,6 @@ struct AttnCfg {
 };
 
 struct AttnParams {
-  __nv_bfloat16* o;
-  long long ldo;
   int sq, sk, heads;
   float scale_log2e;  // softmax scale * log2(e)
 };
@@ -63,10 +62,42 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// p = 2^(s * scale_log2e + off) of 32 scores (keys c .. c+31), masked beyond
+// sk, rounded to bf16 and packed in pairs; returns their fp32 sum.
+__device__ __forceinline__ float attn_p32(const uint32_t (&r)[32], int c, int sk, float sl2e, float off,
+                                          uint32_t (&pk)[16]) {
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float e0 = (c + 2 * i < sk) ? ex2_approx(fmaf(__uint_as_float(r[2 * i]), sl2e, off)) : 0.f;
+    const float e1 = (c + 2 * i + 1 < sk) ? ex2_approx(fmaf(__uint_as_float(r[2 * i + 1]), sl2e, off)) : 0.f;
+    const __nv_bfloat162 b = __floats2bfloat162_rn(e0, e1);
+    const float2 f = __bfloat1622float2(b);
+    sum += f.x;
+    sum += f.y;
+    pk[i] = *reinterpret_cast<const uint32_t*>(&b);
+  }
+  return sum;
+}
+
+// 16 packed words (32 bf16 of columns c .. c+31 of `row`) into a tile of
+// 64-column, 128-row, 128-byte-swizzled regions (the layout TMA and the MMA
+// descriptors use).
+__device__ __forceinline__ void st_sw128_32(uint8_t* tile, int row, int c, const uint32_t (&pk)[16]) {
+  uint8_t* prow = tile + (c >> 6) * (128 * 128) + row * 128;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int chunk = ((c & 63) >> 3) + q;
+    *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) =
+        make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+  }
+}
+
 template <int NKB>
 __global__ void __launch_bounds__(kAttnThreads)
 k_attn_short(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-             const __grid_constant__ CUtensorMap tmVt, const AttnParams p) {
+             const __grid_constant__ CUtensorMap tmVt, const __grid_constant__ CUtensorMap tmO,
+             const AttnParams p) {
   using C = AttnCfg<NKB>;
   extern __shared__ uint8_t attn_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(attn_raw) + 1023) & ~uintptr_t(1023));
@@ -74,6 +105,7 @@ k_attn_short(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
   uint8_t* sK = sQ + C::Q_BYTES;
   uint8_t* sVt = sK + C::K_BYTES;
   uint8_t* sP = NKB == 1 ? sQ : sK;
+  uint8_t* sO = NKB == 1 ? sK : sQ;  // bf16 O staging for the TMA store: the tile P does not hold
   uint64_t* full = reinterpret_cast<uint64_t*>(sVt + C::VT_BYTES);
   uint64_t* sdone = full + 1;
   uint64_t* odone = full + 2;
@@ -92,6 +124,7 @@ k_attn_short(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     tma_prefetch_map(&tmQ);
     tma_prefetch_map(&tmK);
     tma_prefetch_map(&tmVt);
+    tma_prefetch_map(&tmO);
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -116,6 +149,7 @@ k_attn_short(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
   for (int item = blockIdx.x; item < items; item += gridDim.x, phase ^= 1u) {
     const int h = item / q_tiles, m0 = (item - h * q_tiles) * 128;
     if (threadIdx.x == 0) {
+      bulk_wait_read_all();  // the previous item's O store has read its staging tile
       mbar_expect_tx(full, kTxBytes);
 #pragma unroll
       for (int kb = 0; kb < 2; ++kb) {
@@ -142,43 +176,47 @@ k_attn_short(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     if (!mbar_wait(sdone, phase, abort_flag, kTagAttn, 2)) { ok = false; break; }
     tc_fence_after();
 
-    // ---- softmax of this thread's row: max, then 2^(..) as bf16 into P, sum of the rounded values
-    float mx = -INFINITY;
-#pragma unroll 1
-    for (int c = 0; c < C::KEYS; c += 32) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(t_row + C::S_COL + c, r);
-      tmem_ld_wait();
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (c + i < p.sk) mx = fmaxf(mx, __uint_as_float(r[i]));
-    }
-    const float off = -mx * p.scale_log2e;
+    // ---- softmax of this thread's row: max, then 2^(..) as bf16 into P (swizzled),
+    // the fp32 sum of the rounded values.  One key block: the 128 scores stay in
+    // registers (one TMEM pass); two: max pass, then exp pass.
     float sum = 0.f;
-#pragma unroll 1
-    for (int c = 0; c < C::KEYS; c += 32) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(t_row + C::S_COL + c, r);
+    if constexpr (NKB == 1) {
+      uint32_t r[4][32];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) tmem_ld_32x32b_x32(t_row + C::S_COL + 32 * b, r[b]);
       tmem_ld_wait();
-      uint32_t pk[16];
+      float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float e0 = (c + 2 * i < p.sk) ? ex2_approx(fmaf(__uint_as_float(r[2 * i]), p.scale_log2e, off)) : 0.f;
-        const float e1 =
-            (c + 2 * i + 1 < p.sk) ? ex2_approx(fmaf(__uint_as_float(r[2 * i + 1]), p.scale_log2e, off)) : 0.f;
-        const __nv_bfloat162 b = __floats2bfloat162_rn(e0, e1);
-        const float2 f = __bfloat1622float2(b);
-        sum += f.x;
-        sum += f.y;
-        pk[i] = *reinterpret_cast<const uint32_t*>(&b);
+      for (int b = 0; b < 4; ++b)
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (32 * b + i < p.sk) mx = fmaxf(mx, __uint_as_float(r[b][i]));
+      const float off = -mx * p.scale_log2e;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        uint32_t pk[16];
+        sum += attn_p32(r[b], 32 * b, p.sk, p.scale_log2e, off, pk);
+        st_sw128_32(sP, row, 32 * b, pk);
       }
-      // keys c .. c+31: key block c / 64, 16-byte chunks (c % 64) / 8 .. +3 of this row, swizzled
-      uint8_t* prow = sP + (c >> 6) * (128 * 128) + row * 128;
+    } else {
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < C::KEYS; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + C::S_COL + c, r);
+        tmem_ld_wait();
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int chunk = ((c & 63) >> 3) + q;
-        *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) =
-            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        for (int i = 0; i < 32; ++i)
+          if (c + i < p.sk) mx = fmaxf(mx, __uint_as_float(r[i]));
+      }
+      const float off = -mx * p.scale_log2e;
+#pragma unroll 1
+      for (int c = 0; c < C::KEYS; c += 32) {
+        uint32_t r[32], pk[16];
+        tmem_ld_32x32b_x32(t_row + C::S_COL + c, r);
+        tmem_ld_wait();
+        sum += attn_p32(r, c, p.sk, p.scale_log2e, off, pk);
+        st_sw128_32(sP, row, c, pk);
       }
     }
     fence_async_shared();  // P (generic-proxy writes) visible to the tensor core
@@ -198,33 +236,37 @@ k_attn_short(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     if (!mbar_wait(odone, phase, abort_flag, kTagAttn, 3)) { ok = false; break; }
     tc_fence_after();
 
-    // ---- O / sum -> bf16 -> global (row m0 + row, columns h*128 ..)
+    // ---- O / sum -> bf16 into the staging tile (swizzled), then one TMA store
+    // of the 128 x 128 tile at (row m0, column h*128); rows past sq are clipped
     const float inv = 1.0f / sum;
-    const int m = m0 + row;
-#pragma unroll 1
-    for (int c = 0; c < 128; c += 32) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(t_row + C::O_COL + c, r);
+    {
+      uint32_t r[4][32];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) tmem_ld_32x32b_x32(t_row + C::O_COL + 32 * b, r[b]);
       tmem_ld_wait();
-      if (m < p.sq) {
-        uint4* dst = reinterpret_cast<uint4*>(p.o + static_cast<long long>(m) * p.ldo + h * 128 + c);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t w[4];
+      for (int b = 0; b < 4; ++b) {
+        uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(r[8 * q + 2 * i]) * inv,
-                                                           __uint_as_float(r[8 * q + 2 * i + 1]) * inv);
-            w[i] = *reinterpret_cast<const uint32_t*>(&b);
-          }
-          dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int i = 0; i < 16; ++i) {
+          const __nv_bfloat162 v = __floats2bfloat162_rn(__uint_as_float(r[b][2 * i]) * inv,
+                                                         __uint_as_float(r[b][2 * i + 1]) * inv);
+          pk[i] = *reinterpret_cast<const uint32_t*>(&v);
         }
+        st_sw128_32(sO, row, 32 * b, pk);
       }
     }
+    fence_async_shared();  // the staging tile (generic-proxy writes) visible to the TMA store
     // S / O columns and the Q, K, V^T tiles are free for the next item
     tc_fence_before();
     __syncthreads();
+    if (threadIdx.x == 0) {
+#pragma unroll
+      for (int b = 0; b < 2; ++b) tma_store_2d(&tmO, sO + b * 128 * 128, h * 128 + b * 64, m0);
+      bulk_commit_group();
+    }
   }
+  if (threadIdx.x == 0) bulk_wait_all();  // the stores have landed before the CTA exits
   if (!ok && threadIdx.x == 0) {
     // drain: the last item's copies and any MMA still in flight
     if (issued > 0) mbar_wait_drain(full, phase);

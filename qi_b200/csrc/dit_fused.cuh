@@ -155,18 +155,23 @@ __device__ __forceinline__ uint2 quant8(const float (&v)[8], float inv) {
 }
 
 // quant8 of 8 bf16 values whose absolute maximum over the row gave
-// inv = rcp_rn(max(amax / 127, 1e-10)): then |v * inv| <= 127.00002, so the
-// pre-clamp of quant8 never acts and is left out; packed fp32x2 products,
-// the same 1.5 * 2^23 rounding, bytes packed with byte permutes.
+// inv = rcp_rn(max(amax / 127, 1e-10)): then |v * inv| <= 127.00002, so of
+// quant8's clamps only the lower float bound is kept, and only because it
+// keeps the product and the 1.5 * 2^23 rounding add two roundings (without
+// an operation between them the compiler may fuse them into one fma, which
+// rounds differently at ties).  Packed fp32x2 products, bytes packed with
+// byte permutes.
 __device__ __forceinline__ uint2 quant8_bf16x8(const uint4& u, float inv) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
   const float2 inv2 = make_float2(inv, inv), magic = make_float2(12582912.0f, 12582912.0f);
   int qi[8];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    const float2 t = __fadd2_rn(__fmul2_rn(__bfloat1622float2(h[e]), inv2), magic);
-    qi[2 * e] = max(-127, min(127, static_cast<int>(__float_as_uint(t.x)) - 0x4B400000));
-    qi[2 * e + 1] = max(-127, min(127, static_cast<int>(__float_as_uint(t.y)) - 0x4B400000));
+    float2 t = __fmul2_rn(__bfloat1622float2(h[e]), inv2);
+    t = make_float2(fmaxf(t.x, -128.0f), fmaxf(t.y, -128.0f));
+    t = __fadd2_rn(t, magic);
+    qi[2 * e] = max(-127, static_cast<int>(__float_as_uint(t.x)) - 0x4B400000);
+    qi[2 * e + 1] = max(-127, static_cast<int>(__float_as_uint(t.y)) - 0x4B400000);
   }
   const uint32_t lo = __byte_perm(__byte_perm(qi[0], qi[1], 0x0040), __byte_perm(qi[2], qi[3], 0x0040), 0x5410);
   const uint32_t hi = __byte_perm(__byte_perm(qi[4], qi[5], 0x0040), __byte_perm(qi[6], qi[7], 0x0040), 0x5410);

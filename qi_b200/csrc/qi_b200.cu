@@ -1538,11 +1538,12 @@ static int launch_attn_short(const void* q, long long ldq, const void* k, long l
   DeviceInfo* di = nullptr;
   int rc = device_info(&di);
   if (rc) return rc;
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   const uint64_t width = static_cast<uint64_t>(heads) * 128;
   if ((rc = make_tmap_2d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, width, sq, ldq * 2, 64, 128))) return rc;
   if ((rc = make_tmap_2d(&tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, width, sk, ldk * 2, 64, C::KEYS))) return rc;
   if ((rc = make_tmap_2d(&tv, vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, sk, width, ldvt * 2, 64, 128))) return rc;
+  if ((rc = make_tmap_2d(&to, o, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, width, sq, ldo * 2, 64, 128))) return rc;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1553,8 +1554,6 @@ static int launch_attn_short(const void* q, long long ldq, const void* k, long l
     attr_done[dev] = true;
   }
   AttnParams p;
-  p.o = static_cast<__nv_bfloat16*>(o);
-  p.ldo = ldo;
   p.sq = sq;
   p.sk = sk;
   p.heads = heads;
@@ -1562,7 +1561,7 @@ static int launch_attn_short(const void* q, long long ldq, const void* k, long l
   const int items = heads * ((sq + 127) / 128);
   const int per_sm = NKB == 1 ? 2 : 1;  // shared memory (96 / 160 KB) and TMEM (256 / 512 columns)
   const int grid = std::min(items, di->num_sms * per_sm);
-  launch_pdl(k_attn_short<NKB>, dim3(grid), dim3(kAttnThreads), C::SMEM_BYTES, stream, 1, tq, tk, tv, p);
+  launch_pdl(k_attn_short<NKB>, dim3(grid), dim3(kAttnThreads), C::SMEM_BYTES, stream, 1, tq, tk, tv, to, p);
   count_launches(1);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }

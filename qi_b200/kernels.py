@@ -157,7 +157,7 @@ def attention_short(q: torch.Tensor, k: torch.Tensor, vt: torch.Tensor, heads: i
     [Sq, H*128] bf16 (or writes ``out``).  Default scale 1/sqrt(128), the
     default of torch's scaled_dot_product_attention."""
     for t, name in ((q, "q"), (k, "k"), (vt, "vt")):
-        if t.dtype != torch.bfloat16 or t.dim() != 2 or t.stride(1) != 1 or not t.is_cuda:
+        if t.dtype != torch.bfloat16 or t.dim() != 2 or (t.stride(1) != 1 and t.shape[1] > 1) or not t.is_cuda:
             raise ValueError(f"attention_short: {name} must be a 2-D bf16 CUDA tensor with unit column stride.")
     width = heads * 128
     sq, sk = q.shape[0], k.shape[0]

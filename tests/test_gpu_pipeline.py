@@ -1,18 +1,21 @@
-"""GPU: ``HostLinearPipeline`` (pinned host rows, H2D / linear / D2H on three
-streams) gives the device module's result, for every format.
+"""GPU: ``HostLinearPipeline`` (pinned host rows in chunks; host-to-device
+copies, the linear and device-to-host copies on three streams) gives the
+device module's result, for every format.
 
-INT8 outputs are compared bit for bit (exact integer accumulation).  FP8,
-W4A16 and NVFP4 are compared bit for bit too at these shapes (K = 1024: no
-K split of the last wave, so each output element's arithmetic does not
-depend on M).  Ragged last chunks, a single chunk, and dynamic per-tensor
-NVFP4 (always one chunk: its global scale is the amax of all rows) included.
+INT8 outputs are compared bit for bit (exact integer accumulation).  FP8
+and NVFP4 are compared bit for bit too at these shapes (K = 1024: no K
+split of the last wave, so each output element's arithmetic does not depend
+on M); W4A16 picks its kernel by M, so its chunks stay above the small-M
+kernels' 256 rows and match bit for bit as well.  Ragged last chunks, a
+single chunk, and dynamic per-tensor NVFP4 (always one chunk: its global
+scale is the amax of all rows) included.
 """
 
 import pytest
 import torch
 
 from qi_b200 import _lib
-from qi_b200.pipeline import HostLinearPipeline, plan_chunks, rows_independent
+from qi_b200.pipeline import M_VARIANT_MIN_CHUNK, HostLinearPipeline, m_invariant, plan_chunks, rows_independent
 from qi_b200.quantization import WeightActivationQuantConfig, WeightOnlyLinear, WeightOnlyQuantConfig
 from qi_b200.quantization.backends import get_backend
 from qi_b200.quantization.quantize import quantize_linear_weight
@@ -78,11 +81,15 @@ def test_pipeline_matches_device_forward(kind, rows, chunk):
         pipe(xh, out=out2)
     torch.cuda.current_stream().synchronize()
     assert torch.equal(out2, want)
-    expect_chunks = len(plan_chunks(rows, chunk, rows_independent(layer)))
+    min_chunk = 1 if m_invariant(layer) else M_VARIANT_MIN_CHUNK
+    n_chunks = len(plan_chunks(rows, chunk, rows_independent(layer), min_chunk=min_chunk))
     if kind == "nvfp4":
-        assert expect_chunks == 1  # dynamic per-tensor activations
+        assert n_chunks == 1  # dynamic per-tensor activations
+    elif kind == "w4a16":
+        assert not m_invariant(layer)  # chunks stay above the small-M kernels' 256 rows
+        assert n_chunks == (2 if (rows, chunk) == (1000, 256) else 1)
     elif chunk is not None:
-        assert expect_chunks == -(-rows // chunk)
+        assert n_chunks == -(-rows // chunk)
 
 
 def test_pipeline_3d_input_and_errors():
