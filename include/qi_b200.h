@@ -19,7 +19,16 @@
  *     error from the CUDA runtime;
  *   - device-side pipeline waits are bounded; a wait that runs out of time
  *     records its site in the device status word (qi_b200_device_status) and
- *     the kernel returns instead of hanging.
+ *     the kernel returns instead of hanging;
+ *   - kernels are launched with programmatic dependent launch: activations
+ *     and outputs are touched only after the previous kernel in the stream
+ *     has finished, but the small-M W4A16 kernel (qi_b200_w4a16_linear,
+ *     M <= 16) starts fetching its packed weights, scales and zeros before
+ *     that point (M = 1: 7.0 -> 6.7 us; the same for the large GEMMs' B
+ *     tiles measured slower, so they do not).  Weight buffers are layer
+ *     constants: do not write one with a kernel of this library immediately
+ *     before a W4A16 call on the same stream reads it (a torch or other
+ *     kernel in between, or a synchronized stream, is enough).
  */
 #ifndef QI_B200_H_
 #define QI_B200_H_

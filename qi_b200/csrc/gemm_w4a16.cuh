@@ -519,8 +519,6 @@ template <int NT, int KS>
 __global__ void __launch_bounds__(w4s::kThreads)
 k_gemm_w4a16_small(const __nv_bfloat16* __restrict__ X, EpiParams p, W4Params q) {
   constexpr int RB = 8 * NT, KP = w4s::kWarps / NT;
-  griddep_wait();
-  griddep_launch_dependents();
   extern __shared__ __align__(128) uint8_t sm[];
   const W4sLayout L = w4s_layout(NT, KS, p.M, p.K, q.G, q.zw, q.group);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm);
@@ -540,6 +538,12 @@ k_gemm_w4a16_small(const __nv_bfloat16* __restrict__ X, EpiParams p, W4Params q)
     bulk_load(sm + L.s_off, q.scales + static_cast<long long>(n0) * q.G, rows * q.G * 2, bar);
     bulk_load(sm + L.z_off, q.zeros + static_cast<long long>(n0) * q.zw, rows * q.zw * 4, bar);
   }
+  // The packed weights, scales and zeros are layer constants: their copies
+  // above are issued before waiting for the previous kernel in the stream
+  // (programmatic dependent launch), so the fetch overlaps its tail.  X is
+  // read and D written only after the wait.
+  griddep_wait();
+  griddep_launch_dependents();
   // token slice -> shared memory, each 8-element chunk reordered (0,4,1,5,2,6,3,7),
   // and the token sums per quantization group: the group's group/8 chunks sit
   // in consecutive lanes, each lane adds its 8 elements, then a butterfly over
