@@ -240,7 +240,8 @@ int qi_b200_rms_rope_partials(const void* in0, const void* in1, long long ld_in,
  * own code: the DiT blocks call torch's scaled_dot_product_attention,
  * wan_video_dit.py:14-23).  Per head h of `heads` (head_dim must be 128):
  *   O[:, h] = softmax(Q[:, h] K[:, h]^T * scale) V[:, h]
- * for sq query rows and 1 <= sk <= 256 keys, no mask.  q [sq, ldq], k [sk, ldk]
+ * for sq query rows and 1 <= sk <= 128 keys, no mask (the DiT's
+ * cross-attention over its context tokens).  q [sq, ldq], k [sk, ldk]
  * and o [sq, ldo] hold head h in columns h*128 .. h*128+127; V is passed
  * transposed, vt [heads*128, ldvt] with row h*128 + d holding V[:, h, d] over
  * the keys (ldvt >= sk).  bf16 in and out, fp32 scores and accumulation,

@@ -1,25 +1,25 @@
-// Attention over a short key sequence (at most 256 keys, head dim 128) on the
+// Attention over a short key sequence (at most 128 keys, head dim 128) on the
 // tensor cores: O = softmax(Q K^T * scale) V per head, all keys of a head in
 // one tile, so the softmax is exact over the row (no running rescale).
 //
-// The DiT step has three such attentions per layer: the cross-attention of the
-// video queries over the 128 context tokens (wan_video_dit.py:122-140), the
-// first-frame queries over the first-frame keys, and the 32 action queries
-// over first-frame video keys plus their own (mot.py:361-463).  The long
-// video self-attention (3120 keys) is not this kernel's.
+// In the DiT step this is the cross-attention of the video (and action)
+// queries over the 128 context tokens (wan_video_dit.py:122-140); cuDNN's
+// SDPA runs an sm80 kernel for that shape.  The video self-attention (3120
+// keys), the first-frame recompute and the action queries' attention stay on
+// SDPA.
 //
-// One work item = (head h, 128 query rows).  A persistent CTA of 4 warps runs
-// items in turn:
-//   thread 0: TMA loads Q [128 x 128], K [KEYS x 128] and V^T [128 x KEYS]
+// One work item = (head h, 128 query rows):
+//   thread 0: TMA loads Q [128 x 128], K [keys x 128] and V^T [128 x keys]
 //             (bf16, 128-byte swizzled, out-of-range rows / keys read 0),
 //             then S = Q K^T with tcgen05.mma kind::f16 into TMEM (fp32);
-//   4 warps:  each thread owns one query row (its TMEM lane): row max, then
-//             p = 2^((s - max) * scale * log2 e) rounded to bf16, written to
-//             shared memory in the swizzled K-major layout the MMA reads (over
-//             the dead Q or K tile), and the row sum of the rounded p;
+//   warps:    each query row (a TMEM lane) is owned by one or two threads: row
+//             max, then p = 2^((s - max) * scale * log2 e) rounded to bf16,
+//             written to shared memory in the swizzled K-major layout the MMA
+//             reads (over a dead operand tile), and the fp32 row sum of the
+//             rounded p;
 //   thread 0: O = P V (V^T as the K-major B operand) into TMEM;
-//   4 warps:  O / sum -> bf16 into a swizzled staging tile; thread 0 stores it
-//             with TMA (asynchronous: it overlaps the next item's loads).
+//   warps:    O / sum -> bf16 into a swizzled staging tile; thread 0 stores it
+//             with TMA (asynchronous: it overlaps the next item's work).
 // Every wait is bounded; an expired wait records the error, raises the CTA's
 // abort flag and the CTA drains its copies / MMAs and exits.
 #pragma once
@@ -33,23 +33,7 @@
 
 namespace qib {
 
-constexpr int kAttnThreads = 128;
 constexpr unsigned int kTagAttn = 0x600u;
-
-template <int NKB>
-struct AttnCfg {
-  static constexpr int KEYS = 128 * NKB;              // key capacity of one tile
-  static constexpr int Q_BYTES = 2 * 128 * 128;       // 2 head-dim blocks of 64 x 128 rows
-  static constexpr int K_BYTES = 2 * KEYS * 128;      // 2 head-dim blocks of 64 x KEYS rows
-  static constexpr int VT_BYTES = 2 * NKB * 128 * 128;  // KEYS / 64 key blocks x 128 head-dim rows
-  static constexpr int P_BYTES = 2 * NKB * 128 * 128;   // KEYS / 64 key blocks x 128 query rows
-  static_assert(P_BYTES == (NKB == 1 ? Q_BYTES : K_BYTES), "P reuses the Q (one key block) or K tile");
-  static constexpr int SMEM_BYTES = Q_BYTES + K_BYTES + VT_BYTES + 64 + 1024;
-  static constexpr int S_COL = 0, O_COL = KEYS;       // TMEM columns of S and O
-  static constexpr int TMEM_COLS = NKB == 1 ? 256 : 512;
-  static constexpr uint32_t IDESC_S = make_idesc(kDF32, kFmtBF16, kFmtBF16, 128, KEYS);
-  static constexpr uint32_t IDESC_O = make_idesc(kDF32, kFmtBF16, kFmtBF16, 128, 128);
-};
 
 struct AttnParams {
   int sq, sk, heads;
@@ -93,29 +77,51 @@ __device__ __forceinline__ void st_sw128_32(uint8_t* tile, int row, int c, const
   }
 }
 
-template <int NKB>
-__global__ void __launch_bounds__(kAttnThreads)
-k_attn_short(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-             const __grid_constant__ CUtensorMap tmVt, const __grid_constant__ CUtensorMap tmO,
-             const AttnParams p) {
-  using C = AttnCfg<NKB>;
+// ---------------------------------------------------------------------------
+// At most 128 keys, double-buffered (the DiT's cross-attention: 3120 queries x
+// 24 heads = 600 items over 128 context keys).  One CTA per SM takes a
+// contiguous range of items (mostly one head), so K / V^T are loaded once per
+// head; Q and K / V^T have two buffers each, and the next item's loads are
+// issued right after the current item's S MMA, so they overlap its softmax,
+// P V MMA and epilogue.  P and the O staging tile reuse the current item's Q
+// buffer.  Shared memory: 2 x 32 KB Q + 2 x (32 + 32) KB K / V^T = 192 KB.
+// ---------------------------------------------------------------------------
+struct AttnDbCfg {
+  static constexpr int TILE = 128 * 128 * 2;  // one 128 x 128 bf16 operand (2 swizzled 64-column blocks)
+  static constexpr int THREADS = 256;         // 8 warps: two per TMEM lane quadrant, one per 64-column half
+  static constexpr int SMEM_BYTES = 6 * TILE + 128 + 2 * 2 * 128 * 4 + 1024;
+  static constexpr int S_COL = 0, O_COL = 128;
+  static constexpr int TMEM_COLS = 256;
+  static constexpr uint32_t IDESC = make_idesc(kDF32, kFmtBF16, kFmtBF16, 128, 128);
+};
+
+__global__ void __launch_bounds__(AttnDbCfg::THREADS, 1)
+k_attn_short_db(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmVt, const __grid_constant__ CUtensorMap tmO,
+                const AttnParams p) {
+  using C = AttnDbCfg;
   extern __shared__ uint8_t attn_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(attn_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + C::Q_BYTES;
-  uint8_t* sVt = sK + C::K_BYTES;
-  uint8_t* sP = NKB == 1 ? sQ : sK;
-  uint8_t* sO = NKB == 1 ? sK : sQ;  // bf16 O staging for the TMA store: the tile P does not hold
-  uint64_t* full = reinterpret_cast<uint64_t*>(sVt + C::VT_BYTES);
-  uint64_t* sdone = full + 1;
-  uint64_t* odone = full + 2;
-  uint64_t* drain = full + 3;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 4);
+  // buffers: Q b at b * TILE, K b at (2 + b) * TILE, V^T b at (4 + b) * TILE
+  auto sQ = [&](int b) { return smem + b * C::TILE; };
+  auto sK = [&](int b) { return smem + (2 + b) * C::TILE; };
+  auto sVt = [&](int b) { return smem + (4 + b) * C::TILE; };
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + 6 * C::TILE);  // [2]
+  uint64_t* kv_full = q_full + 2;                                       // [2]
+  uint64_t* sdone = q_full + 4;
+  uint64_t* odone = q_full + 5;
+  uint64_t* drain = q_full + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* xchg = reinterpret_cast<float*>(smem + 6 * C::TILE + 128);  // [2 halves][2 (max, sum)][128 rows]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quad = warp & 3, half = warp >> 2;  // TMEM lane quadrant (rows), 64-column half
 
   if (threadIdx.x == 0) {
-    mbar_init(full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&kv_full[i], 1);
+    }
     mbar_init(sdone, 1);
     mbar_init(odone, 1);
     mbar_init(drain, 1);
@@ -138,114 +144,129 @@ k_attn_short(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
   griddep_launch_dependents();
 
   const int q_tiles = (p.sq + 127) / 128;
-  const int items = q_tiles * p.heads;
-  const int row = warp * 32 + lane;  // query row of the tile = TMEM lane
-  const uint32_t t_row = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
-  constexpr uint32_t kTxBytes = C::Q_BYTES + C::K_BYTES + C::VT_BYTES;
-  bool ok = true;
-  uint32_t phase = 0;
-  int issued = 0;  // items whose loads thread 0 has issued
-#pragma unroll 1
-  for (int item = blockIdx.x; item < items; item += gridDim.x, phase ^= 1u) {
-    const int h = item / q_tiles, m0 = (item - h * q_tiles) * 128;
-    if (threadIdx.x == 0) {
-      bulk_wait_read_all();  // the previous item's O store has read its staging tile
-      mbar_expect_tx(full, kTxBytes);
-#pragma unroll
+  const long long items = static_cast<long long>(q_tiles) * p.heads;
+  const int i0 = static_cast<int>(items * blockIdx.x / gridDim.x);
+  const int i1 = static_cast<int>(items * (blockIdx.x + 1) / gridDim.x);
+  const int row = quad * 32 + lane;
+  const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(half * 64);
+
+  // loads of item j: Q into buffer qb; K / V^T of its head into buffer kvb when `kv`
+  auto load_item = [&](int j, int qb, bool kv, int kvb) {
+    const int h = j / q_tiles, m0 = (j - h * q_tiles) * 128;
+    mbar_expect_tx(&q_full[qb], C::TILE);
+    for (int kb = 0; kb < 2; ++kb) tma_load_2d(sQ(qb) + kb * (C::TILE / 2), &tmQ, &q_full[qb], h * 128 + kb * 64, m0);
+    if (kv) {
+      mbar_expect_tx(&kv_full[kvb], 2 * C::TILE);
       for (int kb = 0; kb < 2; ++kb) {
-        tma_load_2d(sQ + kb * 128 * 128, &tmQ, full, h * 128 + kb * 64, m0);
-        tma_load_2d(sK + kb * C::KEYS * 128, &tmK, full, h * 128 + kb * 64, 0);
+        tma_load_2d(sK(kvb) + kb * (C::TILE / 2), &tmK, &kv_full[kvb], h * 128 + kb * 64, 0);
+        tma_load_2d(sVt(kvb) + kb * (C::TILE / 2), &tmVt, &kv_full[kvb], kb * 64, h * 128);
       }
-#pragma unroll
-      for (int j = 0; j < 2 * NKB; ++j) tma_load_2d(sVt + j * 128 * 128, &tmVt, full, j * 64, h * 128);
-      ++issued;
-      if (!mbar_wait(full, phase, abort_flag, kTagAttn, 1)) {
+    }
+  };
+
+  bool ok = true;
+  // thread 0: loads issued and not yet consumed (buffer, phase parity), for the drain
+  int q_pend = -1, kv_pend = -1;
+  uint32_t q_pend_par = 0, kv_pend_par = 0;
+  int seg = 0;  // head segments begun (K / V^T buffer = seg & 1)
+  if (threadIdx.x == 0 && i0 < i1) {
+    load_item(i0, 0, true, 0);
+    q_pend = kv_pend = 0;
+  }
+#pragma unroll 1
+  for (int j = i0; j < i1; ++j) {
+    const int n = j - i0, qb = n & 1;
+    const int h = j / q_tiles, m0 = (j - h * q_tiles) * 128;
+    if (j != i0 && h != (j - 1) / q_tiles) ++seg;
+    const int kvb = seg & 1;
+    if (threadIdx.x == 0) {
+      const bool new_head = (j == i0) || h != (j - 1) / q_tiles;
+      if (!mbar_wait(&q_full[qb], static_cast<uint32_t>(n >> 1) & 1u, abort_flag, kTagAttn, 11) ||
+          (new_head && !mbar_wait(&kv_full[kvb], static_cast<uint32_t>(seg >> 1) & 1u, abort_flag, kTagAttn, 12))) {
         ok = false;
       } else {
+        q_pend = -1;
+        if (new_head) kv_pend = -1;
         tc_fence_after();
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_bf16(tmem_base + C::S_COL, sw128_kmajor_desc(smem_u32(sQ + kb * 128 * 128) + kk * 32),
-                     sw128_kmajor_desc(smem_u32(sK + kb * C::KEYS * 128) + kk * 32), C::IDESC_S,
+            mma_bf16(tmem_base + C::S_COL, sw128_kmajor_desc(smem_u32(sQ(qb) + kb * (C::TILE / 2)) + kk * 32),
+                     sw128_kmajor_desc(smem_u32(sK(kvb) + kb * (C::TILE / 2)) + kk * 32), C::IDESC,
                      (kb | kk) != 0 ? 1u : 0u);
         tc_commit(sdone);
+        if (j + 1 < i1) {
+          // the next item's loads: its Q buffer held item j-1's O staging tile
+          // (its TMA store must have read it); a new head goes to the other
+          // K / V^T buffer, whose last reader (the previous head) is done
+          bulk_wait_read_all();
+          const bool next_new = (j + 1) / q_tiles != h;
+          load_item(j + 1, qb ^ 1, next_new, kvb ^ 1);
+          q_pend = qb ^ 1;
+          q_pend_par = static_cast<uint32_t>((n + 1) >> 1) & 1u;
+          if (next_new) {
+            kv_pend = kvb ^ 1;
+            kv_pend_par = static_cast<uint32_t>((seg + 1) >> 1) & 1u;
+          }
+        }
       }
     }
-    if (!mbar_wait(sdone, phase, abort_flag, kTagAttn, 2)) { ok = false; break; }
+    if (!mbar_wait(sdone, static_cast<uint32_t>(n) & 1u, abort_flag, kTagAttn, 13)) { ok = false; break; }
     tc_fence_after();
 
-    // ---- softmax of this thread's row: max, then 2^(..) as bf16 into P (swizzled),
-    // the fp32 sum of the rounded values.  One key block: the 128 scores stay in
-    // registers (one TMEM pass); two: max pass, then exp pass.
+    // softmax: this thread has keys half*64 .. +63 of its row; the row max and
+    // the row sum are combined with the other half's thread through shared memory
     float sum = 0.f;
-    if constexpr (NKB == 1) {
-      uint32_t r[4][32];
+    {
+      uint32_t r[2][32];
 #pragma unroll
-      for (int b = 0; b < 4; ++b) tmem_ld_32x32b_x32(t_row + C::S_COL + 32 * b, r[b]);
+      for (int b = 0; b < 2; ++b) tmem_ld_32x32b_x32(t_row + C::S_COL + 32 * b, r[b]);
       tmem_ld_wait();
       float mx = -INFINITY;
 #pragma unroll
-      for (int b = 0; b < 4; ++b)
+      for (int b = 0; b < 2; ++b)
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          if (32 * b + i < p.sk) mx = fmaxf(mx, __uint_as_float(r[b][i]));
+          if (half * 64 + 32 * b + i < p.sk) mx = fmaxf(mx, __uint_as_float(r[b][i]));
+      xchg[(half * 2 + 0) * 128 + row] = mx;
+      __syncthreads();
+      mx = fmaxf(mx, xchg[((half ^ 1) * 2 + 0) * 128 + row]);
       const float off = -mx * p.scale_log2e;
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
+      for (int b = 0; b < 2; ++b) {
         uint32_t pk[16];
-        sum += attn_p32(r[b], 32 * b, p.sk, p.scale_log2e, off, pk);
-        st_sw128_32(sP, row, 32 * b, pk);
+        sum += attn_p32(r[b], half * 64 + 32 * b, p.sk, p.scale_log2e, off, pk);
+        st_sw128_32(sQ(qb), row, half * 64 + 32 * b, pk);  // P over the dead Q tile
       }
-    } else {
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < C::KEYS; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + C::S_COL + c, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c + i < p.sk) mx = fmaxf(mx, __uint_as_float(r[i]));
-      }
-      const float off = -mx * p.scale_log2e;
-#pragma unroll 1
-      for (int c = 0; c < C::KEYS; c += 32) {
-        uint32_t r[32], pk[16];
-        tmem_ld_32x32b_x32(t_row + C::S_COL + c, r);
-        tmem_ld_wait();
-        sum += attn_p32(r, c, p.sk, p.scale_log2e, off, pk);
-        st_sw128_32(sP, row, c, pk);
-      }
+      xchg[(half * 2 + 1) * 128 + row] = sum;
     }
-    fence_async_shared();  // P (generic-proxy writes) visible to the tensor core
+    fence_async_shared();
     tc_fence_before();
     __syncthreads();
+    sum = xchg[1 * 128 + row] + xchg[3 * 128 + row];  // both halves, in a fixed order
     if (threadIdx.x == 0) {
       tc_fence_after();
 #pragma unroll
-      for (int j = 0; j < 2 * NKB; ++j)
+      for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_bf16(tmem_base + C::O_COL, sw128_kmajor_desc(smem_u32(sP + j * 128 * 128) + kk * 32),
-                   sw128_kmajor_desc(smem_u32(sVt + j * 128 * 128) + kk * 32), C::IDESC_O,
-                   (j | kk) != 0 ? 1u : 0u);
+          mma_bf16(tmem_base + C::O_COL, sw128_kmajor_desc(smem_u32(sQ(qb) + kb * (C::TILE / 2)) + kk * 32),
+                   sw128_kmajor_desc(smem_u32(sVt(kvb) + kb * (C::TILE / 2)) + kk * 32), C::IDESC,
+                   (kb | kk) != 0 ? 1u : 0u);
       tc_commit(odone);
     }
-    if (!mbar_wait(odone, phase, abort_flag, kTagAttn, 3)) { ok = false; break; }
+    if (!mbar_wait(odone, static_cast<uint32_t>(n) & 1u, abort_flag, kTagAttn, 14)) { ok = false; break; }
     tc_fence_after();
 
-    // ---- O / sum -> bf16 into the staging tile (swizzled), then one TMA store
-    // of the 128 x 128 tile at (row m0, column h*128); rows past sq are clipped
     const float inv = 1.0f / sum;
     {
-      uint32_t r[4][32];
+      uint32_t r[2][32];
 #pragma unroll
-      for (int b = 0; b < 4; ++b) tmem_ld_32x32b_x32(t_row + C::O_COL + 32 * b, r[b]);
+      for (int b = 0; b < 2; ++b) tmem_ld_32x32b_x32(t_row + C::O_COL + 32 * b, r[b]);
       tmem_ld_wait();
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
+      for (int b = 0; b < 2; ++b) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -253,25 +274,27 @@ k_attn_short(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
                                                          __uint_as_float(r[b][2 * i + 1]) * inv);
           pk[i] = *reinterpret_cast<const uint32_t*>(&v);
         }
-        st_sw128_32(sO, row, 32 * b, pk);
+        st_sw128_32(sQ(qb), row, half * 64 + 32 * b, pk);  // O staging over the dead P tile
       }
     }
-    fence_async_shared();  // the staging tile (generic-proxy writes) visible to the TMA store
-    // S / O columns and the Q, K, V^T tiles are free for the next item
+    fence_async_shared();
     tc_fence_before();
     __syncthreads();
     if (threadIdx.x == 0) {
 #pragma unroll
-      for (int b = 0; b < 2; ++b) tma_store_2d(&tmO, sO + b * 128 * 128, h * 128 + b * 64, m0);
+      for (int b = 0; b < 2; ++b) tma_store_2d(&tmO, sQ(qb) + b * (C::TILE / 2), h * 128 + b * 64, m0);
       bulk_commit_group();
     }
   }
-  if (threadIdx.x == 0) bulk_wait_all();  // the stores have landed before the CTA exits
-  if (!ok && threadIdx.x == 0) {
-    // drain: the last item's copies and any MMA still in flight
-    if (issued > 0) mbar_wait_drain(full, phase);
-    tc_commit(drain);
-    mbar_wait_drain(drain, 0);
+  if (threadIdx.x == 0) {
+    bulk_wait_all();  // the stores have landed before the CTA exits
+    if (!ok) {
+      // drain: loads still in flight, then any MMA
+      if (q_pend >= 0) mbar_wait_drain(&q_full[q_pend], q_pend_par);
+      if (kv_pend >= 0) mbar_wait_drain(&kv_full[kv_pend], kv_pend_par);
+      tc_commit(drain);
+      mbar_wait_drain(drain, 0);
+    }
   }
   tc_fence_before();
   __syncthreads();

@@ -1527,28 +1527,28 @@ extern "C" int qi_b200_int8_linear_noalloc(const void* x_bf16, const void* qweig
 }
 
 // ---------------------------------------------------------------------------
-// Attention over at most 256 keys (head dim 128): k_attn_short
+// Attention over at most 128 keys (head dim 128): k_attn_short_db
 // ---------------------------------------------------------------------------
 namespace qib {
-template <int NKB>
-static int launch_attn_short(const void* q, long long ldq, const void* k, long long ldk, const void* vt,
-                             long long ldvt, void* o, long long ldo, int sq, int sk, int heads, float scale,
-                             cudaStream_t stream) {
-  using C = AttnCfg<NKB>;
+// At most 128 keys: the double-buffered kernel, one CTA per SM.
+static int launch_attn_short_db(const void* q, long long ldq, const void* k, long long ldk, const void* vt,
+                                long long ldvt, void* o, long long ldo, int sq, int sk, int heads, float scale,
+                                cudaStream_t stream) {
+  using C = AttnDbCfg;
   DeviceInfo* di = nullptr;
   int rc = device_info(&di);
   if (rc) return rc;
   CUtensorMap tq, tk, tv, to;
   const uint64_t width = static_cast<uint64_t>(heads) * 128;
   if ((rc = make_tmap_2d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, width, sq, ldq * 2, 64, 128))) return rc;
-  if ((rc = make_tmap_2d(&tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, width, sk, ldk * 2, 64, C::KEYS))) return rc;
+  if ((rc = make_tmap_2d(&tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, width, sk, ldk * 2, 64, 128))) return rc;
   if ((rc = make_tmap_2d(&tv, vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, sk, width, ldvt * 2, 64, 128))) return rc;
   if ((rc = make_tmap_2d(&to, o, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, width, sq, ldo * 2, 64, 128))) return rc;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(k_attn_short<NKB>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) !=
+    if (cudaFuncSetAttribute(k_attn_short_db, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) !=
         cudaSuccess)
       return QI_B200_ECUDA;
     attr_done[dev] = true;
@@ -1559,9 +1559,8 @@ static int launch_attn_short(const void* q, long long ldq, const void* k, long l
   p.heads = heads;
   p.scale_log2e = scale * 1.4426950408889634f;
   const int items = heads * ((sq + 127) / 128);
-  const int per_sm = NKB == 1 ? 2 : 1;  // shared memory (96 / 160 KB) and TMEM (256 / 512 columns)
-  const int grid = std::min(items, di->num_sms * per_sm);
-  launch_pdl(k_attn_short<NKB>, dim3(grid), dim3(kAttnThreads), C::SMEM_BYTES, stream, 1, tq, tk, tv, to, p);
+  const int grid = std::min(items, di->num_sms);
+  launch_pdl(k_attn_short_db, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, stream, 1, tq, tk, tv, to, p);
   count_launches(1);
   return cudaGetLastError() == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
@@ -1572,13 +1571,12 @@ extern "C" int qi_b200_attention_short(const void* q, long long ldq, const void*
                                        int head_dim, float scale, cudaStream_t stream) {
   using namespace qib;
   if (q == nullptr || k == nullptr || vt == nullptr || o == nullptr) return QI_B200_EINVAL;
-  if (head_dim != 128 || heads <= 0 || sq < 0 || sk < 1 || sk > 256) return QI_B200_ESHAPE;
+  if (head_dim != 128 || heads <= 0 || sq < 0 || sk < 1 || sk > 128) return QI_B200_ESHAPE;
   if (sq == 0) return QI_B200_OK;
   const long long width = static_cast<long long>(heads) * 128;
   if (ldq < width || ldk < width || ldo < width || ldvt < sk) return QI_B200_ESHAPE;
   if (ldq % 8 || ldk % 8 || ldo % 8 || ldvt % 8) return QI_B200_EALIGN;
   if (!aligned16(q) || !aligned16(k) || !aligned16(vt) || !aligned16(o)) return QI_B200_EALIGN;
   if (!(scale > 0.0f)) return QI_B200_EINVAL;
-  return sk <= 128 ? launch_attn_short<1>(q, ldq, k, ldk, vt, ldvt, o, ldo, sq, sk, heads, scale, stream)
-                   : launch_attn_short<2>(q, ldq, k, ldk, vt, ldvt, o, ldo, sq, sk, heads, scale, stream);
+  return launch_attn_short_db(q, ldq, k, ldk, vt, ldvt, o, ldo, sq, sk, heads, scale, stream);
 }

@@ -630,7 +630,7 @@ class DiTStepRunner:
                 side.wait_stream(main)
             with (torch.cuda.stream(side) if cuda else _nullctx()):
                 qa, ka, va = self._tp_pre(ac_name, li, x, y_ffn, mods, sc1, rope)
-                att_a = self._attn_short(qa, torch.cat([kf, ka], 1), torch.cat([vf, va], 1), heads=hl)
+                att_a = attention(qa, torch.cat([kf, ka], 1), torch.cat([vf, va], 1), hl)
                 self._tp_post(ac_name, li, att_a, x, y_ffn, mods, sc1, ctxq)
             if cuda:
                 kf.record_stream(side)
@@ -674,22 +674,20 @@ class DiTStepRunner:
         ck = K.rms_rope([ckv[:, :a]], [self.plans[n][li].cnk.weight], None, cfg.head_dim, cfg.eps)[0]
         return ck, ckv[:, a:].t().contiguous()
 
-    def _attn_short(self, q, k, v=None, heads=None, vt=None, out=None):
-        """softmax(q k^T / sqrt(d)) v over at most 256 keys on the tensor cores
-        (``attention_short``): the cross-attention over the context tokens, the
-        first-frame recompute and the action queries.  q [.., Sq, W],
-        k [.., Sk, W], v [.., Sk, W] (or vt = V^T [W, Sk]); rows may be strided."""
+    def _attn_short(self, q, k, v=None, heads=None, vt=None):
+        """Cross-attention over the (at most 128) context tokens on the tensor
+        cores (``attention_short``; cuDNN's SDPA runs an sm80 kernel there, 34
+        against 21 us per video layer).  q [.., Sq, W], k [.., Sk, W],
+        v [.., Sk, W] (or vt = V^T [W, Sk]); rows may be strided."""
         h = self.cfg.heads if heads is None else heads
         w = q.shape[-1]
         if self.cfg.head_dim != 128:  # the kernel's head dim; other configs (small tests) use SDPA
             v2 = v.reshape(-1, w) if v is not None else vt.t()
             o = attention(q.reshape(1, -1, w), k.reshape(1, -1, w), v2.unsqueeze(0), h)[0]
-            if out is not None:
-                out.copy_(o)
         else:
             if vt is None:
                 vt = v.reshape(-1, w).t().contiguous()
-            o = self.K.attention_short(q.reshape(-1, w), k.reshape(-1, w), vt, h, out=out)
+            o = self.K.attention_short(q.reshape(-1, w), k.reshape(-1, w), vt, h)
         return o.unsqueeze(0) if q.dim() == 3 else o
 
     def _post(self, n, li, att, x, y_ffn, mods, sc1, ctxq, ctx_kv=None):
@@ -718,7 +716,7 @@ class DiTStepRunner:
         nf = max(0, min(t - self.video_offset, q.shape[1]))
         out = attention(q, k, v, h)
         if nf > 0 and sv > t:
-            self._attn_short(q[:, :nf], k[:, :t], v[:, :t], heads=h, out=out[0, :nf])
+            out[:, :nf] = attention(q[:, :nf], k[:, :t], v[:, :t], h)
         return out
 
     def _step_fused(self, tokens, rope, ctx, t_mod):
@@ -766,7 +764,7 @@ class DiTStepRunner:
                 # the action queries attend the first-frame video keys and their own;
                 # the copies that join them run here, off the video stream
                 qa, ka, va, _ = self._pre("action", li, x, y_ffn, mods, sc1, rope)
-                att_a = self._attn_short(qa, torch.cat([kv[:, :t], ka], 1), torch.cat([vv[:, :t], va], 1))
+                att_a = attention(qa, torch.cat([kv[:, :t], ka], 1), torch.cat([vv[:, :t], va], 1), cfg.heads)
                 self._post("action", li, att_a, x, y_ffn, mods, sc1, ctxq, ckv.pop(("action", li)))
                 if li + 1 < cfg.layers:
                     ctx_kv_ahead(li + 1)

@@ -149,7 +149,7 @@ def rms_rope(inputs, weights, rope: torch.Tensor | None, head_dim: int, eps: flo
 
 def attention_short(q: torch.Tensor, k: torch.Tensor, vt: torch.Tensor, heads: int,
                     scale: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-    """softmax(Q K^T * scale) V per head for at most 256 keys, head dim 128,
+    """softmax(Q K^T * scale) V per head for at most 128 keys, head dim 128,
     on the tensor cores (``qi_b200_attention_short``).  ``q`` [Sq, H*128] and
     ``k`` [Sk, H*128] (row strides may exceed H*128), ``vt`` = V transposed,
     [H*128, Sk] (copied into a padded buffer when its row stride is not a

@@ -1,12 +1,12 @@
 """GPU: the short-key attention kernel (``qi_b200_attention_short``) against an
-fp32 softmax(Q K^T / sqrt(d)) V of the same bf16 inputs.
+fp64 softmax(Q K^T / sqrt(d)) V of the same bf16 inputs.
 
 The kernel rounds the probabilities to bf16 before the P V product, as flash
 attention kernels do; tolerance: relative Frobenius error <= 1e-2 and max
 abs error <= 3e-2 (unit-variance V).  Shapes: the DiT step's cross-attention
-(3120 queries x 128 context keys, 24 heads), its first-frame recompute
-(120 x 120) and action attention (32 x 152, two key blocks), plus ragged
-query / key counts, one key, 256 keys, large logits, strided rows.
+(3120 video or 32 action queries x 128 context keys, 24 heads), plus ragged
+query / key counts, one key, large logits, strided rows; more than 128 keys
+is refused.
 """
 
 import pytest
@@ -40,13 +40,13 @@ def _ref(q, k, v, heads):
 
 
 @pytest.mark.parametrize("sq,sk,heads,qmul", [
-    (3120, 128, 24, 1.0),   # DiT cross-attention
-    (120, 120, 24, 1.0),    # first-frame recompute
-    (32, 152, 24, 1.0),     # action queries over first-frame + action keys
+    (3120, 128, 24, 1.0),   # DiT cross-attention, video queries
+    (32, 128, 24, 1.0),     # action queries
     (1, 1, 2, 1.0),
     (129, 65, 1, 1.0),
-    (300, 256, 3, 1.0),
-    (257, 200, 4, 6.0),     # large logits: the row max matters
+    (300, 120, 3, 1.0),
+    (257, 100, 4, 6.0),     # large logits: the row max matters
+    (1000, 128, 40, 1.0),   # items not a multiple of the grid; several heads per CTA
 ])
 def test_attention_short_matches_fp64(sq, sk, heads, qmul):
     g = torch.Generator(device="cpu").manual_seed(sq * 7 + sk)
@@ -105,6 +105,6 @@ def test_attention_short_rejects_bad_shapes():
     q = torch.zeros(16, 256, dtype=torch.bfloat16, device=DEV)
     k = torch.zeros(300, 256, dtype=torch.bfloat16, device=DEV)
     with pytest.raises(Exception):
-        K.attention_short(q, k, torch.zeros(256, 300, dtype=torch.bfloat16, device=DEV), 2)  # > 256 keys
+        K.attention_short(q, k[:129], torch.zeros(256, 136, dtype=torch.bfloat16, device=DEV)[:, :129], 2)  # > 128 keys
     with pytest.raises(ValueError):
         K.attention_short(q, k[:8], torch.zeros(256, 9, dtype=torch.bfloat16, device=DEV), 2)  # vt shape
