@@ -460,23 +460,24 @@ constexpr int kMaxM = 16;    // one m16 MMA row block
 }  // namespace w4s
 
 // Shared-memory layout of k_gemm_w4a16_small<NT, KS> (byte offsets, all
-// 16-aligned): mbarrier | RB = 8 NT weight rows of this CTA's K range (KC/2
-// bytes + pad) | RB x G fp16 scales | RB x zw zero words | M token rows of the
-// K range (KC + 8 bf16, K-permuted) | token sums [M][KC / group] fp32 |
-// warp partials | CTA partials (read by the cluster's rank 0).
+// 16-aligned): 2 mbarriers (weights, tokens) | RB = 8 NT weight rows of this
+// CTA's K range (KC/2 bytes + pad) | RB x G fp16 scales | RB x zw zero words |
+// M token rows of the K range (KC bf16 + pad, natural order) | warp partials |
+// CTA partials (read by the cluster's rank 0).
 struct W4sLayout {
-  int w_off, w_stride, s_off, z_off, x_off, xsum_off, red_off, part_off, total;
+  int w_off, w_stride, s_off, z_off, x_off, x_stride, red_off, part_off, total;
 };
 __host__ __device__ inline W4sLayout w4s_layout(int NT, int KS, int M, int K, int G, int zw, int group) {
   const int RB = 8 * NT, KC = K / KS;
+  (void)group;
   W4sLayout L;
   L.w_off = 16;
   L.w_stride = KC / 2 + w4s::kRowPad;
   L.s_off = L.w_off + RB * L.w_stride;
   L.z_off = L.s_off + ((RB * G * 2 + 15) & ~15);
   L.x_off = L.z_off + ((RB * zw * 4 + 15) & ~15);
-  L.xsum_off = L.x_off + M * (KC + 8) * 2;
-  L.red_off = L.xsum_off + ((M * (KC / group) * 4 + 15) & ~15);
+  L.x_stride = KC * 2 + w4s::kRowPad;  // bytes; the pad spreads ldmatrix rows over banks
+  L.red_off = L.x_off + M * L.x_stride;
   L.part_off = L.red_off + w4s::kWarps * 32 * 4 * 4;
   L.total = L.part_off + NT * 32 * 4 * 4;
   return L;
@@ -496,88 +497,70 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t (&a)[4], uint32_t addr) {
                : "r"(addr));
 }
 
-// Elements t and t + 4 of a packed word as bf16x2 (128 + q_t, 128 + q_{t+4}):
-// the nibble lands in the low mantissa bits of bf16 128.0 (exact).
-__device__ __forceinline__ uint32_t nibbles_bf16x2(uint32_t w, int t4) {
-  return ((w >> t4) & 0x000F000Fu) | 0x43004300u;
+// Elements 2t and 2t+1 of a packed word (byte t) minus the zero point, as
+// bf16x2 (q_2t - z, q_2t+1 - z): each nibble goes into the low mantissa bits
+// of bf16 128.0 (giving 128 + q exactly), then 128 + z is subtracted (zb =
+// bf16x2 of 128 + z); every value is a small integer, so all of it is exact.
+__device__ __forceinline__ uint32_t nibble_pair_minus_z(uint32_t w, int t8, uint32_t zb) {
+  const uint32_t x = w >> t8;
+  const uint32_t v = (x & 0x0000000Fu) | ((x << 12) & 0x000F0000u) | 0x43004300u;
+  const __nv_bfloat162 r = __hsub2_rn(*reinterpret_cast<const __nv_bfloat162*>(&v),
+                                      *reinterpret_cast<const __nv_bfloat162*>(&zb));
+  return *reinterpret_cast<const uint32_t*>(&r);
 }
 
 // W4A16 for M <= 16 tokens.  A CTA covers RB = 8 NT weight rows and 1/KS of K
 // (KS CTAs of a cluster split K).  Thread 0 brings the CTA's weight row
-// slices, scales and zeros into shared memory with bulk copies; the token
-// slice is staged meanwhile with K permuted inside every 8-element chunk, so
-// that lane t's MMA B fragment is one shift and one LOP of a packed word
-// (elements t, t+4 -> logical k 2t, 2t+1).  The MMAs multiply the tokens by
-// 128 + q exactly; per quantization group the fp32 partial D is turned into
-// s (D - (128 + z) sum_k x_k), the group's exact contribution
-// sum_k x_k (q_k - z) s.  With one-hot token rows this is bf16((q - z) s),
-// the reference's dequantized weight, bit for bit; in general it skips the
-// reference's bf16 rounding of each weight (relative difference ~1e-3).
-// Warps: n-tile warp % NT, K part warp / NT.  Partials are added in K order:
-// warps in the CTA, then the cluster's CTAs by rank (distributed shared memory).
+// slices, scales and zeros into shared memory with bulk copies before waiting
+// for the previous kernel (programmatic dependent launch: the weights are
+// layer constants), then the token rows of its K range.  The MMAs
+// (m16n8k16, bf16, fp32 accumulate) multiply the tokens by (q - z), exact in
+// bf16; per quantization group the fp32 result D (two accumulator chains
+// added) becomes s D, the group's contribution sum_k x_k (q_k - z) s.  With
+// one-hot token rows this is bf16((q - z) s), the reference's dequantized
+// weight, bit for bit; in general it skips the reference's bf16 rounding of
+// each weight (relative difference ~1e-3).  Warps: n-tile warp % NT, K part
+// warp / NT.  Partials are added in K order: warps in the CTA, then the
+// cluster's CTAs by rank (distributed shared memory).
 template <int NT, int KS>
 __global__ void __launch_bounds__(w4s::kThreads)
 k_gemm_w4a16_small(const __nv_bfloat16* __restrict__ X, EpiParams p, W4Params q) {
+  static_assert(NT == KS, "each warp's K range must hold whole quantization groups: K / 8 per warp");
   constexpr int RB = 8 * NT, KP = w4s::kWarps / NT;
   extern __shared__ __align__(128) uint8_t sm[];
   const W4sLayout L = w4s_layout(NT, KS, p.M, p.K, q.G, q.zw, q.group);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm);
+  uint64_t* bar_w = reinterpret_cast<uint64_t*>(sm);
+  uint64_t* bar_x = bar_w + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cr = KS > 1 ? static_cast<int>(cluster_ctarank()) : 0;
   const int n0 = (blockIdx.x / KS) * RB;
   const int rows = min(RB, p.N - n0);
   const int KC = p.K / KS, kc0 = cr * KC;
-  const int GC = KC / q.group;
   if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
+    mbar_init(bar_w, 1);
+    mbar_init(bar_x, 1);
     fence_mbar_init();
-    mbar_expect_tx(bar, static_cast<uint32_t>(rows * (KC / 2 + q.G * 2 + q.zw * 4)));
+    mbar_expect_tx(bar_w, static_cast<uint32_t>(rows * (KC / 2 + q.G * 2 + q.zw * 4)));
 #pragma unroll 1
     for (int r = 0; r < rows; ++r)
-      bulk_load(sm + L.w_off + r * L.w_stride, q.wq + static_cast<long long>(n0 + r) * q.kw + kc0 / 8, KC / 2, bar);
-    bulk_load(sm + L.s_off, q.scales + static_cast<long long>(n0) * q.G, rows * q.G * 2, bar);
-    bulk_load(sm + L.z_off, q.zeros + static_cast<long long>(n0) * q.zw, rows * q.zw * 4, bar);
+      bulk_load(sm + L.w_off + r * L.w_stride, q.wq + static_cast<long long>(n0 + r) * q.kw + kc0 / 8, KC / 2, bar_w);
+    bulk_load(sm + L.s_off, q.scales + static_cast<long long>(n0) * q.G, rows * q.G * 2, bar_w);
+    bulk_load(sm + L.z_off, q.zeros + static_cast<long long>(n0) * q.zw, rows * q.zw * 4, bar_w);
   }
+  __syncthreads();  // both mbarriers are initialized before any thread waits on them
   // The packed weights, scales and zeros are layer constants: their copies
   // above are issued before waiting for the previous kernel in the stream
   // (programmatic dependent launch), so the fetch overlaps its tail.  X is
   // read and D written only after the wait.
   griddep_wait();
   griddep_launch_dependents();
-  // token slice -> shared memory, each 8-element chunk reordered (0,4,1,5,2,6,3,7),
-  // and the token sums per quantization group: the group's group/8 chunks sit
-  // in consecutive lanes, each lane adds its 8 elements, then a butterfly over
-  // those lanes (fixed order) gives the group sum
-  const int ldx = KC + 8;
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(sm + L.x_off);
-  float* xsum = reinterpret_cast<float*>(sm + L.xsum_off);
-  {
-    const int vpr = KC / 8, cpg = q.group / 8;  // chunks per row, per group (a power of two <= 32)
-    const int total = p.M * vpr;
-    for (int base = warp * 32; base < total; base += w4s::kThreads) {
-      const int i = base + lane;
-      const bool on = i < total;  // the group's lanes are all on or all off
-      const int r = on ? i / vpr : 0, c = on ? i - r * vpr : 0;
-      float v = 0.f;
-      if (on) {
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(X + static_cast<long long>(r) * p.K + kc0) + c);
-        *reinterpret_cast<uint4*>(xs + r * ldx + c * 8) =
-            make_uint4(__byte_perm(u.x, u.z, 0x5410), __byte_perm(u.x, u.z, 0x7632),
-                       __byte_perm(u.y, u.w, 0x5410), __byte_perm(u.y, u.w, 0x7632));
-        const uint32_t e[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&e[j]));
-          v += f.x;
-          v += f.y;
-        }
-      }
-      for (int off = cpg >> 1; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-      if (on && (c & (cpg - 1)) == 0) xsum[r * GC + c / cpg] = v;
-    }
+  if (threadIdx.x == 0) {
+    mbar_expect_tx(bar_x, static_cast<uint32_t>(p.M * KC * 2));
+#pragma unroll 1
+    for (int r = 0; r < p.M; ++r)
+      bulk_load(sm + L.x_off + r * L.x_stride, X + static_cast<long long>(r) * p.K + kc0, KC * 2, bar_x);
   }
-  __syncthreads();
-  bool ok = mbar_wait_drain(bar, 0);  // bounded; a bulk copy of valid memory completes
+  bool ok = mbar_wait_drain(bar_w, 0) && mbar_wait_drain(bar_x, 0);  // bounded; copies of valid memory complete
   if (!ok && threadIdx.x == 0) record_error(kDevWaitTimeout, 0x300u, 1);
 
   const int g = lane >> 2, t = lane & 3;
@@ -586,39 +569,36 @@ k_gemm_w4a16_small(const __nv_bfloat16* __restrict__ X, EpiParams p, W4Params q)
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   if (ok) {
     const uint8_t* wrow = sm + L.w_off + (nt * 8 + g) * L.w_stride + kp * KW / 2;
-    // scale / zero of the two weight rows of this lane's D columns
+    // zero point of this lane's B column (weight row nt*8 + g); scales of its D columns (rows r0, r0 + 1)
+    const uint32_t* zgp = reinterpret_cast<const uint32_t*>(sm + L.z_off) + (nt * 8 + g) * q.zw;
     const int r0 = nt * 8 + 2 * t;
     const __half* s0p = reinterpret_cast<const __half*>(sm + L.s_off) + r0 * q.G;
-    const uint32_t* z0p = reinterpret_cast<const uint32_t*>(sm + L.z_off) + r0 * q.zw;
     const int a_row = (lane & 7) + ((lane >> 3) & 1) * 8;
-    const uint32_t a_base =
-        smem_u32(xs + (a_row < p.M ? a_row : 0) * ldx + kp * KW + (lane >> 4) * 8);
-    const int m0 = g < p.M ? g : 0, m1 = g + 8 < p.M ? g + 8 : 0;
-    const int t4 = 4 * t;
+    const uint32_t a_base = smem_u32(sm + L.x_off + (a_row < p.M ? a_row : 0) * L.x_stride) +
+                            static_cast<uint32_t>(kp * KW + (lane >> 4) * 8) * 2u;
+    const int t8 = 8 * t;
 #pragma unroll 1
     for (int gl = 0; gl < KW / q.group; ++gl) {
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      const int grp = (kc0 + kp * KW) / q.group + gl;
+      const uint32_t z = (zgp[grp >> 3] >> (4 * (grp & 7))) & 0xFu;
+      const uint32_t zb = (0x4300u | z) * 0x00010001u;
+      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
       const int kg = gl * q.group;
 #pragma unroll 4
       for (int k = kg; k < kg + q.group; k += 32) {
         const uint4 w = *reinterpret_cast<const uint4*>(wrow + k / 2);  // elements k .. k + 31 of row g
         uint32_t a[4];
         ldmatrix_x4(a, a_base + static_cast<uint32_t>(k) * 2u);
-        mma_bf16_16816(d, a, nibbles_bf16x2(w.x, t4), nibbles_bf16x2(w.y, t4));
+        mma_bf16_16816(d0, a, nibble_pair_minus_z(w.x, t8, zb), nibble_pair_minus_z(w.y, t8, zb));
         ldmatrix_x4(a, a_base + static_cast<uint32_t>(k + 16) * 2u);
-        mma_bf16_16816(d, a, nibbles_bf16x2(w.z, t4), nibbles_bf16x2(w.w, t4));
+        mma_bf16_16816(d1, a, nibble_pair_minus_z(w.z, t8, zb), nibble_pair_minus_z(w.w, t8, zb));
       }
-      // the group's contribution: s (D - (128 + z) sum x), columns r0, r0 + 1
-      const int grp = (kc0 + kp * KW) / q.group + gl;
-      const int glc = kp * KW / q.group + gl;  // group index within this CTA's token sums
+      // the group's contribution: s D, columns r0, r0 + 1
       const float sa = __half2float(s0p[grp]), sb = __half2float(s0p[q.G + grp]);
-      const float za = 128.0f + static_cast<float>((z0p[grp >> 3] >> (4 * (grp & 7))) & 0xFu);
-      const float zb = 128.0f + static_cast<float>((z0p[q.zw + (grp >> 3)] >> (4 * (grp & 7))) & 0xFu);
-      const float x0 = xsum[m0 * GC + glc], x1 = xsum[m1 * GC + glc];
-      acc[0] = fmaf(sa, fmaf(-za, x0, d[0]), acc[0]);
-      acc[1] = fmaf(sb, fmaf(-zb, x0, d[1]), acc[1]);
-      acc[2] = fmaf(sa, fmaf(-za, x1, d[2]), acc[2]);
-      acc[3] = fmaf(sb, fmaf(-zb, x1, d[3]), acc[3]);
+      acc[0] = fmaf(sa, d0[0] + d1[0], acc[0]);
+      acc[1] = fmaf(sb, d0[1] + d1[1], acc[1]);
+      acc[2] = fmaf(sa, d0[2] + d1[2], acc[2]);
+      acc[3] = fmaf(sb, d0[3] + d1[3], acc[3]);
     }
   }
   // warps of one n-tile add their K parts in order

@@ -915,9 +915,10 @@ static int launch_w4a16(const void* X, const void* wq, const void* scales, const
   q.kw = K / 8;
   if (M <= w4s::kMaxM && group >= 32 && group <= 256 && (group & (group - 1)) == 0 && K % (8 * group) == 0 &&
       aligned16(scales) && aligned16(zeros)) {
-    // small M: rows per CTA and the cluster's K split grow with M, so that
-    // each CTA stages at most 4 token rows x K of activations
-    if (M <= 4) rc = launch_w4_small<1, 1>(X, p, q, stream);
+    // small M: weight rows per CTA and the cluster's K split grow with M
+    // (measured at 3072 x 3072, g128: M = 1 6.2 us on <1, 1> against 7.0 on
+    // <2, 2>; M = 4 13.0 us on <1, 1> against 8.5 on <2, 2>)
+    if (M <= 1) rc = launch_w4_small<1, 1>(X, p, q, stream);
     else if (M <= 8) rc = launch_w4_small<2, 2>(X, p, q, stream);
     else rc = launch_w4_small<4, 4>(X, p, q, stream);
     if (rc != QI_B200_ESHAPE) return rc;  // ESHAPE: shared memory too small, use the split-K kernel
