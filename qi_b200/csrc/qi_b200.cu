@@ -915,12 +915,12 @@ static int launch_w4a16(const void* X, const void* wq, const void* scales, const
   q.kw = K / 8;
   if (M <= w4s::kMaxM && group >= 32 && group <= 256 && (group & (group - 1)) == 0 && K % (8 * group) == 0 &&
       aligned16(scales) && aligned16(zeros)) {
-    // small M: weight rows per CTA and the cluster's K split grow with M
-    // (measured at 3072 x 3072, g128: M = 1 6.2 us on <1, 1> against 7.0 on
-    // <2, 2>; M = 4 13.0 us on <1, 1> against 8.5 on <2, 2>)
+    // small M (3072 x 3072, g128, compared in one process): one token, one
+    // column of CTAs (5.2 us against 7.0 as CTA pairs); more, CTA pairs
+    // splitting K (M = 4 / 16: 6.7 / 8.4 us against 13.0 on one column / 9.8
+    // on clusters of 4)
     if (M <= 1) rc = launch_w4_small<1, 1>(X, p, q, stream);
-    else if (M <= 8) rc = launch_w4_small<2, 2>(X, p, q, stream);
-    else rc = launch_w4_small<4, 4>(X, p, q, stream);
+    else rc = launch_w4_small<2, 2>(X, p, q, stream);
     if (rc != QI_B200_ESHAPE) return rc;  // ESHAPE: shared memory too small, use the split-K kernel
   }
   if (M <= 16) return launch_w4_skinny<16>(X, p, q, di->num_sms, stream);
