@@ -58,19 +58,21 @@ def m_invariant(layer) -> bool:
 
 
 def plan_chunks(rows: int, chunk_rows: int | None, independent: bool,
-                row_bytes: int = 0, min_chunk: int = 1) -> list[tuple[int, int]]:
+                row_bytes: int = 0, min_chunk: int = 1, graph: bool = False) -> list[tuple[int, int]]:
     """Row ranges [r0, r1) of the chunks.  By default (``chunk_rows`` None)
     the transfer is split only when it is large: one chunk per 16 MiB of
-    host<->device bytes (``row_bytes`` per row, in + out), at most 8 chunks,
-    each a multiple of 128 rows and at least 256 rows.  Below that the copies
-    take less time than the extra stream synchronisation saves.  Chunks are
-    never shorter than ``min_chunk`` rows (one chunk when rows <= min_chunk)."""
+    host<->device bytes (``row_bytes`` per row, in + out), at most 8 chunks
+    (``graph``: one per 2 MiB, at most 16, since a CUDA-graph replay has no
+    per-chunk host cost), each a multiple of 128 rows and at least 256 rows.
+    Below that the copies take less time than the extra stream
+    synchronisation saves.  Chunks are never shorter than ``min_chunk`` rows
+    (one chunk when rows <= min_chunk)."""
     if rows <= 0:
         return []
     if not independent or rows <= min_chunk:
         return [(0, rows)]
     if chunk_rows is None:
-        n = min(8, (rows * row_bytes) // (16 << 20))
+        n = min(16, (rows * row_bytes) // (2 << 20)) if graph else min(8, (rows * row_bytes) // (16 << 20))
         if n <= 1:
             return [(0, rows)]
         chunk_rows = max(256, 128 * math.ceil(rows / n / 128))
@@ -128,6 +130,34 @@ class HostLinearPipeline:
             b = bufs[s] = torch.empty((rows, cols), dtype=dtype, device=self.device)
         return b[:rows]
 
+    def capture(self, x_host: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Record one call on these pinned buffers as a CUDA graph (after one
+        eager call that sets up the staging buffers); ``replay()`` then reruns
+        all its copies and kernels with no per-chunk host work, so finer chunks
+        pay off.  The buffers' contents may change between replays, their
+        addresses may not.  Returns ``out``."""
+        if out is None:
+            out = torch.empty((*x_host.shape[:-1], self.layer.out_features), dtype=x_host.dtype).pin_memory()
+        self._graph_chunks = True
+        try:
+            self(x_host, out)
+            torch.cuda.current_stream(self.device).synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self(x_host, out)
+        finally:
+            self._graph_chunks = False
+        self._graph, self._graph_out = g, out
+        return out
+
+    def replay(self) -> torch.Tensor:
+        """Rerun the captured call on the caller's current stream's device
+        (asynchronous, as the call itself); returns its ``out``."""
+        if getattr(self, "_graph", None) is None:
+            raise RuntimeError("capture() first.")
+        self._graph.replay()
+        return self._graph_out
+
     def __call__(self, x_host: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         if x_host.is_cuda:
             raise ValueError("HostLinearPipeline takes a host tensor; call the layer directly on device tensors.")
@@ -149,7 +179,9 @@ class HostLinearPipeline:
         y2 = out.view(rows, n_out)
         chunks = plan_chunks(rows, self.chunk_rows, self.independent,
                              row_bytes=kin * x2.element_size() + n_out * out.element_size(),
-                             min_chunk=1 if self.m_invariant else M_VARIANT_MIN_CHUNK)
+                             min_chunk=1 if self.m_invariant else M_VARIANT_MIN_CHUNK,
+                             # weight-only formats dequantize the weights for every chunk: few chunks
+                             graph=getattr(self, "_graph_chunks", False) and self.m_invariant)
         if not chunks:
             return out
         main = torch.cuda.current_stream(self.device)

@@ -92,6 +92,26 @@ def test_pipeline_matches_device_forward(kind, rows, chunk):
         assert n_chunks == -(-rows // chunk)
 
 
+@pytest.mark.parametrize("kind", ["int8", "fp8", "w4a16"])
+def test_pipeline_graph_replay(kind):
+    """capture() records the chunked call as a CUDA graph on fixed pinned
+    buffers; replay() with new input contents gives the device forward."""
+    N, K, rows = 768, 1024, 3000
+    layer = _layer(kind, N, K, gelu=kind != "w4a16", seed=11)
+    pipe = HostLinearPipeline(layer, chunk_rows=512)
+    xh = torch.empty(rows, K, dtype=torch.bfloat16).pin_memory()
+    g = torch.Generator().manual_seed(3)
+    xh.copy_((torch.randn(rows, K, generator=g) * 2).to(torch.bfloat16))
+    out = pipe.capture(xh)
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(out, layer(xh.to(DEV)).cpu())
+    for seed in (4, 5):
+        xh.copy_((torch.randn(rows, K, generator=torch.Generator().manual_seed(seed)) * 2).to(torch.bfloat16))
+        y = pipe.replay()
+        torch.cuda.current_stream().synchronize()
+        assert y is out and torch.equal(out, layer(xh.to(DEV)).cpu()), seed
+
+
 def test_pipeline_3d_input_and_errors():
     layer = _layer("int8", 256, 512, gelu=False, seed=3)
     x = torch.randn(2, 90, 512).to(torch.bfloat16)
