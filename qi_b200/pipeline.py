@@ -62,7 +62,7 @@ def plan_chunks(rows: int, chunk_rows: int | None, independent: bool,
     """Row ranges [r0, r1) of the chunks.  By default (``chunk_rows`` None)
     the transfer is split only when it is large: one chunk per 16 MiB of
     host<->device bytes (``row_bytes`` per row, in + out), at most 8 chunks
-    (``graph``: one per 2 MiB, at most 16, since a CUDA-graph replay has no
+    (``graph``: one per 8 MiB, at most 16, since a CUDA-graph replay has no
     per-chunk host cost), each a multiple of 128 rows and at least 256 rows.
     Below that the copies take less time than the extra stream
     synchronisation saves.  Chunks are never shorter than ``min_chunk`` rows
@@ -72,7 +72,7 @@ def plan_chunks(rows: int, chunk_rows: int | None, independent: bool,
     if not independent or rows <= min_chunk:
         return [(0, rows)]
     if chunk_rows is None:
-        n = min(16, (rows * row_bytes) // (2 << 20)) if graph else min(8, (rows * row_bytes) // (16 << 20))
+        n = min(16, (rows * row_bytes) // (8 << 20)) if graph else min(8, (rows * row_bytes) // (16 << 20))
         if n <= 1:
             return [(0, rows)]
         chunk_rows = max(256, 128 * math.ceil(rows / n / 128))

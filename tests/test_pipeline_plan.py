@@ -29,9 +29,9 @@ def test_plan_chunks_defaults():
     # 4096 x (3072 + 3072) bf16 = 50 MB -> 3 chunks, multiples of 128 rows
     assert plan_chunks(4096, None, True, 2 * (3072 + 3072)) == [(0, 1408), (1408, 2816), (2816, 4096)]
     assert plan_chunks(4096, None, True) == [(0, 4096)]
-    # the graph form: one chunk per 2 MiB, at most 16, >= 256 rows (config 2: 16 chunks of 256 rows; config 1: 2)
+    # the graph form: one chunk per 8 MiB, at most 16, >= 256 rows (config 2: 16 chunks of 256 rows; config 1: 1)
     assert plan_chunks(4096, None, True, 2 * (3072 + 14336), graph=True) == [(i * 256, (i + 1) * 256) for i in range(16)]
-    assert plan_chunks(512, None, True, 2 * (3072 + 3072), graph=True) == [(0, 256), (256, 512)]
+    assert plan_chunks(512, None, True, 2 * (3072 + 3072), graph=True) == [(0, 512)]
     assert plan_chunks(4096, 128, False) == [(0, 4096)]
     assert plan_chunks(0, None, True) == []
     with pytest.raises(ValueError):
