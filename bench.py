@@ -365,6 +365,9 @@ def measure_linear(cfg_name: str, args, world: int, rank: int, local: int, devic
         gemm_ms = g0.elapsed_time(g1) / args.steps
         gemm_src = f"cuda events around {args.steps} back-to-back eager launches"
     gemm_ms = max_over_ranks(gemm_ms, world, device)
+    library = None
+    if world == 1 and pre is not None and c["kind"] in ("fp8", "int8"):
+        library = library_comparison(kind, pre, wqs, ws, bias, ncopy, args.steps, stream)
     _lib.raise_on_device_error()  # a bounded device wait timed out: the numbers are void
 
     flops_total = 2.0 * M * N * Kd
@@ -465,6 +468,8 @@ def measure_linear(cfg_name: str, args, world: int, rank: int, local: int, devic
         label += (" with the all-gather fused into its epilogue (TMA stores to every rank) + 2 barriers "
                   "(activation quantizer included)")
     roofline.update({"kernel": label, "kernel_ms": round(gemm_ms, 5), "kernel_timing": gemm_src})
+    if library is not None:
+        roofline["library"] = library
 
     result = {
         "metric": "quantized_gemm_tops", "value": round(value, 2), "unit": "TOPS", "n_gpus": world,
@@ -719,6 +724,53 @@ def dit_cpu_baseline():
             "sample": "ReferenceBackend.linear port over the 20 INT8 Linears of 1 of 30 layers (full token "
                       "counts), scaled x30; attention and norms not included",
             "ms_per_layer": round(dt * 1e3, 1)}
+
+
+def library_comparison(kind, pre, wqs, ws, bias, ncopy, steps, stream) -> dict:
+    """The same quantized GEMM through NVIDIA's library on the same operands,
+    timed like the dominant kernel (a graph of back-to-back launches), beside
+    this library's kernel with the same epilogue: FP8 through cuBLASLt
+    (torch._scaled_mm: per-row x per-column scales, bias, bf16 out; it fuses
+    no GELU), INT8 through cuBLAS (torch._int_mm: int32 accumulators out, so
+    ours returns its raw int32 accumulators too).  Each side is timed twice,
+    interleaved, best of the two."""
+    from qi_b200 import _lib, kernels as K
+
+    fp8 = kind == _lib.KIND_FP8_E4M3
+    if fp8:
+        f8 = torch.float8_e4m3fn
+        ws_row = ws.reshape(1, -1).float().contiguous()
+        sas = [s.reshape(-1, 1).contiguous() for _, s in pre]
+        name = "cuBLASLt FP8 via torch._scaled_mm (per-row x per-column scales, bias, bf16 out)"
+
+        def lib(i):
+            q, _ = pre[i % ncopy]
+            return torch._scaled_mm(q.view(f8), wqs[i % ncopy].view(f8).t(), scale_a=sas[i % ncopy],
+                                    scale_b=ws_row, bias=bias, out_dtype=torch.bfloat16)
+
+        def ours(i):
+            q, s = pre[i % ncopy]
+            return K.gemm(kind, q, wqs[i % ncopy], s, ws, bias)
+    else:
+        name = "cuBLAS INT8 via torch._int_mm (int32 accumulators out)"
+
+        def lib(i):
+            return torch._int_mm(pre[i % ncopy][0], wqs[i % ncopy].t())
+
+        def ours(i):
+            return K.gemm(kind, pre[i % ncopy][0], wqs[i % ncopy], None, None, raw_acc=True)
+    try:
+        lib(0)  # eager first call: the library sets up its handle and workspace outside graph capture
+        ours(0)
+        torch.cuda.synchronize()
+        t_lib, t_ours = [], []
+        for _ in range(2):
+            t_ours.append(time_gemm_alone(ours, steps, stream))
+            t_lib.append(time_gemm_alone(lib, steps, stream))
+    except Exception as e:  # the library may not take this shape
+        return {"name": name, "error": repr(e)[:200]}
+    return {"name": name, "library_ms": round(min(t_lib), 5), "ours_same_epilogue_ms": round(min(t_ours), 5),
+            "library_over_ours": round(min(t_lib) / min(t_ours), 3)}
 
 
 def time_gemm_alone(step, steps, stream):

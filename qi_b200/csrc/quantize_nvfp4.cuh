@@ -213,15 +213,25 @@ __device__ __forceinline__ uint2 nvfp4_block_fast(const uint4& v0, const uint4& 
     b[k] = __fmul2_rn(f[k], ih2);
   }
   uint32_t lo = e2m1x8(a[0], a[1], a[2], a[3]), hi = e2m1x8(a[4], a[5], a[6], a[7]);
-  if (lo != e2m1x8(b[0], b[1], b[2], b[3]) || hi != e2m1x8(b[4], b[5], b[6], b[7])) {
-    // a quotient within a few ulp of a rounding boundary: the block's codes by
-    // correctly rounded division (identical to the bracket's code elsewhere)
+  // nibbles whose bracket ends convert differently: a quotient within a few
+  // ulp of a rounding boundary.  Only those elements are recomputed by
+  // correctly rounded division.  Exact ties are common with a per-tensor g
+  // (amax / 2688 = amax / (2^7 * 3 * 7) against E4M3 block scales carrying a
+  // factor 3 or 7, such as 1.5 or 1.75):
+  // on N(0, 1) data about 1 % of the blocks have one, so recomputing a whole
+  // block would run 16 divisions in a quarter of all 32-block warp steps;
+  // per element, a division runs only where some lane needs that element.
+  const uint32_t dlo = lo ^ e2m1x8(b[0], b[1], b[2], b[3]), dhi = hi ^ e2m1x8(b[4], b[5], b[6], b[7]);
+  if ((dlo | dhi) != 0u) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k)
-      a[k] = make_float2(fminf(fmaxf(__fdiv_rn(f[k].x, denom), -6.f), 6.f),
-                         fminf(fmaxf(__fdiv_rn(f[k].y, denom), -6.f), 6.f));
-    lo = e2m1x8(a[0], a[1], a[2], a[3]);
-    hi = e2m1x8(a[4], a[5], a[6], a[7]);
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t d = k < 4 ? dlo : dhi;
+      uint32_t& word = k < 4 ? lo : hi;
+      const int sh = 8 * (k & 3);  // element 2k in the low nibble of byte k & 3, element 2k + 1 in the high one
+      if (d & (0xFu << sh)) word = (word & ~(0xFu << sh)) | ((e2m1x2(__fdiv_rn(f[k].x, denom), 0.f) & 0xFu) << sh);
+      if (d & (0xF0u << sh))
+        word = (word & ~(0xF0u << sh)) | ((e2m1x2(__fdiv_rn(f[k].y, denom), 0.f) & 0xFu) << (sh + 4));
+    }
   }
   return make_uint2(lo, hi);
 }
