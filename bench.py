@@ -78,7 +78,7 @@ _REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_
 
 class ClockSampler:
     def __init__(self, device_index: int):
-        self.samples, self.reasons, self.ok = [], 0, False
+        self.samples, self.reasons, self.ok, self.power = [], 0, False, []
         self._stop = threading.Event()
         try:
             import pynvml
@@ -96,6 +96,7 @@ class ClockSampler:
             try:
                 self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
                 self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.power.append(nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0)
             except Exception:
                 pass
             time.sleep(0.002)
@@ -115,8 +116,11 @@ class ClockSampler:
         if not self.ok or not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
         names = [n for b, n in _REASONS.items() if self.reasons & b and n != "gpu_idle"]
-        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": names,
-                "samples": len(self.samples)}
+        out = {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": names,
+               "samples": len(self.samples)}
+        if self.power:
+            out["power_w"] = round(statistics.median(self.power), 1)
+        return out
 
 
 # --------------------------------------------------------------------------
@@ -368,6 +372,10 @@ def measure_linear(cfg_name: str, args, world: int, rank: int, local: int, devic
     library = None
     if world == 1 and pre is not None and c["kind"] in ("fp8", "int8"):
         library = library_comparison(kind, pre, wqs, ws, bias, ncopy, args.steps, stream)
+    sustained = None
+    if args.sustain > 0 and world == 1 and pre is not None:
+        sustained = sustained_gemm(c, kind, pre, wqs, ws, layer, bias, ncopy, args, local, stream,
+                                   2.0 * M * Nl * Kd)
     _lib.raise_on_device_error()  # a bounded device wait timed out: the numbers are void
 
     flops_total = 2.0 * M * N * Kd
@@ -470,6 +478,8 @@ def measure_linear(cfg_name: str, args, world: int, rank: int, local: int, devic
     roofline.update({"kernel": label, "kernel_ms": round(gemm_ms, 5), "kernel_timing": gemm_src})
     if library is not None:
         roofline["library"] = library
+    if sustained is not None:
+        roofline["sustained"] = sustained
 
     result = {
         "metric": "quantized_gemm_tops", "value": round(value, 2), "unit": "TOPS", "n_gpus": world,
@@ -773,6 +783,56 @@ def library_comparison(kind, pre, wqs, ws, bias, ncopy, steps, stream) -> dict:
             "library_over_ours": round(min(t_lib) / min(t_ours), 3)}
 
 
+def sustained_gemm(c, kind, pre, wqs, ws, layer, bias, ncopy, args, local, stream, flops) -> dict:
+    """The dominant GEMM replayed back to back for ``args.sustain`` seconds,
+    with the config's operands and again with all-zero operand codes (same
+    scales), while NVML samples the SM clock, throttle reasons and board power.
+    Zero codes toggle no multiplier bits: the gap between the two rows is what
+    the board power cap takes from the kernel."""
+    from qi_b200 import kernels as K
+
+    def make(zero):
+        if c["kind"] == "nvfp4":
+            ops = [(torch.zeros_like(qa) if zero else qa, sfa, ga) for qa, sfa, ga in pre]
+            ws_ = [torch.zeros_like(w) if zero else w for w in wqs]
+            return lambda i: K.nvfp4_gemm(*ops[i % ncopy][:2], ws_[i % ncopy], layer.scale_factors,
+                                          ops[i % ncopy][2], ws, bias)
+        ops = [(torch.zeros_like(q) if zero else q, s) for q, s in pre]
+        ws_ = [torch.zeros_like(w) if zero else w for w in wqs]
+        return lambda i: K.gemm(kind, ops[i % ncopy][0], ws_[i % ncopy], ops[i % ncopy][1], ws, bias,
+                                gelu=c["gelu"])
+
+    out = {"seconds": args.sustain}
+    for name in ("operands", "zero_operands"):
+        f = make(name == "zero_operands")
+        n = 20
+        f(0)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(n):
+                f(i)
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 0
+        with ClockSampler(local) as clk:
+            time.sleep(0.2)
+            a.record(stream)
+            t0 = time.time()
+            while time.time() - t0 < args.sustain:
+                g.replay()
+                reps += 1
+                if reps % 10 == 0:
+                    torch.cuda.synchronize()
+            b.record(stream)
+            torch.cuda.synchronize()
+        us = a.elapsed_time(b) / (reps * n) * 1e3
+        out[name] = {"us": round(us, 2), "tflops": round(flops / (us * 1e-6) / 1e12, 1), **clk.summary()}
+        del g
+    return out
+
+
 def time_gemm_alone(step, steps, stream):
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
@@ -954,6 +1014,9 @@ def main():
     ap.add_argument("--gather", default="auto", choices=["auto", "peer", "nccl"],
                     help="N > 1, INT8/FP8: all-gather fused into the GEMM epilogue (peer), a separate "
                          "NCCL call (nccl), or auto (peer at 2 ranks, NCCL beyond)")
+    ap.add_argument("--sustain", type=float, default=0.0,
+                    help="single-linear configs, 1 GPU: also replay the dominant GEMM for this many seconds "
+                         "with the config's operands and with all-zero codes, sampling clocks and power")
     ap.add_argument("--layers", type=int, default=0,
                     help="dit only: fewer layers than config 5's 30 (profiling captures; not a bench value)")
     args = ap.parse_args()
