@@ -76,10 +76,17 @@ struct Gemm2Cfg {
   static constexpr int THREADS = (EPI_WARP0 + kEpiWarps) * 32;
   static constexpr int COLPARAM_BYTES = 2 * BN * (4 + 2);
   static constexpr int BAR_BYTES = 512;
-  // fused gather: one 32-row x 64-column bf16 box (128-byte rows) per epilogue
-  // warp (measured on 2 GPUs: 64-column boxes with 5 stages beat 32-column
-  // boxes by 25 % and 128-column boxes with 4 stages by 10 %)
-  static constexpr int STAGING_BYTES = GATHER_ ? kEpiWarps * 32 * 64 * 2 : 0;
+  // bf16 results leave through one 32-row x 64-column box (128-byte rows) of
+  // shared memory per epilogue warp and TMA stores: for the fused gather (to
+  // every rank; measured on 2 GPUs: 64-column boxes with 5 stages beat
+  // 32-column boxes by 25 % and 128-column boxes with 4 stages by 10 %), and
+  // for the NVFP4 256-wide tile, whose single accumulator buffer makes the
+  // MMAs wait for the whole epilogue.  There row-per-lane global stores (32
+  // rows per warp instruction) cost about 5 us per tile; staged in 128-byte
+  // swizzled boxes (conflict-free row writes) and stored by TMA they run
+  // behind the next tile's MMAs (config 4: 92 -> 84 us).
+  static constexpr bool TMA_OUT = GATHER_ || (NVF4 && BN == 256);
+  static constexpr int STAGING_BYTES = TMA_OUT ? kEpiWarps * 32 * 64 * 2 : 0;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + COLPARAM_BYTES + BAR_BYTES + STAGING_BYTES + 1024;
   static constexpr uint32_t IDESC = (KIND == MmaKind::I8)     ? make_idesc(kDS32, kFmtS8, kFmtS8, 256, BN)
                                     : (KIND == MmaKind::F8)   ? make_idesc(kDF32, kFmtE4M3, kFmtE4M3, 256, BN)
@@ -92,7 +99,7 @@ struct Gemm2Cfg {
   static_assert(SF_COLS % 16 == 0, "scale slots are written 16 columns at a time");
   static_assert(BAR_BYTES >= 8 * (3 * STAGES + 2 * SF_SLOTS + 7) + 8, "barrier region");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
-  static_assert(!GATHER_ || BN % 128 == 0, "gather boxes are 64 columns per epilogue warp");
+  static_assert(!TMA_OUT || BN % 128 == 0, "output boxes are 64 columns per epilogue warp");
 };
 
 // One work item of a pair: a whole tile, or (tail split) a K range of one of
@@ -228,7 +235,7 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
   uint8_t* sB = smem + STAGES * C::A_BYTES;
   uint8_t* sSFA = sB + STAGES * C::B_BYTES;      // NVFP4 only
   uint8_t* sSFB = sSFA + STAGES * C::SFA_BYTES;  // NVFP4 only
-  uint8_t* staging = sSFB + STAGES * C::SFB_BYTES;  // 1024-byte aligned: 8 boxes of 32 x 64 bf16 (GATHER)
+  uint8_t* staging = sSFB + STAGES * C::SFB_BYTES;  // 1024-byte aligned: 8 boxes of 32 x 64 bf16 (TMA_OUT)
   float* col_scale = reinterpret_cast<float*>(staging + C::STAGING_BYTES);
   __nv_bfloat16* col_bias = reinterpret_cast<__nv_bfloat16*>(col_scale + 2 * BN);
   uint64_t* full = reinterpret_cast<uint64_t*>(col_bias + 2 * BN);
@@ -493,6 +500,37 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
       for (int c = 0; c < COLS; c += 64) {
         const int n0 = nb * BN + half * COLS + c;
         if (n0 >= p.N) break;  // warp-uniform
+        if constexpr (C::TMA_OUT && !GATHER) {
+          if (!(p.flags & kEpiRawAcc)) {
+            // this warp's 32 x 64 box, one 32-column chunk at a time (fewer
+            // live registers), rows 128-byte swizzled (16-byte chunk q of row
+            // r at q ^ (r & 7)); one TMA store into D, clipped to [M, N]
+            const int j0 = half * COLS + c;
+            uint8_t* box = staging + (warp - kFirstEpi) * (32 * 64 * 2);
+            const int row_base = mb * 256 + static_cast<int>(rank) * C::BM + wq * 32;
+            if (lane == 0) bulk_wait_read_all();  // the previous box has left shared memory
+            __syncwarp();
+            uint4* dst = reinterpret_cast<uint4*>(box + lane * 128);
+            const int sw = lane & 7;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              uint32_t r[32], pk[16];
+              tmem_ld_32x32b_x32(taddr + c + 32 * hh, r);
+              tmem_ld_wait();
+              epilogue_chunk<KIND>(r, p, m, n0 + 32 * hh, sa, sb_t + j0 + 32 * hh, bias_t + j0 + 32 * hh, pk);
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4)
+                dst[(4 * hh + q4) ^ sw] = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&om.map[0], box, n0, row_base);
+              bulk_commit_group();
+            }
+            continue;
+          }
+        }
         uint32_t r0[32], r1[32];
         const bool two = (COLS - c) >= 64;
         tmem_ld_32x32b_x32(taddr + c, r0);
@@ -551,12 +589,13 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
     }
   }
 
-  if (GATHER && warp >= kFirstEpi && lane == 0) {
-    // the fused gather's stores have reached every destination before the
-    // kernel retires (the cross-GPU barrier that follows publishes them)
+  if (C::TMA_OUT && warp >= kFirstEpi && lane == 0) {
+    // the TMA stores have completed before the kernel retires (the fused
+    // gather's have reached every destination; the cross-GPU barrier that
+    // follows publishes them)
     bulk_wait_all();
     fence_proxy_async_global();
-    __threadfence_system();
+    if (GATHER) __threadfence_system();
   }
   tc_fence_before();
   __syncthreads();

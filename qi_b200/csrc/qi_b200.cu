@@ -228,7 +228,16 @@ static int launch_gemm2_cfg(const void* A, const void* B, const EpiParams& p, in
                             const OutMaps* om_in = nullptr) {
   using C = Gemm2Cfg<KIND, BN, STAGES, GATHER>;
   static OutMaps kNoMaps = {};  // n = 0: plain epilogue stores
-  const OutMaps& om = om_in != nullptr ? *om_in : kNoMaps;
+  OutMaps local = {};           // TMA-store epilogue into this GPU's output (bf16 results)
+  if constexpr (C::TMA_OUT && !GATHER) {
+    if (!(p.flags & kEpiRawAcc)) {
+      const int rc = make_tmap_2d(&local.map[0], p.D, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)p.N,
+                                  (uint64_t)p.M, (uint64_t)p.ldd * 2, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+      local.n = 1;
+    }
+  }
+  const OutMaps& om = om_in != nullptr ? *om_in : (C::TMA_OUT && !GATHER ? local : kNoMaps);
   const CUtensorMapDataType dt =
       (KIND == MmaKind::BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const uint64_t ku = C::NVF4 ? (uint64_t)p.K / 2 : (uint64_t)p.K;  // K in TMA elements (fp4: packed bytes)
