@@ -76,16 +76,19 @@ struct Gemm2Cfg {
   static constexpr int THREADS = (EPI_WARP0 + kEpiWarps) * 32;
   static constexpr int COLPARAM_BYTES = 2 * BN * (4 + 2);
   static constexpr int BAR_BYTES = 512;
-  // bf16 results leave through one 32-row x 64-column box (128-byte rows) of
-  // shared memory per epilogue warp and TMA stores: for the fused gather (to
-  // every rank; measured on 2 GPUs: 64-column boxes with 5 stages beat
-  // 32-column boxes by 25 % and 128-column boxes with 4 stages by 10 %), and
-  // for the NVFP4 256-wide tile, whose single accumulator buffer makes the
-  // MMAs wait for the whole epilogue.  There row-per-lane global stores (32
-  // rows per warp instruction) cost about 5 us per tile; staged in 128-byte
-  // swizzled boxes (conflict-free row writes) and stored by TMA they run
-  // behind the next tile's MMAs (config 4: 92 -> 84 us).
-  static constexpr bool TMA_OUT = GATHER_ || (NVF4 && BN == 256);
+  // bf16 results of 256-wide tiles leave through one 32-row x 64-column box
+  // (128-byte rows) of shared memory per epilogue warp and TMA stores: for
+  // the fused gather to every rank (measured on 2 GPUs: 64-column boxes with
+  // 5 stages beat 32-column boxes by 25 % and 128-column boxes with 4 stages
+  // by 10 %), and into this GPU's output, where row-per-lane global stores
+  // (32 rows per warp instruction) cost about 5 us per tile: the NVFP4 tile's
+  // single accumulator buffer makes the MMAs wait for all of it (config 4
+  // 92 -> 84 us), and with two buffers the stores still compete with the
+  // next tile's operand loads (FP8 config 2 157 -> 147 us, INT8 3120 x 14336
+  // x 3072 112 -> 105 us).  Local boxes are 128-byte swizzled (conflict-free
+  // row writes); the gather's are not.  The staging costs the 8-bit and bf16
+  // tiles their sixth pipeline stage (measured: no loss).
+  static constexpr bool TMA_OUT = GATHER_ || BN == 256;
   static constexpr int STAGING_BYTES = TMA_OUT ? kEpiWarps * 32 * 64 * 2 : 0;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + COLPARAM_BYTES + BAR_BYTES + STAGING_BYTES + 1024;
   static constexpr uint32_t IDESC = (KIND == MmaKind::I8)     ? make_idesc(kDS32, kFmtS8, kFmtS8, 256, BN)
@@ -501,7 +504,7 @@ k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUte
         const int n0 = nb * BN + half * COLS + c;
         if (n0 >= p.N) break;  // warp-uniform
         if constexpr (C::TMA_OUT && !GATHER) {
-          if (!(p.flags & kEpiRawAcc)) {
+          if (!(p.flags & kEpiRawAcc) && wk.unit < 0) {  // tail-split units store raw partials below
             // this warp's 32 x 64 box, one 32-column chunk at a time (fewer
             // live registers), rows 128-byte swizzled (16-byte chunk q of row
             // r at q ^ (r & 7)); one TMA store into D, clipped to [M, N]

@@ -402,7 +402,7 @@ static int launch_gemm(const void* A, const void* B, const EpiParams& p, cudaStr
   } else {
     if (force_bn < 0) {  // the CTA-pair kernel with tile width -force_bn
       switch (-force_bn) {
-        case 256: return launch_gemm2_cfg<KIND, 256, 6>(A, B, p, di->num_sms, stream);
+        case 256: return launch_gemm2_cfg<KIND, 256, 5>(A, B, p, di->num_sms, stream);
         case 192: return launch_gemm2_cfg<KIND, 192, 7>(A, B, p, di->num_sms, stream);
         case 128: return launch_gemm2_cfg<KIND, 128, 8>(A, B, p, di->num_sms, stream);
         default: return QI_B200_EINVAL;
@@ -427,7 +427,7 @@ static int launch_gemm(const void* A, const void* B, const EpiParams& p, cudaStr
       const int bk = KIND == MmaKind::BF16 ? 64 : 128;
       const int ptiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
       if (ptiles >= di->num_sms / 2 && tail_plan(ptiles, di->num_sms / 2, (p.K + bk - 1) / bk, p.tail_split) > 1)
-        return launch_gemm2_cfg<KIND, 256, 6>(A, B, p, di->num_sms, stream);
+        return launch_gemm2_cfg<KIND, 256, 5>(A, B, p, di->num_sms, stream);
     }
     const int bn = force_bn > 0 ? force_bn : pick_bn(p.M, p.N, di->num_sms);
     // Large problems on 256-wide tiles run as CTA pairs (256 x 256 tiles on two
@@ -436,7 +436,7 @@ static int launch_gemm(const void* A, const void* B, const EpiParams& p, cudaStr
     // 4096^3 77 -> 85 % of peak; small M stays on single-CTA tiles.
     if (force_bn == 0 && bn == 256 && p.M >= 1024 &&
         (long long)((p.M + 255) / 256) * ((p.N + 255) / 256) >= di->num_sms / 2)
-      return launch_gemm2_cfg<KIND, 256, 6>(A, B, p, di->num_sms, stream);
+      return launch_gemm2_cfg<KIND, 256, 5>(A, B, p, di->num_sms, stream);
     switch (bn) {
       case 256: return launch_gemm_cfg<KIND, 256, 4>(A, B, p, di->num_sms, stream);
       case 192: return launch_gemm_cfg<KIND, 192, 5>(A, B, p, di->num_sms, stream);
