@@ -90,7 +90,13 @@ struct GemmCfg {
   static constexpr int TMEM_COLS = (TMEM_NEED <= 32) ? 32 : (TMEM_NEED <= 64) ? 64 : (TMEM_NEED <= 128) ? 128 : (TMEM_NEED <= 256) ? 256 : 512;
   static constexpr int COLPARAM_BYTES = 2 * BN * (4 + 2);  // double-buffered column scales + bias
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + COLPARAM_BYTES + BAR_BYTES + 1024;  // + alignment slack
+  // 128-wide 8-bit / bf16 tiles store their bf16 results through one
+  // 128-byte-swizzled 32 x 64 shared-memory box per epilogue warp and a TMA
+  // store (row-per-lane global stores write 32 rows per warp instruction)
+  static constexpr bool TMA_OUT = (BN == 128 && !NVF4);
+  static constexpr int STAGING_BYTES = TMA_OUT ? 8 * 32 * 64 * 2 : 0;
+  static constexpr int SMEM_BYTES =
+      STAGES * STAGE_BYTES + STAGING_BYTES + COLPARAM_BYTES + BAR_BYTES + 1024;  // + alignment slack
   static constexpr uint32_t IDESC =
       (KIND == MmaKind::I8)   ? make_idesc(kDS32, kFmtS8, kFmtS8, BM, BN)
       : (KIND == MmaKind::F8) ? make_idesc(kDF32, kFmtE4M3, kFmtE4M3, BM, BN)
@@ -235,7 +241,8 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[W], const Epi
 
 template <MmaKind KIND, int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const EpiParams p) {
+k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const EpiParams p,
+          const __grid_constant__ CUtensorMap tmD) {
   using C = GemmCfg<KIND, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -243,8 +250,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
   uint8_t* sB = smem + STAGES * C::A_BYTES;
   uint8_t* sSFA = sB + STAGES * C::B_BYTES;      // NVFP4 only
   uint8_t* sSFB = sSFA + STAGES * C::SFA_BYTES;  // NVFP4 only
+  uint8_t* staging = sSFB + STAGES * C::SFB_BYTES;  // 1024-byte aligned: 8 output boxes (TMA_OUT)
   // per-tile column parameters, double buffered: [2][BN] fp32 scales, [2][BN] bf16 bias
-  float* col_scale = reinterpret_cast<float*>(sSFB + STAGES * C::SFB_BYTES);
+  float* col_scale = reinterpret_cast<float*>(staging + C::STAGING_BYTES);
   __nv_bfloat16* col_bias = reinterpret_cast<__nv_bfloat16*>(col_scale + 2 * BN);
   uint64_t* full = reinterpret_cast<uint64_t*>(col_bias + 2 * BN);
   uint64_t* empty = full + STAGES;
@@ -422,6 +430,36 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
       for (int c = 0; c < COLS; c += 64) {
         const int n0 = nb * BN + half * COLS + c;
         if (n0 >= p.N) break;  // warp-uniform
+        if constexpr (C::TMA_OUT) {
+          if (!(p.flags & kEpiRawAcc)) {
+            // this warp's 32 x 64 box, one 32-column chunk at a time, rows
+            // swizzled (16-byte chunk q of row r at q ^ (r & 7)); one TMA
+            // store into D, clipped to [M, N]
+            const int j0 = half * COLS + c;
+            uint8_t* box = staging + (warp - kFirstEpiWarp) * (32 * 64 * 2);
+            if (lane == 0) bulk_wait_read_all();  // the previous box has left shared memory
+            __syncwarp();
+            uint4* dst = reinterpret_cast<uint4*>(box + lane * 128);
+            const int sw = lane & 7;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              uint32_t r[32], pk[16];
+              tmem_ld_32x32b_x32(taddr + c + 32 * hh, r);
+              tmem_ld_wait();
+              epilogue_chunk<KIND>(r, p, m, n0 + 32 * hh, sa, sb_t + j0 + 32 * hh, bias_t + j0 + 32 * hh, pk);
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4)
+                dst[(4 * hh + q4) ^ sw] = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmD, box, n0, mb * C::BM + wq * 32);
+              bulk_commit_group();
+            }
+            continue;
+          }
+        }
         uint32_t r0[32], r1[32];
         const bool two = (COLS - c) >= 64;
         tmem_ld_32x32b_x32(taddr + c, r0);
@@ -436,6 +474,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
       }
       tc_fence_before();
       mbar_arrive_relaxed(&tempty[buf]);  // accumulator read (wait::ld); output stores need no ordering
+    }
+    if (C::TMA_OUT && lane == 0) {
+      bulk_wait_all();  // the TMA stores have completed before the kernel retires
+      fence_proxy_async_global();
     }
   }
 

@@ -204,6 +204,12 @@ static int launch_gemm_cfg(const void* A, const void* B, const EpiParams& p, int
   if (rc) return rc;
   rc = make_tmap_2d(&tb, B, dt, ku, (uint64_t)p.N, ku * C::ELEM, C::BK, BN);
   if (rc) return rc;
+  CUtensorMap td = {};  // bf16 output boxes of 32 rows x 64 columns (TMA-store epilogue)
+  if (C::TMA_OUT && !(p.flags & kEpiRawAcc)) {
+    rc = make_tmap_2d(&td, p.D, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)p.N, (uint64_t)p.M, (uint64_t)p.ldd * 2,
+                      64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
   static bool attr_done[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -217,7 +223,7 @@ static int launch_gemm_cfg(const void* A, const void* B, const EpiParams& p, int
   const int grid = tiles < num_sms ? tiles : num_sms;
   g_last_plan = {1 + static_cast<int>(KIND), grid, 1, BN, STAGES, C::SMEM_BYTES};
   const cudaError_t e =
-      launch_pdl(k_gemm_tc<KIND, BN, STAGES>, dim3(grid), dim3(kGemmThreads), C::SMEM_BYTES, stream, 1, ta, tb, p);
+      launch_pdl(k_gemm_tc<KIND, BN, STAGES>, dim3(grid), dim3(kGemmThreads), C::SMEM_BYTES, stream, 1, ta, tb, p, td);
   count_launches(1);
   return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
