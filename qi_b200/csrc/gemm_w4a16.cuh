@@ -77,21 +77,27 @@ struct W4Cfg {
 };
 
 // 8 nibbles of one word -> 8 bf16 (4 packed pairs, even element in the low
-// half), exact reference dequant.
-__device__ __forceinline__ void dequant8(uint32_t w, float s16x, float c, uint32_t* out4) {
-  float f[8];
+// half), exact reference dequant bf16(fp32((q - z) s)).  Each nibble is
+// placed by a byte permute into the mantissa of 0.5 (0x3F00_0000 | q << 16 =
+// 0.5 + q / 256); then fma(0.5 + q / 256, 256 s, -(128 + z) s) equals
+// (q - z) s in exact arithmetic (256 s and (128 + z) s are exact in fp32), so
+// its single rounding is fp32((q - z) s).  s256 = 256 s, c = -(128 + z) s.
+__device__ __forceinline__ void dequant8(uint32_t w, float s256, float c, uint32_t* out4) {
+  const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;  // byte b: nibble 2b / 2b + 1
+  const float2 s2 = make_float2(s256, s256), c2 = make_float2(c, c);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint32_t nib = (w >> (4 * j)) & 0xFu;
-    f[j] = fmaf(__uint_as_float(0x3F800000u | (nib << 19)), s16x, c);
+  for (int b = 0; b < 4; ++b) {
+    const uint32_t sel = 0x7044u | (static_cast<uint32_t>(b) << 8);  // [0, 0, byte b, 0x3F]
+    const float2 v = make_float2(__uint_as_float(__byte_perm(lo, 0x3F000000u, sel)),
+                                 __uint_as_float(__byte_perm(hi, 0x3F000000u, sel)));
+    const float2 f = __ffma2_rn(v, s2, c2);
+    out4[b] = pack_bf16x2(f.x, f.y);
   }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) out4[j] = pack_bf16x2(f[2 * j], f[2 * j + 1]);
 }
 
 // Scale / zero of one (row, group), fetched one group ahead.
 struct GroupScale {
-  float s16x = 0.f, c = 0.f;  // current group: 16*s and -(16+z)*s
+  float s256 = 0.f, c = 0.f;  // current group: 256 s and -(128 + z) s (dequant8)
   float s_next = 0.f;
   uint32_t z_next = 0;
   int cur = -1, next = -1;
@@ -102,8 +108,8 @@ struct GroupScale {
     z = (zw >> (4 * (g & 7))) & 0xFu;
   }
   __device__ __forceinline__ void set(float s, uint32_t z) {
-    s16x = s * 16.0f;
-    c = -(16.0f + static_cast<float>(z)) * s;
+    s256 = s * 256.0f;
+    c = -(128.0f + static_cast<float>(z)) * s;
   }
   __device__ __forceinline__ void advance(const W4Params& q, long long n, int g) {
     if (g == cur) return;
@@ -165,8 +171,8 @@ __device__ __forceinline__ bool dequant_rows_tmem(const W4Params& q, int n, bool
         const int g = group_of(kb0 + i);
         if (row_ok && g < q.G) gs.advance(q, n, g);
         uint32_t v[8];
-        dequant8(raw.x, gs.s16x, gs.c, v);
-        dequant8(raw.y, gs.s16x, gs.c, v + 4);
+        dequant8(raw.x, gs.s256, gs.c, v);
+        dequant8(raw.y, gs.s256, gs.c, v + 4);
         if (!row_ok) {
 #pragma unroll
           for (int t = 0; t < 8; ++t) v[t] = 0u;
@@ -377,15 +383,6 @@ k_gemm_w4a16_skinny(const __grid_constant__ CUtensorMap tmX, const EpiParams p, 
 // bf16((q - z) * s) of the tile kernel.
 // ---------------------------------------------------------------------------
 
-// two nibbles (elements 2t, 2t+1 of word w) -> packed bf16x2 of (q - z) * s:
-// 1 + q/16 is exact in fp32 (exponent 0, q in the top mantissa bits), and
-// fma(1 + q/16, 16 s, -(16 + z) s) rounds the exact (q - z) s once.
-__device__ __forceinline__ uint32_t dequant_pair(uint32_t w, int t, float s16x, float c) {
-  const uint32_t b = w >> (8 * t);
-  const float f0 = fmaf(__uint_as_float(0x3F800000u | ((b << 19) & 0x00780000u)), s16x, c);
-  const float f1 = fmaf(__uint_as_float(0x3F800000u | ((b << 15) & 0x00780000u)), s16x, c);
-  return pack_bf16x2(f0, f1);
-}
 
 // Weight-only quantized weights in the reference's own layout
 // (quantize.py:32-78: one int8 code per value, fp32 scales [N, G], int16
@@ -442,13 +439,15 @@ k_w4a16_dequant(W4Params q, __nv_bfloat16* __restrict__ out, int N, int K) {
     const float sc = __half2float(__ldg(q.scales + static_cast<long long>(n) * q.G + grp));
     const uint32_t z = (static_cast<uint32_t>(__ldg(q.zeros + static_cast<long long>(n) * q.zw + (grp >> 3))) >>
                         (4 * (grp & 7))) & 0xFu;
-    const float s16x = sc * 16.0f, c = -(16.0f + static_cast<float>(z)) * sc;
+    const float s256 = sc * 256.0f, c = -(128.0f + static_cast<float>(z)) * sc;
     const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
     uint4* dst = reinterpret_cast<uint4*>(out + static_cast<long long>(n) * K + k0);
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      dst[j] = make_uint4(dequant_pair(wd[j], 0, s16x, c), dequant_pair(wd[j], 1, s16x, c),
-                          dequant_pair(wd[j], 2, s16x, c), dequant_pair(wd[j], 3, s16x, c));
+    for (int j = 0; j < 4; ++j) {
+      uint32_t o[4];
+      dequant8(wd[j], s256, c, o);
+      dst[j] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
 }
 
