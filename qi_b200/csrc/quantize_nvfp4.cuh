@@ -263,6 +263,12 @@ k_quant_nvfp4_tensor(const __nv_bfloat16* __restrict__ x, int rows, int cols, co
   const float2 rg = make_float2(rg0 * (1.0f - 0x1p-20f), rg0 * (1.0f + 0x1p-20f));
   const int chunks = rows_pad * bpr / 32;  // the host keeps rows_pad * bpr < 2^31
   const int cstride = 256 * gridDim.x / 32;
+  // t / bpr for 0 <= t < 2^31 as mulhi(t, m) >> (l - 1), m = ceil(2^(31 + l) /
+  // bpr), l = ceil(log2 bpr) >= 2 (bpr = cols / 16 >= 4): the product's
+  // excess over t / bpr is below t / 2^(31 + l) < 1 / bpr, so the floor is exact
+  const uint32_t dl = 32u - static_cast<uint32_t>(__clz(bpr - 1));
+  const uint32_t dm = static_cast<uint32_t>(((1ull << (31 + dl)) + static_cast<unsigned>(bpr) - 1) / static_cast<unsigned>(bpr));
+  auto div_bpr = [&](int t) { return static_cast<int>(__umulhi(static_cast<uint32_t>(t), dm) >> (dl - 1)); };
   // quantize + store one block (row < rows), then the atom word of 4 lanes
   auto finish = [&](const uint4& v0, const uint4& v1, int row, int b) {
     uint8_t sfc = 0;
@@ -270,20 +276,19 @@ k_quant_nvfp4_tensor(const __nv_bfloat16* __restrict__ x, int rows, int cols, co
       const uint2 packed = nvfp4_block_fast(v0, v1, g, g6, rg, sfc);
       *reinterpret_cast<uint2*>(q + static_cast<long long>(row) * (cols >> 1) + b * 8) = packed;
     }
-    // blocks b .. b+3 (b % 4 == 0) of one row share a 4-byte word of the atom row
-    const uint32_t s0 = sfc;
-    const uint32_t s1 = __shfl_down_sync(0xffffffffu, s0, 1);
-    const uint32_t s2 = __shfl_down_sync(0xffffffffu, s0, 2);
-    const uint32_t s3 = __shfl_down_sync(0xffffffffu, s0, 3);
-    if ((b & 3) == 0)
-      *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(row, b, ka_per_rowblock)) = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
+    // blocks b .. b+3 (b % 4 == 0) of one row share a 4-byte word of the atom
+    // row: lanes 4i .. 4i + 3 hold them (b & 3 == lane & 3), OR-reduced
+    uint32_t wd = static_cast<uint32_t>(sfc) << (8 * (b & 3));
+    wd |= __shfl_xor_sync(0xffffffffu, wd, 1);
+    wd |= __shfl_xor_sync(0xffffffffu, wd, 2);
+    if ((b & 3) == 0) *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(row, b, ka_per_rowblock)) = wd;
   };
   // two chunks per iteration: both chunks' loads are in flight before either
   // is quantized (chunk indices are warp-uniform, so are the branches)
   for (int ch = (blockIdx.x * 256 + threadIdx.x) / 32; ch < chunks; ch += 2 * cstride) {
     const int ch2 = ch + cstride;
     const int t = (chunks - 1 - ch) * 32 + lane;
-    const int row = t / bpr, b = t - row * bpr;
+    const int row = div_bpr(t), b = t - row * bpr;
     uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0, w0 = v0, w1 = v0;
     if (row < rows) {
       const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<long long>(row) * cols + b * 16);
@@ -293,7 +298,7 @@ k_quant_nvfp4_tensor(const __nv_bfloat16* __restrict__ x, int rows, int cols, co
     int row2 = rows, b2 = 0;
     if (ch2 < chunks) {
       const int t2 = (chunks - 1 - ch2) * 32 + lane;
-      row2 = t2 / bpr;
+      row2 = div_bpr(t2);
       b2 = t2 - row2 * bpr;
       if (row2 < rows) {
         const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<long long>(row2) * cols + b2 * 16);
