@@ -69,7 +69,7 @@ struct EpiParams {
 constexpr int kMaxTailTiles = 128;
 constexpr int kMaxPeers = 8;
 
-template <MmaKind KIND, int BN_, int STAGES_>
+template <MmaKind KIND, int BN_, int STAGES_, bool EPI_TMA_ = false>
 struct GemmCfg {
   static constexpr int BM = 128;
   static constexpr int BN = BN_;
@@ -90,10 +90,11 @@ struct GemmCfg {
   static constexpr int TMEM_COLS = (TMEM_NEED <= 32) ? 32 : (TMEM_NEED <= 64) ? 64 : (TMEM_NEED <= 128) ? 128 : (TMEM_NEED <= 256) ? 256 : 512;
   static constexpr int COLPARAM_BYTES = 2 * BN * (4 + 2);  // double-buffered column scales + bias
   static constexpr int BAR_BYTES = 256;
-  // 128-wide 8-bit / bf16 tiles store their bf16 results through one
-  // 128-byte-swizzled 32 x 64 shared-memory box per epilogue warp and a TMA
-  // store (row-per-lane global stores write 32 rows per warp instruction)
-  static constexpr bool TMA_OUT = (BN == 128 && !NVF4);
+  // k_gemm_tc's 128- and 192-wide 8-bit / bf16 tiles store their bf16
+  // results through one swizzled 32 x 64 (or 32 x 32) shared-memory box per
+  // epilogue warp and a TMA store (row-per-lane global stores write 32 rows
+  // per warp instruction)
+  static constexpr bool TMA_OUT = EPI_TMA_ && !NVF4 && (BN == 128 || BN == 192);
   static constexpr int STAGING_BYTES = TMA_OUT ? 8 * 32 * 64 * 2 : 0;
   static constexpr int SMEM_BYTES =
       STAGES * STAGE_BYTES + STAGING_BYTES + COLPARAM_BYTES + BAR_BYTES + 1024;  // + alignment slack
@@ -242,8 +243,8 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[W], const Epi
 template <MmaKind KIND, int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const EpiParams p,
-          const __grid_constant__ CUtensorMap tmD) {
-  using C = GemmCfg<KIND, BN, STAGES>;
+          const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmD32) {
+  using C = GemmCfg<KIND, BN, STAGES, true>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -432,17 +433,21 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         if (n0 >= p.N) break;  // warp-uniform
         if constexpr (C::TMA_OUT) {
           if (!(p.flags & kEpiRawAcc)) {
-            // this warp's 32 x 64 box, one 32-column chunk at a time, rows
-            // swizzled (16-byte chunk q of row r at q ^ (r & 7)); one TMA
-            // store into D, clipped to [M, N]
+            // this warp's 32 x 64 box (a 32 x 32 box for the last 32 columns
+            // of a 192-wide tile's half), one 32-column chunk at a time; rows
+            // swizzled (64-column box: 16-byte chunk q of row r at q ^ (r & 7),
+            // 128-byte rows; 32-column box: q ^ ((r >> 1) & 3), 64-byte rows);
+            // one TMA store into D, clipped to [M, N]
             const int j0 = half * COLS + c;
+            const bool wide = (COLS - c) >= 64;  // warp-uniform
             uint8_t* box = staging + (warp - kFirstEpiWarp) * (32 * 64 * 2);
             if (lane == 0) bulk_wait_read_all();  // the previous box has left shared memory
             __syncwarp();
-            uint4* dst = reinterpret_cast<uint4*>(box + lane * 128);
-            const int sw = lane & 7;
+            uint4* dst = reinterpret_cast<uint4*>(box + lane * (wide ? 128 : 64));
+            const int sw = wide ? (lane & 7) : ((lane >> 1) & 3);
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
+              if (hh == 1 && !wide) break;
               uint32_t r[32], pk[16];
               tmem_ld_32x32b_x32(taddr + c + 32 * hh, r);
               tmem_ld_wait();
@@ -454,7 +459,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_2d(&tmD, box, n0, mb * C::BM + wq * 32);
+              tma_store_2d(wide ? &tmD : &tmD32, box, n0, mb * C::BM + wq * 32);
               bulk_commit_group();
             }
             continue;

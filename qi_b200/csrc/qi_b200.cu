@@ -195,7 +195,7 @@ enum PlanKernel { kPlanGemmI8 = 1, kPlanGemmF8 = 2, kPlanGemmBF16 = 3, kPlanGemm
 // ---------------------------------------------------------------------------
 template <MmaKind KIND, int BN, int STAGES>
 static int launch_gemm_cfg(const void* A, const void* B, const EpiParams& p, int num_sms, cudaStream_t stream) {
-  using C = GemmCfg<KIND, BN, STAGES>;
+  using C = GemmCfg<KIND, BN, STAGES, true>;
   const CUtensorMapDataType dt =
       (KIND == MmaKind::BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const uint64_t ku = C::NVF4 ? (uint64_t)p.K / 2 : (uint64_t)p.K;  // K in TMA elements (fp4: packed bytes)
@@ -204,11 +204,16 @@ static int launch_gemm_cfg(const void* A, const void* B, const EpiParams& p, int
   if (rc) return rc;
   rc = make_tmap_2d(&tb, B, dt, ku, (uint64_t)p.N, ku * C::ELEM, C::BK, BN);
   if (rc) return rc;
-  CUtensorMap td = {};  // bf16 output boxes of 32 rows x 64 columns (TMA-store epilogue)
+  CUtensorMap td = {}, td32 = {};  // bf16 output boxes of 32 rows x 64 (32) columns (TMA-store epilogue)
   if (C::TMA_OUT && !(p.flags & kEpiRawAcc)) {
     rc = make_tmap_2d(&td, p.D, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)p.N, (uint64_t)p.M, (uint64_t)p.ldd * 2,
                       64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
+    if (BN == 192) {
+      rc = make_tmap_2d(&td32, p.D, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)p.N, (uint64_t)p.M,
+                        (uint64_t)p.ldd * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+      if (rc) return rc;
+    }
   }
   static bool attr_done[kMaxDevices] = {};
   int dev = 0;
@@ -223,7 +228,7 @@ static int launch_gemm_cfg(const void* A, const void* B, const EpiParams& p, int
   const int grid = tiles < num_sms ? tiles : num_sms;
   g_last_plan = {1 + static_cast<int>(KIND), grid, 1, BN, STAGES, C::SMEM_BYTES};
   const cudaError_t e =
-      launch_pdl(k_gemm_tc<KIND, BN, STAGES>, dim3(grid), dim3(kGemmThreads), C::SMEM_BYTES, stream, 1, ta, tb, p, td);
+      launch_pdl(k_gemm_tc<KIND, BN, STAGES>, dim3(grid), dim3(kGemmThreads), C::SMEM_BYTES, stream, 1, ta, tb, p, td, td32);
   count_launches(1);
   return e == cudaSuccess ? QI_B200_OK : QI_B200_ECUDA;
 }
@@ -445,7 +450,7 @@ static int launch_gemm(const void* A, const void* B, const EpiParams& p, cudaStr
       return launch_gemm2_cfg<KIND, 256, 5>(A, B, p, di->num_sms, stream);
     switch (bn) {
       case 256: return launch_gemm_cfg<KIND, 256, 4>(A, B, p, di->num_sms, stream);
-      case 192: return launch_gemm_cfg<KIND, 192, 5>(A, B, p, di->num_sms, stream);
+      case 192: return launch_gemm_cfg<KIND, 192, 4>(A, B, p, di->num_sms, stream);
       case 128: return launch_gemm_cfg<KIND, 128, 6>(A, B, p, di->num_sms, stream);
       case 64: return launch_gemm_cfg<KIND, 64, 8>(A, B, p, di->num_sms, stream);
       default: return QI_B200_EINVAL;
