@@ -109,40 +109,6 @@ k_amax_bf16(const __nv_bfloat16* __restrict__ x, long long n, unsigned int* __re
   }
 }
 
-// Quantize one 16-element block: returns the packed E2M1 codes (8 bytes) and
-// the E4M3 block-scale code.
-__device__ __forceinline__ uint2 nvfp4_block(const uint4& v0, const uint4& v1, float g, uint8_t& sfc) {
-  float f[16];
-  const __nv_bfloat162* h0 = reinterpret_cast<const __nv_bfloat162*>(&v0);
-  const __nv_bfloat162* h1 = reinterpret_cast<const __nv_bfloat162*>(&v1);
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float2 a = __bfloat1622float2(h0[k]), c = __bfloat1622float2(h1[k]);
-    f[2 * k] = a.x;
-    f[2 * k + 1] = a.y;
-    f[8 + 2 * k] = c.x;
-    f[8 + 2 * k + 1] = c.y;
-  }
-  float bm = 0.f;
-#pragma unroll
-  for (int k = 0; k < 16; ++k) bm = fmaxf(bm, fabsf(f[k]));
-  const float sfv = fminf(__fdiv_rn(bm, __fmul_rn(6.0f, g)), 448.0f);
-  sfc = static_cast<uint8_t>(__nv_cvt_float_to_fp8(sfv, __NV_SATFINITE, __NV_E4M3));
-  __half_raw hr = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(sfc), __NV_E4M3);
-  const float sff = __half2float(__half(hr));
-  const float denom = __fmul_rn(sff, g);
-  uint32_t lo = 0, hi = 0;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const float a = denom > 0.f ? fminf(fmaxf(__fdiv_rn(f[2 * k], denom), -6.f), 6.f) : 0.f;
-    const float c = denom > 0.f ? fminf(fmaxf(__fdiv_rn(f[2 * k + 1], denom), -6.f), 6.f) : 0.f;
-    const uint32_t byte = e2m1x2(a, c);
-    if (k < 4) lo |= byte << (8 * k);
-    else hi |= byte << (8 * (k - 4));
-  }
-  return make_uint2(lo, hi);
-}
-
 __device__ __forceinline__ float rcp_approx(float v) {
   float r;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
@@ -172,8 +138,8 @@ __device__ __forceinline__ uint32_t e2m1x8(float2 a, float2 b, float2 c, float2 
   return out;
 }
 
-// nvfp4_block with divisions only where they decide the result, for a
-// per-tensor g.  Each quotient the recipe rounds (bm / fl(6 g) for the block
+// One 16-element block -> its packed E2M1 codes (8 bytes) and E4M3 block-scale
+// code, with divisions only where they decide the result, for a given g.  Each quotient the recipe rounds (bm / fl(6 g) for the block
 // scale, x / fl(sf g) for the codes) is bracketed by two products with a
 // reciprocal widened by +-2^-20 (8 ulp, more than the approximate
 // reciprocal's and the products' rounding): the exact quotient and its fp32
@@ -311,16 +277,17 @@ k_quant_nvfp4_tensor(const __nv_bfloat16* __restrict__ x, int rows, int cols, co
   }
 }
 
-// One thread per 16-element block.  GMODE: 0 = per-tensor g from *g_in,
-// 1 = per-tensor g from *amax_bits (g written to g_out[0]), 2 = per-row g
-// (the row's amax is reduced here first; g written to g_out[row]).
-// cols % 16 == 0.  Scale-factor entries of the padding rows (up to the next
-// multiple of 128) are written as zero so the GEMM never reads stale bytes.
+// Per-row g (GMODE 2; the per-tensor modes run k_quant_nvfp4_tensor): a CTA
+// per row reduces the row's amax, writes g to g_out[row], then one thread per
+// 16-element block.  cols % 16 == 0.  Scale-factor entries of the padding
+// rows (up to the next multiple of 128) are written as zero so the GEMM never
+// reads stale bytes.
 template <int GMODE>
 __global__ void __launch_bounds__(256)
 k_quant_nvfp4(const __nv_bfloat16* __restrict__ x, int rows, int cols, const float* __restrict__ g_in,
               const unsigned int* __restrict__ amax_bits, float* __restrict__ g_out, uint8_t* __restrict__ q,
               uint8_t* __restrict__ sf, int ka_per_rowblock) {
+  static_assert(GMODE == 2, "per-row g only");
   griddep_wait();
   griddep_launch_dependents();
   const int bpr = cols >> 4;  // blocks per row
@@ -364,27 +331,6 @@ k_quant_nvfp4(const __nv_bfloat16* __restrict__ x, int rows, int cols, const flo
       __syncthreads();
     }
     return;
-  }
-  float g;
-  if (GMODE == 0) {
-    g = __ldg(g_in);
-  } else {
-    g = nvfp4_g_from_amax(__uint_as_float(*amax_bits));
-    if (blockIdx.x == 0 && threadIdx.x == 0) g_out[0] = g;
-  }
-  const long long total = static_cast<long long>(rows_pad) * bpr;
-  for (long long t = blockIdx.x * 256ll + threadIdx.x; t < total; t += 256ll * gridDim.x) {
-    const int row = static_cast<int>(t / bpr);
-    const int b = static_cast<int>(t - static_cast<long long>(row) * bpr);
-    if (row >= rows) {
-      sf[sf_atom_offset(row, b, ka_per_rowblock)] = 0;
-      continue;
-    }
-    const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<long long>(row) * cols + b * 16);
-    uint8_t sfc;
-    const uint2 packed = nvfp4_block(__ldg(p), __ldg(p + 1), g, sfc);
-    *reinterpret_cast<uint2*>(q + static_cast<long long>(row) * (cols >> 1) + b * 8) = packed;
-    sf[sf_atom_offset(row, b, ka_per_rowblock)] = sfc;
   }
 }
 
